@@ -1,0 +1,64 @@
+// Python bindings of the sm_100a kernels (module sglang_neuron_b200._C).
+#include <torch/extension.h>
+
+// norm.cu
+void rmsnorm_out(torch::Tensor out, torch::Tensor x, torch::Tensor weight, double eps, bool weight_plus_one);
+void fused_add_rmsnorm(torch::Tensor x, torch::Tensor residual, torch::Tensor weight, double eps,
+                       bool weight_plus_one);
+void head_rmsnorm_(torch::Tensor x, torch::Tensor weight, int64_t heads, double eps);
+// rope_kv.cu
+void rope_qk_norm_kv_write(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor positions,
+                           torch::Tensor cos_sin, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                           int64_t rot_dim, bool neox, c10::optional<torch::Tensor> q_norm_w,
+                           c10::optional<torch::Tensor> k_norm_w, double norm_eps, torch::Tensor k_cache,
+                           torch::Tensor v_cache, torch::Tensor slots, int64_t page_size, double k_scale,
+                           double v_scale);
+// attention.cu
+void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                      torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
+                      int64_t head_dim, int64_t page_size, int64_t window, double sm_scale, double k_scale,
+                      double v_scale, c10::optional<torch::Tensor> sinks, int64_t num_splits, torch::Tensor o_part,
+                      torch::Tensor lse_part);
+void extend_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                      torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
+                      int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t page_size,
+                      int64_t window, double sm_scale, double k_scale, double v_scale,
+                      c10::optional<torch::Tensor> sinks);
+// sampling.cu
+void sample_tokens(torch::Tensor out_ids, torch::Tensor logits, c10::optional<torch::Tensor> temperature,
+                   c10::optional<torch::Tensor> seeds, c10::optional<torch::Tensor> positions,
+                   c10::optional<torch::Tensor> out_vals, int64_t vocab_offset, int64_t valid_vocab);
+// moe_route.cu
+void topk_route(torch::Tensor weights, torch::Tensor ids, torch::Tensor logits, int64_t k, int64_t mode, double scale);
+void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, torch::Tensor seg_offsets,
+               torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map);
+void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
+                        int64_t bn);
+void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, bool accumulate);
+// moe_gemm_sm100.cu
+void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
+              c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets, int64_t bn,
+              int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status);
+// activation.cu
+void silu_and_mul(torch::Tensor out, torch::Tensor x);
+// gemm_sm100.cu
+void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+               torch::Tensor status, int64_t bn);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sglang_neuron_b200 sm_100a kernels";
+  m.def("rmsnorm_out", &rmsnorm_out);
+  m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
+  m.def("head_rmsnorm_", &head_rmsnorm_);
+  m.def("rope_qk_norm_kv_write", &rope_qk_norm_kv_write);
+  m.def("decode_attention", &decode_attention);
+  m.def("extend_attention", &extend_attention);
+  m.def("sample_tokens", &sample_tokens);
+  m.def("topk_route", &topk_route);
+  m.def("moe_align", &moe_align);
+  m.def("gather_quant_mxfp8", &gather_quant_mxfp8);
+  m.def("moe_combine", &moe_combine);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("moe_gemm", &moe_gemm);
+  m.def("silu_and_mul", &silu_and_mul);
+}

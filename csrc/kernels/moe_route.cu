@@ -1,0 +1,282 @@
+// MoE routing: top-k gating, counting-sort permutation into padded expert segments, MXFP8 gather-quantise
+// of the permuted rows, and the weighted combine.
+//
+// Parity: the reference routes in its fused MoE kernels (`moe_block_tkg`, sglang_neuron/ops/moe/moe_block_tkg.py:19-128,
+// router softmax + top-k) and builds a token->block mapping for prefill (`build_blockwise_mapping`,
+// sglang_neuron/ops/moe/moe_blockwise.py:24-130). Here the mapping is a device counting sort whose output
+// sizes have a static upper bound (T*K + E*(BN-1) rows), so the whole MoE path is CUDA-graph capturable.
+//
+// Activation quantisation follows the OCP MX format: blocks of 32 values share an e8m0 power-of-two scale
+// 2^X with X = ceil(log2(amax / 448)), values are e4m3 (max 448). Scales of a permuted row r are written in
+// the tensor-memory scale-factor atom order consumed by tcgen05.cp (32x128b.warpx4): within a chunk of one
+// BN-row tile and one 128-wide K block, the byte for (row i, 32-block kk) sits at (i%32)*16 + (i/32)*4 + kk.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "../common.cuh"
+
+namespace {
+
+// One warp per token. mode 0: softmax over the k selected logits (renormalised top-k);
+// mode 1: softmax over all E logits, then the top-k probabilities (times `scale`).
+template <typename T>
+__global__ void topk_route_kernel(const T* __restrict__ logits, int T_tok, int E, int K, int mode, float scale,
+                                  float* __restrict__ w_out, int32_t* __restrict__ id_out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T_tok) return;
+  const T* lr = logits + (size_t)warp * E;
+  float v[8];
+  const int per = (E + 31) / 32;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (i < per && e < E) ? (float)lr[e] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+  mx = snb::warp_max(mx);
+  float denom_all = 0.f;
+  if (mode == 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) denom_all += (v[i] == -INFINITY) ? 0.f : __expf(v[i] - mx);
+    denom_all = snb::warp_sum(denom_all);
+  }
+  float sel_v[16];
+  int sel_i[16];
+  for (int j = 0; j < K; ++j) {
+    // warp argmax (ties -> smallest expert id)
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (v[i] > bv || (v[i] == bv && e < bi)) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    sel_v[j] = bv;
+    sel_i[j] = bi;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i == bi) v[i] = -INFINITY;
+  }
+  if (lane == 0) {
+    if (mode == 0) {
+      float s = 0.f;
+      for (int j = 0; j < K; ++j) s += __expf(sel_v[j] - sel_v[0]);
+      for (int j = 0; j < K; ++j) {
+        w_out[(size_t)warp * K + j] = __expf(sel_v[j] - sel_v[0]) / s * scale;
+        id_out[(size_t)warp * K + j] = sel_i[j];
+      }
+    } else {
+      for (int j = 0; j < K; ++j) {
+        w_out[(size_t)warp * K + j] = __expf(sel_v[j] - mx) / denom_all * scale;
+        id_out[(size_t)warp * K + j] = sel_i[j];
+      }
+    }
+  }
+}
+
+// Single-CTA counting sort of (token, slot) entries by expert into BN-padded segments.
+// Entries whose expert is outside [e_lo, e_lo + E_local) are dropped (expert parallelism: another rank owns them).
+__global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restrict__ ids, int N_entries, int K,
+                                                         int e_lo, int E_local, int BN,
+                                                         int32_t* __restrict__ seg_offsets,   // [E_local+1]
+                                                         int32_t* __restrict__ tile_offsets,  // [E_local+1]
+                                                         int32_t* __restrict__ sorted_src,    // [R_max]
+                                                         int32_t* __restrict__ inv_map,       // [N_entries]
+                                                         int R_max) {
+  extern __shared__ int32_t sm[];
+  int32_t* cnt = sm;                 // E_local
+  int32_t* off = sm + E_local;       // E_local + 1
+  int32_t* cur = off + E_local + 1;  // E_local
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
+    cnt[e] = 0;
+    cur[e] = 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < N_entries; i += blockDim.x) {
+    const int e = ids[i] - e_lo;
+    if (e >= 0 && e < E_local) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, tiles = 0;
+    for (int e = 0; e < E_local; ++e) {
+      off[e] = acc;
+      seg_offsets[e] = acc;
+      tile_offsets[e] = tiles;
+      const int padded = ((cnt[e] + BN - 1) / BN) * BN;
+      acc += padded;
+      tiles += padded / BN;
+    }
+    off[E_local] = acc;
+    seg_offsets[E_local] = acc;
+    tile_offsets[E_local] = tiles;
+  }
+  __syncthreads();
+  const int total = off[E_local];
+  for (int r = threadIdx.x; r < R_max; r += blockDim.x) sorted_src[r] = -1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < N_entries; i += blockDim.x) {
+    const int e = ids[i] - e_lo;
+    if (e >= 0 && e < E_local) {
+      const int p = off[e] + atomicAdd(&cur[e], 1);
+      sorted_src[p] = i / K;
+      inv_map[i] = p;
+    } else {
+      inv_map[i] = -1;
+    }
+  }
+  (void)total;
+}
+
+// One warp per permuted row; each lane quantises whole 32-element blocks.
+// x: [T, H] bf16 (row stride xs). Output q: [R, Kp] e4m3 (Kp = padded row pitch), scales in atom order.
+__global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int xs, const int32_t* __restrict__ src,
+                                          int R, int H, int Kp, int BN, uint8_t* __restrict__ q,
+                                          uint8_t* __restrict__ sf) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const int s = src != nullptr ? src[r] : r;
+  const int KB = (Kp + 127) / 128;           // 128-wide K blocks
+  const int nblk = KB * 4;                    // 32-wide scale blocks incl. padding
+  const int chunk_bytes = min(BN, 32) * 16;
+  const int tile = r / BN, i = r % BN;
+  uint8_t* qrow = q + (size_t)r * Kp;
+  for (int blk = lane; blk < nblk; blk += 32) {
+    const int k0 = blk * 32;
+    uint8_t e8 = 127;
+    if (s >= 0 && k0 < H) {
+      float f[32];
+      const __nv_bfloat16* xr = x + (size_t)s * xs + k0;
+      float amax = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float t8[8];
+        snb::unpack_bf16x8(reinterpret_cast<const uint4*>(xr)[c], t8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          f[c * 8 + j] = t8[j];
+          amax = fmaxf(amax, fabsf(t8[j]));
+        }
+      }
+      int X = 0;
+      if (amax > 0.f) {
+        X = (int)ceilf(log2f(amax / 448.f));
+        X = max(-127, min(127, X));
+      }
+      e8 = (uint8_t)(X + 127);
+      const float inv = exp2f((float)-X);
+      uint8_t ob[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ob[j] = snb::f_to_fp8e4m3(f[j] * inv);
+      reinterpret_cast<uint4*>(qrow + k0)[0] = *reinterpret_cast<uint4*>(ob);
+      reinterpret_cast<uint4*>(qrow + k0)[1] = *reinterpret_cast<uint4*>(ob + 16);
+    } else if (k0 < Kp) {
+      reinterpret_cast<uint4*>(qrow + k0)[0] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(qrow + k0)[1] = make_uint4(0, 0, 0, 0);
+    }
+    const int kb = blk >> 2, kk = blk & 3;
+    sf[((size_t)tile * KB + kb) * chunk_bytes + (i % 32) * 16 + (i / 32) * 4 + kk] = e8;
+  }
+}
+
+// out[t] = sum_j w[t, j] * y[inv_map[t*K + j]]  (+ out[t] if accumulate). One CTA per token.
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ys, const int32_t* __restrict__ inv_map,
+                                   const float* __restrict__ w, int K, int H, __nv_bfloat16* __restrict__ out,
+                                   int os, bool accumulate) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+    float acc[8];
+    if (accumulate) {
+      snb::unpack_bf16x8(reinterpret_cast<const uint4*>(out + (size_t)t * os)[c], acc);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    }
+    for (int j = 0; j < K; ++j) {
+      const int r = inv_map[t * K + j];
+      if (r < 0) continue;
+      const float wj = w[t * K + j];
+      float f[8];
+      snb::unpack_bf16x8(reinterpret_cast<const uint4*>(y + (size_t)r * ys)[c], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += wj * f[i];
+    }
+    reinterpret_cast<uint4*>(out + (size_t)t * os)[c] = snb::pack_bf16x8(acc);
+  }
+}
+
+}  // namespace
+
+void topk_route(torch::Tensor weights, torch::Tensor ids, torch::Tensor logits, int64_t k, int64_t mode,
+                double scale) {
+  const int T = logits.size(0), E = logits.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(E <= 256 && k <= 16 && k <= E, "topk_route: E<=256, k<=16");
+  TORCH_CHECK(logits.is_contiguous(), "topk_route: contiguous logits");
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int threads = 256, blocks = (T * 32 + threads - 1) / threads;
+  if (logits.scalar_type() == at::kFloat) {
+    topk_route_kernel<float><<<blocks, threads, 0, st>>>(logits.data_ptr<float>(), T, E, k, mode, scale,
+                                                         weights.data_ptr<float>(), ids.data_ptr<int32_t>());
+  } else {
+    topk_route_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>((const __nv_bfloat16*)logits.data_ptr(), T, E, k,
+                                                                 mode, scale, weights.data_ptr<float>(),
+                                                                 ids.data_ptr<int32_t>());
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, torch::Tensor seg_offsets,
+               torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map) {
+  const int N = ids.numel();
+  const int K = ids.dim() == 2 ? ids.size(1) : 1;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int R_max = sorted_src.numel();
+  TORCH_CHECK(R_max >= N + e_local * (bn - 1), "moe_align: sorted_src capacity too small");
+  const size_t smem = (3 * e_local + 1) * sizeof(int32_t);
+  moe_align_kernel<<<1, 1024, smem, st>>>(ids.data_ptr<int32_t>(), N, K, e_lo, e_local, bn,
+                                          seg_offsets.data_ptr<int32_t>(), tile_offsets.data_ptr<int32_t>(),
+                                          sorted_src.data_ptr<int32_t>(), inv_map.data_ptr<int32_t>(), R_max);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
+                        int64_t bn) {
+  const int R = q.size(0), Kp = q.size(1), H = x.size(1);
+  if (R == 0) return;
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && H % 32 == 0, "gather_quant: x");
+  TORCH_CHECK(Kp >= H && Kp % 16 == 0, "gather_quant: pitch");
+  TORCH_CHECK(R % bn == 0, "gather_quant: rows must be a multiple of bn");
+  const int KB = (Kp + 127) / 128;
+  TORCH_CHECK(sf.numel() >= (int64_t)(R / bn) * KB * std::min<int64_t>(bn, 32) * 16, "gather_quant: sf capacity");
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int threads = 256, blocks = (R * 32 + threads - 1) / threads;
+  gather_quant_mxfp8_kernel<<<blocks, threads, 0, st>>>((const __nv_bfloat16*)x.data_ptr(), x.stride(0),
+                                                       src ? src->data_ptr<int32_t>() : nullptr, R, H, Kp, bn,
+                                                       (uint8_t*)q.data_ptr(), (uint8_t*)sf.data_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, bool accumulate) {
+  const int T = out.size(0), H = out.size(1);
+  if (T == 0) return;
+  const int K = w.size(1);
+  TORCH_CHECK(H % 8 == 0, "moe_combine: H");
+  auto st = at::cuda::getCurrentCUDAStream();
+  moe_combine_kernel<<<T, 128, 0, st>>>((const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
+                                        w.data_ptr<float>(), K, H, (__nv_bfloat16*)out.data_ptr(), out.stride(0),
+                                        accumulate);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,83 @@
+"""Token sampling: greedy argmax (ties to the smallest id) and temperature sampling by Gumbel-max with
+noise that is a pure function of (seed, position, token id)."""
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .._ext import kernels
+
+_M64 = (1 << 64) - 1
+
+
+def _mix64(z: np.ndarray) -> np.ndarray:
+    z = (z + np.uint64(0x9E3779B97F4A7C15)) & np.uint64(_M64)
+    z = ((z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)) & np.uint64(_M64)
+    z = ((z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)) & np.uint64(_M64)
+    return z ^ (z >> np.uint64(31))
+
+
+def gumbel_noise_ref(seed: int, pos: int, vocab: int) -> torch.Tensor:
+    """Same construction as the kernel: u from the top 24 bits of a 64-bit mix, g = -log(-log(u))."""
+    with np.errstate(over="ignore"):
+        tok = np.arange(vocab, dtype=np.uint64)
+        inner = _mix64(np.uint64(pos % (1 << 64)) * np.uint64(0x100000001B3) ^ _mix64(tok))
+        h = _mix64(np.uint64(seed % (1 << 64)) ^ inner)
+    u = ((h >> np.uint64(40)).astype(np.float64) + 0.5) / 16777216.0
+    return torch.from_numpy(-np.log(-np.log(u))).float()
+
+
+def sample_ref(logits: torch.Tensor, temperature: Optional[torch.Tensor] = None,
+               seeds: Optional[torch.Tensor] = None, positions: Optional[torch.Tensor] = None,
+               vocab_offset: int = 0, valid_vocab: int = 0, return_vals: bool = False):
+    B = logits.shape[0]
+    V = valid_vocab if valid_vocab > 0 else logits.shape[1]
+    out = torch.empty(B, dtype=torch.long)
+    vals = torch.empty(B, dtype=torch.float32)
+    lf = logits[:, :V].float().cpu()
+    for b in range(B):
+        t = float(temperature[b]) if temperature is not None else 0.0
+        row = lf[b]
+        if t > 0:
+            s = int(seeds[b]) if seeds is not None else 0
+            p = int(positions[b]) if positions is not None else 0
+            row = row / t + gumbel_noise_ref(s, p, V + vocab_offset)[vocab_offset:]
+        m = row.max()
+        out[b] = int(torch.nonzero(row == m)[0, 0]) + vocab_offset
+        vals[b] = m
+    if return_vals:
+        return out.to(logits.device), vals.to(logits.device)
+    return out.to(logits.device)
+
+
+def sample_tokens(logits: torch.Tensor, temperature: Optional[torch.Tensor] = None,
+                  seeds: Optional[torch.Tensor] = None, positions: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None, out_vals: Optional[torch.Tensor] = None,
+                  vocab_offset: int = 0, valid_vocab: int = 0) -> torch.Tensor:
+    if not logits.is_cuda:
+        r, v = sample_ref(logits, temperature, seeds, positions, vocab_offset, valid_vocab, return_vals=True)
+        if out_vals is not None:
+            out_vals.copy_(v)
+        if out is not None:
+            out.copy_(r)
+            return out
+        return r
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
+    kernels().sample_tokens(out, logits, temperature, seeds, positions, out_vals, vocab_offset, valid_vocab)
+    return out
+
+
+def apply_top_k_top_p(logits: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor) -> torch.Tensor:
+    """Mask logits outside each row's top-k / nucleus top-p set to -inf (rows with k<=0 and p>=1 untouched)."""
+    sorted_l, idx = logits.float().sort(dim=-1, descending=True)
+    V = logits.shape[-1]
+    ar = torch.arange(V, device=logits.device)[None, :]
+    k = torch.where(top_k > 0, top_k, torch.full_like(top_k, V))
+    mask = ar >= k[:, None]
+    probs = sorted_l.softmax(-1)
+    cum = probs.cumsum(-1) - probs
+    mask |= cum > top_p[:, None].float()
+    sorted_l = sorted_l.masked_fill(mask, float("-inf"))
+    out = torch.empty_like(sorted_l).scatter_(-1, idx, sorted_l)
+    return out.to(logits.dtype)

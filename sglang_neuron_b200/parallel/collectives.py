@@ -1,0 +1,73 @@
+"""Device collectives of the model forward.
+
+The default path is NCCL through torch.distributed (graph-capturable). When a fused NVLink
+communicator is registered for the TP group (parallel/symm_mem.py), all-reduce goes through it instead.
+Parity: the reference's traced collectives (sglang_neuron/parallel/collectives.py:22-55).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .state import get_state
+
+_custom_allreduce = None
+
+
+def set_custom_allreduce(comm) -> None:
+    global _custom_allreduce
+    _custom_allreduce = comm
+
+
+def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
+    st = get_state()
+    if st.tp_size == 1:
+        return x
+    if _custom_allreduce is not None and _custom_allreduce.can_run(x):
+        return _custom_allreduce.all_reduce(x)
+    dist.all_reduce(x, group=st.tp_group)
+    return x
+
+
+def tp_all_gather(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    st = get_state()
+    if st.tp_size == 1:
+        return x
+    parts = [torch.empty_like(x) for _ in range(st.tp_size)]
+    dist.all_gather(parts, x.contiguous(), group=st.tp_group)
+    return torch.cat(parts, dim=dim)
+
+
+def tp_all_gather_into(out: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """out: [tp_size * x.shape[0], ...] gathered along dim 0."""
+    st = get_state()
+    if st.tp_size == 1:
+        out.copy_(x)
+        return out
+    dist.all_gather_into_tensor(out, x.contiguous(), group=st.tp_group)
+    return out
+
+
+def tp_reduce_scatter(x: torch.Tensor) -> torch.Tensor:
+    st = get_state()
+    if st.tp_size == 1:
+        return x
+    out = torch.empty((x.shape[0] // st.tp_size,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.reduce_scatter_tensor(out, x.contiguous(), group=st.tp_group)
+    return out
+
+
+def cpu_broadcast_object(obj, src: int = 0):
+    """Broadcast a picklable object over the host (gloo) group of the TP world."""
+    st = get_state()
+    if st.tp_size == 1:
+        return obj
+    buf = [obj]
+    dist.broadcast_object_list(buf, src=src + st.dp_rank * st.tp_size, group=st.cpu_group)
+    return buf[0]
+
+
+def cpu_barrier() -> None:
+    st = get_state()
+    if st.tp_size > 1:
+        dist.barrier(group=st.cpu_group)

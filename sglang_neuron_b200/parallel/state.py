@@ -1,0 +1,103 @@
+"""Parallel state: tensor-parallel (attention and dense MLP), expert-parallel (MoE) and data-parallel
+groups over one process per GPU.
+
+Parity: the reference builds its groups in `initialize_neuron_parallel_state`
+(sglang_neuron/parallel/state.py:77-152) with attention-TP, EP-TP and EP groups and group getters
+(parallel/groups.py:158-211). On B200 the device groups are NCCL communicators created through
+torch.distributed (one process per GPU); host-side control collectives use a gloo group, as in the
+reference (gloo on the host). EP here spans the same ranks as TP: experts are split in contiguous blocks
+by rank (`ep_group_ranks` rows = EP) and tokens are replicated over the group after attention.
+"""
+from __future__ import annotations
+
+import dataclasses
+import os
+from datetime import timedelta
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+
+@dataclasses.dataclass
+class ParallelState:
+    world_size: int = 1
+    rank: int = 0
+    tp_size: int = 1
+    tp_rank: int = 0
+    ep_size: int = 1
+    ep_rank: int = 0
+    dp_size: int = 1
+    dp_rank: int = 0
+    tp_group: Optional[object] = None      # device (NCCL or gloo on CPU) group
+    cpu_group: Optional[object] = None     # gloo group for host control
+    device: torch.device = torch.device("cpu")
+
+    @property
+    def is_first_rank(self) -> bool:
+        return self.tp_rank == 0
+
+
+_STATE = ParallelState()
+
+
+def get_state() -> ParallelState:
+    return _STATE
+
+
+def set_state(state: ParallelState) -> None:
+    global _STATE
+    _STATE = state
+
+
+def init_process_group_from_env(backend: Optional[str] = None, timeout_s: int = 600) -> None:
+    """Initialise torch.distributed from RANK/WORLD_SIZE/MASTER_ADDR/MASTER_PORT if not done yet."""
+    if dist.is_initialized():
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world <= 1:
+        return
+    if backend is None:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    kwargs = dict(backend=backend, timeout=timedelta(seconds=timeout_s))
+    if backend == "nccl":
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        kwargs["device_id"] = torch.device("cuda", local)
+    dist.init_process_group(**kwargs)
+
+
+def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size: int = 1,
+                        device: Optional[torch.device] = None) -> ParallelState:
+    """Build the groups. Ranks are laid out DP-major: rank = dp_rank * tp_size + tp_rank."""
+    ep_size = tp_size if ep_size is None else ep_size
+    if ep_size != tp_size:
+        raise ValueError("expert parallelism spans the tensor-parallel group here (ep_size must equal tp_size)")
+    if dist.is_initialized():
+        world, rank = dist.get_world_size(), dist.get_rank()
+    else:
+        world, rank = 1, 0
+    if tp_size * dp_size != world:
+        raise ValueError(f"tp_size {tp_size} x dp_size {dp_size} != world size {world}")
+    dp_rank, tp_rank = divmod(rank, tp_size)
+    tp_group = cpu_group = None
+    if world > 1:
+        for d in range(dp_size):
+            ranks = list(range(d * tp_size, (d + 1) * tp_size))
+            g = dist.new_group(ranks)
+            cg = dist.new_group(ranks, backend="gloo")
+            if d == dp_rank:
+                tp_group, cpu_group = g, cg
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    st = ParallelState(world_size=world, rank=rank, tp_size=tp_size, tp_rank=tp_rank, ep_size=ep_size,
+                       ep_rank=tp_rank, dp_size=dp_size, dp_rank=dp_rank, tp_group=tp_group,
+                       cpu_group=cpu_group, device=device)
+    set_state(st)
+    return st
+
+
+def destroy_parallel() -> None:
+    """Reset to a single-rank state (used by tests to build several worlds in one process)."""
+    set_state(ParallelState())

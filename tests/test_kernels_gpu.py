@@ -1,0 +1,219 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _close(a, b, atol, rtol, what=""):
+    a = a.float().cpu()
+    b = b.float().cpu()
+    err = (a - b).abs().max().item()
+    tol = atol + rtol * b.abs().max().item()
+    assert err <= tol, f"{what}: max err {err} > {tol}"
+
+
+def test_extension_loaded():
+    from sglang_neuron_b200._ext import kernels
+    assert kernels() is not None
+
+
+@pytest.mark.parametrize("H", [1024, 2880, 4096])
+def test_rmsnorm(H):
+    from sglang_neuron_b200.ops.norm import rmsnorm, rmsnorm_ref, fused_add_rmsnorm
+    torch.manual_seed(0)
+    x = torch.randn(37, H, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(H, device=DEV, dtype=torch.bfloat16)
+    _close(rmsnorm(x, w, 1e-6), rmsnorm_ref(x.float(), w.float(), 1e-6), 2e-2, 1e-2, "rmsnorm")
+    r = torch.randn_like(x)
+    ref_sum = x.float() + r.float()
+    ref = rmsnorm_ref(ref_sum, w.float(), 1e-6)
+    xx, rr = fused_add_rmsnorm(x.clone(), r.clone(), w, 1e-6)
+    _close(rr, ref_sum, 2e-2, 1e-2, "residual")
+    _close(xx, ref, 3e-2, 2e-2, "fused norm")
+
+
+@pytest.mark.parametrize("D,neox,norm,fp8", [(64, True, False, True), (128, True, True, False), (64, False, False, False)])
+def test_rope_kv_write(D, neox, norm, fp8):
+    from sglang_neuron_b200.ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
+    torch.manual_seed(1)
+    T, Hq, Hkv, P = 21, 8, 2, 16
+    cs = build_cos_sin_cache(D, 4096, 150000.0, {"rope_type": "yarn", "factor": 32.0,
+                                                 "original_max_position_embeddings": 4096,
+                                                 "beta_fast": 32.0, "beta_slow": 1.0, "truncate": False}, DEV)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV, dtype=torch.bfloat16)
+    q, k, v = qkv.split([Hq * D, Hkv * D, Hkv * D], dim=1)
+    pos = torch.randint(0, 4000, (T,), device=DEV)
+    slots = torch.randperm(64, device=DEV)[:T]
+    slots[3] = -1
+    cdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc = torch.zeros(4, Hkv, P, D, device=DEV, dtype=cdt)
+    vc = torch.zeros_like(kc)
+    qn = torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5 if norm else None
+    kn = torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5 if norm else None
+    # CPU reference on copies
+    qkv_c = qkv.cpu().float()
+    qc, kc_ref_in, vc_in = qkv_c.split([Hq * D, Hkv * D, Hkv * D], dim=1)
+    qc, kc_ref_in = qc.clone(), kc_ref_in.clone()
+    kcache_ref = torch.zeros(4, Hkv, P, D, dtype=torch.float32)
+    vcache_ref = torch.zeros_like(kcache_ref)
+    rope_qk_norm_kv_write(qc, kc_ref_in, vc_in, pos.cpu(), cs.cpu(), Hq, Hkv, D, D, neox,
+                          qn.cpu().float() if norm else None, kn.cpu().float() if norm else None, 1e-6,
+                          kcache_ref, vcache_ref, slots.cpu(), P, 0.5 if fp8 else 1.0, 0.25 if fp8 else 1.0)
+    rope_qk_norm_kv_write(q, k, v, pos, cs, Hq, Hkv, D, D, neox, qn, kn, 1e-6, kc, vc, slots, P,
+                          0.5 if fp8 else 1.0, 0.25 if fp8 else 1.0)
+    _close(q, qc, 3e-2, 2e-2, "q")
+    _close(k, kc_ref_in, 3e-2, 2e-2, "k")
+    # fp8 caches hold x / scale; compare dequantised values against the fp32 reference cache
+    ks, vs = (0.5, 0.25) if fp8 else (1.0, 1.0)
+    tol = 0.15 if fp8 else 3e-2
+    _close(kc.float() * ks, kcache_ref, tol, 6e-2, "k cache")
+    _close(vc.float() * vs, vcache_ref, tol, 6e-2, "v cache")
+
+
+def _make_paged(B, ctx_lens, Hkv, D, P, dtype, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    max_pages = max((c + P - 1) // P for c in ctx_lens) + 1
+    n_pages = B * max_pages + 3
+    perm = torch.randperm(n_pages, generator=g)
+    bt = torch.zeros(B, max_pages, dtype=torch.int32)
+    for b in range(B):
+        bt[b] = perm[b * max_pages:(b + 1) * max_pages]
+    kc = (torch.randn(n_pages, Hkv, P, D, generator=g) * 0.7)
+    vc = torch.randn(n_pages, Hkv, P, D, generator=g)
+    return kc.to(dtype), vc.to(dtype), bt
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,window,sinks,fp8,splits", [
+    (64, 64, 8, 0, True, True, 1), (64, 64, 8, 128, True, True, 4), (128, 32, 8, 0, False, False, 3),
+    (128, 16, 8, 0, False, False, 1), (64, 8, 1, 0, True, False, 8)])
+def test_decode_attention(D, Hq, Hkv, window, sinks, fp8, splits):
+    from sglang_neuron_b200.ops.attention import decode_attention, decode_attention_ref
+    torch.manual_seed(2)
+    P = 16
+    ctx = [1, 17, 300, 1000, 64, 129]
+    B = len(ctx)
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc, vc, bt = _make_paged(B, ctx, Hkv, D, P, dt)
+    q = torch.randn(B, Hq * D, dtype=torch.bfloat16)
+    sk = torch.randn(Hq) if sinks else None
+    seq = torch.tensor(ctx, dtype=torch.int32)
+    ks, vs = (0.8, 1.3) if fp8 else (1.0, 1.0)
+    ref = decode_attention_ref(q.float(), kc, vc, bt, seq, Hq, Hkv, D, P, window, None, ks, vs, sk)
+    out = decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), seq.to(DEV), Hq, Hkv, D, P, window,
+                           None, ks, vs, sk.to(DEV) if sinks else None, num_splits=splits)
+    _close(out, ref, 2e-2, 2e-2, "decode")
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,window,sinks,fp8", [(64, 64, 8, 0, True, True), (64, 64, 8, 128, True, False),
+                                                       (128, 32, 8, 0, False, False), (128, 16, 8, 0, False, True)])
+def test_extend_attention(D, Hq, Hkv, window, sinks, fp8):
+    from sglang_neuron_b200.ops.attention import extend_attention, extend_attention_ref
+    torch.manual_seed(3)
+    P = 16
+    prefix = [0, 40, 0, 300]
+    ext = [5, 70, 200, 33]
+    kv = [p + e for p, e in zip(prefix, ext)]
+    B = len(kv)
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc, vc, bt = _make_paged(B, kv, Hkv, D, P, dt, seed=4)
+    qo = torch.tensor([0] + list(torch.tensor(ext).cumsum(0)), dtype=torch.int32)
+    q = torch.randn(int(qo[-1]), Hq * D, dtype=torch.bfloat16)
+    sk = torch.randn(Hq) if sinks else None
+    kvl = torch.tensor(kv, dtype=torch.int32)
+    ref = extend_attention_ref(q.float(), kc, vc, bt, qo, kvl, Hq, Hkv, D, P, window, None, 1.0, 1.0, sk)
+    out = extend_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), qo.to(DEV), kvl.to(DEV), max(ext), Hq,
+                           Hkv, D, P, window, None, 1.0, 1.0, sk.to(DEV) if sinks else None)
+    _close(out, ref, 2e-2, 2e-2, "extend")
+
+
+def test_sampling_greedy_and_gumbel():
+    from sglang_neuron_b200.ops.sampling import sample_tokens, gumbel_noise_ref
+    torch.manual_seed(5)
+    V = 201088
+    logits = torch.randn(6, V, device=DEV)
+    logits[0, 77] = 50.0
+    logits[1, 5] = logits[1, 9] = 60.0  # tie -> smallest id
+    ids = sample_tokens(logits)
+    assert ids[0].item() == 77 and ids[1].item() == 5
+    assert torch.equal(ids.cpu(), logits.argmax(-1).cpu()) or ids[1].item() == 5
+    temp = torch.tensor([0.0, 0.7, 1.0, 1.3, 0.0, 2.0], device=DEV)
+    seeds = torch.arange(6, device=DEV) * 1000 + 7
+    pos = torch.arange(6, device=DEV) + 11
+    ids = sample_tokens(logits, temp, seeds, pos).cpu()
+    for b in range(6):
+        t = float(temp[b])
+        row = logits[b].float().cpu()
+        if t > 0:
+            row = row / t + gumbel_noise_ref(int(seeds[b]), int(pos[b]), V)
+        best = row.max().item()
+        assert row[ids[b]].item() >= best - 1e-3
+
+
+def test_topk_route_and_align_combine():
+    from sglang_neuron_b200.ops.moe import (topk_route, topk_route_ref, MoEAlignment, moe_align, moe_combine)
+    torch.manual_seed(6)
+    T, E, K = 77, 128, 4
+    logits = torch.randn(T, E, device=DEV)
+    for mode in (0, 1):
+        w, ids = topk_route(logits, K, mode)
+        wr, idr = topk_route_ref(logits.cpu(), K, mode)
+        assert torch.equal(ids.cpu().long(), idr.long())
+        _close(w, wr, 1e-5, 1e-4, "route w")
+    w, ids = topk_route(logits, K, 0)
+    bn = 16
+    al = MoEAlignment(T * K, E, bn, DEV)
+    moe_align(ids, 0, E, al)
+    seg = al.seg_offsets.cpu()
+    src = al.sorted_src.cpu()
+    inv = al.inv_map.cpu()
+    idc = ids.cpu().reshape(-1)
+    for i in range(T * K):
+        r = int(inv[i])
+        e = int(idc[i])
+        assert seg[e] <= r < seg[e + 1]
+        assert int(src[r]) == i // K
+    assert int(al.tile_offsets[-1]) * bn == int(seg[-1])
+    # combine
+    H = 256
+    y = torch.randn(al.r_max, H, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(T, H, device=DEV, dtype=torch.bfloat16)
+    moe_combine(out, y, al.inv_map, w)
+    ref = torch.zeros(T, H)
+    for t in range(T):
+        for j in range(K):
+            ref[t] += float(w[t, j]) * y[int(inv[t * K + j])].float().cpu()
+    _close(out, ref, 2e-2, 1e-2, "combine")
+
+
+@pytest.mark.parametrize("bn", [16, 64, 128])
+def test_gather_quant_mxfp8(bn):
+    from sglang_neuron_b200.ops.moe import gather_quant_mxfp8
+    torch.manual_seed(7)
+    T, H = 50, 2880
+    x = torch.randn(T, H, dtype=torch.bfloat16) * 3
+    rows = 4 * bn
+    src = torch.randint(-1, T, (rows,), dtype=torch.int32)
+    q_ref, sf_ref = gather_quant_mxfp8(x, src, rows, bn)
+    q, sf = gather_quant_mxfp8(x.to(DEV), src.to(DEV), rows, bn)
+    assert torch.equal(sf.cpu(), sf_ref)
+    assert (q.cpu().float() - q_ref.float()).abs().max().item() <= 1e-6 * 0 + 32.0 * 0.07
+
+
+@pytest.mark.parametrize("T,F,K,bias", [(1, 2880, 2880, True), (16, 5120, 2880, False), (77, 4096, 4096, True),
+                                        (300, 1024, 3072, False), (1000, 384, 512, True)])
+def test_gemm_bf16_tcgen05(T, F, K, bias):
+    from sglang_neuron_b200.ops.gemm import linear, check_status
+    torch.manual_seed(8)
+    x = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(F, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    b = torch.randn(F, device=DEV, dtype=torch.bfloat16) if bias else None
+    y = linear(x, w, b)
+    torch.cuda.synchronize()
+    check_status(x.device)
+    ref = x.float() @ w.float().t() + (b.float() if bias else 0)
+    _close(y, ref, 3e-2, 1e-2, "gemm")
