@@ -22,14 +22,52 @@ except ImportError as e:  # pragma: no cover
     _rt_err = e
 
 
+_launches = [0]
+
+
+def launch_count() -> int:
+    """Kernels of this package launched so far (eager calls plus the kernels inside replayed graphs)."""
+    return _launches[0]
+
+
+def add_launches(n: int) -> None:
+    _launches[0] += n
+
+
+class _CountingKernels:
+    """Forwards to the compiled module and counts the kernels each call launches."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if name == "decode_attention":
+            def call(*a, **k):
+                _launches[0] += 2 if (len(a) > 15 and int(a[15]) > 1) else 1
+                return fn(*a, **k)
+        else:
+            def call(*a, **k):
+                _launches[0] += 1
+                return fn(*a, **k)
+        return call
+
+
+_counting = None
+
+
 def kernels():
     """Return the kernel module or raise a clear error if it was not built."""
+    global _counting
     if _C is None:
         raise RuntimeError(
             "sglang_neuron_b200._C is not built; run `python setup.py build_ext --inplace` "
             f"(import error: {_err})"
         )
-    return _C
+    if _counting is None:
+        _counting = _CountingKernels(_C)
+    return _counting
 
 
 def runtime():

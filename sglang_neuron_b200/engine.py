@@ -1,0 +1,104 @@
+"""Public offline API: `Engine(...).generate(...)`.
+
+Parity: sglang.Engine as served by the reference (SGLang's engine + the plugin's runtime). One Engine per
+process group: with tp_size > 1 the caller launches one process per GPU (torchrun or
+`Engine.launch_spmd`), every rank constructs the Engine, and rank 0 owns request intake; the other ranks
+follow the broadcast request stream in lockstep.
+"""
+from __future__ import annotations
+
+import itertools
+import logging
+import os
+import time
+from typing import Dict, List, Optional, Sequence, Union
+
+import torch
+
+from .configs.model_config import ModelConfig, resolve_model_config
+from .managers.schedule_batch import SamplingParams
+from .managers.scheduler import Scheduler
+from .model_executor.model_runner import ModelRunner
+from .parallel.state import get_state, init_process_group_from_env, initialize_parallel
+from .server_args import ServerArgs
+
+logger = logging.getLogger(__name__)
+
+
+class Engine:
+    def __init__(self, args: Optional[ServerArgs] = None, **kwargs):
+        args = args or ServerArgs(**kwargs)
+        if args.device == "cuda" and not torch.cuda.is_available():
+            args.device = "cpu"
+        self.args = args
+        overrides = {}
+        self.cfg: ModelConfig = resolve_model_config(args.model, **overrides)
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            init_process_group_from_env()
+        if args.device == "cuda":
+            local = int(os.environ.get("LOCAL_RANK", "0"))
+            torch.cuda.set_device(local)
+            device = torch.device("cuda", local)
+        else:
+            device = torch.device("cpu")
+        st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device)
+        self.rank = st.rank
+        self.runner = ModelRunner(args, self.cfg, device)
+        self.scheduler = Scheduler(args, self.cfg, self.runner)
+        self.tokenizer = None
+        tok_path = args.tokenizer or (args.model if os.path.isdir(args.model) else None)
+        if tok_path:
+            try:
+                from transformers import AutoTokenizer
+                self.tokenizer = AutoTokenizer.from_pretrained(tok_path)
+            except Exception as e:  # no tokenizer files: token-id mode
+                logger.info("tokenizer unavailable (%s); serving token ids", e)
+        self._ids = itertools.count()
+
+    # ------------------------------------------------------------------------------------------
+    def _to_ids(self, prompt) -> List[int]:
+        if isinstance(prompt, str):
+            if self.tokenizer is None:
+                raise ValueError("text prompts need a tokenizer; pass token ids instead")
+            return self.tokenizer.encode(prompt)
+        return [int(t) for t in prompt]
+
+    def submit(self, prompt, sampling_params: Optional[Union[dict, SamplingParams]] = None, rid: Optional[str] = None):
+        sp = sampling_params if isinstance(sampling_params, SamplingParams) else SamplingParams.from_dict(sampling_params)
+        rid = rid or f"req-{next(self._ids)}"
+        return self.scheduler.add_request(rid, self._to_ids(prompt), sp)
+
+    def step(self) -> None:
+        self.scheduler.step()
+
+    def generate(self, prompts: Sequence, sampling_params=None) -> List[Dict]:
+        """Blocking generation for a list of prompts (token-id lists or strings)."""
+        if isinstance(sampling_params, list):
+            sps = sampling_params
+        else:
+            sps = [sampling_params] * len(prompts)
+        reqs = [self.submit(p, sp) for p, sp in zip(prompts, sps)]
+        self.scheduler.run_until_idle()
+        out = []
+        for r in reqs:
+            d = {"rid": r.rid, "output_ids": list(r.output_ids), "finish_reason": r.finish_reason,
+                 "prompt_tokens": r.prompt_len, "completion_tokens": len(r.output_ids),
+                 "cached_tokens": r.prefix_len}
+            if r.first_token_time is not None:
+                d["ttft_s"] = r.first_token_time - r.arrival
+            if self.tokenizer is not None:
+                d["text"] = self.tokenizer.decode(r.output_ids)
+            out.append(d)
+        return out
+
+    def flush_cache(self) -> None:
+        self.scheduler.drain()
+        if self.scheduler.radix is not None and not self.scheduler.running:
+            freed = self.scheduler.radix.reset()
+            if freed:
+                self.scheduler.alloc.free(list(freed))
+
+    def shutdown(self) -> None:
+        self.scheduler.drain()
+        if self.runner.graph_runner is not None:
+            self.runner.graph_runner.graphs.clear()

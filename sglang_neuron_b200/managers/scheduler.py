@@ -1,0 +1,377 @@
+"""Continuous-batching scheduler with chunked prefill, mixed prefill+decode steps, a page-granular prefix
+cache, retire-aware page frees and an overlapped (one step ahead) launch loop.
+
+Parity:
+  * scheduling loop and prefill chunking: SGLang's Scheduler + PrefillAdder as the reference runs them
+    (sglang_neuron/general_plugin.py:870 one request per prefill, sglang_patches/prefill_chunk_grid.py);
+    here several requests may share a chunk and decode rows ride along (mixed step).
+  * overlap: the reference's async execution (model_executor/async_execution.py: TokenRelay, PendingSample,
+    CompletionEvent) launches step N+1 before reading step N's tokens; results are read after the launch.
+  * frees held until the launches that read them retire (mem_cache/allocator.py:172).
+  * SPMD ranks: every TP rank runs this scheduler on the same request stream (rank 0 broadcasts arrivals),
+    so all ranks build identical batches and their collectives stay in lockstep (parity: DP identity /
+    lockstep plan_step, graph_runner.py:822-869).
+"""
+from __future__ import annotations
+
+import collections
+import logging
+import time
+from typing import Callable, Deque, Dict, List, Optional, Tuple
+
+import numpy as np
+
+from ..mem_cache.allocator import RadixCacheHandle, make_page_allocator
+from ..model_executor.forward_batch import ForwardMode
+from ..parallel.collectives import cpu_broadcast_object
+from ..parallel.state import get_state
+from .schedule_batch import Req, SamplingParams, StepInput
+
+logger = logging.getLogger(__name__)
+
+
+class Scheduler:
+    def __init__(self, args, cfg, runner):
+        self.args = args
+        self.cfg = cfg
+        self.runner = runner
+        self.P = args.page_size
+        self.alloc = make_page_allocator(runner.num_pages, self.P, reserved=1)
+        self.radix = None if args.disable_radix_cache else RadixCacheHandle(self.P)
+        self.waiting: Deque[Req] = collections.deque()
+        self.running: List[Req] = []
+        self.inflight: Deque[Tuple[StepInput, object, object]] = collections.deque()
+        self.free_slots = list(range(runner.max_reqs - 1, -1, -1))
+        self.epoch = 0
+        self.overlap = not args.disable_overlap_schedule
+        self.eos = set(cfg.eos_token_id or [])
+        self.pending_arrivals: List[Req] = []
+        self.finished_reqs: List[Req] = []
+        self.on_token: Optional[Callable[[Req], None]] = None
+        self.stats = collections.Counter()
+        self.step_times: List[Tuple[int, float, int, int]] = []
+
+    # ------------------------------------------------------------------------------------------
+    # request intake
+    def add_request(self, rid: str, input_ids: List[int], params: SamplingParams) -> Req:
+        req = Req(rid, input_ids, params, eos_ids=[] if params.ignore_eos else self.eos)
+        if len(input_ids) + params.max_new_tokens > self.args.context_length:
+            raise ValueError(f"request {rid}: prompt {len(input_ids)} + max_new_tokens {params.max_new_tokens} "
+                             f"exceeds context length {self.args.context_length}")
+        self.pending_arrivals.append(req)
+        return req
+
+    def _sync_arrivals(self) -> None:
+        st = get_state()
+        if st.tp_size > 1:
+            payload = [(r.rid, r.origin_input_ids, r.params) for r in self.pending_arrivals] if st.tp_rank == 0 else None
+            payload = cpu_broadcast_object(payload, src=0)
+            if st.tp_rank != 0:
+                self.pending_arrivals = [Req(rid, ids, p, eos_ids=[] if p.ignore_eos else self.eos)
+                                         for rid, ids, p in payload]
+        self.waiting.extend(self.pending_arrivals)
+        self.pending_arrivals = []
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running or self.inflight or self.pending_arrivals)
+
+    # ------------------------------------------------------------------------------------------
+    # page management
+    def _alloc_pages(self, n: int) -> Optional[List[int]]:
+        if n <= 0:
+            return []
+        pages = self.alloc.alloc(n)
+        if len(pages) == n:
+            return list(pages)
+        if self.radix is not None:
+            freed = self.radix.evict(n - self.alloc.available())
+            if freed:
+                self.alloc.free(list(freed))
+            pages = self.alloc.alloc(n)
+            if len(pages) == n:
+                return list(pages)
+        return None
+
+    def _ensure_pages(self, r: Req, upto_tokens: int, upd: List[int]) -> bool:
+        need = (upto_tokens + self.P - 1) // self.P - len(r.pages)
+        if need <= 0:
+            return True
+        pages = self._alloc_pages(need)
+        if pages is None:
+            return False
+        for p in pages:
+            upd += [r.slot, len(r.pages), p]
+            r.pages.append(p)
+        return True
+
+    def _release(self, r: Req) -> None:
+        """Return a finished (or retracted) request's pages: full pages go to the prefix cache."""
+        owned = r.pages[r.owned_from:]
+        if self.radix is not None and not r.retracted_flag():
+            ids = r.all_ids()
+            n_tok = (min(r.kv_len, len(ids)) // self.P) * self.P
+            n_pages = n_tok // self.P
+            if n_pages > 0:
+                dup = self.radix.insert(ids[:n_tok], r.pages[:n_pages])
+                to_free = list(dup) + r.pages[max(n_pages, r.owned_from):]
+            else:
+                to_free = owned
+            if r.prefix_node is not None:
+                self.radix.dec_lock(r.prefix_node)
+        else:
+            to_free = owned
+            if self.radix is not None and r.prefix_node is not None:
+                self.radix.dec_lock(r.prefix_node)
+        if to_free:
+            self.alloc.free_after(list(to_free), r.last_step)
+        r.pages, r.owned_from, r.prefix_node = [], 0, None
+        if r.slot is not None:
+            self.free_slots.append(r.slot)
+            r.slot = None
+
+    # ------------------------------------------------------------------------------------------
+    def _admit(self) -> None:
+        while self.waiting and self.free_slots:
+            r = self.waiting[0]
+            ids = r.all_ids()
+            prefix_len, prefix_pages, node = 0, [], None
+            if self.radix is not None:
+                matched, pages, node = self.radix.match_prefix(ids[:-1] if len(ids) > 1 else [])
+                prefix_len = (matched // self.P) * self.P
+                prefix_pages = list(pages)[: prefix_len // self.P]
+            need = (len(ids) + 1 + self.P - 1) // self.P - len(prefix_pages)
+            if self.alloc.available() + (self.radix.evictable_pages() if self.radix else 0) < need:
+                break
+            self.waiting.popleft()
+            r.slot = self.free_slots.pop()
+            r.pages = prefix_pages
+            r.owned_from = len(prefix_pages)
+            r.prefix_len = prefix_len
+            r.kv_len = prefix_len
+            r.prefill_target = len(ids)
+            if self.radix is not None and node is not None:
+                self.radix.inc_lock(node)
+                r.prefix_node = node
+            self.stats["cache_hit_tokens"] += prefix_len
+            self.stats["prompt_tokens"] += len(ids)
+            self.running.append(r)
+
+    def _retract_one(self, exclude: Req) -> bool:
+        """Out of pages: drain the in-flight steps, then send the request with the most outstanding work
+        back to the queue (its KV is recomputed when it is re-admitted)."""
+        cands = [r for r in self.running if r is not exclude and not r.finished]
+        if not cands:
+            return False
+        self.drain()
+        victim = max(cands, key=lambda r: r.params.max_new_tokens - len(r.output_ids))
+        self.running.remove(victim)
+        victim._retracted = True
+        self._release(victim)
+        victim._retracted = False
+        victim.kv_len = 0
+        victim.scheduled_outputs = len(victim.output_ids)
+        self.waiting.appendleft(victim)
+        self.stats["retractions"] += 1
+        return True
+
+    def schedule(self) -> Optional[StepInput]:
+        self._admit()
+        prefill = [r for r in self.running if r.kv_len < r.prefill_target]
+        decode = [r for r in self.running if r.kv_len >= r.prefill_target and not r.finished
+                  and r.scheduled_outputs < r.params.max_new_tokens]
+        if prefill:
+            if not self.args.enable_mixed_chunk:
+                decode = []
+            return self._build_extend(prefill, decode)
+        if decode:
+            return self._build_decode(decode)
+        return None
+
+    def _build_decode(self, reqs: List[Req]) -> Optional[StepInput]:
+        upd: List[int] = []
+        ok_reqs = []
+        for r in reqs:
+            while not self._ensure_pages(r, r.kv_len + 1, upd):
+                if not self._retract_one(r):
+                    raise RuntimeError("KV pool exhausted by a single request")
+                if r not in self.running:
+                    break
+            if r in self.running:
+                ok_reqs.append(r)
+        reqs = [r for r in ok_reqs if r.slot is not None]
+        if not reqs:
+            return None
+        B = len(reqs)
+        pos = np.fromiter((r.kv_len for r in reqs), dtype=np.int64, count=B)
+        slots = np.fromiter((r.pages[r.kv_len // self.P] * self.P + r.kv_len % self.P for r in reqs),
+                            dtype=np.int64, count=B)
+        step = self._make_step(ForwardMode.DECODE, reqs, [True] * B, np.zeros(B, np.int64), pos, slots,
+                               np.arange(B, dtype=np.int64), pos.astype(np.int32) + 1, np.zeros(1, np.int32),
+                               upd, num_decode=B, max_extend=0)
+        for r in reqs:
+            r.kv_len += 1
+            r.scheduled_outputs += 1
+            r.last_step = step.epoch
+        return step
+
+    def _build_extend(self, prefill: List[Req], decode: List[Req]) -> Optional[StepInput]:
+        budget = self.args.chunked_prefill_size
+        upd: List[int] = []
+        chunks: List[Tuple[Req, int]] = []
+        for r in prefill:
+            if budget <= 0:
+                break
+            n = min(r.prefill_target - r.kv_len, budget)
+            if not self._ensure_pages(r, r.kv_len + n, upd):
+                break
+            chunks.append((r, n))
+            budget -= n
+        dec_ok = []
+        for r in decode:
+            if self._ensure_pages(r, r.kv_len + 1, upd):
+                dec_ok.append(r)
+        if not chunks and not dec_ok:
+            return None
+        if not chunks:
+            return self._build_decode_from_upd(dec_ok, upd)
+        D = len(dec_ok)
+        reqs = dec_ok + [r for r, _ in chunks]
+        T = D + sum(n for _, n in chunks)
+        ids = np.zeros(T, np.int64)
+        pos = np.empty(T, np.int64)
+        slots = np.empty(T, np.int64)
+        logits_idx = np.empty(len(reqs), np.int64)
+        seq = np.empty(len(reqs), np.int32)
+        qo = np.zeros(len(chunks) + 1, np.int32)
+        sampled = []
+        for i, r in enumerate(dec_ok):
+            pos[i] = r.kv_len
+            slots[i] = r.pages[r.kv_len // self.P] * self.P + r.kv_len % self.P
+            logits_idx[i] = i
+            seq[i] = r.kv_len + 1
+            sampled.append(True)
+        row = D
+        max_ext = 0
+        rt = __import__("sglang_neuron_b200._ext", fromlist=["_runtime"])._runtime
+        for j, (r, n) in enumerate(chunks):
+            all_ids = r.all_ids()
+            ids[row:row + n] = all_ids[r.kv_len:r.kv_len + n]
+            pos[row:row + n] = np.arange(r.kv_len, r.kv_len + n)
+            if rt is not None:
+                slots[row:row + n] = rt.slots_for_range(r.pages, self.P, r.kv_len, r.kv_len + n)
+            else:
+                p = np.arange(r.kv_len, r.kv_len + n)
+                slots[row:row + n] = np.asarray(r.pages, np.int64)[p // self.P] * self.P + p % self.P
+            logits_idx[D + j] = row + n - 1
+            seq[D + j] = r.kv_len + n
+            qo[j + 1] = qo[j] + n
+            sampled.append(r.kv_len + n >= r.prefill_target)
+            row += n
+            max_ext = max(max_ext, n)
+        step = self._make_step(ForwardMode.EXTEND, reqs, sampled, ids, pos, slots, logits_idx, seq, qo, upd,
+                               num_decode=D, max_extend=max_ext)
+        for r in dec_ok:
+            r.kv_len += 1
+            r.scheduled_outputs += 1
+            r.last_step = step.epoch
+        for (r, n), s in zip(chunks, sampled[D:]):
+            r.kv_len += n
+            if s:
+                r.scheduled_outputs += 1
+            r.last_step = step.epoch
+        return step
+
+    def _build_decode_from_upd(self, reqs, upd):
+        B = len(reqs)
+        pos = np.fromiter((r.kv_len for r in reqs), dtype=np.int64, count=B)
+        slots = np.fromiter((r.pages[r.kv_len // self.P] * self.P + r.kv_len % self.P for r in reqs),
+                            dtype=np.int64, count=B)
+        step = self._make_step(ForwardMode.DECODE, reqs, [True] * B, np.zeros(B, np.int64), pos, slots,
+                               np.arange(B, dtype=np.int64), pos.astype(np.int32) + 1, np.zeros(1, np.int32),
+                               upd, num_decode=B, max_extend=0)
+        for r in reqs:
+            r.kv_len += 1
+            r.scheduled_outputs += 1
+            r.last_step = step.epoch
+        return step
+
+    def _make_step(self, mode, reqs, sampled, ids, pos, slots, logits_idx, seq, qo, upd, num_decode, max_extend):
+        B = len(reqs)
+        temp = np.fromiter((r.params.temperature for r in reqs), dtype=np.float32, count=B)
+        top_p = np.fromiter((r.params.top_p for r in reqs), dtype=np.float32, count=B)
+        top_k = np.fromiter((r.params.top_k for r in reqs), dtype=np.int64, count=B)
+        seeds = np.fromiter((r.seed for r in reqs), dtype=np.int64, count=B)
+        slot_idx = np.fromiter((r.slot for r in reqs), dtype=np.int64, count=B)
+        needs = any(r.params.needs_filter for r in reqs)
+        step = StepInput(mode=mode, epoch=self.epoch, reqs=list(reqs), sampled=list(sampled), batch_size=B,
+                         num_tokens=len(pos), num_decode=num_decode, input_ids=ids, positions=pos,
+                         out_cache_loc=slots, logits_idx=logits_idx, req_idx=slot_idx, seeds=seeds, top_k=top_k,
+                         seq_lens=seq, qo_indptr=qo, page_upd=np.asarray(upd, dtype=np.int32), temperature=temp,
+                         top_p=top_p, max_extend=max_extend, max_seq_len=int(seq.max()) if B else 0,
+                         needs_topk_topp=needs)
+        self.epoch += 1
+        return step
+
+    # ------------------------------------------------------------------------------------------
+    def _process(self, step: StepInput, ids_host, event) -> None:
+        if event is not None:
+            event.synchronize()
+        ids = ids_host.numpy() if hasattr(ids_host, "numpy") else np.asarray(ids_host)
+        now = time.perf_counter()
+        for i, (r, s) in enumerate(zip(step.reqs, step.sampled)):
+            if not s or r.finished:
+                continue
+            tok = int(ids[i])
+            r.output_ids.append(tok)
+            if r.first_token_time is None:
+                r.first_token_time = now
+            r.token_times.append(now)
+            self.stats["output_tokens"] += 1
+            if (tok in r.eos_ids) or (r.params.stop_token_ids and tok in r.params.stop_token_ids):
+                self._finish(r, "stop")
+            elif len(r.output_ids) >= r.params.max_new_tokens:
+                self._finish(r, "length")
+            if self.on_token is not None:
+                self.on_token(r)
+        self.alloc.retire(step.epoch)
+
+    def _finish(self, r: Req, reason: str) -> None:
+        r.finished = True
+        r.finish_reason = reason
+        if r in self.running:
+            self.running.remove(r)
+        self._release(r)
+        self.finished_reqs.append(r)
+
+    def drain(self) -> None:
+        while self.inflight:
+            self._process(*self.inflight.popleft())
+
+    def step(self) -> None:
+        """One scheduler iteration: admit, launch one forward, and process the previous step's tokens."""
+        self._sync_arrivals()
+        step = self.schedule()
+        if step is not None:
+            t0 = time.perf_counter()
+            ids_host, ev = self.runner.run_step(step)
+            self.inflight.append((step, ids_host, ev))
+            self.stats["steps"] += 1
+            self.stats["decode_steps" if step.mode == ForwardMode.DECODE else "extend_steps"] += 1
+            self.step_times.append((step.epoch, t0, step.batch_size, step.num_tokens))
+        keep = 1 if (self.overlap and step is not None) else 0
+        while len(self.inflight) > keep:
+            self._process(*self.inflight.popleft())
+
+    def run_until_idle(self, max_steps: int = 1 << 62) -> None:
+        n = 0
+        while self.has_work() and n < max_steps:
+            self.step()
+            n += 1
+        self.drain()
+
+
+def _retracted_flag(self) -> bool:
+    return getattr(self, "_retracted", False)
+
+
+Req.retracted_flag = _retracted_flag

@@ -1,0 +1,111 @@
+"""CUDA-graph capture of decode steps for every batch-size bucket at startup.
+
+Parity: the reference compiles every prefill and decode shape at warm-up (NeuronModelRuntime.warmup_all,
+sglang_neuron/model_executor/graph_runner.py:692-757; BucketConfig decode batch buckets :149-253) and its
+`NeuronGraphRunner.can_run_graph` (:1692-1768) serves decode/idle batches up to the largest bucket. Here each
+bucket is a torch.cuda.CUDAGraph whose inputs live in one static device buffer with a fixed layout; a step
+packs its host arrays in the same layout, one cudaMemcpyAsync lands them in that buffer, and replay() runs
+embedding -> layers -> LM head -> sampler -> token relay with no host work in between.
+"""
+from __future__ import annotations
+
+import bisect
+import logging
+from typing import Dict
+
+import numpy as np
+import torch
+
+from .. import _ext
+from .forward_batch import ForwardBatch, ForwardMode
+
+logger = logging.getLogger(__name__)
+
+
+class CudaGraphRunner:
+    def __init__(self, runner):
+        self.r = runner
+        self.args = runner.args
+        self.bs_list = self.args.graph_batch_sizes()
+        self.max_bs = self.bs_list[-1]
+        from .model_runner import Layout
+        mb = self.max_bs
+        self.layout = Layout([
+            ("req_idx", torch.int64, mb), ("positions", torch.int64, mb), ("out_cache_loc", torch.int64, mb),
+            ("seeds", torch.int64, mb), ("seq_lens", torch.int32, mb), ("page_upd", torch.int32, 3 * mb),
+            ("temperature", torch.float32, mb),
+        ])
+        self.static = torch.zeros(self.layout.nbytes, dtype=torch.uint8, device=runner.device)
+        self.views = self.layout.views(self.static)
+        self.out_ids = torch.zeros(mb, dtype=torch.int64, device=runner.device)
+        self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.launches: Dict[int, int] = {}
+        self.pool = None
+        self.capture_all()
+
+    def can_run(self, step) -> bool:
+        return step.batch_size <= self.max_bs and not step.needs_topk_topp
+
+    def _fb(self, bs: int) -> ForwardBatch:
+        v = self.views
+        r = self.r
+        req_idx = v["req_idx"][:bs]
+        block_table = r.req_to_page.table.index_select(0, req_idx)
+        input_ids = r.relay.index_select(0, req_idx)
+        splits = r.backend.splits_for(bs, r.model.attention_layers()[0].num_kv_heads, self.args.context_length)
+        return ForwardBatch(mode=ForwardMode.DECODE, batch_size=bs, num_tokens=bs, input_ids=input_ids,
+                            positions=v["positions"][:bs], out_cache_loc=v["out_cache_loc"][:bs],
+                            seq_lens=v["seq_lens"][:bs], block_table=block_table,
+                            logits_idx=torch.arange(bs, device=r.device), temperature=v["temperature"][:bs],
+                            seeds=v["seeds"][:bs], decode_splits=splits, max_seq_len=self.args.context_length)
+
+    def _body(self, bs: int) -> None:
+        r = self.r
+        r.apply_page_updates(self.views["page_upd"][: 3 * bs])
+        fb = self._fb(bs)
+        h = r.model(fb)
+        r.sample(h, fb, self.views["req_idx"][:bs], out=self.out_ids[:bs])
+
+    def capture_all(self) -> None:
+        r = self.r
+        # padding state: every row points at the dummy request, writes nothing, attends to nothing
+        self._fill_padding(0, self.max_bs)
+        stream = torch.cuda.Stream(device=r.device)
+        stream.wait_stream(torch.cuda.current_stream(r.device))
+        with torch.cuda.stream(stream):
+            for bs in reversed(self.bs_list):
+                for _ in range(2):  # warm-up (allocator, lazy init) outside the graph
+                    self._body(bs)
+                g = torch.cuda.CUDAGraph()
+                n0 = _ext.launch_count()
+                with torch.cuda.graph(g, pool=self.pool, stream=stream):
+                    self._body(bs)
+                self.launches[bs] = _ext.launch_count() - n0
+                if self.pool is None:
+                    self.pool = g.pool()
+                self.graphs[bs] = g
+        torch.cuda.current_stream(r.device).wait_stream(stream)
+        torch.cuda.synchronize(r.device)
+        logger.info("captured %d decode graphs (bs %s)", len(self.graphs), self.bs_list)
+
+    def _fill_padding(self, start: int, end: int) -> None:
+        v = self.views
+        v["req_idx"][start:end] = self.r.dummy_req
+        v["positions"][start:end] = 0
+        v["out_cache_loc"][start:end] = -1
+        v["seeds"][start:end] = 0
+        v["seq_lens"][start:end] = 0
+        v["temperature"][start:end] = 0
+        pu = v["page_upd"].view(-1, 3)
+        pu[start:end, 0] = self.r.dummy_req
+        pu[start:end, 1] = 0
+        pu[start:end, 2] = 0
+
+    def replay(self, step) -> torch.Tensor:
+        B = step.batch_size
+        bs = self.bs_list[bisect.bisect_left(self.bs_list, B)]
+        arrays = step.decode_arrays(bs, self.r.dummy_req)
+        self.r.io.upload(self.layout, arrays, dst=self.static)
+        self.graphs[bs].replay()
+        _ext.add_launches(self.launches[bs])
+        return self.out_ids[:B]

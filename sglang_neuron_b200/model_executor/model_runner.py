@@ -1,0 +1,319 @@
+"""Model runner: owns the model, the KV pool, the block tables, the token relay and the step I/O, and runs
+one forward (eager for prefill/mixed steps, CUDA-graph replay for decode steps).
+
+Parity: NeuronModelRuntime (sglang_neuron/model_executor/graph_runner.py:273-1654): `build_model_inputs`
+pads to a bucket and stages uploads (:990-1197), `_run` launches and records a pending sample (:1233),
+`run_decode`/`run_prefill` (:1359, :1577). The reference's device_io (backend/device_io.py:150-413) keeps a
+pinned upload ring and one readback per step; here `StepIO` is that ring: each step's inputs are packed
+into one pinned buffer and land on the device with a single cudaMemcpyAsync, and the sampled tokens come
+back with one async device->host copy into a pinned slot guarded by a CUDA event.
+
+Token relay (parity: async_execution.TokenRelay, async_execution.py:508): the sampler writes every
+request's next token into `relay[req_slot]` on the device, and the next decode step gathers its input ids
+from there, so the host never waits for a token before launching the next step.
+"""
+from __future__ import annotations
+
+import logging
+import math
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from ..attention.backend import AttentionBackend
+from ..configs.model_config import ModelConfig
+from ..mem_cache.memory_pool import MHATokenToKVPool, MLATokenToKVPool, ReqToPagePool
+from ..models.families import get_model_class
+from ..models.weights import RandomSource, SafetensorsSource, load_model_weights
+from ..ops.sampling import apply_top_k_top_p, sample_tokens
+from ..parallel.collectives import tp_all_gather_into
+from ..parallel.state import get_state
+from ..server_args import ServerArgs
+from .forward_batch import ForwardBatch, ForwardMode
+
+logger = logging.getLogger(__name__)
+
+_ALIGN = 16
+
+
+class PinnedRing:
+    """A ring of pinned host buffers; a slot is reused only after the event recorded on it completed."""
+
+    def __init__(self, nbytes: int, slots: int, pin: bool):
+        self.bufs = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=pin) for _ in range(slots)]
+        self.events: List[Optional[torch.cuda.Event]] = [None] * slots
+        self.i = 0
+
+    def acquire(self) -> Tuple[int, torch.Tensor]:
+        i = self.i
+        self.i = (self.i + 1) % len(self.bufs)
+        ev = self.events[i]
+        if ev is not None:
+            ev.synchronize()
+        return i, self.bufs[i]
+
+    def mark(self, i: int, ev) -> None:
+        self.events[i] = ev
+
+
+class Layout:
+    """Byte layout of one packed step: named sections (dtype, count) at 16-byte aligned offsets."""
+
+    def __init__(self, sections: List[Tuple[str, torch.dtype, int]]):
+        self.slots: Dict[str, Tuple[int, torch.dtype, int]] = {}
+        off = 0
+        for name, dt, n in sections:
+            sz = torch.empty(0, dtype=dt).element_size() * n
+            self.slots[name] = (off, dt, n)
+            off += (sz + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.nbytes = max(off, _ALIGN)
+
+    def views(self, buf: torch.Tensor) -> Dict[str, torch.Tensor]:
+        out = {}
+        for name, (off, dt, n) in self.slots.items():
+            el = torch.empty(0, dtype=dt).element_size()
+            out[name] = buf[off:off + n * el].view(dt)
+        return out
+
+
+_NP = {torch.int64: np.int64, torch.int32: np.int32, torch.float32: np.float32}
+
+
+class StepIO:
+    """Packs host arrays into one pinned buffer and uploads them with one copy; reads sampled ids back."""
+
+    def __init__(self, device, max_bytes: int, max_batch: int):
+        self.device = torch.device(device)
+        self.cuda = self.device.type == "cuda"
+        self.up = PinnedRing(max_bytes, 4, self.cuda)
+        self.down = PinnedRing(max_batch * 8, 8, self.cuda)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+
+    def upload(self, layout: Layout, arrays: Dict[str, np.ndarray], dst: Optional[torch.Tensor] = None):
+        slot, host = self.up.acquire()
+        hv = layout.views(host[:layout.nbytes])
+        for name, arr in arrays.items():
+            v = hv[name]
+            n = len(arr)
+            v.numpy()[:n] = arr
+        if dst is None:
+            dst = torch.empty(layout.nbytes, dtype=torch.uint8, device=self.device)
+        dst[:layout.nbytes].copy_(host[:layout.nbytes], non_blocking=self.cuda)
+        self.h2d_bytes += layout.nbytes
+        if self.cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+            self.up.mark(slot, ev)
+        return layout.views(dst[:layout.nbytes])
+
+    def readback(self, ids: torch.Tensor):
+        """Async copy of [B] int64 ids into a pinned slot; returns (host view, event)."""
+        slot, host = self.down.acquire()
+        n = ids.numel()
+        hv = host[: n * 8].view(torch.int64)
+        hv.copy_(ids, non_blocking=self.cuda)
+        self.d2h_bytes += n * 8
+        ev = None
+        if self.cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+            self.down.mark(slot, ev)
+        return hv, ev
+
+
+class ModelRunner:
+    def __init__(self, args: ServerArgs, cfg: ModelConfig, device=None):
+        self.args = args
+        self.cfg = cfg
+        st = get_state()
+        self.device = torch.device(device if device is not None else st.device)
+        self.cuda = self.device.type == "cuda"
+        self.dtype = args.torch_dtype() if self.cuda else torch.float32
+        cls = get_model_class(cfg.architecture)
+        self.model = cls(cfg, self.dtype, self.device, max_pos=args.context_length + 128)
+        self.load_weights()
+        self.page_size = args.page_size
+        self.max_pages_per_req = (args.context_length + self.page_size - 1) // self.page_size + 1
+        self.max_reqs = args.max_running_requests
+        self.kv_dtype = args.resolved_kv_dtype(cfg.architecture) if self.cuda else torch.float32
+        self.init_kv_pool()
+        # one extra request slot: padding rows of a captured batch point at it
+        self.dummy_req = self.max_reqs
+        self.req_to_page = ReqToPagePool(self.max_reqs + 1, self.max_pages_per_req, self.device)
+        a0 = self.model.attention_layers()[0]
+        num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.cuda else 148
+        self.backend = AttentionBackend(max(self.max_reqs, 1) + 1, a0.num_heads, getattr(a0, "head_dim", 128),
+                                        self.device, num_sms=num_sms)
+        self.model.bind_kv_cache(self.kv_pool, self.backend)
+        self.relay = torch.zeros(self.max_reqs + 1, dtype=torch.int64, device=self.device)
+        self.vocab_start = self.model.lm_head.start
+        self.vocab_valid = self.model.lm_head.end - self.model.lm_head.start
+        max_tokens = max(args.chunked_prefill_size, args.max_prefill_tokens) + self.max_reqs
+        self.max_step_tokens = max_tokens
+        self.io = StepIO(self.device, self._extend_layout(max_tokens, self.max_reqs + 1,
+                                                          self.max_reqs * self.max_pages_per_req).nbytes,
+                         self.max_reqs + 1)
+        self.graph_runner = None
+        self.logits_hook = None  # test seam: called with (ForwardBatch, local logits) of eager steps
+        if self.cuda and not args.disable_cuda_graph:
+            from .graph_runner import CudaGraphRunner
+            self.graph_runner = CudaGraphRunner(self)
+
+    # ------------------------------------------------------------------------------------------
+    def load_weights(self) -> None:
+        fmt = self.args.load_format
+        if fmt == "auto":
+            import os
+            fmt = "safetensors" if os.path.isdir(self.args.model) else "random"
+        if fmt == "random":
+            src = RandomSource(self.cfg, self.device, seed=self.args.seed, std=self.args.random_weight_std)
+        else:
+            src = SafetensorsSource(self.args.model, self.device)
+        load_model_weights(self.model, src)
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+            torch.cuda.empty_cache()
+
+    def init_kv_pool(self) -> None:
+        cfg, args = self.cfg, self.args
+        attn = self.model.attention_layers()
+        P = self.page_size
+        if cfg.is_mla:
+            per_page = MLATokenToKVPool.bytes_per_page(cfg.num_layers, P, cfg.kv_lora_rank, cfg.qk_rope_head_dim,
+                                                       self.kv_dtype)
+        else:
+            per_page = MHATokenToKVPool.bytes_per_page(cfg.num_layers, P, attn[0].num_kv_heads, cfg.head_dim,
+                                                       self.kv_dtype)
+        if args.max_total_tokens:
+            num_pages = args.max_total_tokens // P + 1
+        elif self.cuda:
+            free, total = torch.cuda.mem_get_info(self.device)
+            reserve = 6 * (1 << 30) + int(0.04 * total)
+            budget = max(0, int(free * args.mem_fraction_static) - reserve)
+            num_pages = max(2, budget // per_page)
+            cap = (self.max_reqs * self.max_pages_per_req) + 1
+            num_pages = min(num_pages, max(cap, 2))
+        else:
+            num_pages = (self.max_reqs * self.max_pages_per_req) + 1
+        self.num_pages = int(num_pages)
+        if cfg.is_mla:
+            self.kv_pool = MLATokenToKVPool(cfg.num_layers, self.num_pages, P, cfg.kv_lora_rank,
+                                            cfg.qk_rope_head_dim, self.kv_dtype, self.device)
+        else:
+            self.kv_pool = MHATokenToKVPool(cfg.num_layers, self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
+                                            self.kv_dtype, self.device)
+        logger.info("KV pool: %d pages x %d tokens (%.2f GB, %s)", self.num_pages, P,
+                    self.num_pages * per_page / 1e9, self.kv_dtype)
+
+    # ------------------------------------------------------------------------------------------
+    @staticmethod
+    def _extend_layout(T: int, B: int, U: int) -> Layout:
+        return Layout([
+            ("input_ids", torch.int64, T), ("positions", torch.int64, T), ("out_cache_loc", torch.int64, T),
+            ("logits_idx", torch.int64, B), ("req_idx", torch.int64, B), ("seeds", torch.int64, B),
+            ("top_k", torch.int64, B), ("seq_lens", torch.int32, B), ("qo_indptr", torch.int32, B + 1),
+            ("page_upd", torch.int32, 3 * U), ("temperature", torch.float32, B), ("top_p", torch.float32, B),
+        ])
+
+    def apply_page_updates(self, upd: torch.Tensor) -> None:
+        """upd: [U*3] int32 (req_slot, page_index, page_id) triples."""
+        if upd.numel() == 0:
+            return
+        u = upd.view(-1, 3).long()
+        self.req_to_page.table[u[:, 0], u[:, 1]] = u[:, 2].to(torch.int32)
+
+    def run_step(self, step) -> Tuple[torch.Tensor, Optional[torch.cuda.Event]]:
+        """Launch one forward for a host-built StepInput; returns (pinned host ids view, event)."""
+        if step.mode == ForwardMode.DECODE and self.graph_runner is not None and self.graph_runner.can_run(step):
+            ids = self.graph_runner.replay(step)
+        else:
+            ids = self.forward_eager(step)
+        return self.io.readback(ids)
+
+    def forward_eager(self, step) -> torch.Tensor:
+        B, T = step.batch_size, step.num_tokens
+        U = len(step.page_upd) // 3
+        layout = self._extend_layout(T, B, U)
+        arrays = step.arrays()
+        v = self.io.upload(layout, arrays)
+        self.apply_page_updates(v["page_upd"])
+        req_idx = v["req_idx"]
+        input_ids = v["input_ids"]
+        D = step.num_decode
+        if D > 0:
+            # decode rows take their token from the device relay (the host may not know it yet)
+            input_ids[:D] = self.relay.index_select(0, req_idx[:D])
+        if step.mode == ForwardMode.EXTEND and step.relay_first_token is not None:
+            pass
+        block_table = self.req_to_page.table.index_select(0, req_idx.view(-1))
+        fb = ForwardBatch(
+            mode=step.mode, batch_size=B, num_tokens=T, input_ids=input_ids, positions=v["positions"],
+            out_cache_loc=v["out_cache_loc"], seq_lens=v["seq_lens"], block_table=block_table,
+            logits_idx=v["logits_idx"], qo_indptr=v["qo_indptr"], max_extend=step.max_extend,
+            max_seq_len=step.max_seq_len, temperature=v["temperature"], seeds=v["seeds"], top_k=v["top_k"],
+            top_p=v["top_p"], needs_topk_topp=step.needs_topk_topp)
+        fb.extra["num_decode"] = D
+        if step.mode == ForwardMode.DECODE:
+            fb.decode_splits = self.backend.splits_for(B, self.model.attention_layers()[0].num_kv_heads,
+                                                       step.max_seq_len)
+        else:
+            fb.decode_splits = self.backend.splits_for(max(D, 1), self.model.attention_layers()[0].num_kv_heads,
+                                                       step.max_seq_len)
+        h = self.forward_model(fb)
+        return self.sample(h, fb, req_idx)
+
+    def forward_model(self, fb: ForwardBatch) -> torch.Tensor:
+        if fb.mode == ForwardMode.EXTEND and fb.extra.get("num_decode", 0) > 0:
+            return self._forward_mixed(fb)
+        return self.model(fb)
+
+    def _forward_mixed(self, fb: ForwardBatch) -> torch.Tensor:
+        """Decode rows [0, D) and extend rows [D, T) share every GEMM; attention splits per part."""
+        D = fb.extra["num_decode"]
+        dec = ForwardBatch(mode=ForwardMode.DECODE, batch_size=D, num_tokens=D, input_ids=fb.input_ids[:D],
+                           positions=fb.positions[:D], out_cache_loc=fb.out_cache_loc[:D],
+                           seq_lens=fb.seq_lens[:D], block_table=fb.block_table[:D], logits_idx=fb.logits_idx[:D],
+                           decode_splits=fb.decode_splits)
+        ext = ForwardBatch(mode=ForwardMode.EXTEND, batch_size=fb.batch_size - D, num_tokens=fb.num_tokens - D,
+                           input_ids=fb.input_ids[D:], positions=fb.positions[D:], out_cache_loc=fb.out_cache_loc[D:],
+                           seq_lens=fb.seq_lens[D:], block_table=fb.block_table[D:], logits_idx=fb.logits_idx[D:],
+                           qo_indptr=fb.qo_indptr, max_extend=fb.max_extend)
+        fb.extra["parts"] = (D, dec, ext)
+        return self.model(fb)
+
+    def sample(self, h_last: torch.Tensor, fb: ForwardBatch, req_idx: torch.Tensor,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        st = get_state()
+        logits = self.model.compute_logits(h_last)
+        if self.logits_hook is not None:
+            self.logits_hook(fb, logits)
+        B = h_last.shape[0]
+        positions = fb.positions.index_select(0, fb.logits_idx) + 1
+        if fb.needs_topk_topp:
+            full = logits[:, : self.vocab_valid]
+            if st.tp_size > 1:
+                from ..parallel.collectives import tp_all_gather
+                full = tp_all_gather(full.contiguous(), dim=-1)
+            full = apply_top_k_top_p(full.float(), fb.top_k, fb.top_p)
+            ids = sample_tokens(full, fb.temperature, fb.seeds, positions, out=out)
+        elif st.tp_size == 1:
+            ids = sample_tokens(logits, fb.temperature, fb.seeds, positions, out=out,
+                                valid_vocab=self.vocab_valid)
+        else:
+            vals = torch.empty(B, dtype=torch.float32, device=logits.device)
+            local = sample_tokens(logits, fb.temperature, fb.seeds, positions, out_vals=vals,
+                                  vocab_offset=self.vocab_start, valid_vocab=self.vocab_valid)
+            pair = torch.stack([vals, local.float()], dim=1).contiguous()
+            gathered = torch.empty(st.tp_size * B, 2, dtype=torch.float32, device=logits.device)
+            tp_all_gather_into(gathered, pair)
+            g = gathered.view(st.tp_size, B, 2)
+            best = g[:, :, 0].argmax(dim=0)  # first max = lowest rank = lowest token id on ties
+            ids_f = g[:, :, 1].gather(0, best[None, :])[0]
+            ids = ids_f.long()
+            if out is not None:
+                out.copy_(ids)
+                ids = out
+        self.relay.index_copy_(0, req_idx.view(-1), ids.view(-1))
+        return ids

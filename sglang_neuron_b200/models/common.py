@@ -1,0 +1,275 @@
+"""Building blocks shared by the decoder families: RMSNorm, GQA attention over the paged pool, dense and
+MoE MLPs, the decoder layer and the causal-LM shell.
+
+Parity (reference layer by layer):
+  * attention: sglang_neuron/models/transformer/model.py:95-153 (fused QKV + QK-norm + RoPE + paged write,
+    paged attention, o_proj + all-reduce) and models/gpt_oss/mxfp4/common.py:123 (QKV bias, sinks,
+    sliding window on alternating layers).
+  * dense MLP: models/transformer/model.py:156-173 (gate_up, SiLU*up, down + all-reduce).
+  * MoE: models/qwen3_moe/moe.py:20-77 and gpt_oss/mxfp4/common.py:186-363 (replicated router, experts split
+    in contiguous blocks by EP rank, one all-reduce of the expert partials).
+  * causal LM: models/transformer/model.py:236-252 (vocab-sharded embedding, layers, final norm of the
+    sampled rows only, vocab-sharded LM head).
+"""
+from __future__ import annotations
+
+import math
+from typing import Iterable, List, Optional, Tuple
+
+import torch
+from torch import nn
+
+from ..configs.model_config import ModelConfig
+from ..layers.embedding import ParallelLMHead, VocabParallelEmbedding
+from ..layers.linear import (MergedColumnParallelLinear, QKVParallelLinear, ReplicatedLinear,
+                             RowParallelLinear)
+from ..model_executor.forward_batch import ForwardBatch
+from ..ops import activation as act_ops
+from ..ops import moe as moe_ops
+from ..ops.norm import fused_add_rmsnorm, rmsnorm
+from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
+from ..parallel.collectives import tp_all_reduce
+from ..parallel.state import get_state
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float, dtype=torch.bfloat16, device=None):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim, dtype=dtype, device=device), requires_grad=False)
+
+    def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None):
+        if residual is None:
+            return rmsnorm(x, self.weight, self.eps)
+        return fused_add_rmsnorm(x, residual, self.weight, self.eps)
+
+
+class RotaryCache:
+    """cos/sin table shared by all layers of a model (one per device)."""
+
+    _cache = {}
+
+    @classmethod
+    def get(cls, cfg: ModelConfig, device, max_pos: Optional[int] = None) -> torch.Tensor:
+        max_pos = max_pos or cfg.max_position_embeddings
+        key = (cfg.rot_dim, max_pos, cfg.rope_theta, str(cfg.rope_scaling), str(device))
+        t = cls._cache.get(key)
+        if t is None:
+            t = build_cos_sin_cache(cfg.rot_dim, max_pos, cfg.rope_theta, cfg.rope_scaling, device)
+            cls._cache[key] = t
+        return t
+
+
+class GQAAttention(nn.Module):
+    def __init__(self, cfg: ModelConfig, layer_id: int, dtype, device, max_pos: int):
+        super().__init__()
+        self.cfg = cfg
+        self.layer_id = layer_id
+        self.head_dim = cfg.head_dim
+        self.qkv_proj = QKVParallelLinear(cfg.hidden_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads,
+                                          bias=cfg.attention_bias, dtype=dtype, device=device)
+        self.num_heads = self.qkv_proj.num_heads
+        self.num_kv_heads = self.qkv_proj.num_kv_heads
+        self.o_proj = RowParallelLinear(cfg.num_heads * cfg.head_dim, cfg.hidden_size, bias=cfg.o_proj_bias,
+                                        reduce=True, dtype=dtype, device=device)
+        self.q_norm = RMSNorm(cfg.head_dim, cfg.rms_norm_eps, dtype, device) if cfg.qk_norm else None
+        self.k_norm = RMSNorm(cfg.head_dim, cfg.rms_norm_eps, dtype, device) if cfg.qk_norm else None
+        self.window = cfg.layer_window(layer_id)
+        self.scaling = cfg.head_dim ** -0.5
+        self.sinks = (nn.Parameter(torch.zeros(self.num_heads, dtype=torch.float32, device=device),
+                                   requires_grad=False) if cfg.attention_sinks else None)
+        self.cos_sin = RotaryCache.get(cfg, device, max_pos)
+        self.kv_pool = None
+        self.backend = None
+
+    def sinks_f32(self):
+        return self.sinks
+
+    def kv_cache(self):
+        return self.kv_pool.kv(self.layer_id)
+
+    def forward(self, h: torch.Tensor, fb: ForwardBatch) -> torch.Tensor:
+        qkv = self.qkv_proj(h)
+        qs, kvs = self.qkv_proj.q_size, self.qkv_proj.kv_size
+        q = qkv[:, :qs]
+        k = qkv[:, qs:qs + kvs]
+        v = qkv[:, qs + kvs:]
+        kc, vc = self.kv_cache()
+        rope_qk_norm_kv_write(q, k, v, fb.positions, self.cos_sin, self.num_heads, self.num_kv_heads,
+                              self.head_dim, self.cfg.rot_dim, self.cfg.rope_neox,
+                              self.q_norm.weight if self.q_norm is not None else None,
+                              self.k_norm.weight if self.k_norm is not None else None, self.cfg.rms_norm_eps,
+                              kc, vc, fb.out_cache_loc, self.kv_pool.page_size, self.kv_pool.k_scale,
+                              self.kv_pool.v_scale)
+        o = self.backend.attend(q, self, fb)
+        return self.o_proj(o)
+
+    def load(self, get):
+        p = f"model.layers.{self.layer_id}.self_attn."
+        b = self.cfg.attention_bias
+        self.qkv_proj.load(get(p + "q_proj.weight"), get(p + "k_proj.weight"), get(p + "v_proj.weight"),
+                           get(p + "q_proj.bias") if b else None, get(p + "k_proj.bias") if b else None,
+                           get(p + "v_proj.bias") if b else None)
+        self.o_proj.load(get(p + "o_proj.weight"), get(p + "o_proj.bias") if self.cfg.o_proj_bias else None)
+        if self.q_norm is not None:
+            self.q_norm.weight.data.copy_(get(p + "q_norm.weight"))
+            self.k_norm.weight.data.copy_(get(p + "k_norm.weight"))
+        if self.sinks is not None:
+            st = get_state()
+            s = get(p + "sinks").float()
+            self.sinks.data.copy_(s.narrow(0, st.tp_rank * self.num_heads, self.num_heads))
+
+
+class DenseMLP(nn.Module):
+    def __init__(self, hidden: int, inter: int, dtype, device, reduce: bool = True):
+        super().__init__()
+        self.gate_up = MergedColumnParallelLinear(hidden, [inter, inter], dtype=dtype, device=device)
+        self.down = RowParallelLinear(inter, hidden, reduce=reduce, dtype=dtype, device=device)
+
+    def forward(self, x):
+        return self.down(act_ops.silu_and_mul(self.gate_up(x)))
+
+    def load(self, get, prefix: str):
+        self.gate_up.load_part(0, get(prefix + "gate_proj.weight"))
+        self.gate_up.load_part(1, get(prefix + "up_proj.weight"))
+        self.down.load(get(prefix + "down_proj.weight"))
+
+
+class MoEBlock(nn.Module):
+    """Router (replicated) + this rank's block of experts; partial outputs are all-reduced over EP (=TP).
+
+    Expert weights are kept in the tcgen05 block-scaled layout (ops.moe.ExpertWeights): MXFP4 for
+    checkpoints that ship MXFP4 (GPT-OSS), MXFP8 (e4m3 + e8m0 per 32) quantised at load for bf16
+    checkpoints (Qwen3-MoE, DeepSeek-V2) - the "block-scaled FP8 expert GEMM" configuration.
+    """
+
+    def __init__(self, cfg: ModelConfig, layer_id: int, dtype, device, shared_inter: int = 0):
+        super().__init__()
+        st = get_state()
+        self.cfg = cfg
+        self.layer_id = layer_id
+        E = cfg.num_experts
+        assert E % st.ep_size == 0, "experts must divide over EP ranks"
+        self.e_local = E // st.ep_size
+        self.e_lo = st.ep_rank * self.e_local
+        self.top_k = cfg.num_experts_per_tok
+        self.router = ReplicatedLinear(cfg.hidden_size, E, bias=cfg.router_bias, dtype=dtype, device=device)
+        self.route_mode = 0 if (cfg.norm_topk_prob or cfg.architecture == "GptOssForCausalLM") else 1
+        self.activation = "swiglu_clamp" if cfg.swiglu_limit > 0 else "silu"
+        self.experts: Optional[moe_ops.ExpertWeights] = None
+        self.shared = DenseMLP(cfg.hidden_size, shared_inter, dtype, device, reduce=False) if shared_inter else None
+        self.device = device
+        self.alignment_cache = {}
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        logits = self.router(x)
+        w, ids = moe_ops.topk_route(logits, self.top_k, self.route_mode, self.cfg.routed_scaling_factor)
+        out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
+                                self.cfg.swiglu_limit, e_lo=self.e_lo)
+        if self.shared is not None:
+            out = out + self.shared(x)
+        return tp_all_reduce(out)
+
+    # -- weights ------------------------------------------------------------------------------
+    def set_experts_from_dense(self, w13: torch.Tensor, w2: torch.Tensor, b13=None, b2=None,
+                               interleaved: bool = False):
+        """w13: [E_local, 2I, H] (gate rows then up rows unless interleaved), w2: [E_local, H, I] bf16/fp32.
+        Quantised here to MXFP8 for the block-scaled grouped GEMM."""
+        q13, s13 = moe_ops.quant_mxfp8_ref(w13)
+        q2, s2 = moe_ops.quant_mxfp8_ref(w2)
+        I = w2.shape[2]
+        self.experts = moe_ops.ExpertWeights(q13, s13, b13, q2, s2, b2, self.cfg.hidden_size, I, interleaved)
+
+    def set_experts_mxfp4(self, blocks13, scales13, b13, blocks2, scales2, b2, interleaved: bool = True):
+        I = self.cfg.moe_intermediate_size
+        self.experts = moe_ops.ExpertWeights(blocks13, scales13, b13, blocks2, scales2, b2, self.cfg.hidden_size, I,
+                                             interleaved)
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: ModelConfig, layer_id: int, dtype, device, max_pos: int, attn=None, mlp=None):
+        super().__init__()
+        self.layer_id = layer_id
+        self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, dtype, device)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, dtype, device)
+        self.self_attn = attn if attn is not None else GQAAttention(cfg, layer_id, dtype, device, max_pos)
+        self.mlp = mlp
+
+    def forward(self, h: torch.Tensor, residual: Optional[torch.Tensor], fb: ForwardBatch):
+        if residual is None:
+            residual = h.clone()
+            h = self.input_layernorm(h)
+        else:
+            h, residual = self.input_layernorm(h, residual)
+        h = self.self_attn(h, fb)
+        h, residual = self.post_attention_layernorm(h, residual)
+        h = self.mlp(h)
+        return h, residual
+
+
+class CausalLM(nn.Module):
+    """Shared shell: embedding -> decoder layers -> final norm on the sampled rows -> vocab-sharded head."""
+
+    def __init__(self, cfg: ModelConfig, dtype=torch.bfloat16, device="cpu", max_pos: Optional[int] = None):
+        super().__init__()
+        self.cfg = cfg
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.max_pos = max_pos or min(cfg.max_position_embeddings, 131072)
+        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, dtype, device)
+        self.layers = nn.ModuleList([self.make_layer(i) for i in range(cfg.num_layers)])
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, dtype, device)
+        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype, device)
+
+    def make_layer(self, i: int) -> DecoderLayer:  # overridden by families
+        raise NotImplementedError
+
+    def attention_layers(self) -> List[nn.Module]:
+        return [l.self_attn for l in self.layers]
+
+    def bind_kv_cache(self, pool, backend) -> None:
+        """Parity: NeuronModel.bind_kv_cache (sglang_neuron/models/base.py:123) binds pool buffers by layer id."""
+        for a in self.attention_layers():
+            a.kv_pool = pool
+            a.backend = backend
+
+    def forward(self, fb: ForwardBatch) -> torch.Tensor:
+        h = self.embed_tokens(fb.input_ids)
+        residual = None
+        for layer in self.layers:
+            h, residual = layer(h, residual, fb)
+        # only the rows that are sampled go through the final norm and the LM head
+        h_last = h.index_select(0, fb.logits_idx)
+        r_last = residual.index_select(0, fb.logits_idx)
+        h_last, _ = self.norm(h_last, r_last)
+        return h_last
+
+    def compute_logits(self, h_last: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(h_last)
+
+    # -- weights ------------------------------------------------------------------------------
+    def load_common(self, get) -> None:
+        self.embed_tokens.load(get("model.embed_tokens.weight"))
+        self.norm.weight.data.copy_(get("model.norm.weight"))
+        if self.cfg.tie_word_embeddings:
+            self.lm_head.load(get("model.embed_tokens.weight"))
+        else:
+            self.lm_head.load(get("lm_head.weight"))
+        for l in self.layers:
+            p = f"model.layers.{l.layer_id}."
+            l.input_layernorm.weight.data.copy_(get(p + "input_layernorm.weight"))
+            l.post_attention_layernorm.weight.data.copy_(get(p + "post_attention_layernorm.weight"))
+
+    def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
+        table = dict(weights)
+
+        def get(name):
+            if name not in table:
+                raise KeyError(f"checkpoint tensor {name!r} missing")
+            return table[name].to(self.device)
+
+        self.load_common(get)
+        self.load_layers(get)
+
+    def load_layers(self, get) -> None:
+        raise NotImplementedError
