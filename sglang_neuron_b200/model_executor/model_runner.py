@@ -157,7 +157,7 @@ class ModelRunner:
                          self.max_reqs + 1)
         self.graph_runner = None
         self.logits_hook = None  # test seam: called with (ForwardBatch, local logits) of eager steps
-        if self.cuda and not args.disable_cuda_graph:
+        if self.cuda and not args.disable_cuda_graph and self.model.graph_capturable:
             from .graph_runner import CudaGraphRunner
             self.graph_runner = CudaGraphRunner(self)
 

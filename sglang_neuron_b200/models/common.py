@@ -210,6 +210,8 @@ class DecoderLayer(nn.Module):
 class CausalLM(nn.Module):
     """Shared shell: embedding -> decoder layers -> final norm on the sampled rows -> vocab-sharded head."""
 
+    graph_capturable = True
+
     def __init__(self, cfg: ModelConfig, dtype=torch.bfloat16, device="cpu", max_pos: Optional[int] = None):
         super().__init__()
         self.cfg = cfg
