@@ -150,23 +150,32 @@ def main():
     sched = eng.scheduler
     counter = [0]
 
+    # Every rank runs this same code (SPMD): rank 0 owns intake and broadcasts arrivals inside
+    # scheduler steps; requests are tracked by rid so followers see the same state once they arrive.
     def new_req(ctx_len, out_len):
         counter[0] += 1
+        rid = f"b{counter[0]}"
         ids = rng.integers(0, V, size=ctx_len).tolist()
-        return eng.submit(ids, SamplingParams(max_new_tokens=out_len, temperature=0.0, ignore_eos=True),
-                          rid=f"b{counter[0]}")
+        eng.submit(ids, SamplingParams(max_new_tokens=out_len, temperature=0.0, ignore_eos=True), rid=rid)
+        return rid
+
+    def req(rid):
+        return sched.reqs_by_rid.get(rid)
+
+    def done(rid):
+        r = req(rid)
+        return r is not None and r.finished
 
     # steady-state construction (untimed): staggered progress across the 64 slots
     live = [new_req(IL + S * i, max(1, OL - S * i)) for i in range(C)]
-    while any(r.first_token_time is None for r in live):
+    while any(req(rid) is None or req(rid).first_token_time is None for rid in live):
         sched.step()
     sched.drain()
 
     def refill():
-        n_live = sum(1 for r in live if not r.finished)
-        for _ in range(C - n_live):
+        live[:] = [rid for rid in live if not done(rid)]
+        for _ in range(C - len(live)):
             live.append(new_req(IL, OL))
-        live[:] = [r for r in live if not r.finished]
 
     for _ in range(a.warmup):
         refill()
@@ -188,6 +197,9 @@ def main():
     produced = 0
     delivered0 = sched.stats["output_tokens"]
     wall0 = time.perf_counter()
+    prof = os.environ.get("SNB_PROFILE_WINDOW") == "1"
+    if prof:  # ncu --profile-from-start off captures only the timed steps
+        torch.cuda.cudart().cudaProfilerStart()
     start_ev.record()
     timed_steps = []
     for _ in range(a.steps):
@@ -205,6 +217,8 @@ def main():
         while len(sched.inflight) > 1:
             sched._process(*sched.inflight.popleft())
     end_ev.record()
+    if prof:
+        torch.cuda.cudart().cudaProfilerStop()
     sched.drain()
     torch.cuda.synchronize(dev)
     wall = time.perf_counter() - wall0
@@ -221,7 +235,7 @@ def main():
         dev_ms, wall = float(t[0]), float(t[1])
     # latency stats from the requests that received tokens in the window
     ttfts, itls = [], []
-    for r in sched.finished_reqs + live:
+    for r in sched.finished_reqs + [req(rid) for rid in live if req(rid) is not None]:
         if r.first_token_time is not None and r.first_token_time >= wall0 and r.arrival >= wall0:
             ttfts.append((r.first_token_time - r.arrival) * 1e3)
         tt = [t for t in r.token_times if t >= wall0]

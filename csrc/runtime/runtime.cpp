@@ -329,21 +329,21 @@ PYBIND11_MODULE(_runtime, m) {
       .def("staged", &PageAllocator::staged)
       .def("num_pages", &PageAllocator::num_pages)
       .def("page_size", &PageAllocator::page_size)
-      .def("alloc", &PageAllocator::alloc)
-      .def("free", &PageAllocator::free)
-      .def("free_after", &PageAllocator::free_after)
-      .def("retire", &PageAllocator::retire)
+      .def("alloc", &PageAllocator::alloc, py::arg("n"))
+      .def("free", &PageAllocator::free, py::arg("pages"))
+      .def("free_after", &PageAllocator::free_after, py::arg("pages"), py::arg("epoch"))
+      .def("retire", &PageAllocator::retire, py::arg("epoch"))
       .def("reset", &PageAllocator::reset);
   py::class_<RadixCache>(m, "RadixCache")
       .def(py::init<int64_t>())
       .def("page_size", &RadixCache::page_size)
       .def("cached_pages", &RadixCache::cached_pages)
       .def("evictable_pages", &RadixCache::evictable_pages)
-      .def("match_prefix", &RadixCache::match_prefix)
-      .def("insert", &RadixCache::insert)
-      .def("inc_lock", &RadixCache::inc_lock)
-      .def("dec_lock", &RadixCache::dec_lock)
-      .def("evict", &RadixCache::evict)
+      .def("match_prefix", &RadixCache::match_prefix, py::arg("tokens"))
+      .def("insert", &RadixCache::insert, py::arg("tokens"), py::arg("pages"))
+      .def("inc_lock", &RadixCache::inc_lock, py::arg("node"))
+      .def("dec_lock", &RadixCache::dec_lock, py::arg("node"))
+      .def("evict", &RadixCache::evict, py::arg("num_pages"))
       .def("reset", &RadixCache::reset);
   m.def("build_page_table_rows", &build_page_table_rows);
   m.def("slots_for_range", &slots_for_range);

@@ -1,0 +1,134 @@
+"""Kernel microbenchmarks with roofline fractions (CUDA-event timed, warm, L2 flushed between iterations).
+
+    python -m sglang_neuron_b200.benchmarks.kernels moe --tokens 64        # one GPT-OSS-120B MoE layer
+    python -m sglang_neuron_b200.benchmarks.kernels gemm --tokens 64 --n 5120 --k 2880
+    python -m sglang_neuron_b200.benchmarks.kernels attn --batch 64 --ctx 1536
+
+Peaks come from MEASURED_PEAKS.json at the repository root when present (hbm_gbs, bf16_tflops), else the
+pool's fallback figures (6650 GB/s, 1590 TFLOP/s). Pass --iters 1 --warmup 1 for a profiler capture.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+_flush = None
+
+
+def flush_l2():
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _flush.zero_()
+
+
+def timeit(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(iters):
+        flush_l2()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        tot += s.elapsed_time(e)
+    return tot / iters * 1e3  # us
+
+
+def bench_moe(a):
+    from ..ops import moe
+    E, H, I, K = a.experts, 2880, 2880, 4
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w13 = torch.randint(0, 256, (E, 2 * I, H // 2), device="cuda", dtype=torch.uint8, generator=g)
+    s13 = torch.randint(119, 122, (E, 2 * I, H // 32), device="cuda", dtype=torch.uint8, generator=g)
+    w2 = torch.randint(0, 256, (E, H, I // 2), device="cuda", dtype=torch.uint8, generator=g)
+    s2 = torch.randint(119, 122, (E, H, I // 32), device="cuda", dtype=torch.uint8, generator=g)
+    b13 = torch.zeros(E, 2 * I, device="cuda", dtype=torch.bfloat16)
+    b2 = torch.zeros(E, H, device="cuda", dtype=torch.bfloat16)
+    ew = moe.ExpertWeights(w13, s13, b13, w2, s2, b2, H, I, True)
+    T = a.tokens
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    w, ids = moe.topk_route(torch.randn(T, E, device="cuda"), K)
+    n_active = int(torch.unique(ids).numel())
+    fn = lambda: moe.fused_moe(x, w, ids, ew)  # noqa: E731
+    us = timeit(fn, a.iters, a.warmup)
+    bytes_w = n_active * (ew.w13.shape[1] * ew.w13.shape[2] + ew.w2.shape[1] * ew.w2.shape[2]
+                          + ew.sfa13[0].numel() + ew.sfa2[0].numel())
+    flops = 2 * T * K * (2 * I * H + H * I)
+    hbm, tf, src = peaks()
+    ach = bytes_w / (us * 1e-6) / 1e9
+    print(json.dumps({"kernel": "fused_moe (route+align+quant+2x tcgen05 mxf8f6f4 grouped GEMM+combine)",
+                      "tokens": T, "experts": E, "active_experts": n_active, "us": round(us, 2),
+                      "weight_GBps": round(ach, 1), f"hbm_frac_of_{src}": round(ach / hbm, 3),
+                      "tflops": round(flops / (us * 1e-6) / 1e12, 2)}))
+
+
+def bench_gemm(a):
+    from ..ops.gemm import linear
+    T, N, K = a.tokens, a.n, a.k
+    x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    us = timeit(lambda: linear(x, w), a.iters, a.warmup)
+    hbm, tf, src = peaks()
+    byt = (N * K + T * K + T * N) * 2
+    fl = 2 * T * N * K
+    print(json.dumps({"kernel": "gemm_bf16 (tcgen05 kind::f16)", "T": T, "N": N, "K": K, "us": round(us, 2),
+                      f"hbm_frac_of_{src}": round(byt / (us * 1e-6) / 1e9 / hbm, 3),
+                      f"tensor_frac_of_{src}": round(fl / (us * 1e-6) / 1e12 / tf, 3)}))
+
+
+def bench_attn(a):
+    from ..ops.attention import DecodeScratch, decode_attention, default_num_splits
+    B, L, P, Hq, Hkv, D = a.batch, a.ctx, 16, 64, 8, 64
+    pages_per = (L + P - 1) // P
+    n_pages = B * pages_per + 1
+    kc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(torch.float8_e4m3fn)
+    vc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(torch.float8_e4m3fn)
+    bt = (torch.arange(B * pages_per, device="cuda", dtype=torch.int32) + 1).view(B, pages_per)
+    seq = torch.full((B,), L, device="cuda", dtype=torch.int32)
+    q = torch.randn(B, Hq * D, device="cuda").to(torch.bfloat16)
+    sinks = torch.randn(Hq, device="cuda")
+    S = default_num_splits(B, Hkv, L)
+    sc = DecodeScratch(B, Hq, D, S, "cuda")
+    us = timeit(lambda: decode_attention(q, kc, vc, bt, seq, Hq, Hkv, D, P, 0, None, 1.0, 1.0, sinks, S, sc),
+                a.iters, a.warmup)
+    hbm, tf, src = peaks()
+    byt = B * L * Hkv * D * 2
+    print(json.dumps({"kernel": "decode_attention (paged GQA, fp8 KV, sinks)", "batch": B, "ctx": L, "splits": S,
+                      "us": round(us, 2), f"hbm_frac_of_{src}": round(byt / (us * 1e-6) / 1e9 / hbm, 3)}))
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("which", choices=["moe", "gemm", "attn"])
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--experts", type=int, default=128)
+    p.add_argument("--n", type=int, default=5120)
+    p.add_argument("--k", type=int, default=2880)
+    p.add_argument("--batch", type=int, default=64)
+    p.add_argument("--ctx", type=int, default=1536)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    a = p.parse_args()
+    {"moe": bench_moe, "gemm": bench_gemm, "attn": bench_attn}[a.which](a)
+
+
+if __name__ == "__main__":
+    main()

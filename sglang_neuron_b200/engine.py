@@ -64,8 +64,12 @@ class Engine:
         return [int(t) for t in prompt]
 
     def submit(self, prompt, sampling_params: Optional[Union[dict, SamplingParams]] = None, rid: Optional[str] = None):
+        """Queue one request. On a follower rank (tp_rank > 0) nothing is queued locally: requests arrive
+        through rank 0's broadcast, and the returned rid is the one rank 0 assigns to the same call."""
         sp = sampling_params if isinstance(sampling_params, SamplingParams) else SamplingParams.from_dict(sampling_params)
         rid = rid or f"req-{next(self._ids)}"
+        if get_state().tp_rank != 0:
+            return rid
         return self.scheduler.add_request(rid, self._to_ids(prompt), sp)
 
     def step(self) -> None:
@@ -77,8 +81,17 @@ class Engine:
             sps = sampling_params
         else:
             sps = [sampling_params] * len(prompts)
-        reqs = [self.submit(p, sp) for p, sp in zip(prompts, sps)]
-        self.scheduler.run_until_idle()
+        handles = [self.submit(p, sp) for p, sp in zip(prompts, sps)]
+        if get_state().tp_rank != 0:
+            # follower: step in lockstep until rank 0's matching requests have finished here too
+            want = set(handles)
+            while not want.issubset(self.scheduler.finished_by_rid):
+                self.scheduler.step()
+            self.scheduler.drain()
+            reqs = [self.scheduler.finished_by_rid[r] for r in handles]
+        else:
+            reqs = handles
+            self.scheduler.run_until_idle()
         out = []
         for r in reqs:
             d = {"rid": r.rid, "output_ids": list(r.output_ids), "finish_reason": r.finish_reason,

@@ -47,6 +47,8 @@ class Scheduler:
         self.eos = set(cfg.eos_token_id or [])
         self.pending_arrivals: List[Req] = []
         self.finished_reqs: List[Req] = []
+        self.finished_by_rid: Dict[str, Req] = {}
+        self.reqs_by_rid: Dict[str, Req] = {}
         self.on_token: Optional[Callable[[Req], None]] = None
         self.stats = collections.Counter()
         self.step_times: List[Tuple[int, float, int, int]] = []
@@ -69,6 +71,8 @@ class Scheduler:
             if st.tp_rank != 0:
                 self.pending_arrivals = [Req(rid, ids, p, eos_ids=[] if p.ignore_eos else self.eos)
                                          for rid, ids, p in payload]
+        for r in self.pending_arrivals:
+            self.reqs_by_rid[r.rid] = r
         self.waiting.extend(self.pending_arrivals)
         self.pending_arrivals = []
 
@@ -342,6 +346,7 @@ class Scheduler:
             self.running.remove(r)
         self._release(r)
         self.finished_reqs.append(r)
+        self.finished_by_rid[r.rid] = r
 
     def drain(self) -> None:
         while self.inflight:

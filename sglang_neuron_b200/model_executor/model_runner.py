@@ -168,7 +168,8 @@ class ModelRunner:
             import os
             fmt = "safetensors" if os.path.isdir(self.args.model) else "random"
         if fmt == "random":
-            src = RandomSource(self.cfg, self.device, seed=self.args.seed, std=self.args.random_weight_std)
+            src = RandomSource(self.cfg, self.device, seed=self.args.seed, std=self.args.random_weight_std,
+                               gen_device=self.args.random_gen_device)
         else:
             src = SafetensorsSource(self.args.model, self.device)
         load_model_weights(self.model, src)
@@ -255,12 +256,11 @@ class ModelRunner:
             max_seq_len=step.max_seq_len, temperature=v["temperature"], seeds=v["seeds"], top_k=v["top_k"],
             top_p=v["top_p"], needs_topk_topp=step.needs_topk_topp)
         fb.extra["num_decode"] = D
-        if step.mode == ForwardMode.DECODE:
-            fb.decode_splits = self.backend.splits_for(B, self.model.attention_layers()[0].num_kv_heads,
-                                                       step.max_seq_len)
-        else:
-            fb.decode_splits = self.backend.splits_for(max(D, 1), self.model.attention_layers()[0].num_kv_heads,
-                                                       step.max_seq_len)
+        # split count depends only on (rows, kv heads, context length) so eager and captured decode
+        # reduce in the same order and produce identical tokens
+        kvh = self.model.attention_layers()[0].num_kv_heads
+        fb.decode_splits = self.backend.splits_for(B if step.mode == ForwardMode.DECODE else max(D, 1), kvh,
+                                                   self.args.context_length)
         h = self.forward_model(fb)
         return self.sample(h, fb, req_idx)
 

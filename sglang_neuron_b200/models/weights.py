@@ -131,27 +131,33 @@ class RandomSource:
     """Deterministic random weights: each tensor is a pure function of (seed, name), so every TP rank
     builds identical replicated tensors and consistent shards."""
 
-    def __init__(self, cfg: ModelConfig, device, seed: int = 0, std: float = 0.02, mx_scale_exp: int = -7):
+    def __init__(self, cfg: ModelConfig, device, seed: int = 0, std: float = 0.02, mx_scale_exp: int = -7,
+                 gen_device=None):
         self.cfg, self.device, self.seed, self.std = cfg, torch.device(device), seed, std
         self.mx_scale = 127 + mx_scale_exp
+        # CPU and CUDA generators give different streams for one seed: generate on `gen_device` (default:
+        # the target device) when two devices must see identical weights.
+        self.gen_device = torch.device(gen_device) if gen_device is not None else self.device
 
     def __contains__(self, name):
         return True
 
     def get(self, name: str) -> torch.Tensor:
         shape, dtype = hf_shape(self.cfg, name)
-        g = torch.Generator(device=self.device)
+        gd = self.gen_device
+        g = torch.Generator(device=gd)
         g.manual_seed(_seed_of(self.seed, name))
         if name.endswith("norm.weight"):
-            return torch.ones(shape, dtype=dtype, device=self.device)
-        if name.endswith("_blocks"):
-            return torch.randint(0, 256, shape, generator=g, device=self.device, dtype=torch.uint8)
-        if name.endswith("_scales"):
-            return torch.randint(self.mx_scale - 1, self.mx_scale + 2, shape, generator=g, device=self.device,
-                                 dtype=torch.uint8)
-        if name.endswith("sinks"):
-            return torch.randn(shape, generator=g, device=self.device).to(dtype)
-        return (torch.randn(shape, generator=g, device=self.device) * self.std).to(dtype)
+            t = torch.ones(shape, dtype=dtype, device=gd)
+        elif name.endswith("_blocks"):
+            t = torch.randint(0, 256, shape, generator=g, device=gd, dtype=torch.uint8)
+        elif name.endswith("_scales"):
+            t = torch.randint(self.mx_scale - 1, self.mx_scale + 2, shape, generator=g, device=gd, dtype=torch.uint8)
+        elif name.endswith("sinks"):
+            t = torch.randn(shape, generator=g, device=gd).to(dtype)
+        else:
+            t = (torch.randn(shape, generator=g, device=gd) * self.std).to(dtype)
+        return t.to(self.device)
 
 
 def load_model_weights(model, source) -> None:

@@ -46,6 +46,7 @@ class ServerArgs:
     enable_metrics: bool = False
     host_trace_dir: Optional[str] = None
     random_weight_std: float = 0.02
+    random_gen_device: Optional[str] = None   # device whose RNG draws random-init weights (default: `device`)
 
     def resolved_kv_dtype(self, arch: str):
         import torch

@@ -25,7 +25,7 @@ def _engine(base, over, device, graph=True, kv="auto", std=0.05):
     args = ServerArgs(model=name, device=device, dtype="bfloat16" if device == "cuda" else "float32", page_size=16,
                       context_length=512, max_running_requests=8, chunked_prefill_size=48,
                       disable_cuda_graph=not graph, cuda_graph_bs=[1, 2, 4, 8], kv_cache_dtype=kv,
-                      random_weight_std=std)
+                      random_weight_std=std, random_gen_device="cpu")
     return Engine(args)
 
 
@@ -43,8 +43,10 @@ def test_graph_equals_eager(base, over, kv):
     assert [o["output_ids"] for o in a] == [o["output_ids"] for o in b]
 
 
-@pytest.mark.parametrize("base,over", [("gpt-oss-120b", TINY_OSS), ("qwen3-8b", TINY_QWEN)])
-def test_gpu_tracks_cpu_oracle(base, over):
+@pytest.mark.parametrize("base,over,tol", [("gpt-oss-120b", TINY_OSS, 0.2), ("qwen3-8b", TINY_QWEN, 0.08)])
+def test_gpu_tracks_cpu_oracle(base, over, tol):
+    """The MoE family's GPU path quantises expert activations to MXFP8 (e4m3 + e8m0 per 32, the block-scaled
+    tcgen05 GEMM's input format) while the fp32 oracle does not, hence its wider relative tolerance."""
     prompts = _prompts(3)
     got = {}
     for dev in ("cuda", "cpu"):
@@ -55,7 +57,7 @@ def test_gpu_tracks_cpu_oracle(base, over):
         got[dev] = torch.cat(rows, 0)
     g, c = got["cuda"], got["cpu"]
     rel = (g - c).norm() / c.norm()
-    assert rel < 0.08, f"GPU bf16 logits deviate from the fp32 oracle: rel {rel}"
+    assert rel < tol, f"GPU bf16 logits deviate from the fp32 oracle: rel {rel}"
     assert (g.argmax(-1) == c.argmax(-1)).float().mean() >= 0.66
 
 

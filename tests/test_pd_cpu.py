@@ -1,0 +1,107 @@
+"""Disaggregated prefill/decode on CPU ranks (gloo): rank 0 is the prefill group, rank 1 the decode group;
+KV pages move rank to rank, and the decoded tokens equal the aggregated engine's. A second case drops the
+decode side's acknowledgement (host-injected failure) and checks the prefill side aborts and frees pages."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+TINY = dict(num_hidden_layers=2, vocab_size=1000, hidden_size=256, intermediate_size=512,
+            num_attention_heads=4, num_key_value_heads=2, head_dim=64)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(9)
+    return [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (21, 40, 9)]
+
+
+def _engine(dp_size):
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.parallel.state import destroy_parallel
+    from sglang_neuron_b200.server_args import ServerArgs
+    destroy_parallel()
+    mc.PRESETS["pd-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], **TINY)
+    return Engine(ServerArgs(model="pd-tiny", device="cpu", dtype="float32", tp_size=1, dp_size=dp_size,
+                             context_length=256, max_running_requests=4, chunked_prefill_size=32,
+                             random_weight_std=0.05))
+
+
+def _worker(rank, port, drop_ack, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE="2", RANK=str(rank), LOCAL_RANK="0")
+    import time
+    import torch.distributed as dist
+    from sglang_neuron_b200.disaggregation.pd import DecodeSide, PDLink, PrefillSide
+    from sglang_neuron_b200.managers.schedule_batch import SamplingParams
+    eng = _engine(2)
+    store = dist.distributed_c10d._get_default_store()
+    role = "prefill" if rank == 0 else "decode"
+    link = PDLink(role, 1, store, timeout_s=3.0 if drop_ack else 60.0)
+    prompts = _prompts()
+    result = None
+    if role == "prefill":
+        side = PrefillSide(eng, link)
+        for i, p in enumerate(prompts):
+            side.submit(f"pd{i}", p, SamplingParams(max_new_tokens=7))
+        t0 = time.time()
+        while (eng.scheduler.has_work() or side.pending or side.sending) and time.time() - t0 < 120:
+            side.step()
+            time.sleep(0.001)
+        result = {"sent": side.sent, "aborted": sorted(side.aborted), "free": eng.scheduler.alloc.available()
+                  + eng.scheduler.alloc.staged()}
+    elif drop_ack:
+        # injected failure: the decode group never answers (it stays up but never polls the store)
+        time.sleep(6)
+        result = {}
+    else:
+        side = DecodeSide(eng, link)
+        t0 = time.time()
+        want = {"pd0", "pd1", "pd2"}
+        while time.time() - t0 < (8 if drop_ack else 120):
+            side.step()
+            if want.issubset(eng.scheduler.finished_by_rid):
+                break
+            time.sleep(0.001)
+        eng.scheduler.drain()
+        result = {rid: eng.scheduler.finished_by_rid[rid].output_ids for rid in sorted(want)
+                  if rid in eng.scheduler.finished_by_rid}
+    q.put((rank, result))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run(drop_ack):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, port, drop_ack, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    return res
+
+
+def test_pd_matches_aggregated():
+    res = _run(drop_ack=False)
+    eng = _engine(1)
+    ref = eng.generate(_prompts(), {"max_new_tokens": 7})
+    assert res[0]["sent"] == 3 and res[0]["aborted"] == []
+    assert [res[1][f"pd{i}"] for i in range(3)] == [o["output_ids"] for o in ref]
+
+
+def test_pd_prefill_aborts_when_decode_never_answers():
+    res = _run(drop_ack=True)
+    assert res[0]["sent"] == 0 and res[0]["aborted"] == ["pd0", "pd1", "pd2"]
+    assert res[1] == {}

@@ -1,0 +1,110 @@
+"""Native host runtime (C++ page allocator, radix prefix cache) against its Python twins, plus the platform
+surface: env registry, serving policy, catalog refusals, hook registry."""
+import random
+
+import pytest
+
+from sglang_neuron_b200.mem_cache.allocator import PyPageAllocator, PyRadixCache, RadixCacheHandle, make_page_allocator
+
+
+def test_allocator_retire_aware_frees():
+    for native in (True, False):
+        a = make_page_allocator(10, 16, reserved=1, native=native)
+        assert a.available() == 9
+        p = list(a.alloc(4))
+        assert len(p) == 4 and 0 not in p
+        assert list(a.alloc(6)) == []  # all-or-nothing
+        a.free_after(p[:2], epoch=5)
+        assert a.available() == 5 and a.staged() == 2
+        assert a.retire(4) == 0 and a.available() == 5
+        assert a.retire(5) == 2 and a.available() == 7
+        with pytest.raises((IndexError, Exception)):
+            a.free([0])
+
+
+def test_radix_native_matches_python_twin():
+    rng = random.Random(0)
+    P = 4
+    nat, py = RadixCacheHandle(P, native=True), RadixCacheHandle(P, native=False)
+    assert nat.native
+    next_page = [1]
+    seqs = []
+    for i in range(60):
+        if seqs and rng.random() < 0.6:
+            base = rng.choice(seqs)
+            cut = rng.randrange(0, len(base) + 1)
+            s = base[:cut] + [rng.randrange(50) for _ in range(rng.randrange(0, 20))]
+        else:
+            s = [rng.randrange(50) for _ in range(rng.randrange(1, 30))]
+        seqs.append(s)
+        m1 = nat.match_prefix(s)
+        m2 = py.match_prefix(s)
+        assert m1[0] == m2[0] and list(m1[1]) == list(m2[1])
+        n_pages = len(s) // P
+        pages = list(m1[1]) + list(range(next_page[0], next_page[0] + n_pages - len(m1[1])))
+        next_page[0] += n_pages
+        d1 = nat.insert(s, pages)
+        d2 = py.insert(s, pages)
+        assert sorted(d1) == sorted(d2)
+        assert nat.cached_pages() == py.cached_pages()
+    for k in (3, 7, 100):
+        assert sorted(nat.evict(k)) == sorted(py.evict(k))
+        assert nat.cached_pages() == py.cached_pages()
+
+
+def test_radix_lock_blocks_eviction():
+    r = RadixCacheHandle(2, native=True)
+    r.insert([1, 2, 3, 4], [10, 11])
+    _, pages, node = r.match_prefix([1, 2, 3, 4, 9])
+    assert list(pages) == [10, 11]
+    r.inc_lock(node)
+    assert r.evict(5) == [] or list(r.evict(5)) == []
+    r.dec_lock(node)
+    assert sorted(r.evict(5)) == [10, 11]
+
+
+def test_env_registry_and_policy(monkeypatch):
+    from sglang_neuron_b200 import env_registry, serving_policy
+    from sglang_neuron_b200.server_args import ServerArgs
+    env = {"SGLANG_B200_HOST_TRACE": "/tmp/x"}
+    env_registry.refuse_unknown(env)
+    with pytest.raises(env_registry.UnknownEnvError):
+        env_registry.refuse_unknown({"SGLANG_B200_HOST_TRAC": "1"})
+    pol = serving_policy.resolve(ServerArgs(tp_size=2, disable_radix_cache=True))
+    e = {}
+    serving_policy.export(pol, e)
+    back = serving_policy.current(e)
+    assert back == pol and back.prefix_cache == "none" and back.tp_size == 2
+
+
+def test_catalog_and_platform_refusals():
+    from sglang_neuron_b200.models.catalog import model_spec
+    from sglang_neuron_b200.platform import B200SRTPlatform, check_kv_cache, refuse_unserved
+    from sglang_neuron_b200.server_args import ServerArgs
+    spec = model_spec("GptOssForCausalLM")
+    assert spec.expert_format == "mxfp4" and spec.sinks
+    with pytest.raises(ValueError):
+        model_spec("KimiK3ForCausalLM")
+    with pytest.raises(ValueError):
+        refuse_unserved(ServerArgs(speculative_algorithm="MTP"), spec)
+    with pytest.raises(ValueError):
+        check_kv_cache(ServerArgs(page_size=12), spec)
+    p = B200SRTPlatform()
+    args = p.apply_server_args_defaults(ServerArgs(model="qwen3-0.6b", device="cpu"))
+    assert args.model == "qwen3-0.6b"
+    assert p.get_kv_pool_cls(kind="mla").__name__ == "MLATokenToKVPool"
+
+
+def test_hook_registry_resolves_and_refuses_double_replace():
+    from sglang_neuron_b200 import general_plugin as gp
+    reg = gp.ResolvingHookRegistry()
+    target = "sglang_neuron_b200.sglang_tree:rank_label"
+    pin = gp.source_md5(gp.resolve_target(target)[2])
+    reg.register(target, "AROUND", lambda orig: "wrapped-" + orig(), pin_md5=pin)
+    from sglang_neuron_b200 import sglang_tree
+    assert sglang_tree.rank_label().startswith("wrapped-")
+    with pytest.raises(gp.HookError):
+        reg.register("sglang_neuron_b200.sglang_tree:dp_widths", "REPLACE", lambda: (1, 1), pin_md5="0" * 32)
+    reg.undo_all()
+    assert not sglang_tree.rank_label().startswith("wrapped-")
+    assert gp.register() == "sglang_neuron_b200.platform.B200SRTPlatform"
