@@ -38,7 +38,7 @@ void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torc
 // moe_gemm_sm100.cu
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets, int64_t bn,
-              int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status);
+              int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status, int64_t F);
 // activation.cu
 void silu_and_mul(torch::Tensor out, torch::Tensor x);
 // gemm_sm100.cu

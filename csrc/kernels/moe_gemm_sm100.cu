@@ -33,18 +33,23 @@ constexpr int BM = 128;
 constexpr int BK = 128;           // K elements per pipeline stage (4 MMAs of K=32)
 constexpr int A_SMEM = BM * BK;   // 16 KB: one byte per element in shared memory for fp8 and unpacked fp4
 constexpr int SF_SMEM = 512;      // one 32x128-bit scale atom
-constexpr int TMEM_COLS = 512;
 constexpr int MAX_EXPERTS = 256;
 
 enum Epi : int { EPI_SWIGLU_CLAMP = 0, EPI_SILU = 1, EPI_BIAS = 2 };
 
+// Small-N tiles (decode: a few tokens per expert) run two CTAs per SM so two independent TMA pipelines
+// stream weights per SM; each then owns 128 TMEM columns (2 accumulators + per-stage scale factors).
 template <int BN>
 struct MoeCfg {
+  static constexpr int CTAS_PER_SM = BN <= 32 ? 2 : 1;
   static constexpr int B_SMEM = BN * BK;
   static constexpr int STAGE = A_SMEM + B_SMEM + 2 * SF_SMEM;
-  static constexpr int STAGES = (176 * 1024) / STAGE > 8 ? 8 : (176 * 1024) / STAGE;
+  static constexpr int BUDGET = CTAS_PER_SM == 2 ? 96 * 1024 : 176 * 1024;
+  static constexpr int STAGES = BUDGET / STAGE > 8 ? 8 : BUDGET / STAGE;
   static constexpr int ACC_BUFS = BN <= 128 ? 2 : 1;
   static constexpr int SF_COL0 = ACC_BUFS * BN;  // scale-factor columns start after the accumulators
+  static constexpr int TMEM_COLS = CTAS_PER_SM == 2 ? 128 : 512;
+  static_assert(SF_COL0 + 8 * STAGES <= TMEM_COLS, "TMEM plan overflows the allocation");
   static constexpr int XBUF = 64 * 32 * 4;       // epilogue exchange buffer (64 rows x 32 cols fp32)
   static constexpr int SMEM = STAGES * STAGE + XBUF + 1024 + 2048;
 };
@@ -85,7 +90,7 @@ SNB_DEVICE void locate(const int32_t* tile_off_s, const int32_t* seg_off_s, int 
 }
 
 template <int BN, bool A_FP4, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, MoeCfg<BN>::CTAS_PER_SM)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const MoeParams p) {
   using C = MoeCfg<BN>;
@@ -127,7 +132,7 @@ __global__ void __launch_bounds__(192, 1)
     snb::prefetch_tmap(&tmap_b);
   }
   if (warp == 1) {
-    snb::tmem_alloc(tmem_slot, TMEM_COLS);
+    snb::tmem_alloc(tmem_slot, C::TMEM_COLS);
     snb::tmem_relinquish();
   }
   snb::tc_fence_before();
@@ -141,6 +146,7 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      const uint64_t stream_once = snb::l2_policy_evict_first();
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
         int e, mt, r0;
         locate(tile_off_s, seg_off_s, E, p.MT, BN, t, e, mt, r0);
@@ -153,7 +159,9 @@ __global__ void __launch_bounds__(192, 1)
           }
           const uint32_t a_bytes = A_FP4 ? A_SMEM / 2 : A_SMEM;
           snb::mbar_arrive_expect_tx(&full[s], a_bytes + C::B_SMEM + SF_SMEM + chunk);
-          snb::tma_load_3d(sA + s * A_SMEM, &tmap_a, &full[s], kb * BK, mt * BM, e);
+          // weights are pre-tiled [E][MT][KB][128 rows]: every stage reads one contiguous block
+          snb::tma_load_2d_hint(sA + s * A_SMEM, &tmap_a, &full[s], 0, ((e * p.MT + mt) * p.KB + kb) * BM,
+                                stream_once);
           snb::tma_load_2d(sB + s * C::B_SMEM, &tmap_b, &full[s], kb * BK, r0);
           snb::bulk_load(sSF + s * 2 * SF_SMEM, p.sfa + ((size_t)(e * p.MT + mt) * p.KB + kb) * SF_SMEM, SF_SMEM,
                          &full[s]);
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(192, 1)
   }
   snb::tc_fence_before();
   __syncthreads();
-  if (warp == 1) snb::tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 1) snb::tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 template <int BN, bool A_FP4, int EPI>
@@ -323,19 +331,19 @@ void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const Moe
 // out: [R, ldo] bf16. epi: 0 clamped SwiGLU, 1 SiLU-gated, 2 bias only.
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets,
-              int64_t bn, int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status) {
+              int64_t bn, int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status,
+              int64_t F) {
+  // w: tiled weights [E, MT, KB, 128, bpr] (bpr = 64 bytes of packed fp4 or 128 bytes of fp8 per row of a
+  // 128-wide K block), zero-padded past F rows and K columns.
+  TORCH_CHECK(w.dim() == 5 && w.size(3) == BM, "moe_gemm: weights must be tiled [E, MT, KB, 128, bytes]");
   const bool fp4 = w.scalar_type() == at::kByte;
-  const int E = w.size(0), F = w.size(1);
+  const int E = w.size(0), MT = w.size(1), KBw = w.size(2);
+  const int bpr = w.size(4);
   const int K = xq.size(1);
-  // Weight rows may be zero-padded past K: the packed 4-bit TMA format needs the inner extent to be a
-  // multiple of 128 elements (64 bytes) and a 32-byte aligned base.
-  const int Kw = fp4 ? (int)w.size(2) * 2 : (int)w.size(2);
   TORCH_CHECK(E <= MAX_EXPERTS, "moe_gemm: at most 256 local experts");
-  TORCH_CHECK(Kw >= K && Kw - K < 128, "moe_gemm: weight K extent ", Kw, " vs activation K ", K);
-  if (fp4) {
-    TORCH_CHECK(Kw % 128 == 0, "moe_gemm: fp4 weight rows must hold a multiple of 128 elements");
-    TORCH_CHECK((reinterpret_cast<uintptr_t>(w.data_ptr()) & 31) == 0, "moe_gemm: fp4 weights must be 32-byte aligned");
-  }
+  TORCH_CHECK(bpr == (fp4 ? 64 : 128), "moe_gemm: tile row bytes");
+  TORCH_CHECK(KBw == (K + BK - 1) / BK && MT == (F + BM - 1) / BM, "moe_gemm: tile grid does not match K/F");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(w.data_ptr()) & 127) == 0, "moe_gemm: weights must be 128-byte aligned");
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && xq.is_contiguous(), "moe_gemm: xq");
   TORCH_CHECK(K % 32 == 0, "moe_gemm: K must be a multiple of 32");
   TORCH_CHECK(w.is_contiguous() && sfa.is_contiguous() && sfb.is_contiguous(), "moe_gemm: contiguity");
@@ -353,30 +361,20 @@ void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Ten
   p.num_experts = E;
   p.F = F;
   p.K = K;
-  p.MT = (F + BM - 1) / BM;
-  p.KB = (K + BK - 1) / BK;
+  p.MT = MT;
+  p.KB = KBw;
   p.alpha = (float)alpha;
   p.limit = (float)limit;
   p.status = status.data_ptr<int>();
   TORCH_CHECK(sfa.numel() >= (int64_t)E * p.MT * p.KB * SF_SMEM, "moe_gemm: sfa size");
-  CUtensorMap ta;
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)Kw, (cuuint64_t)F, (cuuint64_t)E};
-    const uint64_t row_bytes = fp4 ? Kw / 2 : Kw;
-    cuuint64_t strides[2] = {row_bytes, row_bytes * F};
-    cuuint32_t box[3] = {BK, BM, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    TORCH_CHECK(row_bytes % 16 == 0, "moe_gemm: weight row pitch must be a multiple of 16 bytes");
-    CUresult r = snb_host::encode_fn()(&ta, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8,
-                                       3, w.data_ptr(), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    TORCH_CHECK(r == CUDA_SUCCESS, "moe_gemm: weight tensor map failed (", (int)r, ")");
-  }
+  // One 2D view over all tiles: rows = E*MT*KB*128, each row one 128-value K slice of one weight row.
+  CUtensorMap ta = snb_host::make_tmap_2d(w.data_ptr(),
+                                          fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                                          BK, (uint64_t)E * MT * KBw * BM, bpr, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tb = snb_host::make_tmap_2d(xq.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, R, K, BK, bn,
                                           CU_TENSOR_MAP_SWIZZLE_128B);
   auto st = at::cuda::getCurrentCUDAStream();
-  const int grid = (int)num_sms;
+  const int grid = (int)num_sms * (bn <= 32 ? 2 : 1);
 #define SNB_MOE(FP4, EP) dispatch_bn<FP4, EP>(bn, ta, tb, p, grid, st)
   if (fp4) {
     if (epi == 0) SNB_MOE(true, EPI_SWIGLU_CLAMP);

@@ -109,19 +109,46 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
     if (e >= 0 && e < E_local) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, tiles = 0;
-    for (int e = 0; e < E_local; ++e) {
-      off[e] = acc;
-      seg_offsets[e] = acc;
-      tile_offsets[e] = tiles;
-      const int padded = ((cnt[e] + BN - 1) / BN) * BN;
-      acc += padded;
-      tiles += padded / BN;
+  // Exclusive scan of the BN-padded segment sizes by warp 0 (E_local <= 256: 8 experts per lane).
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int per = (E_local + 31) / 32;
+    int local_rows = 0, local_tiles = 0;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < E_local) {
+        const int padded = ((cnt[e] + BN - 1) / BN) * BN;
+        local_rows += padded;
+        local_tiles += padded / BN;
+      }
     }
-    off[E_local] = acc;
-    seg_offsets[E_local] = acc;
-    tile_offsets[E_local] = tiles;
+    int inc_rows = local_rows, inc_tiles = local_tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int r = __shfl_up_sync(0xffffffffu, inc_rows, o);
+      const int t = __shfl_up_sync(0xffffffffu, inc_tiles, o);
+      if (lane >= o) {
+        inc_rows += r;
+        inc_tiles += t;
+      }
+    }
+    int acc = inc_rows - local_rows, tiles = inc_tiles - local_tiles;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < E_local) {
+        off[e] = acc;
+        seg_offsets[e] = acc;
+        tile_offsets[e] = tiles;
+        const int padded = ((cnt[e] + BN - 1) / BN) * BN;
+        acc += padded;
+        tiles += padded / BN;
+      }
+    }
+    if (lane == 31) {
+      off[E_local] = inc_rows;
+      seg_offsets[E_local] = inc_rows;
+      tile_offsets[E_local] = inc_tiles;
+    }
   }
   __syncthreads();
   const int total = off[E_local];

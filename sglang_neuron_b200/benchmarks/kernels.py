@@ -69,8 +69,7 @@ def bench_moe(a):
     n_active = int(torch.unique(ids).numel())
     fn = lambda: moe.fused_moe(x, w, ids, ew)  # noqa: E731
     us = timeit(fn, a.iters, a.warmup)
-    bytes_w = n_active * (ew.w13.shape[1] * ew.w13.shape[2] + ew.w2.shape[1] * ew.w2.shape[2]
-                          + ew.sfa13[0].numel() + ew.sfa2[0].numel())
+    bytes_w = n_active * (ew.w13[0].numel() + ew.w2[0].numel() + ew.sfa13[0].numel() + ew.sfa2[0].numel())
     flops = 2 * T * K * (2 * I * H + H * I)
     hbm, tf, src = peaks()
     ach = bytes_w / (us * 1e-6) / 1e9

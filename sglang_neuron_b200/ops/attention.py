@@ -83,10 +83,11 @@ def extend_attention_ref(q, k_cache, v_cache, block_table, qo_indptr, kv_lens, n
 
 
 def default_num_splits(batch: int, num_kv_heads: int, max_ctx: int, num_sms: int = 148) -> int:
-    """Flash-decoding split count: enough CTAs for ~2 waves, at least 256 tokens per split."""
+    """Flash-decoding split count: enough CTAs for ~6 resident per SM (latency hiding of the tile loads),
+    at least 128 tokens per split."""
     ctas = max(1, batch * num_kv_heads)
-    want = max(1, (2 * num_sms + ctas - 1) // ctas)
-    cap = max(1, (max_ctx + 255) // 256)
+    want = max(1, (6 * num_sms + ctas - 1) // ctas)
+    cap = max(1, (max_ctx + 127) // 128)
     return int(min(want, cap, 32))
 
 

@@ -52,10 +52,14 @@ class MoEAlignment:
         self.bn = bn
         self.num_local_experts = num_local_experts
         self.r_max = max_sorted_rows(max_entries, num_local_experts, bn)
-        self.seg_offsets = torch.zeros(num_local_experts + 1, dtype=torch.int32, device=device)
-        self.tile_offsets = torch.zeros(num_local_experts + 1, dtype=torch.int32, device=device)
-        self.sorted_src = torch.full((self.r_max,), -1, dtype=torch.int32, device=device)
-        self.inv_map = torch.full((max_entries,), -1, dtype=torch.int32, device=device)
+        # every element is written by moe_align before any reader runs, so no fill kernels are needed
+        alloc = torch.empty if torch.device(device).type == "cuda" else torch.zeros
+        self.seg_offsets = alloc(num_local_experts + 1, dtype=torch.int32, device=device)
+        self.tile_offsets = alloc(num_local_experts + 1, dtype=torch.int32, device=device)
+        self.sorted_src = torch.full((self.r_max,), -1, dtype=torch.int32, device=device) if alloc is torch.zeros \
+            else torch.empty(self.r_max, dtype=torch.int32, device=device)
+        self.inv_map = torch.full((max_entries,), -1, dtype=torch.int32, device=device) if alloc is torch.zeros \
+            else torch.empty(max_entries, dtype=torch.int32, device=device)
 
 
 def moe_align_ref(ids: torch.Tensor, e_lo: int, e_local: int, bn: int, al: MoEAlignment):
@@ -162,10 +166,13 @@ def gather_quant_mxfp8(x: torch.Tensor, src: Optional[torch.Tensor], rows: int, 
     KB = (kp + 127) // 128
     nsf = (rows // bn) * KB * sf_chunk_bytes(bn)
     q = torch.empty(rows, kp, dtype=torch.float8_e4m3fn, device=x.device)
-    sf = torch.full((nsf,), 127, dtype=torch.uint8, device=x.device)
     if x.is_cuda:
+        # the kernel writes every scale byte the MMA reads (rows < BN of each chunk, all K blocks); the
+        # remaining bytes of a chunk belong to rows the MMA never reads, so no fill is needed
+        sf = torch.empty(nsf, dtype=torch.uint8, device=x.device)
         kernels().gather_quant_mxfp8(q, sf, x, src, bn)
         return q, sf
+    sf = torch.full((nsf,), 127, dtype=torch.uint8, device=x.device)
     s = src.long() if src is not None else torch.arange(rows)
     xs = torch.zeros(rows, kp, dtype=torch.float32)
     valid = s >= 0
@@ -219,13 +226,26 @@ def arrange_sf_atoms(scales: torch.Tensor, F: int, K: int) -> torch.Tensor:
     return v.view(E, MT, KB, SF_ATOM)
 
 
-def _pad_k(w: torch.Tensor, fp4: bool) -> torch.Tensor:
-    """Zero-pad packed MXFP4 rows to a multiple of 128 values (64 bytes), the inner-extent rule of the
-    packed 4-bit TMA format. FP8 rows need no padding."""
-    if not fp4 or (w.shape[-1] % 64) == 0:
-        return w.contiguous()
-    pad = 64 - w.shape[-1] % 64
-    return torch.nn.functional.pad(w, (0, pad)).contiguous()
+def tile_weights(w: torch.Tensor, fp4: bool) -> torch.Tensor:
+    """[E, F, row_bytes] packed MXFP4 (two values per byte) or MXFP8 rows -> [E, MT, KB, 128, bpr]: every
+    (expert, 128-row tile, 128-value K block) becomes one contiguous block (8 KB for fp4, 16 KB for fp8), so
+    each pipeline stage of the grouped GEMM reads a single sequential run of HBM. Rows past F and values past
+    K are zero (they contribute nothing: the matching scales are 2^0 and the activations are zero there)."""
+    E, F, rb = w.shape
+    bpr = 64 if fp4 else 128
+    MT, KB = (F + 127) // 128, (rb + bpr - 1) // bpr
+    src = w if w.dtype == torch.uint8 else w.view(torch.uint8)
+    out = torch.zeros(E, MT * 128, KB * bpr, dtype=torch.uint8, device=w.device)
+    out[:, :F, :rb] = src
+    out = out.view(E, MT, 128, KB, bpr).permute(0, 1, 3, 2, 4).contiguous()
+    return out if w.dtype == torch.uint8 else out.view(w.dtype)
+
+
+def untile_weights(t: torch.Tensor, F: int, row_bytes: int) -> torch.Tensor:
+    E, MT, KB, _, bpr = t.shape
+    u = t.view(torch.uint8) if t.dtype != torch.uint8 else t
+    u = u.permute(0, 1, 3, 2, 4).reshape(E, MT * 128, KB * bpr)[:, :F, :row_bytes]
+    return u if t.dtype == torch.uint8 else u.contiguous().view(t.dtype)
 
 
 class ExpertWeights:
@@ -240,10 +260,10 @@ class ExpertWeights:
         self.hidden, self.inter = hidden, inter
         order = gated_row_order(inter, interleaved).to(w13.device)
         self.fp4 = w13.dtype == torch.uint8
-        self.w13 = _pad_k(w13.index_select(1, order), self.fp4)
+        self.w13 = tile_weights(w13.index_select(1, order), self.fp4)
         self.sfa13 = arrange_sf_atoms(s13.index_select(1, order), 2 * inter, hidden)
         self.b13 = b13.index_select(1, order).to(torch.bfloat16).contiguous() if b13 is not None else None
-        self.w2 = _pad_k(w2, self.fp4)
+        self.w2 = tile_weights(w2, self.fp4)
         self.sfa2 = arrange_sf_atoms(s2, hidden, inter)
         self.b2 = b2.to(torch.bfloat16).contiguous() if b2 is not None else None
         self.num_experts = w13.shape[0]
@@ -259,11 +279,15 @@ def _status(device):
     return _status_bufs[key]
 
 
-def moe_gemm(out, xq, sfb, w, sfa, bias, al: MoEAlignment, epi: int, alpha=1.702, limit=7.0, num_sms=None):
-    if num_sms is None:
-        num_sms = torch.cuda.get_device_properties(out.device).multi_processor_count
+_sms = {}
+
+
+def moe_gemm(out, xq, sfb, w, sfa, bias, al: MoEAlignment, epi: int, F: int, alpha=1.702, limit=7.0):
+    key = out.device.index
+    if key not in _sms:
+        _sms[key] = torch.cuda.get_device_properties(out.device).multi_processor_count
     kernels().moe_gemm(out, xq, sfb, w, sfa, bias, al.seg_offsets, al.tile_offsets, al.bn, epi, alpha, limit,
-                       num_sms, _status(out.device))
+                       _sms[key], _status(out.device), F)
     return out
 
 
@@ -296,10 +320,10 @@ def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew:
     xq, sfb = gather_quant_mxfp8(x, al.sorted_src, R, bn)
     epi = EPI_SWIGLU_CLAMP if activation == "swiglu_clamp" else EPI_SILU
     act = torch.empty(R, ew.inter, dtype=torch.bfloat16, device=x.device)
-    moe_gemm(act, xq, sfb, ew.w13, ew.sfa13, ew.b13, al, epi, alpha, limit)
+    moe_gemm(act, xq, sfb, ew.w13, ew.sfa13, ew.b13, al, epi, 2 * ew.inter, alpha, limit)
     aq, sfb2 = gather_quant_mxfp8(act, None, R, bn)
     y = torch.empty(R, H, dtype=torch.bfloat16, device=x.device)
-    moe_gemm(y, aq, sfb2, ew.w2, ew.sfa2, ew.b2, al, EPI_BIAS)
+    moe_gemm(y, aq, sfb2, ew.w2, ew.sfa2, ew.b2, al, EPI_BIAS, H)
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
     moe_combine(out, y, al.inv_map, topk_w)
@@ -324,11 +348,11 @@ def expert_dense_weights(ew: ExpertWeights, e: int):
     s2 = ew.sfa2[e].view(MT2, KB2, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(MT2 * 128, KB2 * 4)
     s2 = s2[: ew.hidden, : ew.inter // 32]
     if ew.fp4:
-        w13 = dequant_mxfp4(ew.w13[e][:, : ew.hidden // 2], s13)
-        w2 = dequant_mxfp4(ew.w2[e][:, : ew.inter // 2], s2)
+        w13 = dequant_mxfp4(untile_weights(ew.w13[e:e + 1], 2 * ew.inter, ew.hidden // 2)[0], s13)
+        w2 = dequant_mxfp4(untile_weights(ew.w2[e:e + 1], ew.hidden, ew.inter // 2)[0], s2)
     else:
-        w13 = dequant_mxfp8(ew.w13[e], s13)
-        w2 = dequant_mxfp8(ew.w2[e], s2)
+        w13 = dequant_mxfp8(untile_weights(ew.w13[e:e + 1], 2 * ew.inter, ew.hidden)[0], s13)
+        w2 = dequant_mxfp8(untile_weights(ew.w2[e:e + 1], ew.hidden, ew.inter)[0], s2)
     return w13, w2
 
 

@@ -200,7 +200,14 @@ def test_gather_quant_mxfp8(bn):
     src = torch.randint(-1, T, (rows,), dtype=torch.int32)
     q_ref, sf_ref = gather_quant_mxfp8(x, src, rows, bn)
     q, sf = gather_quant_mxfp8(x.to(DEV), src.to(DEV), rows, bn)
-    assert torch.equal(sf.cpu(), sf_ref)
+    # compare the scale bytes the MMA reads: (row i of each BN tile, 32-block kk) of every K block
+    from sglang_neuron_b200.ops.moe import sf_atom_offset, sf_chunk_bytes
+    KB = (H + 127) // 128
+    i = torch.arange(bn).repeat_interleave(4)
+    kk = torch.arange(4).repeat(bn)
+    offs = sf_atom_offset(i, kk)
+    idx = torch.cat([(c * sf_chunk_bytes(bn)) + offs for c in range((rows // bn) * KB)])
+    assert torch.equal(sf.cpu()[idx], sf_ref[idx])
     assert (q.cpu().float() - q_ref.float()).abs().max().item() <= 1e-6 * 0 + 32.0 * 0.07
 
 
