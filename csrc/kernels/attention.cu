@@ -385,6 +385,11 @@ void launch_extend_g(int G, int max_ext, int B, int Hkv, cudaStream_t st, const 
 
 }  // namespace
 
+bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                          torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
+                          int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
+                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part);
+
 // q: [B, Hq*D] bf16 (row stride arbitrary). Caches: [pages, Hkv, page_size, D].
 // block_table: [B, max_pages] int32; seq_lens: [B] int32 (tokens including the new one).
 // o_part/lse_part: fp32 scratch of at least B*Hq*num_splits*D and B*Hq*num_splits elements.
@@ -417,6 +422,10 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   auto outp = (__nv_bfloat16*)out.data_ptr();
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
   TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16, "decode_attention: cache dtype");
+  // tensor-core path (mma.sync) for every GQA group up to 16 heads; the CUDA-core kernel below covers the rest
+  const bool mma_done = decode_attention_mma(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads,
+                                             num_kv_heads, head_dim, page_size, window, scale, vs, sk, S, op, lp);
+  if (!mma_done) {
 #define SNB_DEC_D(DD)                                                                                      \
   if (fp8)                                                                                                 \
     launch_decode_g<DD, uint8_t>(G, grid, st, qp, q.stride(0), (const uint8_t*)k_cache.data_ptr(),         \
@@ -437,6 +446,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   }
 #undef SNB_DEC_D
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   if (S > 1) {
     decode_merge_kernel<<<B * num_q_heads, 64, 0, st>>>(op, lp, sk, outp, out.stride(0), num_q_heads, head_dim, S,
                                                         (float)v_scale);
