@@ -43,7 +43,7 @@ void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Ten
 void silu_and_mul(torch::Tensor out, torch::Tensor x);
 // gemm_sm100.cu
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-               torch::Tensor status, int64_t bn);
+               torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sglang_neuron_b200 sm_100a kernels";

@@ -31,11 +31,14 @@ struct GemmCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Split-K: blockIdx.z selects a contiguous range of K blocks; with more than one split every CTA writes its
+// fp32 partial tile to `partial` [splits, T, F] and splitk_reduce_kernel sums them (plus the bias) to bf16.
+// Decode-sized GEMMs (few tokens, F/128 CTAs) use it to put every SM to work on the weight stream.
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                      __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ bias, int F, int T,
-                     int K, int ldo, int* status) {
+                     int K, int ldo, int* status, float* __restrict__ partial) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -48,7 +51,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int f0 = blockIdx.x * BM, t0 = blockIdx.y * BN;
-  const int nk = (K + BK - 1) / BK;
+  const int nk_all = (K + BK - 1) / BK;
+  const int per_split = (nk_all + gridDim.z - 1) / gridDim.z;
+  const int kb0 = blockIdx.z * per_split;
+  const int nk = max(0, min(nk_all, kb0 + per_split) - kb0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -76,8 +82,8 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ph = (kb / C::STAGES) & 1;
         if (!snb::mbar_wait_bounded(&empty[s], ph ^ 1, status, SNB_ERR_TIMEOUT_TMA)) break;
         snb::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        snb::tma_load_2d(sA + s * C::A_BYTES, &tmap_w, &full[s], kb * BK, f0);
-        snb::tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kb * BK, t0);
+        snb::tma_load_2d(sA + s * C::A_BYTES, &tmap_w, &full[s], (kb0 + kb) * BK, f0);
+        snb::tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], (kb0 + kb) * BK, t0);
       }
     }
   } else if (warp == 1) {
@@ -106,8 +112,14 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // Epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31.
     const int q = warp & 3;
-    const bool ok = snb::mbar_wait_bounded(accum, 0, status, SNB_ERR_TIMEOUT_EPI);
+    const bool ok = nk > 0 && snb::mbar_wait_bounded(accum, 0, status, SNB_ERR_TIMEOUT_EPI);
     snb::tc_fence_after();
+    if (nk == 0 && partial != nullptr) {
+      // empty split (K range past the end): contribute zeros
+      const int f = f0 + q * 32 + lane;
+      if (f < F)
+        for (int t = t0; t < min(T, t0 + BN); ++t) partial[((size_t)blockIdx.z * T + t) * F + f] = 0.f;
+    }
     if (ok) {
       const int f = f0 + q * 32 + lane;
       const float bf = (bias != nullptr && f < F) ? __bfloat162float(bias[f]) : 0.f;
@@ -129,10 +141,19 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (f < F) {
           const int ncol = BN >= 32 ? 32 : BN;
+          if (partial != nullptr) {
+            float* pz = partial + (size_t)blockIdx.z * T * F;
 #pragma unroll
-          for (int j = 0; j < ncol; ++j) {
-            const int t = t0 + c * 32 + j;
-            if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(__uint_as_float(r[j]) + bf);
+            for (int j = 0; j < ncol; ++j) {
+              const int t = t0 + c * 32 + j;
+              if (t < T) pz[(size_t)t * F + f] = __uint_as_float(r[j]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < ncol; ++j) {
+              const int t = t0 + c * 32 + j;
+              if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(__uint_as_float(r[j]) + bf);
+            }
           }
         }
       }
@@ -143,9 +164,19 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) snb::tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, const __nv_bfloat16* __restrict__ bias,
+                                     __nv_bfloat16* __restrict__ out, int T, int F, int ldo, int splits) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * F) return;
+  const int t = i / F, f = i % F;
+  float a = bias != nullptr ? __bfloat162float(bias[f]) : 0.f;
+  for (int z = 0; z < splits; ++z) a += partial[(size_t)z * T * F + i];
+  out[(size_t)t * ldo + f] = __float2bfloat16(a);
+}
+
 template <int BN>
 void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::Tensor& w,
-                 const __nv_bfloat16* bias, int* status, cudaStream_t st) {
+                 const __nv_bfloat16* bias, int* status, cudaStream_t st, int splits, float* partial) {
   using C = GemmCfg<BN>;
   const int T = x.size(0), K = x.size(1), F = w.size(0);
   CUtensorMap tw = snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, F, w.stride(0) * 2, BK,
@@ -157,9 +188,14 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
     cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr_set = true;
   }
-  dim3 grid((F + BM - 1) / BM, (T + BN - 1) / BN);
+  dim3 grid((F + BM - 1) / BM, (T + BN - 1) / BN, splits);
   gemm_bf16_kernel<BN><<<grid, 192, C::SMEM, st>>>(tw, tx, (__nv_bfloat16*)out.data_ptr(), bias, F, T, K,
-                                                   out.stride(0), status);
+                                                   out.stride(0), status, splits > 1 ? partial : nullptr);
+  if (splits > 1) {
+    const int n = T * F;
+    splitk_reduce_kernel<<<(n + 255) / 256, 256, 0, st>>>(partial, bias, (__nv_bfloat16*)out.data_ptr(), T, F,
+                                                          out.stride(0), splits);
+  }
 }
 
 }  // namespace
@@ -167,7 +203,7 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
 // out: [T, F] bf16 (row stride arbitrary, multiple of 8), x: [T, K] bf16, w: [F, K] bf16, bias [F] or None.
 // status: int32 CUDA tensor (>= 1 element) that receives a non-zero code if a bounded wait timed out.
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-               torch::Tensor status, int64_t bn) {
+               torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace) {
   const int T = x.size(0);
   if (T == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 inputs");
@@ -178,12 +214,20 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
   const __nv_bfloat16* bp = bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr;
   int* sp = status.data_ptr<int>();
   if (bn <= 0) bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  if (splits < 1) splits = 1;
+  float* part = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(workspace && workspace->scalar_type() == at::kFloat &&
+                    workspace->numel() >= (int64_t)splits * T * w.size(0),
+                "gemm_bf16: split-K needs a fp32 workspace of splits*T*F");
+    part = workspace->data_ptr<float>();
+  }
   switch (bn) {
-    case 16: launch_gemm<16>(out, x, w, bp, sp, st); break;
-    case 32: launch_gemm<32>(out, x, w, bp, sp, st); break;
-    case 64: launch_gemm<64>(out, x, w, bp, sp, st); break;
-    case 128: launch_gemm<128>(out, x, w, bp, sp, st); break;
-    case 256: launch_gemm<256>(out, x, w, bp, sp, st); break;
+    case 16: launch_gemm<16>(out, x, w, bp, sp, st, splits, part); break;
+    case 32: launch_gemm<32>(out, x, w, bp, sp, st, splits, part); break;
+    case 64: launch_gemm<64>(out, x, w, bp, sp, st, splits, part); break;
+    case 128: launch_gemm<128>(out, x, w, bp, sp, st, splits, part); break;
+    case 256: launch_gemm<256>(out, x, w, bp, sp, st, splits, part); break;
     default: TORCH_CHECK(false, "gemm_bf16: bn must be 16/32/64/128/256");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -47,6 +47,10 @@ class _CountingKernels:
             def call(*a, **k):
                 _launches[0] += 2 if (len(a) > 15 and int(a[15]) > 1) else 1
                 return fn(*a, **k)
+        elif name == "gemm_bf16":
+            def call(*a, **k):
+                _launches[0] += 2 if (len(a) > 6 and int(a[6]) > 1) else 1
+                return fn(*a, **k)
         else:
             def call(*a, **k):
                 _launches[0] += 1

@@ -211,15 +211,17 @@ def test_gather_quant_mxfp8(bn):
     assert (q.cpu().float() - q_ref.float()).abs().max().item() <= 1e-6 * 0 + 32.0 * 0.07
 
 
-@pytest.mark.parametrize("T,F,K,bias", [(1, 2880, 2880, True), (16, 5120, 2880, False), (77, 4096, 4096, True),
-                                        (300, 1024, 3072, False), (1000, 384, 512, True)])
-def test_gemm_bf16_tcgen05(T, F, K, bias):
+@pytest.mark.parametrize("T,F,K,bias,splits", [(1, 2880, 2880, True, None), (16, 5120, 2880, False, None),
+                                               (77, 4096, 4096, True, None), (300, 1024, 3072, False, None),
+                                               (1000, 384, 512, True, None), (64, 2880, 4096, True, 5),
+                                               (5, 128, 2880, True, 3), (64, 5120, 2880, False, 1)])
+def test_gemm_bf16_tcgen05(T, F, K, bias, splits):
     from sglang_neuron_b200.ops.gemm import linear, check_status
     torch.manual_seed(8)
     x = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(F, K, device=DEV, dtype=torch.bfloat16) * 0.05
     b = torch.randn(F, device=DEV, dtype=torch.bfloat16) if bias else None
-    y = linear(x, w, b)
+    y = linear(x, w, b, splits=splits)
     torch.cuda.synchronize()
     check_status(x.device)
     ref = x.float() @ w.float().t() + (b.float() if bias else 0)
