@@ -45,6 +45,13 @@ void silu_and_mul(torch::Tensor out, torch::Tensor x);
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace);
 
+// allreduce.cu
+std::tuple<int64_t, py::bytes> symm_alloc(int64_t capacity, int64_t world);
+int64_t symm_open(py::bytes handle);
+void symm_close(int64_t ptr, bool owned);
+void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
+                        int64_t capacity, int64_t num_ctas, torch::Tensor status);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sglang_neuron_b200 sm_100a kernels";
   m.def("rmsnorm_out", &rmsnorm_out);
@@ -61,4 +68,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &gemm_bf16);
   m.def("moe_gemm", &moe_gemm);
   m.def("silu_and_mul", &silu_and_mul);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("one_shot_allreduce", &one_shot_allreduce);
 }

@@ -33,7 +33,8 @@ def pick_splits(T: int, F: int, K: int, num_sms: int = 148) -> int:
     nk = (K + 63) // 64
     if ctas >= num_sms:
         return 1
-    return int(max(1, min((2 * num_sms + ctas - 1) // ctas, nk // 4, 16)))
+    # one CTA per SM (the kernel's pipeline takes ~200 KB of shared memory): stay within one wave
+    return int(max(1, min(num_sms // ctas, nk // 2, 16)))
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, out=None,

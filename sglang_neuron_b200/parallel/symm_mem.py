@@ -1,0 +1,55 @@
+"""Symmetric device buffers over CUDA IPC and the one-shot NVLink all-reduce built on them.
+
+Every rank of the TP group allocates one buffer, exports its IPC handle, gathers the others' handles over
+the host (gloo) group and maps them, so a kernel on any rank can store into any peer's buffer over NVLink.
+Parity: the reference lowers its TP all-reduce into the compiled graph over CCOM
+(sglang_neuron/parallel/collectives.py:22-55); on B200 the equivalent low-latency path is peer memory.
+"""
+from __future__ import annotations
+
+import logging
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .._ext import kernels
+from .state import get_state
+
+logger = logging.getLogger(__name__)
+
+
+class IpcAllReduce:
+    def __init__(self, capacity_bytes: int = 8 << 20, max_ctas: int = 64):
+        st = get_state()
+        self.rank, self.world = st.tp_rank, st.tp_size
+        self.capacity = capacity_bytes
+        self.max_ctas = max_ctas
+        k = kernels()
+        ptr, handle = k.symm_alloc(capacity_bytes, self.world)
+        self.own = ptr
+        handles: List = [None] * self.world
+        dist.all_gather_object(handles, (self.rank, handle), group=st.cpu_group)
+        self.ptrs = [0] * self.world
+        for r, h in handles:
+            self.ptrs[r] = ptr if r == self.rank else k.symm_open(h)
+        self.status = torch.zeros(4, dtype=torch.int32, device=st.device)
+
+    def can_run(self, x: torch.Tensor) -> bool:
+        return (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.numel() % 8 == 0
+                and x.numel() * 2 <= self.capacity)
+
+    def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(x)
+        nvec = x.numel() // 8
+        ctas = max(1, min(self.max_ctas, (nvec + 2047) // 2048))
+        kernels().one_shot_allreduce(out, x, self.ptrs, self.rank, self.capacity, ctas, self.status)
+        return out
+
+    def close(self) -> None:
+        k = kernels()
+        for r, p in enumerate(self.ptrs):
+            if p:
+                k.symm_close(p, r == self.rank)
+        self.ptrs = []
