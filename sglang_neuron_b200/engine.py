@@ -43,6 +43,14 @@ class Engine:
             device = torch.device("cpu")
         st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device)
         self.rank = st.rank
+        self.custom_ar = None
+        if st.tp_size > 1 and device.type == "cuda":
+            from . import env_registry
+            if not env_registry.get_bool("SGLANG_B200_DISABLE_FUSED_COLLECTIVES", False):
+                from .parallel.collectives import set_custom_allreduce
+                from .parallel.symm_mem import IpcAllReduce
+                self.custom_ar = IpcAllReduce()
+                set_custom_allreduce(self.custom_ar)
         self.runner = ModelRunner(args, self.cfg, device)
         self.scheduler = Scheduler(args, self.cfg, self.runner)
         self.tokenizer = None
@@ -115,3 +123,9 @@ class Engine:
         self.scheduler.drain()
         if self.runner.graph_runner is not None:
             self.runner.graph_runner.graphs.clear()
+        if self.custom_ar is not None:
+            from .parallel.collectives import set_custom_allreduce
+            torch.cuda.synchronize()
+            set_custom_allreduce(None)
+            self.custom_ar.close()
+            self.custom_ar = None

@@ -1,0 +1,103 @@
+"""Multi-GPU tier (needs >= 2 GPUs): the one-shot NVLink all-reduce against NCCL, and a TP=2 engine whose
+ranks agree token for token. Each rank is its own process on its own GPU; the process group has a short
+timeout so a lost peer ends the test with an error instead of a hang."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+needs2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from sglang_neuron_b200.parallel.state import init_process_group_from_env
+    init_process_group_from_env(timeout_s=60)
+
+
+def _ar_worker(rank, world, port, q):
+    _init(rank, world, port)
+    import torch.distributed as dist
+    from sglang_neuron_b200.parallel.state import initialize_parallel
+    from sglang_neuron_b200.parallel.symm_mem import IpcAllReduce
+    initialize_parallel(world, device=torch.device("cuda", rank))
+    ar = IpcAllReduce(capacity_bytes=4 << 20)
+    errs = []
+    for i, n in enumerate([8, 2880 * 64, 4096 * 3, 1 << 20, 2880 * 64]):
+        g = torch.Generator(device="cuda").manual_seed(100 * i + rank)
+        x = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16)
+        ref = x.float().clone()
+        dist.all_reduce(ref)
+        out = ar.all_reduce(x)
+        torch.cuda.synchronize()
+        errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    status = int(ar.status[0])
+    ar.close()
+    q.put((rank, errs, status))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _engine_worker(rank, world, port, q):
+    _init(rank, world, port)
+    import torch.distributed as dist
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.server_args import ServerArgs
+    mc.PRESETS["mg-oss"] = dict(mc.PRESETS["gpt-oss-120b"], num_hidden_layers=2, vocab_size=2048, hidden_size=512,
+                                intermediate_size=256, num_local_experts=8, num_attention_heads=8,
+                                num_key_value_heads=2, head_dim=64, sliding_window=16)
+    eng = Engine(ServerArgs(model="mg-oss", tp_size=world, page_size=16, context_length=256,
+                            max_running_requests=4, chunked_prefill_size=64, cuda_graph_bs=[1, 2, 4],
+                            random_weight_std=0.05))
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, 2048, (n,), generator=g).tolist() for n in (9, 40)]
+    out = eng.generate(prompts, {"max_new_tokens": 8})
+    eng.shutdown()
+    q.put((rank, [o["output_ids"] for o in out]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _spawn(fn, world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in ps:
+        item = q.get(timeout=240)
+        res[item[0]] = item[1:]
+    for p in ps:
+        p.join(timeout=60)
+    return res
+
+
+@needs2
+def test_one_shot_allreduce_matches_nccl():
+    res = _spawn(_ar_worker, 2)
+    for rank, (errs, status) in res.items():
+        assert status == 0, f"rank {rank}: bounded wait expired"
+        assert max(errs) < 1e-2, f"rank {rank}: {errs}"
+
+
+@needs2
+def test_tp2_engine_ranks_agree():
+    res = _spawn(_engine_worker, 2)
+    assert res[0][0] == res[1][0]
+    assert all(len(o) == 8 for o in res[0][0])
