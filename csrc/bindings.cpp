@@ -45,12 +45,18 @@ void silu_and_mul(torch::Tensor out, torch::Tensor x);
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace);
 
+void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                         torch::Tensor status, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
+                         int64_t num_sms);
 // allreduce.cu
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t capacity, int64_t world);
 int64_t symm_open(py::bytes handle);
 void symm_close(int64_t ptr, bool owned);
 void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
                         int64_t capacity, int64_t num_ctas, torch::Tensor status);
+void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w,
+                           std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas,
+                           torch::Tensor status);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sglang_neuron_b200 sm_100a kernels";
@@ -72,4 +78,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("one_shot_allreduce", &one_shot_allreduce);
+  m.def("moe_combine_allreduce", &moe_combine_allreduce);
+  m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
 }

@@ -2,7 +2,8 @@
 // the decode path, plus the IPC plumbing that maps every rank's buffer into every other rank.
 //
 // Each rank owns one device buffer laid out as [2 halves][world slots][capacity bytes] followed by per-CTA
-// flags [world][max CTAs] and per-CTA epochs. A call with epoch e uses half (e & 1):
+// flags [world][max CTAs], a call counter and a completion ticket. Every CTA of a call reads the same epoch
+// e = counter + 1 (the last CTA to finish stores it), and the call uses half (e & 1):
 //   1. CTA c stores its chunk of the local input into every peer's buffer, slot = my rank (P2P stores),
 //   2. then publishes flag[peer][my rank][c] = e with a system-scope release store,
 //   3. waits (bounded, acquire loads) until flag[me][q][c] >= e for every rank q,
@@ -18,87 +19,63 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <cuda_runtime.h>
 #include "../common.cuh"
+#include "../ar_common.cuh"
+
+using namespace snb_ar;
 
 namespace {
 
-constexpr int kMaxRanks = 8;
-constexpr int kMaxCtas = 64;
 constexpr int kThreadsAR = 512;
-
-struct ARPeers {
-  uint8_t* buf[kMaxRanks];  // mapped base of every rank's buffer (mine included)
-};
-
-SNB_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-SNB_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(kThreadsAR) one_shot_allreduce_kernel(
     ARPeers peers, int rank, int world, size_t capacity, const __nv_bfloat16* __restrict__ in,
     __nv_bfloat16* __restrict__ out, int64_t n, int* status) {
-  const int c = blockIdx.x;
-  uint8_t* mine = peers.buf[rank];
-  const size_t data_bytes = 2 * (size_t)world * capacity;
-  uint32_t* flags_mine = reinterpret_cast<uint32_t*>(mine + data_bytes);   // [world][kMaxCtas]
-  uint32_t* epochs = flags_mine + kMaxRanks * kMaxCtas;                     // [kMaxCtas], local only
-  __shared__ uint32_t e_s;
-  if (threadIdx.x == 0) e_s = epochs[c] + 1;
-  __syncthreads();
-  const uint32_t e = e_s;
+  const ARBuf b = ar_layout(peers, rank, world, capacity);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
   const int half = e & 1;
-  // chunk of this CTA, in 16-byte vectors
   const int64_t nvec = n / 8;
   const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
-  const int64_t v0 = c * per, v1 = min(nvec, v0 + per);
-  // 1. push my chunk into every peer's slot `rank`
+  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
   for (int p = 0; p < world; ++p) {
-    uint4* dst = reinterpret_cast<uint4*>(peers.buf[p] + ((size_t)half * world + rank) * capacity);
+    uint4* dst = reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity));
     const uint4* src = reinterpret_cast<const uint4*>(in);
     for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
   }
-  __syncthreads();
-  // 2. publish (release orders the stores above for the peers' acquire loads)
-  if (threadIdx.x < world) {
-    const int p = threadIdx.x;
-    uint32_t* fp = reinterpret_cast<uint32_t*>(peers.buf[p] + data_bytes);
-    __threadfence_system();
-    st_release_sys(fp + rank * kMaxCtas + c, e);
-  }
-  // 3. wait for every rank's chunk (bounded)
-  __shared__ int ok_s;
-  if (threadIdx.x == 0) ok_s = 1;
-  __syncthreads();
-  if (threadIdx.x < world) {
-    const uint32_t* fp = flags_mine + threadIdx.x * kMaxCtas + c;
-    const uint64_t t0 = snb::globaltimer_ns();
-    while (ld_acquire_sys(fp) < e) {
-      if (snb::globaltimer_ns() - t0 > SNB_WAIT_NS) {
-        snb::record_status(status, SNB_ERR_TIMEOUT_PEER);
-        ok_s = 0;
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) epochs[c] = e;
-  if (!ok_s) return;
-  // 4. reduce over the world slots of my buffer
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  ar_finish(b, e);
+}
+
+// MoE combine fused with the expert-parallel all-reduce: each rank forms its partial
+// sum_j w[t,j] * y[inv_map[t*K+j]] over the experts it owns, stores it straight into every peer's slot,
+// and reduces the world's partials for its chunk of tokens. One launch replaces combine + all-reduce.
+__global__ void __launch_bounds__(kThreadsAR) moe_combine_allreduce_kernel(
+    ARPeers peers, int rank, int world, size_t capacity, const __nv_bfloat16* __restrict__ y, int ys,
+    const int32_t* __restrict__ inv_map, const float* __restrict__ w, int K, int T, int H,
+    __nv_bfloat16* __restrict__ out, int* status) {
+  const ARBuf b = ar_layout(peers, rank, world, capacity);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
+  const int half = e & 1;
+  const int64_t nvec = (int64_t)T * H / 8;
+  const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
+  const int hv = H / 8;
   for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    const int t = (int)(v / hv), c = (int)(v % hv);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < world; ++q) {
-      const uint4 u = reinterpret_cast<const uint4*>(mine + ((size_t)half * world + q) * capacity)[v];
+    for (int j = 0; j < K; ++j) {
+      const int r = inv_map[t * K + j];
+      if (r < 0) continue;
+      const float wj = w[t * K + j];
       float f[8];
-      snb::unpack_bf16x8(u, f);
+      snb::unpack_bf16x8(reinterpret_cast<const uint4*>(y + (size_t)r * ys)[c], f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += f[i];
+      for (int i = 0; i < 8; ++i) acc[i] += wj * f[i];
     }
-    reinterpret_cast<uint4*>(out)[v] = snb::pack_bf16x8(acc);
+    const uint4 packed = snb::pack_bf16x8(acc);
+    for (int p = 0; p < world; ++p) reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity))[v] = packed;
   }
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  ar_finish(b, e);
 }
 
 }  // namespace
@@ -108,7 +85,7 @@ __global__ void __launch_bounds__(kThreadsAR) one_shot_allreduce_kernel(
 // and return (device pointer, IPC handle bytes).
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t capacity, int64_t world) {
   TORCH_CHECK(world >= 1 && world <= kMaxRanks, "symm_alloc: world size");
-  const size_t bytes = 2 * (size_t)world * capacity + (kMaxRanks * kMaxCtas + kMaxCtas) * sizeof(uint32_t);
+  const size_t bytes = 2 * (size_t)world * capacity + (kMaxRanks * kMaxCtas + 2) * sizeof(uint32_t);
   void* p = nullptr;
   TORCH_CHECK(cudaMalloc(&p, bytes) == cudaSuccess, "symm_alloc: cudaMalloc failed");
   TORCH_CHECK(cudaMemset(p, 0, bytes) == cudaSuccess, "symm_alloc: memset failed");
@@ -146,5 +123,22 @@ void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t
   one_shot_allreduce_kernel<<<num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream()>>>(
       peers, rank, world, capacity, (const __nv_bfloat16*)in.data_ptr(), (__nv_bfloat16*)out.data_ptr(), n,
       status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w,
+                           std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas,
+                           torch::Tensor status) {
+  const int world = (int)bufs.size();
+  const int T = out.size(0), H = out.size(1), K = w.size(1);
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && H % 8 == 0, "moe_combine_allreduce: shape");
+  TORCH_CHECK((size_t)T * H * 2 <= (size_t)capacity, "moe_combine_allreduce: over capacity");
+  TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "moe_combine_allreduce: CTA count");
+  if (T == 0) return;
+  ARPeers peers;
+  for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  moe_combine_allreduce_kernel<<<num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream()>>>(
+      peers, rank, world, capacity, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
+      w.data_ptr<float>(), K, T, H, (__nv_bfloat16*)out.data_ptr(), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

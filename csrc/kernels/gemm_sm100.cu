@@ -15,6 +15,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include "../common.cuh"
 #include "../tma_host.h"
+#include "../ar_common.cuh"
 
 namespace {
 
@@ -34,11 +35,23 @@ struct GemmCfg {
 // Split-K: blockIdx.z selects a contiguous range of K blocks; with more than one split every CTA writes its
 // fp32 partial tile to `partial` [splits, T, F] and splitk_reduce_kernel sums them (plus the bias) to bf16.
 // Decode-sized GEMMs (few tokens, F/128 CTAs) use it to put every SM to work on the weight stream.
-template <int BN>
+// AR = true: the epilogue all-reduces its output tile over the tensor-parallel group inside this kernel:
+// the bf16 tile is stored straight into every peer's symmetric buffer (slot = my rank, NVLink P2P stores),
+// the tile's flag is released to every peer, the CTA waits (bounded) for the same tile from every rank and
+// writes the sum. Communication of a finished tile overlaps the MMAs of the tiles still running.
+struct GemmAR {
+  snb_ar::ARPeers peers;
+  int rank, world;
+  size_t capacity;
+};
+
+SNB_DEVICE void bar_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int BN, bool AR>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                      __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ bias, int F, int T,
-                     int K, int ldo, int* status, float* __restrict__ partial) {
+                     int K, int ldo, int* status, float* __restrict__ partial, const GemmAR ar) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -120,6 +133,14 @@ __global__ void __launch_bounds__(192, 1)
       if (f < F)
         for (int t = t0; t < min(T, t0 + BN); ++t) partial[((size_t)blockIdx.z * T + t) * F + f] = 0.f;
     }
+    uint32_t ar_epoch = 0;
+    int ar_half = 0;
+    snb_ar::ARBuf arb;
+    if constexpr (AR) {
+      arb = snb_ar::ar_layout(ar.peers, ar.rank, ar.world, ar.capacity);
+      ar_epoch = *reinterpret_cast<volatile uint32_t*>(arb.counter) + 1;
+      ar_half = ar_epoch & 1;
+    }
     if (ok) {
       const int f = f0 + q * 32 + lane;
       const float bf = (bias != nullptr && f < F) ? __bfloat162float(bias[f]) : 0.f;
@@ -141,7 +162,18 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (f < F) {
           const int ncol = BN >= 32 ? 32 : BN;
-          if (partial != nullptr) {
+          if constexpr (AR) {
+#pragma unroll
+            for (int j = 0; j < ncol; ++j) {
+              const int t = t0 + c * 32 + j;
+              if (t < T) {
+                const __nv_bfloat16 v = __float2bfloat16(__uint_as_float(r[j]) + bf);
+                for (int p = 0; p < ar.world; ++p)
+                  reinterpret_cast<__nv_bfloat16*>(
+                      snb_ar::ar_slot(ar.peers, p, ar_half, ar.rank, ar.world, ar.capacity))[(size_t)t * F + f] = v;
+              }
+            }
+          } else if (partial != nullptr) {
             float* pz = partial + (size_t)blockIdx.z * T * F;
 #pragma unroll
             for (int j = 0; j < ncol; ++j) {
@@ -155,6 +187,51 @@ __global__ void __launch_bounds__(192, 1)
               if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(__uint_as_float(r[j]) + bf);
             }
           }
+        }
+      }
+    }
+    if constexpr (AR) {
+      // publish this tile, wait for it from every rank, reduce (epilogue warps only: named barrier 1)
+      __shared__ int ar_ok;
+      const int tile = blockIdx.x + blockIdx.y * gridDim.x;
+      bar_epilogue();
+      if (warp == 2 && lane == 0) ar_ok = ok ? 1 : 0;
+      if (warp == 2 && lane < ar.world) {
+        uint32_t* fp = reinterpret_cast<uint32_t*>(ar.peers.buf[lane] + 2 * (size_t)ar.world * ar.capacity);
+        __threadfence_system();
+        snb_ar::st_release_sys(fp + ar.rank * snb_ar::kMaxCtas + tile, ar_epoch);
+      }
+      bar_epilogue();
+      if (warp == 2 && lane < ar.world) {
+        const uint32_t* fp = arb.flags + lane * snb_ar::kMaxCtas + tile;
+        const uint64_t tw = snb::globaltimer_ns();
+        while (snb_ar::ld_acquire_sys(fp) < ar_epoch) {
+          if (snb::globaltimer_ns() - tw > SNB_WAIT_NS) {
+            snb::record_status(status, SNB_ERR_TIMEOUT_PEER);
+            ar_ok = 0;
+            break;
+          }
+        }
+      }
+      bar_epilogue();
+      const int f = f0 + q * 32 + lane;
+      if (ar_ok && f < F) {
+        for (int t = t0; t < min(T, t0 + BN); ++t) {
+          float acc = 0.f;
+          for (int p = 0; p < ar.world; ++p)
+            acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(
+                snb_ar::ar_slot(ar.peers, ar.rank, ar_half, p, ar.world, ar.capacity))[(size_t)t * F + f]);
+          out[(size_t)t * ldo + f] = __float2bfloat16(acc);
+        }
+      }
+      bar_epilogue();
+      if (warp == 2 && lane == 0) {
+        __threadfence();
+        const uint32_t tk = atomicAdd(arb.ticket, 1u);
+        if (tk == gridDim.x * gridDim.y - 1) {
+          *arb.counter = ar_epoch;
+          *arb.ticket = 0;
+          __threadfence();
         }
       }
     }
@@ -174,9 +251,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const __
   out[(size_t)t * ldo + f] = __float2bfloat16(a);
 }
 
-template <int BN>
+template <int BN, bool AR = false>
 void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::Tensor& w,
-                 const __nv_bfloat16* bias, int* status, cudaStream_t st, int splits, float* partial) {
+                 const __nv_bfloat16* bias, int* status, cudaStream_t st, int splits, float* partial,
+                 const GemmAR& ar = GemmAR{}) {
   using C = GemmCfg<BN>;
   const int T = x.size(0), K = x.size(1), F = w.size(0);
   CUtensorMap tw = snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, F, w.stride(0) * 2, BK,
@@ -185,12 +263,12 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
                                           BN, CU_TENSOR_MAP_SWIZZLE_128B);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaFuncSetAttribute(gemm_bf16_kernel<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr_set = true;
   }
   dim3 grid((F + BM - 1) / BM, (T + BN - 1) / BN, splits);
-  gemm_bf16_kernel<BN><<<grid, 192, C::SMEM, st>>>(tw, tx, (__nv_bfloat16*)out.data_ptr(), bias, F, T, K,
-                                                   out.stride(0), status, splits > 1 ? partial : nullptr);
+  gemm_bf16_kernel<BN, AR><<<grid, 192, C::SMEM, st>>>(tw, tx, (__nv_bfloat16*)out.data_ptr(), bias, F, T, K,
+                                                       out.stride(0), status, splits > 1 ? partial : nullptr, ar);
   if (splits > 1) {
     const int n = T * F;
     splitk_reduce_kernel<<<(n + 255) / 256, 256, 0, st>>>(partial, bias, (__nv_bfloat16*)out.data_ptr(), T, F,
@@ -229,6 +307,40 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
     case 128: launch_gemm<128>(out, x, w, bp, sp, st, splits, part); break;
     case 256: launch_gemm<256>(out, x, w, bp, sp, st, splits, part); break;
     default: TORCH_CHECK(false, "gemm_bf16: bn must be 16/32/64/128/256");
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// GEMM whose epilogue all-reduces the output over the TP group through the symmetric peer buffers
+// (see gemm_bf16_kernel, AR = true). Requires one wave of CTAs (every tile co-resident) and T*F*2 bytes of
+// buffer capacity; out: [T, F] contiguous.
+void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                         torch::Tensor status, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
+                         int64_t num_sms) {
+  const int T = x.size(0), F = w.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_bf16_allreduce: bf16");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.is_contiguous(), "gemm_bf16_allreduce: layout");
+  const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  const int tiles = ((F + BM - 1) / BM) * ((T + bn - 1) / bn);
+  TORCH_CHECK(tiles <= num_sms && tiles <= snb_ar::kMaxCtas, "gemm_bf16_allreduce: more tiles than one wave");
+  TORCH_CHECK((size_t)T * F * 2 <= (size_t)capacity, "gemm_bf16_allreduce: over buffer capacity");
+  GemmAR ar;
+  ar.rank = rank;
+  ar.world = (int)bufs.size();
+  ar.capacity = capacity;
+  TORCH_CHECK(ar.world >= 1 && ar.world <= snb_ar::kMaxRanks, "gemm_bf16_allreduce: world size");
+  for (int i = 0; i < snb_ar::kMaxRanks; ++i)
+    ar.peers.buf[i] = i < ar.world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const __nv_bfloat16* bp = bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr;
+  int* sp = status.data_ptr<int>();
+  switch (bn) {
+    case 16: launch_gemm<16, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
+    case 32: launch_gemm<32, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
+    case 64: launch_gemm<64, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
+    case 128: launch_gemm<128, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
+    default: launch_gemm<256, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -13,7 +13,7 @@ import torch
 from torch import nn
 
 from ..ops.gemm import linear
-from ..parallel.collectives import tp_all_reduce
+from ..parallel.collectives import fused_gemm_all_reduce, tp_all_reduce
 from ..parallel.state import get_state
 
 
@@ -137,6 +137,10 @@ class RowParallelLinear(nn.Module):
         st = get_state()
         # the bias is added once (on rank 0) so the all-reduce sums it exactly once
         b = self.bias if (self.bias is not None and st.tp_rank == 0) else None
+        if self.reduce and st.tp_size > 1:
+            y = fused_gemm_all_reduce(x, self.weight, b)
+            if y is not None:
+                return y
         y = linear(x, self.weight, b)
         if self.reduce and st.tp_size > 1:
             y = tp_all_reduce(y)

@@ -28,7 +28,7 @@ from ..ops import activation as act_ops
 from ..ops import moe as moe_ops
 from ..ops.norm import fused_add_rmsnorm, rmsnorm
 from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
-from ..parallel.collectives import tp_all_reduce
+from ..parallel.collectives import fused_combine_all_reduce, tp_all_reduce
 from ..parallel.state import get_state
 
 
@@ -164,6 +164,17 @@ class MoEBlock(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         logits = self.router(x)
         w, ids = moe_ops.topk_route(logits, self.top_k, self.route_mode, self.cfg.routed_scaling_factor)
+        if self.shared is None and x.is_cuda and get_state().tp_size > 1:
+            # combine + expert-parallel all-reduce fused into one NVLink kernel when available
+            reduced = [False]
+
+            def combine(out, y, inv_map, topk_w):
+                reduced[0] = fused_combine_all_reduce(out, y, inv_map, topk_w)
+                return reduced[0]
+
+            out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
+                                    self.cfg.swiglu_limit, e_lo=self.e_lo, combine_fn=combine)
+            return out if reduced[0] else tp_all_reduce(out)
         out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
                                 self.cfg.swiglu_limit, e_lo=self.e_lo)
         if self.shared is not None:

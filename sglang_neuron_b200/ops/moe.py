@@ -304,8 +304,11 @@ def pick_bn(num_tokens: int, top_k: int, num_experts: int) -> int:
 
 def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew: ExpertWeights,
               activation: str = "swiglu_clamp", alpha: float = 1.702, limit: float = 7.0,
-              e_lo: int = 0, bn: int = 0, al: Optional[MoEAlignment] = None, out=None) -> torch.Tensor:
-    """sum_j w[t,j] * expert_{id[t,j]}(x[t]) over the experts owned here ([e_lo, e_lo + E_local))."""
+              e_lo: int = 0, bn: int = 0, al: Optional[MoEAlignment] = None, out=None,
+              combine_fn=None) -> torch.Tensor:
+    """sum_j w[t,j] * expert_{id[t,j]}(x[t]) over the experts owned here ([e_lo, e_lo + E_local)).
+    `combine_fn(out, y, inv_map, w) -> bool` may replace the final combine (e.g. with the combine fused into
+    the expert-parallel all-reduce); it returns False to fall back to the local combine."""
     T, H = x.shape
     K = topk_ids.shape[1]
     if not x.is_cuda:
@@ -326,6 +329,8 @@ def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew:
     moe_gemm(y, aq, sfb2, ew.w2, ew.sfa2, ew.b2, al, EPI_BIAS, H)
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    if combine_fn is not None and combine_fn(out, y, al.inv_map[: T * K], topk_w):
+        return out
     moe_combine(out, y, al.inv_map, topk_w)
     return out
 

@@ -29,6 +29,35 @@ def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
+def fused_combine_all_reduce(out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor, w: torch.Tensor) -> bool:
+    """MoE combine + TP/EP all-reduce in one NVLink kernel; returns False when that path is unavailable."""
+    st = get_state()
+    if st.tp_size == 1 or _custom_allreduce is None or not _custom_allreduce.can_run(out):
+        return False
+    _custom_allreduce.combine_all_reduce(out, y, inv_map, w)
+    return True
+
+
+_num_sms = {}
+
+
+def fused_gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias):
+    """Row-parallel GEMM + all-reduce in one NVLink kernel, or None when that path does not apply."""
+    st = get_state()
+    if st.tp_size == 1 or _custom_allreduce is None or not x.is_cuda or x.dtype != torch.bfloat16:
+        return None
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    dev = x.device.index
+    if dev not in _num_sms:
+        _num_sms[dev] = torch.cuda.get_device_properties(x.device).multi_processor_count
+    if not _custom_allreduce.gemm_can_run(x2.shape[0], w.shape[0], _num_sms[dev]):
+        return None
+    out = _custom_allreduce.gemm_all_reduce(x2, w, bias, _num_sms[dev])
+    return out.view(*x.shape[:-1], w.shape[0])
+
+
 def tp_all_gather(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
     st = get_state()
     if st.tp_size == 1:

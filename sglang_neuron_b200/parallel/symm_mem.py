@@ -47,6 +47,27 @@ class IpcAllReduce:
         kernels().one_shot_allreduce(out, x, self.ptrs, self.rank, self.capacity, ctas, self.status)
         return out
 
+    def combine_all_reduce(self, out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor,
+                           w: torch.Tensor) -> torch.Tensor:
+        """MoE combine (weighted sum of this rank's expert rows per token) fused with the all-reduce."""
+        nvec = out.numel() // 8
+        ctas = max(1, min(self.max_ctas, (nvec + 2047) // 2048))
+        kernels().moe_combine_allreduce(out, y, inv_map, w, self.ptrs, self.rank, self.capacity, ctas, self.status)
+        return out
+
+    def gemm_can_run(self, T: int, F: int, num_sms: int) -> bool:
+        bn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
+        tiles = ((F + 127) // 128) * ((T + bn - 1) // bn)
+        return tiles <= min(num_sms, 1024) and T * F * 2 <= self.capacity
+
+    def gemm_all_reduce(self, x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
+                        num_sms: int) -> torch.Tensor:
+        """out = all_reduce(x @ w.T (+ bias on rank 0 only)) in one kernel: tcgen05 GEMM whose epilogue
+        stores its tiles into every peer's buffer and reduces them."""
+        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+        kernels().gemm_bf16_allreduce(out, x, w, bias, self.status, self.ptrs, self.rank, self.capacity, num_sms)
+        return out
+
     def close(self) -> None:
         k = kernels()
         for r, p in enumerate(self.ptrs):

@@ -44,6 +44,35 @@ def _ar_worker(rank, world, port, q):
         out = ar.all_reduce(x)
         torch.cuda.synchronize()
         errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    # MoE combine fused with the all-reduce vs combine + NCCL all-reduce
+    from sglang_neuron_b200.ops.moe import MoEAlignment, moe_align, moe_combine, topk_route
+    T, H, E = 64, 2880, 16
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    w, ids = topk_route(torch.randn(T, E, device="cuda", generator=g), 4)
+    al = MoEAlignment(T * 4, E // world, 16, "cuda")
+    moe_align(ids, rank * (E // world), E // world, al)
+    y = torch.randn(al.r_max, H, device="cuda", generator=g).to(torch.bfloat16)
+    ref = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    moe_combine(ref, y, al.inv_map, w)
+    ref = ref.float()
+    dist.all_reduce(ref)
+    out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):  # repeated calls cycle the epoch / buffer halves
+        ar.combine_all_reduce(out, y, al.inv_map[: T * 4], w)
+    torch.cuda.synchronize()
+    errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    # row-parallel GEMM with the all-reduce in its epilogue vs GEMM + NCCL
+    from sglang_neuron_b200.ops.gemm import linear
+    for T, F, Kl in [(64, 2880, 512), (7, 2880, 4096 // world), (1, 1024, 256)]:
+        g = torch.Generator(device="cuda").manual_seed(11 + rank + T)
+        x = torch.randn(T, Kl, device="cuda", generator=g).to(torch.bfloat16)
+        wt = (torch.randn(F, Kl, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        ref = (x.float() @ wt.float().t())
+        dist.all_reduce(ref)
+        for _ in range(2):
+            out = ar.gemm_all_reduce(x, wt, None, torch.cuda.get_device_properties(0).multi_processor_count)
+        torch.cuda.synchronize()
+        errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
     status = int(ar.status[0])
     ar.close()
     q.put((rank, errs, status))
