@@ -89,6 +89,8 @@ class Engine:
             sps = sampling_params
         else:
             sps = [sampling_params] * len(prompts)
+        if self.args.speculative_algorithm == "MTP":
+            return self._generate_spec(prompts, sps)
         handles = [self.submit(p, sp) for p, sp in zip(prompts, sps)]
         if get_state().tp_rank != 0:
             # follower: step in lockstep until rank 0's matching requests have finished here too
@@ -110,6 +112,33 @@ class Engine:
             if self.tokenizer is not None:
                 d["text"] = self.tokenizer.decode(r.output_ids)
             out.append(d)
+        return out
+
+    def _generate_spec(self, prompts, sps) -> List[Dict]:
+        """Speculative (MTP) generation: greedy, host-synchronous verify/accept steps."""
+        from .managers.schedule_batch import Req
+        from .speculative.mtp import MTPWorker
+        if not hasattr(self, "_mtp"):
+            self._mtp = MTPWorker(self, self.args.speculative_num_draft_tokens)
+        sched = self.scheduler
+        reqs = []
+        for p, sp in zip(prompts, sps):
+            sp = sp if isinstance(sp, SamplingParams) else SamplingParams.from_dict(sp)
+            if sp.temperature > 0:
+                raise ValueError("MTP speculative decoding serves greedy sampling only")
+            r = Req(f"req-{next(self._ids)}", self._to_ids(p), sp)
+            if not sched.free_slots:
+                raise RuntimeError("no free request slot")
+            r.slot = sched.free_slots.pop()
+            reqs.append(r)
+        self._mtp.generate(reqs)
+        out = []
+        for r in reqs:
+            out.append({"rid": r.rid, "output_ids": list(r.output_ids), "finish_reason": r.finish_reason,
+                        "prompt_tokens": r.prompt_len, "completion_tokens": len(r.output_ids)})
+            sched.alloc.free(list(r.pages))
+            r.pages = []
+            sched.free_slots.append(r.slot)
         return out
 
     def flush_cache(self) -> None:

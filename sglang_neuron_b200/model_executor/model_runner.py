@@ -133,6 +133,10 @@ class ModelRunner:
         self.dtype = args.torch_dtype() if self.cuda else torch.float32
         cls = get_model_class(cfg.architecture)
         self.model = cls(cfg, self.dtype, self.device, max_pos=args.context_length + 128)
+        self.draft = None
+        if args.speculative_algorithm == "MTP":
+            from ..speculative.mtp import MTPDraftHead
+            self.draft = MTPDraftHead(self.model, self.dtype, self.device)
         self.load_weights()
         self.page_size = args.page_size
         self.max_pages_per_req = (args.context_length + self.page_size - 1) // self.page_size + 1
@@ -147,6 +151,9 @@ class ModelRunner:
         self.backend = AttentionBackend(max(self.max_reqs, 1) + 1, a0.num_heads, getattr(a0, "head_dim", 128),
                                         self.device, num_sms=num_sms)
         self.model.bind_kv_cache(self.kv_pool, self.backend)
+        if self.draft is not None:
+            self.draft.block.self_attn.kv_pool = self.kv_pool
+            self.draft.block.self_attn.backend = self.backend
         self.relay = torch.zeros(self.max_reqs + 1, dtype=torch.int64, device=self.device)
         self.vocab_start = self.model.lm_head.start
         self.vocab_valid = self.model.lm_head.end - self.model.lm_head.start
@@ -157,7 +164,8 @@ class ModelRunner:
                          self.max_reqs + 1)
         self.graph_runner = None
         self.logits_hook = None  # test seam: called with (ForwardBatch, local logits) of eager steps
-        if self.cuda and not args.disable_cuda_graph and self.model.graph_capturable:
+        if (self.cuda and not args.disable_cuda_graph and self.model.graph_capturable
+                and self.draft is None):
             from .graph_runner import CudaGraphRunner
             self.graph_runner = CudaGraphRunner(self)
 
@@ -173,6 +181,8 @@ class ModelRunner:
         else:
             src = SafetensorsSource(self.args.model, self.device)
         load_model_weights(self.model, src)
+        if self.draft is not None:
+            self.draft.load(src.get)
         if self.cuda:
             torch.cuda.synchronize(self.device)
             torch.cuda.empty_cache()
@@ -181,11 +191,12 @@ class ModelRunner:
         cfg, args = self.cfg, self.args
         attn = self.model.attention_layers()
         P = self.page_size
+        n_layers = cfg.num_layers + (1 if self.draft is not None else 0)  # the MTP block keeps one extra layer
         if cfg.is_mla:
-            per_page = MLATokenToKVPool.bytes_per_page(cfg.num_layers, P, cfg.kv_lora_rank, cfg.qk_rope_head_dim,
+            per_page = MLATokenToKVPool.bytes_per_page(n_layers, P, cfg.kv_lora_rank, cfg.qk_rope_head_dim,
                                                        self.kv_dtype)
         else:
-            per_page = MHATokenToKVPool.bytes_per_page(cfg.num_layers, P, attn[0].num_kv_heads, cfg.head_dim,
+            per_page = MHATokenToKVPool.bytes_per_page(n_layers, P, attn[0].num_kv_heads, cfg.head_dim,
                                                        self.kv_dtype)
         if args.max_total_tokens:
             num_pages = args.max_total_tokens // P + 1
@@ -200,10 +211,10 @@ class ModelRunner:
             num_pages = (self.max_reqs * self.max_pages_per_req) + 1
         self.num_pages = int(num_pages)
         if cfg.is_mla:
-            self.kv_pool = MLATokenToKVPool(cfg.num_layers, self.num_pages, P, cfg.kv_lora_rank,
+            self.kv_pool = MLATokenToKVPool(n_layers, self.num_pages, P, cfg.kv_lora_rank,
                                             cfg.qk_rope_head_dim, self.kv_dtype, self.device)
         else:
-            self.kv_pool = MHATokenToKVPool(cfg.num_layers, self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
+            self.kv_pool = MHATokenToKVPool(n_layers, self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
                                             self.kv_dtype, self.device)
         logger.info("KV pool: %d pages x %d tokens (%.2f GB, %s)", self.num_pages, P,
                     self.num_pages * per_page / 1e9, self.kv_dtype)

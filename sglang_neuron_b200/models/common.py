@@ -254,7 +254,8 @@ class CausalLM(nn.Module):
         # only the rows that are sampled go through the final norm and the LM head
         h_last = h.index_select(0, fb.logits_idx)
         r_last = residual.index_select(0, fb.logits_idx)
-        h_last, _ = self.norm(h_last, r_last)
+        h_last, pre = self.norm(h_last, r_last)
+        self.last_prenorm = pre  # h + residual of the sampled rows (consumed by the MTP draft head)
         return h_last
 
     def compute_logits(self, h_last: torch.Tensor) -> torch.Tensor:

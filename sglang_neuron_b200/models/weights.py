@@ -75,6 +75,8 @@ def hf_shape(cfg: ModelConfig, name: str) -> Tuple[Tuple[int, ...], torch.dtype]
     leaf = name.split(".")
     if name in ("model.embed_tokens.weight", "lm_head.weight"):
         return (cfg.vocab_size, H), bf
+    if name.endswith("eh_proj.weight"):
+        return (H, 2 * H), bf
     if name.endswith("norm.weight"):
         if "q_norm" in name or "k_norm" in name:
             return (D,), bf
