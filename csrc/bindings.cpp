@@ -43,11 +43,16 @@ void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Ten
 void silu_and_mul(torch::Tensor out, torch::Tensor x);
 // gemm_sm100.cu
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-               torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace);
+               torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace,
+               bool reduce_partials, int64_t tiled_f);
+void set_pdl(bool on);
+bool get_pdl();
+void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
+                      std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status);
 
 void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                          torch::Tensor status, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
-                         int64_t num_sms);
+                         int64_t num_sms, int64_t tiled_f);
 // allreduce.cu
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t capacity, int64_t world);
 int64_t symm_open(py::bytes handle);
@@ -80,4 +85,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("one_shot_allreduce", &one_shot_allreduce);
   m.def("moe_combine_allreduce", &moe_combine_allreduce);
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
+  m.def("splitk_allreduce", &splitk_allreduce);
+  m.def("set_pdl", &set_pdl);
+  m.def("get_pdl", &get_pdl);
 }

@@ -9,6 +9,8 @@ namespace {
 
 __global__ void silu_and_mul_kernel(const __nv_bfloat16* __restrict__ x, int xs, __nv_bfloat16* __restrict__ out,
                                     int os, int I) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int t = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element chunk
   if (c * 8 >= I) return;
@@ -27,7 +29,7 @@ void silu_and_mul(torch::Tensor out, torch::Tensor x) {
   if (T == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && I % 8 == 0 && x.stride(1) == 1, "silu_and_mul: layout");
   dim3 grid((I / 8 + 127) / 128, T);
-  silu_and_mul_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  snb::launch_pdl(silu_and_mul_kernel, grid, 128, 0, at::cuda::getCurrentCUDAStream(),
       (const __nv_bfloat16*)x.data_ptr(), x.stride(0), (__nv_bfloat16*)out.data_ptr(), out.stride(0), I);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -30,6 +30,8 @@ constexpr int kThreadsAR = 512;
 __global__ void __launch_bounds__(kThreadsAR) one_shot_allreduce_kernel(
     ARPeers peers, int rank, int world, size_t capacity, const __nv_bfloat16* __restrict__ in,
     __nv_bfloat16* __restrict__ out, int64_t n, int* status) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const ARBuf b = ar_layout(peers, rank, world, capacity);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
   const int half = e & 1;
@@ -52,6 +54,8 @@ __global__ void __launch_bounds__(kThreadsAR) moe_combine_allreduce_kernel(
     ARPeers peers, int rank, int world, size_t capacity, const __nv_bfloat16* __restrict__ y, int ys,
     const int32_t* __restrict__ inv_map, const float* __restrict__ w, int K, int T, int H,
     __nv_bfloat16* __restrict__ out, int* status) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const ARBuf b = ar_layout(peers, rank, world, capacity);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
   const int half = e & 1;
@@ -70,6 +74,43 @@ __global__ void __launch_bounds__(kThreadsAR) moe_combine_allreduce_kernel(
       snb::unpack_bf16x8(reinterpret_cast<const uint4*>(y + (size_t)r * ys)[c], f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] += wj * f[i];
+    }
+    const uint4 packed = snb::pack_bf16x8(acc);
+    for (int p = 0; p < world; ++p) reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity))[v] = packed;
+  }
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  ar_finish(b, e);
+}
+
+// Split-K GEMM epilogue fused with the all-reduce: sum the S fp32 partial tiles of this rank (+ bias),
+// push the bf16 result into every peer's slot, and reduce the world's copies. Together with the split-K
+// tcgen05 GEMM this makes a row-parallel projection + all-reduce two launches with every SM busy.
+__global__ void __launch_bounds__(kThreadsAR) splitk_allreduce_kernel(
+    ARPeers peers, int rank, int world, size_t capacity, const float* __restrict__ partial, int splits,
+    const __nv_bfloat16* __restrict__ bias, int T, int F, __nv_bfloat16* __restrict__ out, int* status) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
+  const ARBuf b = ar_layout(peers, rank, world, capacity);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
+  const int half = e & 1;
+  const int64_t nvec = (int64_t)T * F / 8;
+  const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
+  const int fv = F / 8;
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    const int f8 = (int)(v % fv) * 8;
+    float acc[8];
+    if (bias != nullptr) {
+      snb::unpack_bf16x8(*reinterpret_cast<const uint4*>(bias + f8), acc);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    }
+    for (int z = 0; z < splits; ++z) {
+      const float4* pz = reinterpret_cast<const float4*>(partial + (size_t)z * T * F + v * 8);
+      const float4 a0 = pz[0], a1 = pz[1];
+      acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w;
+      acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
     }
     const uint4 packed = snb::pack_bf16x8(acc);
     for (int p = 0; p < world; ++p) reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity))[v] = packed;
@@ -120,7 +161,7 @@ void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t
   TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "one_shot_allreduce: CTA count");
   ARPeers peers;
   for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
-  one_shot_allreduce_kernel<<<num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream()>>>(
+  snb::launch_pdl(one_shot_allreduce_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, (const __nv_bfloat16*)in.data_ptr(), (__nv_bfloat16*)out.data_ptr(), n,
       status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -137,8 +178,26 @@ void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv
   if (T == 0) return;
   ARPeers peers;
   for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
-  moe_combine_allreduce_kernel<<<num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream()>>>(
+  snb::launch_pdl(moe_combine_allreduce_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
       w.data_ptr<float>(), K, T, H, (__nv_bfloat16*)out.data_ptr(), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
+                      std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status) {
+  const int world = (int)bufs.size();
+  const int T = out.size(0), F = out.size(1);
+  TORCH_CHECK(F % 8 == 0 && out.is_contiguous() && partial.scalar_type() == at::kFloat, "splitk_allreduce: layout");
+  TORCH_CHECK(partial.numel() >= (int64_t)splits * T * F, "splitk_allreduce: partial size");
+  TORCH_CHECK((size_t)T * F * 2 <= (size_t)capacity, "splitk_allreduce: over capacity");
+  TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "splitk_allreduce: CTA count");
+  if (T == 0) return;
+  ARPeers peers;
+  for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  snb::launch_pdl(splitk_allreduce_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
+      peers, rank, world, capacity, partial.data_ptr<float>(), splits,
+      bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr, T, F, (__nv_bfloat16*)out.data_ptr(),
+      status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

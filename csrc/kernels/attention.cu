@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(
     const int32_t* __restrict__ seq_lens, int page_size, int Hkv, int window, float qk_scale_log2,
     float v_scale, const float* __restrict__ sinks, __nv_bfloat16* __restrict__ out, int out_stride_tok,
     float* __restrict__ o_part, float* __restrict__ lse_part, int num_splits) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   constexpr int RS = D + 8;  // padded smem row (bf16 elements) -> conflict-free 16B row reads
   __shared__ __align__(16) __nv_bfloat16 k_s[kTile * RS];
   __shared__ __align__(16) __nv_bfloat16 v_s[kTile * RS];
@@ -204,6 +206,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(
 __global__ void decode_merge_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part,
                                     const float* __restrict__ sinks, __nv_bfloat16* __restrict__ out,
                                     int out_stride_tok, int Hq, int D, int S, float v_scale) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int bh = blockIdx.x;  // b * Hq + h
   const int b = bh / Hq, h = bh % Hq;
   const float* lse = lse_part + (size_t)bh * S;
@@ -236,6 +240,8 @@ __global__ void __launch_bounds__(kThreads) extend_attn_kernel(
     const int32_t* __restrict__ qo_indptr, const int32_t* __restrict__ kv_lens, int page_size, int Hkv,
     int window, float qk_scale_log2, float v_scale, const float* __restrict__ sinks,
     __nv_bfloat16* __restrict__ out, int out_stride_tok) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   constexpr int RS = D + 8;
   constexpr int DH = D / TPR;                   // row elements held by one thread
   constexpr int ROWS = kThreads / TPR;          // (query, head) rows per CTA
@@ -346,7 +352,7 @@ void launch_decode_g(int G, dim3 grid, cudaStream_t st, const __nv_bfloat16* q, 
                      float scale, float vs, const float* sinks, __nv_bfloat16* out, int os, float* op,
                      float* lp, int S) {
 #define SNB_DEC(GG)                                                                                   \
-  decode_attn_kernel<D, GG, CacheT><<<grid, kThreads, 0, st>>>(q, qs, kc, vc, bt, bts, sl, ps, Hkv, win, \
+  snb::launch_pdl(decode_attn_kernel<D, GG, CacheT>, grid, kThreads, 0, st, q, qs, kc, vc, bt, bts, sl, ps, Hkv, win, \
                                                                 scale, vs, sinks, out, os, op, lp, S)
   switch (G) {
     case 1: SNB_DEC(1); break;
@@ -368,7 +374,7 @@ void launch_extend_g(int G, int max_ext, int B, int Hkv, cudaStream_t st, const 
   {                                                                                                 \
     constexpr int QT = (kThreads / TPR) / GG;                                                       \
     dim3 grid((max_ext + QT - 1) / QT, B, Hkv);                                                     \
-    extend_attn_kernel<D, GG, TPR, CacheT><<<grid, kThreads, 0, st>>>(q, qs, kc, vc, bt, bts, qo, kvl, \
+    snb::launch_pdl(extend_attn_kernel<D, GG, TPR, CacheT>, grid, kThreads, 0, st, q, qs, kc, vc, bt, bts, qo, kvl, \
                                                                        ps, Hkv, win, scale, vs, sinks, \
                                                                        out, os);                   \
   }
@@ -389,6 +395,11 @@ bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
                           torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
                           int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
                           const float* sinks, int64_t num_splits, float* o_part, float* lse_part);
+
+bool extend_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                          torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
+                          int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
+                          float scale_log2, float v_scale, const float* sinks);
 
 // q: [B, Hq*D] bf16 (row stride arbitrary). Caches: [pages, Hkv, page_size, D].
 // block_table: [B, max_pages] int32; seq_lens: [B] int32 (tokens including the new one).
@@ -448,7 +459,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   if (S > 1) {
-    decode_merge_kernel<<<B * num_q_heads, 64, 0, st>>>(op, lp, sk, outp, out.stride(0), num_q_heads, head_dim, S,
+    snb::launch_pdl(decode_merge_kernel, B * num_q_heads, 64, 0, st, op, lp, sk, outp, out.stride(0), num_q_heads, head_dim, S,
                                                         (float)v_scale);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
@@ -470,6 +481,9 @@ void extend_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   auto qp = (const __nv_bfloat16*)q.data_ptr();
   auto outp = (__nv_bfloat16*)out.data_ptr();
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  if (extend_attention_mma(out, q, k_cache, v_cache, block_table, qo_indptr, kv_lens, max_extend, num_q_heads,
+                           num_kv_heads, head_dim, page_size, window, scale, (float)v_scale, sk))
+    return;
 #define SNB_EXT_D(DD, TPR)                                                                                 \
   if (fp8)                                                                                                 \
     launch_extend_g<DD, TPR, uint8_t>(G, max_extend, B, num_kv_heads, st, qp, q.stride(0),                 \

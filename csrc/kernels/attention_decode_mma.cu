@@ -103,6 +103,8 @@ __global__ void __launch_bounds__(kThr) decode_attn_mma_kernel(
     int Hkv, int G, int window, float scale_log2, float v_scale, const float* __restrict__ sinks,
     __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part, float* __restrict__ lse_part,
     int num_splits) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   constexpr int KS = D + 8, VS = kT + 8;
   constexpr int NT = D / 8;  // n8 tiles of the output
   // one buffer: K tile [kT][KS] then V^T tile [D][VS]; reused as the fp32 merge area after the loop
@@ -274,6 +276,168 @@ __global__ void __launch_bounds__(kThr) decode_attn_mma_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Extend (prefill over a paged prior) on tensor cores. Grid (ceil(max_extend / 64), B, Hq), 128 threads:
+// each warp owns 16 query rows of one query head; K/V tiles of 64 tokens are staged as in decode (the
+// G heads of a KV head re-read the same tile through L2). Causal + sliding-window masks come from the
+// query and key positions; sinks join the final normaliser.
+// ---------------------------------------------------------------------------------------------------
+template <int D, typename CacheT>
+__global__ void __launch_bounds__(kThr) extend_attn_mma_kernel(
+    const __nv_bfloat16* __restrict__ q, int q_stride, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
+    const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ qo_indptr,
+    const int32_t* __restrict__ kv_lens, int page_size, int Hkv, int G, int window, float scale_log2, float v_scale,
+    const float* __restrict__ sinks, __nv_bfloat16* __restrict__ out, int out_stride) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
+  constexpr int KS = D + 8, VS = kT + 8;
+  constexpr int NT = D / 8;
+  constexpr int KV_ELEMS = kT * KS + D * VS;
+  __shared__ __align__(16) __nv_bfloat16 kv_smem[KV_ELEMS];
+  __nv_bfloat16* ks = kv_smem;
+  __nv_bfloat16* vts = kv_smem + kT * KS;
+
+  const int b = blockIdx.y, h = blockIdx.z, hk = h / G;
+  const int q_begin = qo_indptr[b], ext = qo_indptr[b + 1] - q_begin;
+  const int qi0 = blockIdx.x * (kWarps * 16);
+  if (qi0 >= ext) return;
+  const int kv_len = kv_lens[b];
+  const int prefix = kv_len - ext;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, qd = lane & 3;
+  const int row0 = qi0 + warp * 16;  // first query index of this warp
+  // positions of this thread's two rows
+  const int qa_i = row0 + gq, qb_i = row0 + gq + 8;
+  const int pos_a = prefix + qa_i, pos_b = prefix + qb_i;
+  const bool va = qa_i < ext, vb = qb_i < ext;
+
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int ks_ = 0; ks_ < D / 16; ++ks_) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int qi = row0 + gq + (r & 1) * 8;
+      const int col = ks_ * 16 + qd * 2 + (r >> 1) * 8;
+      qf[ks_][r] = qi < ext ? *reinterpret_cast<const uint32_t*>(q + (size_t)(q_begin + qi) * q_stride +
+                                                                   (size_t)h * D + col)
+                            : 0u;
+    }
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+
+  // key range needed by the CTA's queries
+  const int last_q = min(ext, qi0 + kWarps * 16) - 1;
+  const int hi = prefix + last_q + 1;
+  int lo = 0;
+  if (window > 0) lo = max(0, prefix + qi0 - window + 1);
+  lo = (lo / kT) * kT;
+  const int32_t* bt = block_table + (size_t)b * bt_stride;
+  const int srow = tid >> 1, shalf = tid & 1;
+  RowRegs<D, CacheT> regs;
+  fetch_half_row<D, CacheT>(regs, kc, vc, bt, lo + srow, hi, page_size, Hkv, hk, shalf);
+  stage_half_row<D, CacheT>(regs, ks, vts, srow, shalf);
+  __syncthreads();
+  for (int t0 = lo; t0 < hi; t0 += kT) {
+    const bool more = t0 + kT < hi;
+    if (more) fetch_half_row<D, CacheT>(regs, kc, vc, bt, t0 + kT + srow, hi, page_size, Hkv, hk, shalf);
+    // S = Q K^T over the 64 tile tokens: 8 n8 tiles
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int ks_ = 0; ks_ < D / 16; ++ks_) {
+        const __nv_bfloat16* kr = ks + (nt * 8 + gq) * KS + ks_ * 16 + qd * 2;
+        mma_bf16_16816(s[nt], qf[ks_], *reinterpret_cast<const uint32_t*>(kr),
+                       *reinterpret_cast<const uint32_t*>(kr + 8));
+      }
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kp = t0 + nt * 8 + qd * 2 + (j & 1);
+        const int pos = (j >> 1) ? pos_b : pos_a;
+        const bool valid = (j >> 1) ? vb : va;
+        bool ok = valid && kp < hi && kp <= pos;
+        if (window > 0) ok = ok && (pos - kp < window);
+        const float v = ok ? s[nt][j] * scale_log2 : -INFINITY;
+        s[nt][j] = v;
+        mx[j >> 1] = fmaxf(mx[j >> 1], v);
+      }
+    }
+    float alpha[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 1));
+      mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 2));
+      const float mn = fmaxf(m_r[hh], mx[hh]);
+      alpha[hh] = (m_r[hh] == -INFINITY) ? (mn == -INFINITY ? 1.f : 0.f) : exp2f(m_r[hh] - mn);
+      m_r[hh] = mn;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = (s[nt][j] == -INFINITY) ? 0.f : exp2f(s[nt][j] - m_r[j >> 1]);
+        s[nt][j] = p;
+        rs[j >> 1] += p;
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      rs[hh] += __shfl_xor_sync(0xffffffffu, rs[hh], 1);
+      rs[hh] += __shfl_xor_sync(0xffffffffu, rs[hh], 2);
+      l_r[hh] = l_r[hh] * alpha[hh] + rs[hh];
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
+    }
+    // O += P V over 4 k16 steps of 16 tokens
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const __nv_bfloat16* vr = vts + (n * 8 + gq) * VS + kk * 16 + qd * 2;
+        mma_bf16_16816(o[n], pa, *reinterpret_cast<const uint32_t*>(vr), *reinterpret_cast<const uint32_t*>(vr + 8));
+      }
+    }
+    __syncthreads();
+    if (more) {
+      stage_half_row<D, CacheT>(regs, ks, vts, srow, shalf);
+      __syncthreads();
+    }
+  }
+  // finalise the two rows of this thread
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int qi = hh ? qb_i : qa_i;
+    if (qi >= ext) continue;
+    float denom = l_r[hh];
+    if (sinks != nullptr) denom = (m_r[hh] == -INFINITY) ? 1.f : denom + exp2f(sinks[h] * kL2e - m_r[hh]);
+    const float inv = denom > 0.f ? v_scale / denom : 0.f;
+    __nv_bfloat16* orow = out + (size_t)(q_begin + qi) * out_stride + (size_t)h * D;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int col = n * 8 + qd * 2;
+      *reinterpret_cast<uint32_t*>(orow + col) = pack_bf16x2(o[n][hh * 2] * inv, o[n][hh * 2 + 1] * inv);
+    }
+  }
+}
+
 }  // namespace
 
 // Same contract as decode_attention() in attention.cu; returns false when the shape is not covered
@@ -289,7 +453,7 @@ bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
   dim3 grid(num_splits, num_kv_heads, B);
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
 #define SNB_MMA(DD, CT)                                                                                          \
-  decode_attn_mma_kernel<DD, CT><<<grid, kThr, 0, st>>>(                                                         \
+  snb::launch_pdl(decode_attn_mma_kernel<DD, CT>, grid, kThr, 0, st,                                                          \
       (const __nv_bfloat16*)q.data_ptr(), q.stride(0), (const CT*)k_cache.data_ptr(), (const CT*)v_cache.data_ptr(), \
       block_table.data_ptr<int32_t>(), block_table.stride(0), seq_lens.data_ptr<int32_t>(), page_size,          \
       num_kv_heads, G, window, scale_log2, v_scale_final, sinks, (__nv_bfloat16*)out.data_ptr(), out.stride(0),   \
@@ -300,6 +464,33 @@ bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
     if (fp8) SNB_MMA(128, uint8_t); else SNB_MMA(128, __nv_bfloat16);
   }
 #undef SNB_MMA
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return true;
+}
+
+// Extend attention on tensor cores; false when the shape is not covered (head_dim not 64/128).
+bool extend_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                          torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
+                          int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
+                          float scale_log2, float v_scale, const float* sinks) {
+  if (head_dim != 64 && head_dim != 128) return false;
+  const int B = kv_lens.size(0);
+  const int G = num_q_heads / num_kv_heads;
+  auto st = at::cuda::getCurrentCUDAStream();
+  dim3 grid((max_extend + kWarps * 16 - 1) / (kWarps * 16), B, num_q_heads);
+  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+#define SNB_EXT_MMA(DD, CT)                                                                                       \
+  snb::launch_pdl(extend_attn_mma_kernel<DD, CT>, grid, kThr, 0, st,                                                          \
+      (const __nv_bfloat16*)q.data_ptr(), q.stride(0), (const CT*)k_cache.data_ptr(), (const CT*)v_cache.data_ptr(), \
+      block_table.data_ptr<int32_t>(), block_table.stride(0), qo_indptr.data_ptr<int32_t>(),                     \
+      kv_lens.data_ptr<int32_t>(), page_size, num_kv_heads, G, window, scale_log2, v_scale, sinks,               \
+      (__nv_bfloat16*)out.data_ptr(), out.stride(0))
+  if (head_dim == 64) {
+    if (fp8) SNB_EXT_MMA(64, uint8_t); else SNB_EXT_MMA(64, __nv_bfloat16);
+  } else {
+    if (fp8) SNB_EXT_MMA(128, uint8_t); else SNB_EXT_MMA(128, __nv_bfloat16);
+  }
+#undef SNB_EXT_MMA
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return true;
 }

@@ -16,6 +16,7 @@
 #include "../common.cuh"
 #include "../tma_host.h"
 #include "../ar_common.cuh"
+#include <algorithm>
 
 namespace {
 
@@ -32,9 +33,13 @@ struct GemmCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-// Split-K: blockIdx.z selects a contiguous range of K blocks; with more than one split every CTA writes its
-// fp32 partial tile to `partial` [splits, T, F] and splitk_reduce_kernel sums them (plus the bias) to bf16.
-// Decode-sized GEMMs (few tokens, F/128 CTAs) use it to put every SM to work on the weight stream.
+// Split-K: blockIdx.z selects a contiguous range of K blocks. Decode-sized GEMMs (few tokens, F/128 tiles)
+// split K so every SM works on the weight stream. Default (cluster_reduce): the S splits of a tile form one
+// (1, 1, S) thread-block cluster and are summed through distributed shared memory in the same kernel.
+// Explicit split counts instead write fp32 partial tiles to `partial` [splits, T, F], summed by
+// splitk_reduce_kernel or by a fused consumer (the tensor-parallel all-reduce).
+// Programmatic dependent launch: the producer issues the weight loads of the first ring slots before
+// griddepcontrol.wait, so the weight stream starts while the previous kernel is still running.
 // AR = true: the epilogue all-reduces its output tile over the tensor-parallel group inside this kernel:
 // the bf16 tile is stored straight into every peer's symmetric buffer (slot = my rank, NVLink P2P stores),
 // the tile's flag is released to every peer, the CTA waits (bounded) for the same tile from every rank and
@@ -51,7 +56,8 @@ template <int BN, bool AR>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                      __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ bias, int F, int T,
-                     int K, int ldo, int* status, float* __restrict__ partial, const GemmAR ar) {
+                     int K, int ldo, int* status, float* __restrict__ partial, const GemmAR ar, int cluster_reduce,
+                     int w_tiled) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -61,13 +67,14 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* accum = empty + C::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* loads = reinterpret_cast<int*>(tmem_slot + 1);  // [0] issued, [1] consumed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int f0 = blockIdx.x * BM, t0 = blockIdx.y * BN;
   const int nk_all = (K + BK - 1) / BK;
-  const int per_split = (nk_all + gridDim.z - 1) / gridDim.z;
-  const int kb0 = blockIdx.z * per_split;
-  const int nk = max(0, min(nk_all, kb0 + per_split) - kb0);
+  const int S = gridDim.z;
+  const int kb0 = (int)((long long)blockIdx.z * nk_all / S);
+  const int nk = (int)((long long)(blockIdx.z + 1) * nk_all / S) - kb0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -75,6 +82,7 @@ __global__ void __launch_bounds__(192, 1)
       snb::mbar_init(&empty[s], 1);
     }
     snb::mbar_init(accum, 1);
+    loads[0] = loads[1] = 0;
     snb::fence_mbar_init();
     snb::prefetch_tmap(&tmap_w);
     snb::prefetch_tmap(&tmap_x);
@@ -87,23 +95,49 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   snb::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  snb::pdl_trigger();
+  bool ep_ok = false;
 
   if (warp == 0) {
     if (lane == 0) {
+      // Weight tile (kb, f0): row-major [F, K] weights, or pre-tiled ones where each 128 x 64 tile is one
+      // contiguous 16 KB block ([F/128][K/64][128][64]) so every load is a single DRAM stream.
+      // Decode grids (one token tile) read each weight byte once: evict-first keeps L2 for activations.
+      const uint64_t pol = snb::l2_policy_evict_first();
+      const bool once = gridDim.y == 1;
+      auto load_w = [&](int s, int kb) {
+        const int c0 = w_tiled ? 0 : (kb0 + kb) * BK;
+        const int c1 = w_tiled ? (blockIdx.x * nk_all + kb0 + kb) * BM : f0;
+        if (once) snb::tma_load_2d_hint(sA + s * C::A_BYTES, &tmap_w, &full[s], c0, c1, pol);
+        else snb::tma_load_2d(sA + s * C::A_BYTES, &tmap_w, &full[s], c0, c1);
+      };
+      // The weights are constant: the first ring slots are filled before waiting for the previous kernel.
+      const int npre = min(nk, C::STAGES);
+      for (int kb = 0; kb < npre; ++kb) {
+        snb::mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+        load_w(kb, kb);
+      }
+      snb::pdl_wait();
+      int issued = npre;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % C::STAGES;
         const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!snb::mbar_wait_bounded(&empty[s], ph ^ 1, status, SNB_ERR_TIMEOUT_TMA)) break;
-        snb::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        snb::tma_load_2d(sA + s * C::A_BYTES, &tmap_w, &full[s], (kb0 + kb) * BK, f0);
+        if (kb >= npre) {
+          if (!snb::mbar_wait_bounded(&empty[s], ph ^ 1, status, SNB_ERR_TIMEOUT_TMA)) break;
+          snb::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          load_w(s, kb);
+          issued = kb + 1;
+        }
         snb::tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], (kb0 + kb) * BK, t0);
       }
+      loads[0] = issued;
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = snb::idesc_bf16_f32(BM, BN);
       bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
+      int kb = 0;
+      for (; kb < nk; ++kb) {
         const int s = kb % C::STAGES;
         const uint32_t ph = (kb / C::STAGES) & 1;
         if (!snb::mbar_wait_bounded(&full[s], ph, status, SNB_ERR_TIMEOUT_MMA)) {
@@ -120,12 +154,17 @@ __global__ void __launch_bounds__(192, 1)
         }
         snb::mma_commit(&empty[s]);
       }
-      if (ok) snb::mma_commit(accum);
+      loads[1] = kb;
+      // with ok, the epilogue waits on `accum`; otherwise this commit lets in-flight MMAs be waited for below
+      snb::mma_commit(accum);
+      if (!ok) snb::mbar_wait_bounded(accum, 0, status, SNB_ERR_TIMEOUT_MMA);
     }
   } else {
+    snb::pdl_wait();
     // Epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31.
     const int q = warp & 3;
     const bool ok = nk > 0 && snb::mbar_wait_bounded(accum, 0, status, SNB_ERR_TIMEOUT_EPI);
+    ep_ok = ok;
     snb::tc_fence_after();
     if (nk == 0 && partial != nullptr) {
       // empty split (K range past the end): contribute zeros
@@ -141,7 +180,7 @@ __global__ void __launch_bounds__(192, 1)
       ar_epoch = *reinterpret_cast<volatile uint32_t*>(arb.counter) + 1;
       ar_half = ar_epoch & 1;
     }
-    if (ok) {
+    if (ok && !cluster_reduce) {
       const int f = f0 + q * 32 + lane;
       const float bf = (bias != nullptr && f < F) ? __bfloat162float(bias[f]) : 0.f;
 #pragma unroll 1
@@ -236,13 +275,104 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   }
+  if (cluster_reduce) {
+    // Split-K inside a (1, 1, S) cluster: the S CTAs of one output tile sum their fp32 accumulators in the
+    // leader's (cluster rank 0) shared memory. After the first cluster barrier every CTA's MMAs are done, so
+    // the leader's ring is free; the others store their TMEM tiles into it over DSMEM ([f][BN + 4] rows, 16-
+    // byte stores, conflict-free); after the second the leader adds them in rank order (deterministic),
+    // adds the bias and writes bf16.
+    constexpr int RS = BN + 4;
+    constexpr int CH = BN >= 32 ? 32 : BN;
+    __syncwarp();
+    snb::tc_fence_before();
+    snb::cluster_sync();
+    snb::tc_fence_after();
+    const uint32_t rank = snb::cluster_ctarank();
+    const int q = warp & 3, fl = q * 32 + lane;
+    if (warp >= 2 && rank != 0 && ep_ok) {
+      const uint32_t dst = snb::mapa_shared(snb::smem_u32(smem) + (((int)rank - 1) * BM + fl) * RS * 4, 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / CH; ++c) {
+        uint32_t r[CH];
+        if constexpr (CH == 32) {
+          snb::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * CH, r);
+          snb::tmem_ld_wait();
+        } else {
+          uint32_t r8[8];
+#pragma unroll
+          for (int h = 0; h < CH / 8; ++h) {
+            snb::tmem_ld_32x32b_x8(tmem + ((uint32_t)(q * 32) << 16) + c * CH + h * 8, r8);
+            snb::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) r[h * 8 + j] = r8[j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < CH; j += 4)
+          snb::st_cluster_v4(dst + (c * CH + j) * 4, __uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                             __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+      }
+    }
+    __syncwarp();
+    snb::cluster_sync();
+    if (warp >= 2 && rank == 0 && ep_ok) {
+      const int f = f0 + fl;
+      const float bf = (bias != nullptr && f < F) ? __bfloat162float(bias[f]) : 0.f;
+      const float* slots = reinterpret_cast<const float*>(smem) + fl * RS;
+#pragma unroll 1
+      for (int c = 0; c < BN / CH; ++c) {
+        uint32_t r[CH];
+        if constexpr (CH == 32) {
+          snb::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * CH, r);
+          snb::tmem_ld_wait();
+        } else {
+          uint32_t r8[8];
+#pragma unroll
+          for (int h = 0; h < CH / 8; ++h) {
+            snb::tmem_ld_32x32b_x8(tmem + ((uint32_t)(q * 32) << 16) + c * CH + h * 8, r8);
+            snb::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) r[h * 8 + j] = r8[j];
+          }
+        }
+        float acc[CH];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) acc[j] = __uint_as_float(r[j]);
+        for (int rr = 1; rr < S; ++rr) {
+          const float4* src = reinterpret_cast<const float4*>(slots + (size_t)(rr - 1) * BM * RS + c * CH);
+#pragma unroll
+          for (int j = 0; j < CH / 4; ++j) {
+            const float4 v = src[j];
+            acc[4 * j] += v.x;
+            acc[4 * j + 1] += v.y;
+            acc[4 * j + 2] += v.z;
+            acc[4 * j + 3] += v.w;
+          }
+        }
+        if (f < F) {
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const int t = t0 + c * CH + j;
+            if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(acc[j] + bf);
+          }
+        }
+      }
+    }
+  }
   snb::tc_fence_before();
   __syncthreads();
+  if (warp == 0 && lane == 0) {
+    // a CTA that stopped early still waits (bounded) for the loads it issued before its memory goes away
+    for (int i = loads[1]; i < loads[0]; ++i)
+      if (!snb::mbar_wait_bounded(&full[i % C::STAGES], (i / C::STAGES) & 1, status, SNB_ERR_TIMEOUT_TMA)) break;
+  }
   if (warp == 1) snb::tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const __nv_bfloat16* __restrict__ bias,
                                      __nv_bfloat16* __restrict__ out, int T, int F, int ldo, int splits) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * F) return;
   const int t = i / F, f = i % F;
@@ -251,28 +381,90 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const __
   out[(size_t)t * ldo + f] = __float2bfloat16(a);
 }
 
+// Largest split count whose (S - 1) partial tiles ([128][BN + 4] fp32 each) fit in the leader's ring.
+template <int BN>
+constexpr int max_cluster_splits() {
+  using C = GemmCfg<BN>;
+  const int slot = BM * (BN + 4) * 4;
+  const int s = (C::STAGES * C::STAGE_BYTES) / slot + 1;
+  return s > 8 ? 8 : s;
+}
+
+// Split count for the in-cluster reduction: as many K splits as keep every tile's cluster co-resident in
+// one wave (checked with the occupancy calculator once per shape class).
+template <int BN>
+int pick_cluster_splits(int tiles, int nk, int num_sms) {
+  using C = GemmCfg<BN>;
+  if (tiles * 2 > num_sms) return 1;
+  int S = std::min({max_cluster_splits<BN>(), num_sms / tiles, nk});
+  static int max_clusters[9] = {0};
+  while (S > 1) {
+    if (max_clusters[S] == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1, S);
+      cfg.blockDim = dim3(192);
+      cfg.dynamicSmemBytes = C::SMEM;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = S;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_kernel<BN, false>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = -1;
+      }
+      max_clusters[S] = n;
+    }
+    if (max_clusters[S] >= tiles) break;
+    --S;
+  }
+  return S;
+}
+
 template <int BN, bool AR = false>
 void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::Tensor& w,
                  const __nv_bfloat16* bias, int* status, cudaStream_t st, int splits, float* partial,
-                 const GemmAR& ar = GemmAR{}) {
+                 const GemmAR& ar = GemmAR{}, bool reduce_partials = true, int num_sms = 148, int tiled_f = 0) {
   using C = GemmCfg<BN>;
-  const int T = x.size(0), K = x.size(1), F = w.size(0);
-  CUtensorMap tw = snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, F, w.stride(0) * 2, BK,
-                                          BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int T = x.size(0), K = x.size(1), F = tiled_f ? tiled_f : w.size(0);
+  const int wt = tiled_f ? 1 : 0;
+  CUtensorMap tw = tiled_f ? snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, BK, w.size(0),
+                                                    BK * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)
+                           : snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, F,
+                                                    w.stride(0) * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tx = snb_host::make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, T, x.stride(0) * 2, BK,
                                           BN, CU_TENSOR_MAP_SWIZZLE_128B);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_bf16_kernel<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(gemm_bf16_kernel<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
-  dim3 grid((F + BM - 1) / BM, (T + BN - 1) / BN, splits);
-  gemm_bf16_kernel<BN, AR><<<grid, 192, C::SMEM, st>>>(tw, tx, (__nv_bfloat16*)out.data_ptr(), bias, F, T, K,
-                                                       out.stride(0), status, splits > 1 ? partial : nullptr, ar);
-  if (splits > 1) {
+  const int tiles_f = (F + BM - 1) / BM, tiles_t = (T + BN - 1) / BN;
+  __nv_bfloat16* op = (__nv_bfloat16*)out.data_ptr();
+  const int ldo = out.stride(0);
+  if (splits <= 0) {
+    // default: split K inside a thread-block cluster when the tiles alone leave SMs idle
+    int S = 1;
+    if constexpr (!AR) S = pick_cluster_splits<BN>(tiles_f * tiles_t, (K + BK - 1) / BK, num_sms);
+    if (S > 1) {
+      C10_CUDA_CHECK(snb::launch_pdl_cluster(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, S), 192, C::SMEM, st,
+                                             S, tw, tx, op, bias, F, T, K, ldo, status, nullptr, ar, 1, wt));
+    } else {
+      C10_CUDA_CHECK(snb::launch_pdl(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, 1), 192, C::SMEM, st, tw, tx,
+                                     op, bias, F, T, K, ldo, status, nullptr, ar, 0, wt));
+    }
+    return;
+  }
+  C10_CUDA_CHECK(snb::launch_pdl(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, splits), 192, C::SMEM, st, tw, tx,
+                                 op, bias, F, T, K, ldo, status, splits > 1 ? partial : nullptr, ar, 0, wt));
+  if (splits > 1 && reduce_partials) {
     const int n = T * F;
-    splitk_reduce_kernel<<<(n + 255) / 256, 256, 0, st>>>(partial, bias, (__nv_bfloat16*)out.data_ptr(), T, F,
-                                                          out.stride(0), splits);
+    C10_CUDA_CHECK(snb::launch_pdl(splitk_reduce_kernel, (n + 255) / 256, 256, 0, st, partial, bias, op, T, F, ldo,
+                                   splits));
   }
 }
 
@@ -280,32 +472,47 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
 
 // out: [T, F] bf16 (row stride arbitrary, multiple of 8), x: [T, K] bf16, w: [F, K] bf16, bias [F] or None.
 // status: int32 CUDA tensor (>= 1 element) that receives a non-zero code if a bounded wait timed out.
+// splits <= 0: automatic (K split inside a thread-block cluster for decode-sized GEMMs, one launch);
+// splits == 1: one CTA per tile; splits > 1: fp32 partials [splits, T, F] in `workspace`, summed by a second
+// launch when reduce_partials (else left for a fused consumer).
+static void check_weight(const torch::Tensor& x, const torch::Tensor& w, int64_t tiled_f, const char* who) {
+  if (tiled_f > 0) {
+    const int64_t nk = (x.size(1) + BK - 1) / BK, ntf = (tiled_f + BM - 1) / BM;
+    TORCH_CHECK(w.dim() == 2 && w.size(1) == BK && w.size(0) == ntf * nk * BM && w.is_contiguous(), who,
+                ": tiled weight must be [ceil(F/128) * ceil(K/64) * 128, 64]");
+  } else {
+    TORCH_CHECK(x.size(1) == w.size(1), who, ": K mismatch");
+  }
+}
+
+// tiled_f > 0: `w` is the pre-tiled layout of a [tiled_f, K] weight (see tile_weight_bf16 in ops/gemm.py).
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-               torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace) {
+               torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace,
+               bool reduce_partials, int64_t tiled_f) {
   const int T = x.size(0);
   if (T == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 inputs");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm_bf16: inner stride");
-  TORCH_CHECK(x.size(1) == w.size(1), "gemm_bf16: K mismatch");
+  check_weight(x, w, tiled_f, "gemm_bf16");
   TORCH_CHECK(x.size(1) % 8 == 0, "gemm_bf16: K must be a multiple of 8");
   auto st = at::cuda::getCurrentCUDAStream();
   const __nv_bfloat16* bp = bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr;
   int* sp = status.data_ptr<int>();
   if (bn <= 0) bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-  if (splits < 1) splits = 1;
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   float* part = nullptr;
   if (splits > 1) {
     TORCH_CHECK(workspace && workspace->scalar_type() == at::kFloat &&
-                    workspace->numel() >= (int64_t)splits * T * w.size(0),
+                    workspace->numel() >= (int64_t)splits * T * (tiled_f ? tiled_f : w.size(0)),
                 "gemm_bf16: split-K needs a fp32 workspace of splits*T*F");
     part = workspace->data_ptr<float>();
   }
   switch (bn) {
-    case 16: launch_gemm<16>(out, x, w, bp, sp, st, splits, part); break;
-    case 32: launch_gemm<32>(out, x, w, bp, sp, st, splits, part); break;
-    case 64: launch_gemm<64>(out, x, w, bp, sp, st, splits, part); break;
-    case 128: launch_gemm<128>(out, x, w, bp, sp, st, splits, part); break;
-    case 256: launch_gemm<256>(out, x, w, bp, sp, st, splits, part); break;
+    case 16: launch_gemm<16>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
+    case 32: launch_gemm<32>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
+    case 64: launch_gemm<64>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
+    case 128: launch_gemm<128>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
+    case 256: launch_gemm<256>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
     default: TORCH_CHECK(false, "gemm_bf16: bn must be 16/32/64/128/256");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -316,11 +523,12 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
 // buffer capacity; out: [T, F] contiguous.
 void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                          torch::Tensor status, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
-                         int64_t num_sms) {
-  const int T = x.size(0), F = w.size(0);
+                         int64_t num_sms, int64_t tiled_f) {
+  const int T = x.size(0), F = tiled_f ? tiled_f : w.size(0);
   if (T == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_bf16_allreduce: bf16");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.is_contiguous(), "gemm_bf16_allreduce: layout");
+  check_weight(x, w, tiled_f, "gemm_bf16_allreduce");
   const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
   const int tiles = ((F + BM - 1) / BM) * ((T + bn - 1) / bn);
   TORCH_CHECK(tiles <= num_sms && tiles <= snb_ar::kMaxCtas, "gemm_bf16_allreduce: more tiles than one wave");
@@ -336,11 +544,11 @@ void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c1
   const __nv_bfloat16* bp = bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr;
   int* sp = status.data_ptr<int>();
   switch (bn) {
-    case 16: launch_gemm<16, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
-    case 32: launch_gemm<32, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
-    case 64: launch_gemm<64, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
-    case 128: launch_gemm<128, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
-    default: launch_gemm<256, true>(out, x, w, bp, sp, st, 1, nullptr, ar); break;
+    case 16: launch_gemm<16, true>(out, x, w, bp, sp, st, 1, nullptr, ar, true, num_sms, tiled_f); break;
+    case 32: launch_gemm<32, true>(out, x, w, bp, sp, st, 1, nullptr, ar, true, num_sms, tiled_f); break;
+    case 64: launch_gemm<64, true>(out, x, w, bp, sp, st, 1, nullptr, ar, true, num_sms, tiled_f); break;
+    case 128: launch_gemm<128, true>(out, x, w, bp, sp, st, 1, nullptr, ar, true, num_sms, tiled_f); break;
+    default: launch_gemm<256, true>(out, x, w, bp, sp, st, 1, nullptr, ar, true, num_sms, tiled_f); break;
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

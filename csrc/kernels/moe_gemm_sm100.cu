@@ -93,6 +93,8 @@ template <int BN, bool A_FP4, int EPI>
 __global__ void __launch_bounds__(192, MoeCfg<BN>::CTAS_PER_SM)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const MoeParams p) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   using C = MoeCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -310,7 +312,7 @@ void launch_moe(const CUtensorMap& ta, const CUtensorMap& tb, const MoeParams& p
                 "moe_gemm: smem attribute");
     attr = true;
   }
-  moe_gemm_kernel<BN, A_FP4, EPI><<<grid, 192, C::SMEM, st>>>(ta, tb, p);
+  snb::launch_pdl(moe_gemm_kernel<BN, A_FP4, EPI>, grid, 192, C::SMEM, st, ta, tb, p);
 }
 
 template <bool A_FP4, int EPI>

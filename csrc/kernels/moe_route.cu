@@ -21,6 +21,8 @@ namespace {
 template <typename T>
 __global__ void topk_route_kernel(const T* __restrict__ logits, int T_tok, int E, int K, int mode, float scale,
                                   float* __restrict__ w_out, int32_t* __restrict__ id_out) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T_tok) return;
   const T* lr = logits + (size_t)warp * E;
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
                                                          int32_t* __restrict__ sorted_src,    // [R_max]
                                                          int32_t* __restrict__ inv_map,       // [N_entries]
                                                          int R_max) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   extern __shared__ int32_t sm[];
   int32_t* cnt = sm;                 // E_local
   int32_t* off = sm + E_local;       // E_local + 1
@@ -172,6 +176,8 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
 __global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int xs, const int32_t* __restrict__ src,
                                           int R, int H, int Kp, int BN, uint8_t* __restrict__ q,
                                           uint8_t* __restrict__ sf) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (r >= R) return;
   const int s = src != nullptr ? src[r] : r;
@@ -222,6 +228,8 @@ __global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, i
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ys, const int32_t* __restrict__ inv_map,
                                    const float* __restrict__ w, int K, int H, __nv_bfloat16* __restrict__ out,
                                    int os, bool accumulate) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int t = blockIdx.x;
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
     float acc[8];
@@ -255,10 +263,10 @@ void topk_route(torch::Tensor weights, torch::Tensor ids, torch::Tensor logits, 
   auto st = at::cuda::getCurrentCUDAStream();
   const int threads = 256, blocks = (T * 32 + threads - 1) / threads;
   if (logits.scalar_type() == at::kFloat) {
-    topk_route_kernel<float><<<blocks, threads, 0, st>>>(logits.data_ptr<float>(), T, E, k, mode, scale,
+    snb::launch_pdl(topk_route_kernel<float>, blocks, threads, 0, st, logits.data_ptr<float>(), T, E, k, mode, scale,
                                                          weights.data_ptr<float>(), ids.data_ptr<int32_t>());
   } else {
-    topk_route_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>((const __nv_bfloat16*)logits.data_ptr(), T, E, k,
+    snb::launch_pdl(topk_route_kernel<__nv_bfloat16>, blocks, threads, 0, st, (const __nv_bfloat16*)logits.data_ptr(), T, E, k,
                                                                  mode, scale, weights.data_ptr<float>(),
                                                                  ids.data_ptr<int32_t>());
   }
@@ -273,7 +281,7 @@ void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, tor
   const int R_max = sorted_src.numel();
   TORCH_CHECK(R_max >= N + e_local * (bn - 1), "moe_align: sorted_src capacity too small");
   const size_t smem = (3 * e_local + 1) * sizeof(int32_t);
-  moe_align_kernel<<<1, 1024, smem, st>>>(ids.data_ptr<int32_t>(), N, K, e_lo, e_local, bn,
+  snb::launch_pdl(moe_align_kernel, 1, 1024, smem, st, ids.data_ptr<int32_t>(), N, K, e_lo, e_local, bn,
                                           seg_offsets.data_ptr<int32_t>(), tile_offsets.data_ptr<int32_t>(),
                                           sorted_src.data_ptr<int32_t>(), inv_map.data_ptr<int32_t>(), R_max);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -290,7 +298,7 @@ void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10:
   TORCH_CHECK(sf.numel() >= (int64_t)(R / bn) * KB * std::min<int64_t>(bn, 32) * 16, "gather_quant: sf capacity");
   auto st = at::cuda::getCurrentCUDAStream();
   const int threads = 256, blocks = (R * 32 + threads - 1) / threads;
-  gather_quant_mxfp8_kernel<<<blocks, threads, 0, st>>>((const __nv_bfloat16*)x.data_ptr(), x.stride(0),
+  snb::launch_pdl(gather_quant_mxfp8_kernel, blocks, threads, 0, st, (const __nv_bfloat16*)x.data_ptr(), x.stride(0),
                                                        src ? src->data_ptr<int32_t>() : nullptr, R, H, Kp, bn,
                                                        (uint8_t*)q.data_ptr(), (uint8_t*)sf.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -302,7 +310,7 @@ void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torc
   const int K = w.size(1);
   TORCH_CHECK(H % 8 == 0, "moe_combine: H");
   auto st = at::cuda::getCurrentCUDAStream();
-  moe_combine_kernel<<<T, 128, 0, st>>>((const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
+  snb::launch_pdl(moe_combine_kernel, T, 128, 0, st, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
                                         w.data_ptr<float>(), K, H, (__nv_bfloat16*)out.data_ptr(), out.stride(0),
                                         accumulate);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -41,6 +41,8 @@ template <typename T, typename W, bool kResidual>
 __global__ void rmsnorm_kernel(T* __restrict__ out, T* __restrict__ x, T* __restrict__ residual,
                                const W* __restrict__ weight, int H, int stride_x, int stride_out,
                                int stride_res, float eps, bool weight_plus_one) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int row = blockIdx.x;
   const int nvec = H / 8;
   T* xr = x + (size_t)row * stride_x;
@@ -92,6 +94,8 @@ __global__ void rmsnorm_kernel(T* __restrict__ out, T* __restrict__ x, T* __rest
 template <typename T, typename W>
 __global__ void head_rmsnorm_kernel(T* __restrict__ x, const W* __restrict__ weight, int rows, int D,
                                     int heads, int stride_tok, float eps) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -128,13 +132,13 @@ void rmsnorm_out(torch::Tensor out, torch::Tensor x, torch::Tensor weight, doubl
   const int threads = 256;
   if (x.scalar_type() == at::kBFloat16) {
     TORCH_CHECK(weight.scalar_type() == at::kBFloat16, "rmsnorm: bf16 x needs bf16 weight");
-    rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16, false><<<T, threads, 0, stream>>>(
+    snb::launch_pdl(rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16, false>, T, threads, 0, stream,
         (__nv_bfloat16*)out.data_ptr(), (__nv_bfloat16*)x.data_ptr(), nullptr,
         (const __nv_bfloat16*)weight.data_ptr(), H, x.stride(0), out.stride(0), 0, (float)eps,
         weight_plus_one);
   } else {
     TORCH_CHECK(x.scalar_type() == at::kFloat && weight.scalar_type() == at::kFloat, "rmsnorm: dtype");
-    rmsnorm_kernel<float, float, false><<<T, threads, 0, stream>>>(
+    snb::launch_pdl(rmsnorm_kernel<float, float, false>, T, threads, 0, stream,
         out.data_ptr<float>(), x.data_ptr<float>(), nullptr, weight.data_ptr<float>(), H, x.stride(0),
         out.stride(0), 0, (float)eps, weight_plus_one);
   }
@@ -149,12 +153,12 @@ void fused_add_rmsnorm(torch::Tensor x, torch::Tensor residual, torch::Tensor we
   if (T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (x.scalar_type() == at::kBFloat16) {
-    rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16, true><<<T, 256, 0, stream>>>(
+    snb::launch_pdl(rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16, true>, T, 256, 0, stream,
         (__nv_bfloat16*)x.data_ptr(), (__nv_bfloat16*)x.data_ptr(), (__nv_bfloat16*)residual.data_ptr(),
         (const __nv_bfloat16*)weight.data_ptr(), H, x.stride(0), x.stride(0), residual.stride(0),
         (float)eps, weight_plus_one);
   } else {
-    rmsnorm_kernel<float, float, true><<<T, 256, 0, stream>>>(
+    snb::launch_pdl(rmsnorm_kernel<float, float, true>, T, 256, 0, stream,
         x.data_ptr<float>(), x.data_ptr<float>(), residual.data_ptr<float>(), weight.data_ptr<float>(),
         H, x.stride(0), x.stride(0), residual.stride(0), (float)eps, weight_plus_one);
   }
@@ -172,11 +176,11 @@ void head_rmsnorm_(torch::Tensor x, torch::Tensor weight, int64_t heads, double 
   auto stream = at::cuda::getCurrentCUDAStream();
   const int threads = 256, blocks = (rows * 32 + threads - 1) / threads;
   if (x.scalar_type() == at::kBFloat16) {
-    head_rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, threads, 0, stream>>>(
+    snb::launch_pdl(head_rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16>, blocks, threads, 0, stream,
         (__nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)weight.data_ptr(), rows, D, heads,
         x.stride(0), (float)eps);
   } else {
-    head_rmsnorm_kernel<float, float><<<blocks, threads, 0, stream>>>(
+    snb::launch_pdl(head_rmsnorm_kernel<float, float>, blocks, threads, 0, stream,
         x.data_ptr<float>(), weight.data_ptr<float>(), rows, D, heads, x.stride(0), (float)eps);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

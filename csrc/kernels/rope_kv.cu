@@ -25,6 +25,8 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
                                CacheT* __restrict__ k_cache, CacheT* __restrict__ v_cache,
                                const int64_t* __restrict__ slots, int page_size, float inv_k_scale,
                                float inv_v_scale, int T_tokens) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   __shared__ float rowbuf[kWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kWarps + warp;
@@ -144,7 +146,7 @@ void rope_qk_norm_kv_write(torch::Tensor q, torch::Tensor k, torch::Tensor v, to
   const float iks = (float)(1.0 / k_scale), ivs = (float)(1.0 / v_scale);
   const int blocks = (rows + kWarps - 1) / kWarps;
 #define SNB_ROPE_LAUNCH(T_, C_)                                                                      \
-  rope_kv_kernel<T_, C_><<<blocks, kWarps * 32, 0, stream>>>(                                        \
+  snb::launch_pdl(rope_kv_kernel<T_, C_>, blocks, kWarps * 32, 0, stream,                                         \
       (T_*)q.data_ptr(), (T_*)k.data_ptr(), (const T_*)v.data_ptr(), q.stride(0), k.stride(0),       \
       v.stride(0), num_q_heads, num_kv_heads, head_dim, rot_dim, neox, positions.data_ptr<int64_t>(), \
       cos_sin.data_ptr<float>(), q_norm_w ? (const T_*)q_norm_w->data_ptr() : nullptr,              \

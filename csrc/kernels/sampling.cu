@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(1024) sample_kernel(const T* __restrict__ logi
                                                       const int64_t* __restrict__ positions,
                                                       int64_t* __restrict__ out_ids, float* __restrict__ out_vals,
                                                       int vocab_offset) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
   const int row = blockIdx.x;
   const T* lr = logits + (size_t)row * stride;
   const float temp = temperature != nullptr ? temperature[row] : 0.f;
@@ -108,11 +110,11 @@ void sample_tokens(torch::Tensor out_ids, torch::Tensor logits, c10::optional<to
   const int64_t* pp = positions ? positions->data_ptr<int64_t>() : nullptr;
   float* vp = out_vals ? out_vals->data_ptr<float>() : nullptr;
   if (logits.scalar_type() == at::kFloat) {
-    sample_kernel<float><<<B, 1024, 0, st>>>(logits.data_ptr<float>(), V, logits.stride(0), tp, sp, pp,
+    snb::launch_pdl(sample_kernel<float>, B, 1024, 0, st, logits.data_ptr<float>(), V, logits.stride(0), tp, sp, pp,
                                               out_ids.data_ptr<int64_t>(), vp, (int)vocab_offset);
   } else {
     TORCH_CHECK(logits.scalar_type() == at::kBFloat16, "sample_tokens: dtype");
-    sample_kernel<__nv_bfloat16><<<B, 1024, 0, st>>>((const __nv_bfloat16*)logits.data_ptr(), V, logits.stride(0),
+    snb::launch_pdl(sample_kernel<__nv_bfloat16>, B, 1024, 0, st, (const __nv_bfloat16*)logits.data_ptr(), V, logits.stride(0),
                                                       tp, sp, pp, out_ids.data_ptr<int64_t>(), vp,
                                                       (int)vocab_offset);
   }

@@ -25,12 +25,14 @@ def main():
     from ..parallel.state import init_process_group_from_env, initialize_parallel
     from ..parallel.symm_mem import IpcAllReduce
     from ..ops.gemm import linear
+    from ..parallel.collectives import fused_gemm_all_reduce, set_custom_allreduce
     from ..ops.moe import MoEAlignment, moe_align, moe_combine, topk_route
     init_process_group_from_env(timeout_s=120)
     world, rank = dist.get_world_size(), dist.get_rank()
     st = initialize_parallel(world, device=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
     dev = st.device
     ar = IpcAllReduce()
+    set_custom_allreduce(ar)
     T, H = a.tokens, a.hidden
     K = a.k_local or (4096 // world)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -67,6 +69,7 @@ def main():
            "gemm_splitk_then_nccl_us": t_op(lambda: dist.all_reduce(linear(xa, wt))),
            "gemm_then_oneshot_us": t_op(lambda: ar.all_reduce(linear(xa, wt), out)),
            "gemm_allreduce_fused_us": t_op(lambda: ar.gemm_all_reduce(xa, wt, None, sms)),
+           "gemm_splitk_allreduce_fused_us": t_op(lambda: fused_gemm_all_reduce(xa, wt, None)),
            "status": int(ar.status[0])}
     if rank == 0:
         print(json.dumps(res), flush=True)

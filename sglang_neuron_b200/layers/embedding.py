@@ -10,6 +10,7 @@ import torch
 from torch import nn
 
 from ..ops.gemm import linear
+from .linear import PackedWeight
 from ..parallel.collectives import tp_all_reduce
 from ..parallel.state import get_state
 
@@ -44,7 +45,7 @@ class VocabParallelEmbedding(nn.Module):
         self.weight.data[:n].copy_(w[self.start:self.end])
 
 
-class ParallelLMHead(nn.Module):
+class ParallelLMHead(PackedWeight, nn.Module):
     def __init__(self, vocab: int, hidden: int, dtype=torch.bfloat16, device=None):
         super().__init__()
         st = get_state()
@@ -54,8 +55,9 @@ class ParallelLMHead(nn.Module):
 
     def forward(self, h: torch.Tensor) -> torch.Tensor:
         """Local logits [B, per] (columns past the vocabulary end are masked by the sampler)."""
-        return linear(h, self.weight)
+        return linear(h, self.gemm_weight)
 
     def load(self, w: torch.Tensor):
+        self.unpack()
         n = self.end - self.start
         self.weight.data[:n].copy_(w[self.start:self.end])

@@ -12,7 +12,7 @@ from typing import List, Optional
 import torch
 from torch import nn
 
-from ..ops.gemm import linear
+from ..ops.gemm import TiledWeight, linear
 from ..parallel.collectives import fused_gemm_all_reduce, tp_all_reduce
 from ..parallel.state import get_state
 
@@ -21,22 +21,58 @@ def _param(shape, dtype, device) -> nn.Parameter:
     return nn.Parameter(torch.empty(shape, dtype=dtype, device=device), requires_grad=False)
 
 
-class ReplicatedLinear(nn.Module):
+class PackedWeight:
+    """Mixin of the GEMM layers: after loading, `pack()` re-lays a CUDA bf16 weight out as contiguous
+    128 x 64 tiles (ops/gemm.TiledWeight) and frees the row-major copy; `gemm_weight` is what forward() hands
+    to the GEMM (the tiled weight when packed, else the parameter)."""
+
+    _packed: Optional[TiledWeight] = None
+
+    @property
+    def gemm_weight(self):
+        return self._packed if self._packed is not None else self.weight
+
+    def pack(self) -> None:
+        w = self.weight
+        if self._packed is not None or not w.is_cuda or w.dtype != torch.bfloat16 or w.dim() != 2 or not w.numel():
+            return
+        self._packed = TiledWeight(w.data)
+        self.weight = nn.Parameter(torch.empty(0, dtype=w.dtype, device=w.device), requires_grad=False)
+
+    def unpack(self) -> None:
+        """Back to a row-major parameter (before loading new weights into a packed layer)."""
+        if self._packed is not None:
+            self.weight = nn.Parameter(self._packed.untiled().contiguous(), requires_grad=False)
+            self._packed = None
+
+
+def pack_linear_weights(model: nn.Module) -> int:
+    """Pack every GEMM layer of `model`; returns how many were packed."""
+    n = 0
+    for m in model.modules():
+        if isinstance(m, PackedWeight) and m._packed is None:
+            m.pack()
+            n += m._packed is not None
+    return n
+
+
+class ReplicatedLinear(PackedWeight, nn.Module):
     def __init__(self, in_features: int, out_features: int, bias: bool = False, dtype=torch.bfloat16, device=None):
         super().__init__()
         self.weight = _param((out_features, in_features), dtype, device)
         self.bias = _param((out_features,), dtype, device) if bias else None
 
     def forward(self, x):
-        return linear(x, self.weight, self.bias)
+        return linear(x, self.gemm_weight, self.bias)
 
     def load(self, w: torch.Tensor, b: Optional[torch.Tensor] = None):
+        self.unpack()
         self.weight.data.copy_(w)
         if b is not None:
             self.bias.data.copy_(b)
 
 
-class ColumnParallelLinear(nn.Module):
+class ColumnParallelLinear(PackedWeight, nn.Module):
     """Output features split over TP ranks; no communication."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = False, dtype=torch.bfloat16, device=None):
@@ -48,13 +84,14 @@ class ColumnParallelLinear(nn.Module):
         self.bias = _param((self.out_local,), dtype, device) if bias else None
 
     def forward(self, x):
-        return linear(x, self.weight, self.bias)
+        return linear(x, self.gemm_weight, self.bias)
 
     def shard(self, full: torch.Tensor, dim: int = 0) -> torch.Tensor:
         st = get_state()
         return full.narrow(dim, st.tp_rank * self.out_local, self.out_local)
 
     def load(self, w: torch.Tensor, b: Optional[torch.Tensor] = None):
+        self.unpack()
         self.weight.data.copy_(self.shard(w))
         if b is not None:
             self.bias.data.copy_(self.shard(b))
@@ -70,6 +107,7 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
         self.parts_local = [p // st.tp_size for p in parts]
 
     def load_part(self, idx: int, w: torch.Tensor, b: Optional[torch.Tensor] = None):
+        self.unpack()
         st = get_state()
         n = self.parts_local[idx]
         off = sum(self.parts_local[:idx])
@@ -78,7 +116,7 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
             self.bias.data[off:off + n].copy_(b.narrow(0, st.tp_rank * n, n))
 
 
-class QKVParallelLinear(nn.Module):
+class QKVParallelLinear(PackedWeight, nn.Module):
     """Fused Q/K/V projection with heads split over TP; KV heads are replicated when tp > num_kv_heads."""
 
     def __init__(self, hidden: int, head_dim: int, num_heads: int, num_kv_heads: int, bias: bool = False,
@@ -104,9 +142,10 @@ class QKVParallelLinear(nn.Module):
         self.bias = _param((out,), dtype, device) if bias else None
 
     def forward(self, x):
-        return linear(x, self.weight, self.bias)
+        return linear(x, self.gemm_weight, self.bias)
 
     def load(self, q, k, v, qb=None, kb=None, vb=None):
+        self.unpack()
         st = get_state()
         D = self.head_dim
         qs = q.narrow(0, st.tp_rank * self.q_size, self.q_size)
@@ -119,7 +158,7 @@ class QKVParallelLinear(nn.Module):
                                             vb.narrow(0, self.kv_head_start * D, self.kv_size)], 0))
 
 
-class RowParallelLinear(nn.Module):
+class RowParallelLinear(PackedWeight, nn.Module):
     """Input features split over TP ranks; the partial outputs are summed with an all-reduce (unless
     reduce=False, when the caller fuses the reduction with a later one)."""
 
@@ -138,15 +177,16 @@ class RowParallelLinear(nn.Module):
         # the bias is added once (on rank 0) so the all-reduce sums it exactly once
         b = self.bias if (self.bias is not None and st.tp_rank == 0) else None
         if self.reduce and st.tp_size > 1:
-            y = fused_gemm_all_reduce(x, self.weight, b)
+            y = fused_gemm_all_reduce(x, self.gemm_weight, b)
             if y is not None:
                 return y
-        y = linear(x, self.weight, b)
+        y = linear(x, self.gemm_weight, b)
         if self.reduce and st.tp_size > 1:
             y = tp_all_reduce(y)
         return y
 
     def load(self, w: torch.Tensor, b: Optional[torch.Tensor] = None):
+        self.unpack()
         st = get_state()
         self.weight.data.copy_(w.narrow(1, st.tp_rank * self.in_local, self.in_local))
         if b is not None:

@@ -184,6 +184,11 @@ class ModelRunner:
         if self.draft is not None:
             self.draft.load(src.get)
         if self.cuda:
+            # GEMM weights as contiguous 128 x 64 tiles (one DRAM stream per TMA box)
+            from ..layers.linear import pack_linear_weights
+            pack_linear_weights(self.model)
+            if self.draft is not None:
+                pack_linear_weights(self.draft)
             torch.cuda.synchronize(self.device)
             torch.cuda.empty_cache()
 

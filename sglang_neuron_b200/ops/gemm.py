@@ -1,4 +1,8 @@
-"""Dense linear layers: the tcgen05 bf16 GEMM on CUDA, torch matmul on CPU."""
+"""Dense linear layers: the tcgen05 bf16 GEMM on CUDA, torch matmul on CPU.
+
+By default a decode-sized GEMM splits K across the CTAs of a thread-block cluster and reduces the partial
+tiles through distributed shared memory inside the kernel; an explicit `splits` > 1 writes fp32 partials
+that a second launch (or a fused consumer) sums."""
 from typing import Optional
 
 import torch
@@ -26,6 +30,46 @@ def check_status(device) -> None:
             raise RuntimeError(f"sm_100a kernel reported status {code} (bounded wait expired)")
 
 
+class TiledWeight:
+    """A bf16 [F, K] weight re-laid out for the tcgen05 GEMM: every 128-row x 64-column tile is one contiguous
+    16 KB block, `data` = [ceil(F/128) * ceil(K/64) * 128, 64] (tile (f, k) at rows ((f * nk) + k) * 128),
+    zero padded. One TMA box then reads one contiguous DRAM stream instead of 128 strided 128-byte rows."""
+
+    __slots__ = ("data", "F", "K")
+
+    def __init__(self, w: torch.Tensor):
+        F, K = w.shape
+        ntf, nk = (F + 127) // 128, (K + 63) // 64
+        pad = torch.zeros(ntf * 128, nk * 64, dtype=w.dtype, device=w.device)
+        pad[:F, :K] = w
+        self.data = pad.view(ntf, 128, nk, 64).permute(0, 2, 1, 3).contiguous().view(ntf * nk * 128, 64)
+        self.F, self.K = F, K
+
+    @property
+    def shape(self):
+        return (self.F, self.K)
+
+    @property
+    def dtype(self):
+        return self.data.dtype
+
+    @property
+    def device(self):
+        return self.data.device
+
+    def untiled(self) -> torch.Tensor:
+        ntf, nk = (self.F + 127) // 128, (self.K + 63) // 64
+        full = self.data.view(ntf, nk, 128, 64).permute(0, 2, 1, 3).reshape(ntf * 128, nk * 64)
+        return full[: self.F, : self.K]
+
+
+def _weight_args(w):
+    """(tensor handed to the kernel, logical F, tiled_f flag value)."""
+    if isinstance(w, TiledWeight):
+        return w.data, w.F, w.F
+    return w, w.shape[0], 0
+
+
 def pick_splits(T: int, F: int, K: int, num_sms: int = 148) -> int:
     """Split K when the output tiles alone cannot occupy the SMs (decode-sized GEMMs)."""
     bn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
@@ -39,8 +83,10 @@ def pick_splits(T: int, F: int, K: int, num_sms: int = 148) -> int:
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, out=None,
            bn: int = 0, splits: Optional[int] = None) -> torch.Tensor:
-    """y = x @ w.T (+ bias). x: [..., K], w: [F, K]."""
+    """y = x @ w.T (+ bias). x: [..., K], w: [F, K] tensor or TiledWeight."""
     if not x.is_cuda or x.dtype != torch.bfloat16:
+        if isinstance(w, TiledWeight):
+            w = w.untiled()
         y = torch.nn.functional.linear(x, w, bias)
         if out is not None:
             out.copy_(y)
@@ -50,12 +96,22 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     x2 = x.reshape(-1, shape[-1])
     if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16 != 0 or x2.data_ptr() % 16 != 0:
         x2 = x2.contiguous()
-    F = w.shape[0]
+    wk, F, tiled_f = _weight_args(w)
     T = x2.shape[0]
     if out is None:
         out = torch.empty(T, F, dtype=x.dtype, device=x.device)
     if splits is None:
-        splits = pick_splits(T, F, x2.shape[1])
+        splits = 0  # automatic: K split inside a thread-block cluster where tiles < SMs
     ws = torch.empty(splits * T * F, dtype=torch.float32, device=x.device) if splits > 1 else None
-    kernels().gemm_bf16(out.view(-1, F), x2, w, bias, _status_buf(x.device), bn, splits, ws)
+    kernels().gemm_bf16(out.view(-1, F), x2, wk, bias, _status_buf(x.device), bn, splits, ws, True, tiled_f)
     return out.view(*shape[:-1], F)
+
+
+def linear_partials(x2: torch.Tensor, w: torch.Tensor, splits: int) -> torch.Tensor:
+    """Split-K fp32 partial products [splits, T, F] of x2 @ w.T, left unreduced (a fused reduce follows)."""
+    wk, F, tiled_f = _weight_args(w)
+    T = x2.shape[0]
+    ws = torch.empty(splits * T * F, dtype=torch.float32, device=x2.device)
+    dummy = torch.empty((0, F), dtype=x2.dtype, device=x2.device)
+    kernels().gemm_bf16(dummy, x2, wk, None, _status_buf(x2.device), 0, splits, ws, False, tiled_f)
+    return ws

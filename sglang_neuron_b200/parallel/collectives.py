@@ -42,20 +42,35 @@ _num_sms = {}
 
 
 def fused_gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias):
-    """Row-parallel GEMM + all-reduce in one NVLink kernel, or None when that path does not apply."""
+    """Row-parallel GEMM + all-reduce over NVLink, or None when that path does not apply.
+
+    Decode-sized GEMMs (split-K > 1) run as two launches: the split-K tcgen05 GEMM writes fp32 partials and
+    one kernel sums them, adds the bias, pushes the tile to every peer and reduces; larger GEMMs run the
+    GEMM then the one-shot all-reduce. (The tcgen05 GEMM with the all-reduce inside its epilogue,
+    IpcAllReduce.gemm_all_reduce, covers one-wave grids but keeps only F/128 CTAs busy, so it loses to the
+    split-K form at the shapes measured; it stays available.)"""
     st = get_state()
     if st.tp_size == 1 or _custom_allreduce is None or not x.is_cuda or x.dtype != torch.bfloat16:
         return None
+    from ..ops.gemm import linear, linear_partials, pick_splits
     x2 = x.reshape(-1, x.shape[-1])
     if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16 or x2.data_ptr() % 16:
         x2 = x2.contiguous()
+    T, F = x2.shape[0], w.shape[0]
+    if T * F * 2 > _custom_allreduce.capacity or F % 8:
+        return None
     dev = x.device.index
     if dev not in _num_sms:
         _num_sms[dev] = torch.cuda.get_device_properties(x.device).multi_processor_count
-    if not _custom_allreduce.gemm_can_run(x2.shape[0], w.shape[0], _num_sms[dev]):
-        return None
-    out = _custom_allreduce.gemm_all_reduce(x2, w, bias, _num_sms[dev])
-    return out.view(*x.shape[:-1], w.shape[0])
+    splits = pick_splits(T, F, x2.shape[1], _num_sms[dev])
+    out = torch.empty(T, F, dtype=x.dtype, device=x.device)
+    if splits > 1:
+        part = linear_partials(x2, w, splits)
+        _custom_allreduce.splitk_all_reduce(part, splits, T, F, bias, out)
+    else:
+        y = linear(x2, w, bias, splits=1)
+        _custom_allreduce.all_reduce(y, out)
+    return out.view(*x.shape[:-1], F)
 
 
 def tp_all_gather(x: torch.Tensor, dim: int = -1) -> torch.Tensor:

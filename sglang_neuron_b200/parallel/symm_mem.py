@@ -43,7 +43,7 @@ class IpcAllReduce:
         if out is None:
             out = torch.empty_like(x)
         nvec = x.numel() // 8
-        ctas = max(1, min(self.max_ctas, (nvec + 2047) // 2048))
+        ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))  # ~4 KB per CTA: many SMs drive NVLink
         kernels().one_shot_allreduce(out, x, self.ptrs, self.rank, self.capacity, ctas, self.status)
         return out
 
@@ -51,7 +51,7 @@ class IpcAllReduce:
                            w: torch.Tensor) -> torch.Tensor:
         """MoE combine (weighted sum of this rank's expert rows per token) fused with the all-reduce."""
         nvec = out.numel() // 8
-        ctas = max(1, min(self.max_ctas, (nvec + 2047) // 2048))
+        ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))
         kernels().moe_combine_allreduce(out, y, inv_map, w, self.ptrs, self.rank, self.capacity, ctas, self.status)
         return out
 
@@ -64,8 +64,19 @@ class IpcAllReduce:
                         num_sms: int) -> torch.Tensor:
         """out = all_reduce(x @ w.T (+ bias on rank 0 only)) in one kernel: tcgen05 GEMM whose epilogue
         stores its tiles into every peer's buffer and reduces them."""
-        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-        kernels().gemm_bf16_allreduce(out, x, w, bias, self.status, self.ptrs, self.rank, self.capacity, num_sms)
+        from ..ops.gemm import _weight_args
+        wk, F, tiled_f = _weight_args(w)
+        out = torch.empty(x.shape[0], F, dtype=x.dtype, device=x.device)
+        kernels().gemm_bf16_allreduce(out, x, wk, bias, self.status, self.ptrs, self.rank, self.capacity, num_sms,
+                                      tiled_f)
+        return out
+
+    def splitk_all_reduce(self, partial: torch.Tensor, splits: int, T: int, F: int,
+                          bias: Optional[torch.Tensor], out: torch.Tensor) -> torch.Tensor:
+        """Sum split-K partials (+ bias), all-reduce over the group: one launch after the split-K GEMM."""
+        nvec = T * F // 8
+        ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))
+        kernels().splitk_allreduce(out, partial, splits, bias, self.ptrs, self.rank, self.capacity, ctas, self.status)
         return out
 
     def close(self) -> None:

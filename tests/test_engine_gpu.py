@@ -58,7 +58,10 @@ def test_gpu_tracks_cpu_oracle(base, over, tol):
     g, c = got["cuda"], got["cpu"]
     rel = (g - c).norm() / c.norm()
     assert rel < tol, f"GPU bf16 logits deviate from the fp32 oracle: rel {rel}"
-    assert (g.argmax(-1) == c.argmax(-1)).float().mean() >= 0.66
+    # the argmax must agree wherever the oracle's top-1 margin exceeds the row's worst logit error
+    top2 = c.topk(2, dim=-1).values
+    confident = (top2[:, 0] - top2[:, 1]) > (g - c).abs().amax(-1)
+    assert torch.equal(g.argmax(-1)[confident], c.argmax(-1)[confident]), f"rel {rel}"
 
 
 def test_sampling_temperature_is_reproducible():

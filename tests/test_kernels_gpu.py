@@ -226,3 +226,47 @@ def test_gemm_bf16_tcgen05(T, F, K, bias, splits):
     check_status(x.device)
     ref = x.float() @ w.float().t() + (b.float() if bias else 0)
     _close(y, ref, 3e-2, 1e-2, "gemm")
+
+
+@pytest.mark.parametrize("T,F,K,bias", [(1, 2880, 2880, True), (64, 5120, 2880, False), (64, 2880, 4096, True),
+                                        (64, 128, 2880, True), (33, 201088 // 16, 2880, False),
+                                        (130, 2880, 4096, True), (600, 5120, 2880, True), (7, 1000, 520, True),
+                                        (2048, 1536, 1024, False)])
+def test_gemm_default_path(T, F, K, bias):
+    _gemm_default_path(T, F, K, bias, tiled=False)
+
+
+@pytest.mark.parametrize("T,F,K,bias", [(1, 2880, 2880, True), (64, 5120, 2880, False), (64, 2880, 4096, True),
+                                        (64, 128, 2880, True), (7, 1000, 520, True), (130, 2880, 4096, True),
+                                        (600, 5120, 2880, True)])
+def test_gemm_tiled_weight(T, F, K, bias):
+    """Pre-tiled weights (contiguous 128 x 64 tiles) through the same kernel."""
+    _gemm_default_path(T, F, K, bias, tiled=True)
+
+
+def _gemm_default_path(T, F, K, bias, tiled):
+    """Default GEMM path (K split across a thread-block cluster, partials summed through distributed shared
+    memory, for decode shapes): repeated calls give bit-identical results (fixed summation order)."""
+    from sglang_neuron_b200.ops.gemm import TiledWeight, linear, linear_partials, check_status
+    torch.manual_seed(9)
+    x = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(F, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    b = torch.randn(F, device=DEV, dtype=torch.bfloat16) if bias else None
+    wg = TiledWeight(w) if tiled else w
+    y1 = linear(x, wg, b)
+    y2 = linear(x, wg, b)
+    if tiled:
+        assert torch.equal(wg.untiled(), w)
+        ys = linear(x, wg, b, splits=3)
+        part = linear_partials(x, wg, 2).view(2, T, F).sum(0)
+        torch.cuda.synchronize()
+        _close(ys, x.float() @ w.float().t() + (b.float() if bias else 0), 3e-2, 1e-2, "gemm_tiled_splitk")
+        _close(part, x.float() @ w.float().t(), 3e-2, 1e-2, "gemm_tiled_partials")
+    out = torch.empty(T, F + 8, device=DEV, dtype=torch.bfloat16)[:, :F]  # strided output rows
+    linear(x, wg, b, out=out)
+    torch.cuda.synchronize()
+    check_status(x.device)
+    ref = x.float() @ w.float().t() + (b.float() if bias else 0)
+    _close(y1, ref, 3e-2, 1e-2, "gemm_default")
+    assert torch.equal(y1, y2)
+    assert torch.equal(out, y1)

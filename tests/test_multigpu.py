@@ -73,6 +73,21 @@ def _ar_worker(rank, world, port, q):
             out = ar.gemm_all_reduce(x, wt, None, torch.cuda.get_device_properties(0).multi_processor_count)
         torch.cuda.synchronize()
         errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    # split-K GEMM + (partial sum, bias, all-reduce) kernel: the row-parallel path the engine takes
+    from sglang_neuron_b200.parallel.collectives import fused_gemm_all_reduce, set_custom_allreduce
+    set_custom_allreduce(ar)
+    for T, F, Kl in [(64, 2880, 2048), (3, 2880, 4096 // world), (200, 1024, 512)]:
+        g = torch.Generator(device="cuda").manual_seed(23 + rank + T)
+        x = torch.randn(T, Kl, device="cuda", generator=g).to(torch.bfloat16)
+        wt = (torch.randn(F, Kl, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        b = (torch.randn(F, device="cuda", generator=g)).to(torch.bfloat16)
+        ref = (x.float() @ wt.float().t()) + b.float()
+        dist.all_reduce(ref)
+        for _ in range(2):
+            out = fused_gemm_all_reduce(x, wt, b)
+        torch.cuda.synchronize()
+        errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    set_custom_allreduce(None)
     status = int(ar.status[0])
     ar.close()
     q.put((rank, errs, status))
