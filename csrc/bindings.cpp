@@ -18,7 +18,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
                       int64_t head_dim, int64_t page_size, int64_t window, double sm_scale, double k_scale,
                       double v_scale, c10::optional<torch::Tensor> sinks, int64_t num_splits, torch::Tensor o_part,
-                      torch::Tensor lse_part);
+                      torch::Tensor lse_part, c10::optional<torch::Tensor> status);
 void extend_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                       torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
                       int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t page_size,
@@ -69,7 +69,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("head_rmsnorm_", &head_rmsnorm_);
   m.def("rope_qk_norm_kv_write", &rope_qk_norm_kv_write);
-  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention", &decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_table"), py::arg("seq_lens"), py::arg("num_q_heads"), py::arg("num_kv_heads"),
+        py::arg("head_dim"), py::arg("page_size"), py::arg("window"), py::arg("sm_scale"), py::arg("k_scale"),
+        py::arg("v_scale"), py::arg("sinks"), py::arg("num_splits"), py::arg("o_part"), py::arg("lse_part"),
+        py::arg("status") = py::none());
   m.def("extend_attention", &extend_attention);
   m.def("sample_tokens", &sample_tokens);
   m.def("topk_route", &topk_route);

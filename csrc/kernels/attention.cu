@@ -396,6 +396,11 @@ bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
                           int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
                           const float* sinks, int64_t num_splits, float* o_part, float* lse_part);
 
+bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                          torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
+                          int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
+                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status);
+
 bool extend_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                           torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
@@ -408,7 +413,8 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads,
                       int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
                       double sm_scale, double k_scale, double v_scale, c10::optional<torch::Tensor> sinks,
-                      int64_t num_splits, torch::Tensor o_part, torch::Tensor lse_part) {
+                      int64_t num_splits, torch::Tensor o_part, torch::Tensor lse_part,
+                      c10::optional<torch::Tensor> status) {
   const int B = q.size(0);
   if (B == 0) return;
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16, "decode_attention: bf16 q/out");
@@ -433,9 +439,15 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   auto outp = (__nv_bfloat16*)out.data_ptr();
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
   TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16, "decode_attention: cache dtype");
-  // tensor-core path (mma.sync) for every GQA group up to 16 heads; the CUDA-core kernel below covers the rest
-  const bool mma_done = decode_attention_mma(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads,
-                                             num_kv_heads, head_dim, page_size, window, scale, vs, sk, S, op, lp);
+  // fp8 cache: bulk-async pipelined tensor-core kernel; else the register-prefetch tensor-core kernel for every
+  // GQA group up to 16 heads; the CUDA-core kernel below covers the rest
+  int* stp = status ? status->data_ptr<int>() : nullptr;
+  const bool mma_done =
+      (stp != nullptr && decode_attention_fp8(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads,
+                                              num_kv_heads, head_dim, page_size, window, scale, vs, sk, S, op, lp,
+                                              stp)) ||
+      decode_attention_mma(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads, num_kv_heads, head_dim,
+                           page_size, window, scale, vs, sk, S, op, lp);
   if (!mma_done) {
 #define SNB_DEC_D(DD)                                                                                      \
   if (fp8)                                                                                                 \

@@ -276,21 +276,26 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   if (cluster_reduce) {
-    // Split-K inside a (1, 1, S) cluster: the S CTAs of one output tile sum their fp32 accumulators in the
-    // leader's (cluster rank 0) shared memory. After the first cluster barrier every CTA's MMAs are done, so
-    // the leader's ring is free; the others store their TMEM tiles into it over DSMEM ([f][BN + 4] rows, 16-
-    // byte stores, conflict-free); after the second the leader adds them in rank order (deterministic),
-    // adds the bias and writes bf16.
-    constexpr int RS = BN + 4;
+    // Split-K inside a (1, 1, S) cluster, reduced by a reduce-scatter over distributed shared memory: the
+    // tile's BN columns are cut into S contiguous ranges of 4-column groups, CTA r owns range r. After the
+    // first cluster barrier every CTA's MMAs are done (its ring is free); each CTA stores every 4-column
+    // group of its TMEM tile into the owner's ring, slot = its own rank ([src][128 rows][RS] fp32, 16-byte
+    // stores, odd 16-byte row stride: conflict-free). After the second barrier each CTA sums its groups over
+    // the S slots in rank order (deterministic), adds the bias and writes bf16. Every SM moves about
+    // (S - 1)/S of one tile instead of one SM receiving S - 1 tiles.
+    constexpr int NG = BN / 4;
     constexpr int CH = BN >= 32 ? 32 : BN;
+    const int maxg = (NG + S - 1) / S;
+    const int rs = 4 * (maxg + ((maxg & 1) ? 2 : 1));  // floats per row: odd number of 16-byte units
     __syncwarp();
     snb::tc_fence_before();
     snb::cluster_sync();
     snb::tc_fence_after();
-    const uint32_t rank = snb::cluster_ctarank();
+    const int rank = (int)snb::cluster_ctarank();
     const int q = warp & 3, fl = q * 32 + lane;
-    if (warp >= 2 && rank != 0 && ep_ok) {
-      const uint32_t dst = snb::mapa_shared(snb::smem_u32(smem) + (((int)rank - 1) * BM + fl) * RS * 4, 0);
+    if (warp >= 2 && ep_ok) {
+      const uint32_t my_slot = snb::smem_u32(smem) + (uint32_t)((rank * BM + fl) * rs) * 4u;
+      int owner = 0;
 #pragma unroll 1
       for (int c = 0; c < BN / CH; ++c) {
         uint32_t r[CH];
@@ -308,53 +313,38 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
 #pragma unroll
-        for (int j = 0; j < CH; j += 4)
-          snb::st_cluster_v4(dst + (c * CH + j) * 4, __uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                             __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        for (int j = 0; j < CH / 4; ++j) {
+          const int g = c * (CH / 4) + j;
+          while (owner + 1 < S && (owner + 1) * NG / S <= g) ++owner;
+          const int gl = g - owner * NG / S;
+          const uint32_t dst = snb::mapa_shared(my_slot + (uint32_t)(gl * 16), (uint32_t)owner);
+          snb::st_cluster_v4(dst, __uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                             __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        }
       }
     }
     __syncwarp();
     snb::cluster_sync();
-    if (warp >= 2 && rank == 0 && ep_ok) {
+    if (warp >= 2 && ep_ok) {
       const int f = f0 + fl;
       const float bf = (bias != nullptr && f < F) ? __bfloat162float(bias[f]) : 0.f;
-      const float* slots = reinterpret_cast<const float*>(smem) + fl * RS;
-#pragma unroll 1
-      for (int c = 0; c < BN / CH; ++c) {
-        uint32_t r[CH];
-        if constexpr (CH == 32) {
-          snb::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * CH, r);
-          snb::tmem_ld_wait();
-        } else {
-          uint32_t r8[8];
-#pragma unroll
-          for (int h = 0; h < CH / 8; ++h) {
-            snb::tmem_ld_32x32b_x8(tmem + ((uint32_t)(q * 32) << 16) + c * CH + h * 8, r8);
-            snb::tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) r[h * 8 + j] = r8[j];
-          }
-        }
-        float acc[CH];
-#pragma unroll
-        for (int j = 0; j < CH; ++j) acc[j] = __uint_as_float(r[j]);
-        for (int rr = 1; rr < S; ++rr) {
-          const float4* src = reinterpret_cast<const float4*>(slots + (size_t)(rr - 1) * BM * RS + c * CH);
-#pragma unroll
-          for (int j = 0; j < CH / 4; ++j) {
-            const float4 v = src[j];
-            acc[4 * j] += v.x;
-            acc[4 * j + 1] += v.y;
-            acc[4 * j + 2] += v.z;
-            acc[4 * j + 3] += v.w;
-          }
+      const int g0 = rank * NG / S, g1 = (rank + 1) * NG / S;
+      const float* rows = reinterpret_cast<const float*>(smem) + fl * rs;
+      for (int g = g0; g < g1; ++g) {
+        float4 acc = make_float4(bf, bf, bf, bf);
+        for (int src = 0; src < S; ++src) {
+          const float4 v = *reinterpret_cast<const float4*>(rows + (size_t)src * BM * rs + (g - g0) * 4);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
         }
         if (f < F) {
-#pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const int t = t0 + c * CH + j;
-            if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(acc[j] + bf);
-          }
+          const int t = t0 + g * 4;
+          if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(acc.x);
+          if (t + 1 < T) out[(size_t)(t + 1) * ldo + f] = __float2bfloat16(acc.y);
+          if (t + 2 < T) out[(size_t)(t + 2) * ldo + f] = __float2bfloat16(acc.z);
+          if (t + 3 < T) out[(size_t)(t + 3) * ldo + f] = __float2bfloat16(acc.w);
         }
       }
     }
@@ -381,13 +371,18 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const __
   out[(size_t)t * ldo + f] = __float2bfloat16(a);
 }
 
-// Largest split count whose (S - 1) partial tiles ([128][BN + 4] fp32 each) fit in the leader's ring.
+// Largest split count (<= 8, the portable cluster size) whose reduce-scatter slots
+// (S x 128 rows x rs floats) fit in the ring.
 template <int BN>
-constexpr int max_cluster_splits() {
+int max_cluster_splits() {
   using C = GemmCfg<BN>;
-  const int slot = BM * (BN + 4) * 4;
-  const int s = (C::STAGES * C::STAGE_BYTES) / slot + 1;
-  return s > 8 ? 8 : s;
+  int best = 1;
+  for (int S = 2; S <= 8; ++S) {
+    const int ng = BN / 4, maxg = (ng + S - 1) / S;
+    const int rs = 4 * (maxg + ((maxg & 1) ? 2 : 1));
+    if (S * BM * rs * 4 <= C::STAGES * C::STAGE_BYTES) best = S;
+  }
+  return best;
 }
 
 // Split count for the in-cluster reduction: as many K splits as keep every tile's cluster co-resident in

@@ -122,9 +122,10 @@ def decode_attention(q, k_cache, v_cache, block_table, seq_lens, num_q_heads, nu
         o_part, lse_part = scratch.o, scratch.lse
     else:
         o_part = lse_part = torch.empty(0, dtype=torch.float32, device=q.device)
+    from .gemm import _status_buf
     kernels().decode_attention(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads, num_kv_heads,
                                head_dim, page_size, window, sm_scale, k_scale, v_scale, sinks, num_splits,
-                               o_part, lse_part)
+                               o_part, lse_part, _status_buf(q.device))
     return out
 
 

@@ -88,17 +88,24 @@ def _make_paged(B, ctx_lens, Hkv, D, P, dtype, seed=0):
     return kc.to(dtype), vc.to(dtype), bt
 
 
-@pytest.mark.parametrize("D,Hq,Hkv,window,sinks,fp8,splits", [
-    (64, 64, 8, 0, True, True, 1), (64, 64, 8, 128, True, True, 4), (128, 32, 8, 0, False, False, 3),
-    (128, 16, 8, 0, False, False, 1), (64, 8, 1, 0, True, False, 8)])
-def test_decode_attention(D, Hq, Hkv, window, sinks, fp8, splits):
+@pytest.mark.parametrize("D,Hq,Hkv,window,sinks,fp8,splits,P", [
+    (64, 64, 8, 0, True, True, 1, 16), (64, 64, 8, 128, True, True, 4, 16), (128, 32, 8, 0, False, False, 3, 16),
+    (128, 16, 8, 0, False, False, 1, 16), (64, 8, 1, 0, True, False, 8, 16), (64, 64, 8, 100, True, True, 2, 16),
+    (128, 32, 8, 0, True, True, 3, 16), (128, 64, 8, 77, False, True, 1, 16), (64, 32, 8, 0, True, True, 2, 64),
+    (64, 64, 8, 0, False, True, 3, 128), (64, 16, 2, 0, True, True, 1, 32)])
+def test_decode_attention(D, Hq, Hkv, window, sinks, fp8, splits, P):
     from sglang_neuron_b200.ops.attention import decode_attention, decode_attention_ref
     torch.manual_seed(2)
-    P = 16
     ctx = [1, 17, 300, 1000, 64, 129]
     B = len(ctx)
     dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
     kc, vc, bt = _make_paged(B, ctx, Hkv, D, P, dt)
+    if fp8:  # stale bytes past each request's end (NaN patterns included) must not leak into the output
+        for b, c in enumerate(ctx):
+            for t in range(c, ((c + P - 1) // P + 1) * P):
+                pg = int(bt[b, t // P])
+                kc[pg, :, t % P] = float("nan")
+                vc[pg, :, t % P] = float("nan")
     q = torch.randn(B, Hq * D, dtype=torch.bfloat16)
     sk = torch.randn(Hq) if sinks else None
     seq = torch.tensor(ctx, dtype=torch.int32)
