@@ -114,6 +114,30 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _profile_steps(eng, sched, refill, rank, n, dev):
+    """Run n more steps under torch.profiler (CUPTI kernel activity, graph-replayed kernels included) and
+    write the per-kernel device-time table of this rank to gpurun_out/torchprof_rank<r>.txt."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize(dev)
+    with profile(activities=[ProfilerActivity.CUDA]) as p:
+        for _ in range(n):
+            refill()
+            sched._sync_arrivals()
+            step = sched.schedule()
+            if step is None:
+                continue
+            ids_host, ev = eng.runner.run_step(step)
+            sched.inflight.append((step, ids_host, ev))
+            while len(sched.inflight) > 1:
+                sched._process(*sched.inflight.popleft())
+        sched.drain()
+        torch.cuda.synchronize(dev)
+    os.makedirs("gpurun_out", exist_ok=True)
+    with open(f"gpurun_out/torchprof_rank{rank}.txt", "w") as f:
+        f.write(p.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=90))
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -266,6 +290,9 @@ def main():
             "init_s": round(init_s, 1),
         }
         print(json.dumps(line), flush=True)
+    if os.environ.get("SNB_TORCH_PROFILE"):
+        # attribution only (after the timed region): per-kernel device time of a few more steps, every rank
+        _profile_steps(eng, sched, refill, rank, int(os.environ.get("SNB_TORCH_PROFILE")), dev)
     eng.shutdown()
     if world > 1:
         dist.barrier()

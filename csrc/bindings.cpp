@@ -46,6 +46,15 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
                torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace,
                bool reduce_partials, int64_t tiled_f);
 void set_pdl(bool on);
+int64_t nvls_flag_bytes();
+void nvls_allreduce(torch::Tensor out, torch::Tensor x, int64_t uc, int64_t mc, int64_t capacity, int64_t rank,
+                    int64_t world, int64_t max_ctas, torch::Tensor status);
+void nvls_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, int64_t uc,
+                            int64_t mc, int64_t capacity, int64_t rank, int64_t world, int64_t max_ctas,
+                            torch::Tensor status);
+void nvls_splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits,
+                           c10::optional<torch::Tensor> bias, int64_t uc, int64_t mc, int64_t capacity, int64_t rank,
+                           int64_t world, int64_t max_ctas, torch::Tensor status);
 bool get_pdl();
 void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
                       std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status);
@@ -91,5 +100,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
   m.def("splitk_allreduce", &splitk_allreduce);
   m.def("set_pdl", &set_pdl);
+  m.def("nvls_flag_bytes", &nvls_flag_bytes);
+  m.def("nvls_allreduce", &nvls_allreduce);
+  m.def("nvls_combine_allreduce", &nvls_combine_allreduce);
+  m.def("nvls_splitk_allreduce", &nvls_splitk_allreduce);
   m.def("get_pdl", &get_pdl);
 }

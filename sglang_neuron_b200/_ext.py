@@ -34,7 +34,7 @@ def add_launches(n: int) -> None:
     _launches[0] += n
 
 
-_HOST_ONLY = {"set_pdl", "get_pdl", "symm_alloc", "symm_open", "symm_close"}
+_HOST_ONLY = {"set_pdl", "get_pdl", "symm_alloc", "symm_open", "symm_close", "nvls_flag_bytes"}
 
 
 class _CountingKernels:

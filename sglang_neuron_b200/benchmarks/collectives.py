@@ -71,6 +71,18 @@ def main():
            "gemm_allreduce_fused_us": t_op(lambda: ar.gemm_all_reduce(xa, wt, None, sms)),
            "gemm_splitk_allreduce_fused_us": t_op(lambda: fused_gemm_all_reduce(xa, wt, None)),
            "status": int(ar.status[0])}
+    try:
+        from ..parallel.symm_mem import NvlsAllReduce
+        nv = NvlsAllReduce()
+        set_custom_allreduce(nv)
+        res.update({"nvls_allreduce_us": t_op(lambda: nv.all_reduce(x, out)),
+                    "nvls_combine_allreduce_us": t_op(lambda: nv.combine_all_reduce(out, y, al.inv_map[: T * 4], w)),
+                    "nvls_gemm_splitk_allreduce_us": t_op(lambda: fused_gemm_all_reduce(xa, wt, None)),
+                    "nvls_status": int(nv.status[0])})
+        set_custom_allreduce(None)
+        nv.close()
+    except RuntimeError as e:
+        res["nvls"] = f"unavailable: {e}"
     if rank == 0:
         print(json.dumps(res), flush=True)
     ar.close()

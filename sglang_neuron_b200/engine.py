@@ -48,8 +48,8 @@ class Engine:
             from . import env_registry
             if not env_registry.get_bool("SGLANG_B200_DISABLE_FUSED_COLLECTIVES", False):
                 from .parallel.collectives import set_custom_allreduce
-                from .parallel.symm_mem import IpcAllReduce
-                self.custom_ar = IpcAllReduce()
+                from .parallel.symm_mem import make_tp_allreduce
+                self.custom_ar = make_tp_allreduce()
                 set_custom_allreduce(self.custom_ar)
         self.runner = ModelRunner(args, self.cfg, device)
         self.scheduler = Scheduler(args, self.cfg, self.runner)

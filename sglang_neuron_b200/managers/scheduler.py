@@ -320,6 +320,9 @@ class Scheduler:
     def _process(self, step: StepInput, ids_host, event) -> None:
         if event is not None:
             event.synchronize()
+        watch = getattr(self.runner, "status_watch", None)
+        if watch is not None:
+            watch.check()
         ids = ids_host.numpy() if hasattr(ids_host, "numpy") else np.asarray(ids_host)
         now = time.perf_counter()
         for i, (r, s) in enumerate(zip(step.reqs, step.sampled)):

@@ -123,6 +123,26 @@ class StepIO:
         return hv, ev
 
 
+class KernelStatusWatch:
+    """The kernels' bounded-wait status words, copied to pinned memory after every step (stream-ordered,
+    a few bytes) and checked once the step's event has completed: a kernel that gave up on a wait makes the
+    engine raise at the next step boundary instead of letting every later wait run into its time limit."""
+
+    def __init__(self, sources: List[torch.Tensor]):
+        self.sources = sources
+        self.host = torch.zeros(4 * len(sources), dtype=torch.int32, pin_memory=True)
+
+    def snapshot(self, io: "StepIO") -> None:
+        for i, s in enumerate(self.sources):
+            self.host[4 * i:4 * i + 4].copy_(s[:4], non_blocking=True)
+        io.d2h_bytes += 16 * len(self.sources)
+
+    def check(self) -> None:
+        if bool(self.host.any()):
+            codes = self.host.view(-1, 4)[:, 0].tolist()
+            raise RuntimeError(f"an sm_100a kernel reported a bounded-wait timeout (status codes {codes})")
+
+
 class ModelRunner:
     def __init__(self, args: ServerArgs, cfg: ModelConfig, device=None):
         self.args = args
@@ -164,6 +184,14 @@ class ModelRunner:
                          self.max_reqs + 1)
         self.graph_runner = None
         self.logits_hook = None  # test seam: called with (ForwardBatch, local logits) of eager steps
+        self.status_watch = None
+        if self.cuda:
+            from ..ops import gemm as gemm_ops, moe as moe_ops
+            from ..parallel import collectives
+            srcs = [gemm_ops._status_buf(self.device), moe_ops._status(self.device)]
+            if collectives._custom_allreduce is not None:
+                srcs.append(collectives._custom_allreduce.status)
+            self.status_watch = KernelStatusWatch(srcs)
         if (self.cuda and not args.disable_cuda_graph and self.model.graph_capturable
                 and self.draft is None):
             from .graph_runner import CudaGraphRunner
@@ -247,6 +275,8 @@ class ModelRunner:
             ids = self.graph_runner.replay(step)
         else:
             ids = self.forward_eager(step)
+        if self.status_watch is not None:
+            self.status_watch.snapshot(self.io)
         return self.io.readback(ids)
 
     def forward_eager(self, step) -> torch.Tensor:

@@ -95,6 +95,64 @@ def _ar_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
+def _nvls_worker(rank, world, port, q):
+    """NVLS (multicast) all-reduce vs NCCL: plain, fused MoE combine, fused split-K partial sum."""
+    _init(rank, world, port)
+    import torch.distributed as dist
+    from sglang_neuron_b200.parallel.state import initialize_parallel
+    from sglang_neuron_b200.parallel.symm_mem import NvlsAllReduce
+    initialize_parallel(world, device=torch.device("cuda", rank))
+    try:
+        ar = NvlsAllReduce(capacity_bytes=4 << 20)
+    except Exception as e:  # no multicast on this machine
+        q.put((rank, None, repr(e)))
+        dist.barrier()
+        dist.destroy_process_group()
+        return
+    errs = []
+    for i, n in enumerate([8, 2880 * 64, 4096 * 3, 1 << 20, 2880 * 7]):
+        g = torch.Generator(device="cuda").manual_seed(100 * i + rank)
+        x = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16)
+        ref = x.float().clone()
+        dist.all_reduce(ref)
+        for _ in range(3):  # repeated calls advance the epoch
+            out = ar.all_reduce(x)
+        torch.cuda.synchronize()
+        errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    from sglang_neuron_b200.ops.moe import MoEAlignment, moe_align, moe_combine, topk_route
+    T, H, E = 64, 2880, 16
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    w, ids = topk_route(torch.randn(T, E, device="cuda", generator=g), 4)
+    al = MoEAlignment(T * 4, E // world, 16, "cuda")
+    moe_align(ids, rank * (E // world), E // world, al)
+    y = torch.randn(al.r_max, H, device="cuda", generator=g).to(torch.bfloat16)
+    ref = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    moe_combine(ref, y, al.inv_map, w)
+    ref = ref.float()
+    dist.all_reduce(ref)
+    out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    ar.combine_all_reduce(out, y, al.inv_map[: T * 4], w)
+    torch.cuda.synchronize()
+    errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    from sglang_neuron_b200.ops.gemm import linear_partials
+    T, F, Kl = 64, 2880, 512
+    x = torch.randn(T, Kl, device="cuda", generator=g).to(torch.bfloat16)
+    wt = (torch.randn(F, Kl, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    b = torch.randn(F, device="cuda", generator=g).to(torch.bfloat16)
+    ref = x.float() @ wt.float().t() + b.float()
+    dist.all_reduce(ref)
+    part = linear_partials(x, wt, 4)
+    out = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    ar.splitk_all_reduce(part, 4, T, F, b, out)
+    torch.cuda.synchronize()
+    errs.append(((out.float() - ref).abs().max() / ref.abs().max()).item())
+    status = int(ar.status[0])
+    ar.close()
+    q.put((rank, errs, status))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _engine_worker(rank, world, port, q):
     _init(rank, world, port)
     import torch.distributed as dist
@@ -138,6 +196,16 @@ def test_one_shot_allreduce_matches_nccl():
     for rank, (errs, status) in res.items():
         assert status == 0, f"rank {rank}: bounded wait expired"
         assert max(errs) < 1e-2, f"rank {rank}: {errs}"
+
+
+@needs2
+def test_nvls_allreduce_matches_nccl():
+    res = _spawn(_nvls_worker, 2)
+    for rank, (errs, status) in res.items():
+        if errs is None:
+            pytest.skip(f"no NVLink multicast: {status}")
+        assert status == 0, f"rank {rank}: bounded wait expired"
+        assert max(errs) < 2e-2, f"rank {rank}: {errs}"
 
 
 @needs2
