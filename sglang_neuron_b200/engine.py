@@ -41,7 +41,7 @@ class Engine:
             device = torch.device("cuda", local)
         else:
             device = torch.device("cpu")
-        st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device)
+        st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device, pp_size=args.pp_size)
         self.rank = st.rank
         self.custom_ar = None
         if st.tp_size > 1 and device.type == "cuda":
@@ -72,11 +72,11 @@ class Engine:
         return [int(t) for t in prompt]
 
     def submit(self, prompt, sampling_params: Optional[Union[dict, SamplingParams]] = None, rid: Optional[str] = None):
-        """Queue one request. On a follower rank (tp_rank > 0) nothing is queued locally: requests arrive
+        """Queue one request. On a follower rank (replica rank > 0) nothing is queued locally: requests arrive
         through rank 0's broadcast, and the returned rid is the one rank 0 assigns to the same call."""
         sp = sampling_params if isinstance(sampling_params, SamplingParams) else SamplingParams.from_dict(sampling_params)
         rid = rid or f"req-{next(self._ids)}"
-        if get_state().tp_rank != 0:
+        if get_state().replica_rank != 0:
             return rid
         return self.scheduler.add_request(rid, self._to_ids(prompt), sp)
 
@@ -92,7 +92,7 @@ class Engine:
         if self.args.speculative_algorithm == "MTP":
             return self._generate_spec(prompts, sps)
         handles = [self.submit(p, sp) for p, sp in zip(prompts, sps)]
-        if get_state().tp_rank != 0:
+        if get_state().replica_rank != 0:
             # follower: step in lockstep until rank 0's matching requests have finished here too
             want = set(handles)
             while not want.issubset(self.scheduler.finished_by_rid):

@@ -65,10 +65,11 @@ class Scheduler:
 
     def _sync_arrivals(self) -> None:
         st = get_state()
-        if st.tp_size > 1:
-            payload = [(r.rid, r.origin_input_ids, r.params) for r in self.pending_arrivals] if st.tp_rank == 0 else None
+        if st.replica_size > 1:
+            payload = ([(r.rid, r.origin_input_ids, r.params) for r in self.pending_arrivals]
+                       if st.replica_rank == 0 else None)
             payload = cpu_broadcast_object(payload, src=0)
-            if st.tp_rank != 0:
+            if st.replica_rank != 0:
                 self.pending_arrivals = [Req(rid, ids, p, eos_ids=[] if p.ignore_eos else self.eos)
                                          for rid, ids, p in payload]
         for r in self.pending_arrivals:

@@ -53,7 +53,7 @@ class MLATokenToKVPool:
     """Per-layer paged latent rows: [num_pages, 1, page_size, kv_lora_rank + rope_dim]."""
 
     def __init__(self, num_layers: int, num_pages: int, page_size: int, kv_lora_rank: int, rope_dim: int,
-                 dtype: torch.dtype, device):
+                 dtype: torch.dtype, device, layer_ids: Optional[List[int]] = None):
         self.num_pages = num_pages
         self.page_size = page_size
         self.kv_lora_rank = kv_lora_rank
@@ -62,10 +62,12 @@ class MLATokenToKVPool:
         self.k_scale = 1.0
         self.v_scale = 1.0
         shape = (num_pages, 1, page_size, kv_lora_rank + rope_dim)
-        self.buffers = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
+        self.layer_ids = list(range(num_layers)) if layer_ids is None else list(layer_ids)
+        self.buffers = [torch.zeros(shape, dtype=dtype, device=device) for _ in self.layer_ids]
+        self._index = {lid: i for i, lid in enumerate(self.layer_ids)}
 
     def kv(self, layer_id: int):
-        b = self.buffers[layer_id]
+        b = self.buffers[self._index[layer_id]]
         return b, b
 
     @staticmethod

@@ -175,8 +175,9 @@ class ModelRunner:
             self.draft.block.self_attn.kv_pool = self.kv_pool
             self.draft.block.self_attn.backend = self.backend
         self.relay = torch.zeros(self.max_reqs + 1, dtype=torch.int64, device=self.device)
-        self.vocab_start = self.model.lm_head.start
-        self.vocab_valid = self.model.lm_head.end - self.model.lm_head.start
+        head = self.model.lm_head  # None on pipeline stages before the last
+        self.vocab_start = head.start if head is not None else 0
+        self.vocab_valid = head.end - head.start if head is not None else 0
         max_tokens = max(args.chunked_prefill_size, args.max_prefill_tokens) + self.max_reqs
         self.max_step_tokens = max_tokens
         self.io = StepIO(self.device, self._extend_layout(max_tokens, self.max_reqs + 1,
@@ -193,7 +194,7 @@ class ModelRunner:
                 srcs.append(collectives._custom_allreduce.status)
             self.status_watch = KernelStatusWatch(srcs)
         if (self.cuda and not args.disable_cuda_graph and self.model.graph_capturable
-                and self.draft is None):
+                and self.draft is None and st.pp_size == 1):
             from .graph_runner import CudaGraphRunner
             self.graph_runner = CudaGraphRunner(self)
 
@@ -224,7 +225,9 @@ class ModelRunner:
         cfg, args = self.cfg, self.args
         attn = self.model.attention_layers()
         P = self.page_size
-        n_layers = cfg.num_layers + (1 if self.draft is not None else 0)  # the MTP block keeps one extra layer
+        # this pipeline stage's layers (+ the MTP block's one extra layer)
+        layer_ids = [a.layer_id for a in attn] + ([cfg.num_layers] if self.draft is not None else [])
+        n_layers = len(layer_ids)
         if cfg.is_mla:
             per_page = MLATokenToKVPool.bytes_per_page(n_layers, P, cfg.kv_lora_rank, cfg.qk_rope_head_dim,
                                                        self.kv_dtype)
@@ -245,10 +248,10 @@ class ModelRunner:
         self.num_pages = int(num_pages)
         if cfg.is_mla:
             self.kv_pool = MLATokenToKVPool(n_layers, self.num_pages, P, cfg.kv_lora_rank,
-                                            cfg.qk_rope_head_dim, self.kv_dtype, self.device)
+                                            cfg.qk_rope_head_dim, self.kv_dtype, self.device, layer_ids=layer_ids)
         else:
             self.kv_pool = MHATokenToKVPool(n_layers, self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
-                                            self.kv_dtype, self.device)
+                                            self.kv_dtype, self.device, layer_ids=layer_ids)
         logger.info("KV pool: %d pages x %d tokens (%.2f GB, %s)", self.num_pages, P,
                     self.num_pages * per_page / 1e9, self.kv_dtype)
 
@@ -308,7 +311,22 @@ class ModelRunner:
         fb.decode_splits = self.backend.splits_for(B if step.mode == ForwardMode.DECODE else max(D, 1), kvh,
                                                    self.args.context_length)
         h = self.forward_model(fb)
+        if get_state().pp_size > 1:
+            return self._pp_sample(h, fb, req_idx)
         return self.sample(h, fb, req_idx)
+
+    def _pp_sample(self, h, fb: ForwardBatch, req_idx: torch.Tensor) -> torch.Tensor:
+        """Pipeline parallelism: the last stage samples; its ids reach every rank of the replica (scheduler
+        and token relay), so the first stage can feed them back as the next decode input."""
+        from ..parallel.collectives import pp_broadcast_ids
+        B = int(fb.logits_idx.numel())
+        if h is not None:
+            ids = self.sample(h, fb, req_idx)
+        else:
+            ids = torch.empty(B, dtype=torch.int64, device=self.device)
+        ids = pp_broadcast_ids(ids.contiguous())
+        self.relay.index_copy_(0, req_idx.view(-1), ids.view(-1))
+        return ids
 
     def forward_model(self, fb: ForwardBatch) -> torch.Tensor:
         if fb.mode == ForwardMode.EXTEND and fb.extra.get("num_decode", 0) > 0:

@@ -28,8 +28,8 @@ from ..ops import activation as act_ops
 from ..ops import moe as moe_ops
 from ..ops.norm import fused_add_rmsnorm, rmsnorm
 from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
-from ..parallel.collectives import fused_combine_all_reduce, tp_all_reduce
-from ..parallel.state import get_state
+from ..parallel.collectives import fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden, tp_all_reduce
+from ..parallel.state import get_state, pp_layer_range
 
 
 class RMSNorm(nn.Module):
@@ -229,10 +229,16 @@ class CausalLM(nn.Module):
         self.dtype = dtype
         self.device = torch.device(device)
         self.max_pos = max_pos or min(cfg.max_position_embeddings, 131072)
-        self.embed_tokens = VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, dtype, device)
-        self.layers = nn.ModuleList([self.make_layer(i) for i in range(cfg.num_layers)])
-        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, dtype, device)
-        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype, device)
+        st = get_state()
+        # pipeline stage: a contiguous block of layers; the embedding on the first stage, the final norm and
+        # the LM head on the last
+        self.layer_start, self.layer_end = pp_layer_range(cfg.num_layers, st.pp_size, st.pp_rank)
+        self.first_stage, self.last_stage = st.is_first_stage, st.is_last_stage
+        self.embed_tokens = (VocabParallelEmbedding(cfg.vocab_size, cfg.hidden_size, dtype, device)
+                             if self.first_stage else None)
+        self.layers = nn.ModuleList([self.make_layer(i) for i in range(self.layer_start, self.layer_end)])
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps, dtype, device) if self.last_stage else None
+        self.lm_head = ParallelLMHead(cfg.vocab_size, cfg.hidden_size, dtype, device) if self.last_stage else None
 
     def make_layer(self, i: int) -> DecoderLayer:  # overridden by families
         raise NotImplementedError
@@ -246,11 +252,21 @@ class CausalLM(nn.Module):
             a.kv_pool = pool
             a.backend = backend
 
-    def forward(self, fb: ForwardBatch) -> torch.Tensor:
-        h = self.embed_tokens(fb.input_ids)
-        residual = None
+    def forward(self, fb: ForwardBatch) -> Optional[torch.Tensor]:
+        """Sampled rows after the final norm (last pipeline stage), or None on earlier stages (their output
+        went to the next stage)."""
+        if self.first_stage:
+            h = self.embed_tokens(fb.input_ids)
+            residual = None
+        else:
+            h, residual = pp_recv_hidden(fb.num_tokens, self.cfg.hidden_size, self.dtype, self.device)
         for layer in self.layers:
             h, residual = layer(h, residual, fb)
+        if not self.last_stage:
+            if residual is None:
+                residual = torch.zeros_like(h)
+            pp_send_hidden(h, residual)
+            return None
         # only the rows that are sampled go through the final norm and the LM head
         h_last = h.index_select(0, fb.logits_idx)
         r_last = residual.index_select(0, fb.logits_idx)
@@ -263,12 +279,14 @@ class CausalLM(nn.Module):
 
     # -- weights ------------------------------------------------------------------------------
     def load_common(self, get) -> None:
-        self.embed_tokens.load(get("model.embed_tokens.weight"))
-        self.norm.weight.data.copy_(get("model.norm.weight"))
-        if self.cfg.tie_word_embeddings:
-            self.lm_head.load(get("model.embed_tokens.weight"))
-        else:
-            self.lm_head.load(get("lm_head.weight"))
+        if self.embed_tokens is not None:
+            self.embed_tokens.load(get("model.embed_tokens.weight"))
+        if self.last_stage:
+            self.norm.weight.data.copy_(get("model.norm.weight"))
+            if self.cfg.tie_word_embeddings:
+                self.lm_head.load(get("model.embed_tokens.weight"))
+            else:
+                self.lm_head.load(get("lm_head.weight"))
         for l in self.layers:
             p = f"model.layers.{l.layer_id}."
             l.input_layernorm.weight.data.copy_(get(p + "input_layernorm.weight"))

@@ -102,16 +102,44 @@ def tp_reduce_scatter(x: torch.Tensor) -> torch.Tensor:
 
 
 def cpu_broadcast_object(obj, src: int = 0):
-    """Broadcast a picklable object over the host (gloo) group of the TP world."""
+    """Broadcast a picklable object from replica rank `src` over the host (gloo) group of the DP replica
+    (every TP rank of every pipeline stage)."""
     st = get_state()
-    if st.tp_size == 1:
+    if st.replica_size == 1:
         return obj
     buf = [obj]
-    dist.broadcast_object_list(buf, src=src + st.dp_rank * st.tp_size, group=st.cpu_group)
+    dist.broadcast_object_list(buf, src=src + st.replica_base, group=st.replica_cpu_group)
     return buf[0]
 
 
 def cpu_barrier() -> None:
     st = get_state()
-    if st.tp_size > 1:
-        dist.barrier(group=st.cpu_group)
+    if st.replica_size > 1:
+        dist.barrier(group=st.replica_cpu_group)
+
+
+# ---- pipeline parallelism -------------------------------------------------------------------------------
+# Stage boundaries move (hidden, residual) of every token from stage s to stage s+1 (same TP rank) with one
+# point-to-point send (NCCL on GPUs, gloo on the CPU tier); the last stage's sampled ids are broadcast to the
+# whole replica so every rank's scheduler and token relay see them. Parity: the reference's PP seam moves the
+# boundary HBM->HBM and relays tokens back to the first stage (sglang_neuron/distributed/pp_seam.py:306).
+
+def pp_send_hidden(h: torch.Tensor, residual: torch.Tensor) -> None:
+    st = get_state()
+    dist.send(torch.stack([h, residual]).contiguous(), dst=st.stage_rank(st.pp_rank + 1))
+
+
+def pp_recv_hidden(num_tokens: int, hidden: int, dtype, device):
+    st = get_state()
+    buf = torch.empty(2, num_tokens, hidden, dtype=dtype, device=device)
+    dist.recv(buf, src=st.stage_rank(st.pp_rank - 1))
+    return buf[0], buf[1]
+
+
+def pp_broadcast_ids(ids: torch.Tensor) -> torch.Tensor:
+    """ids: [B] int64, valid on the last stage; returned on every rank of the replica."""
+    st = get_state()
+    if st.pp_size == 1:
+        return ids
+    dist.broadcast(ids, src=st.replica_base + (st.pp_size - 1) * st.tp_size, group=st.replica_group)
+    return ids

@@ -1,5 +1,5 @@
-"""Parallel state: tensor-parallel (attention and dense MLP), expert-parallel (MoE) and data-parallel
-groups over one process per GPU.
+"""Parallel state: tensor-parallel (attention and dense MLP), expert-parallel (MoE), pipeline-parallel
+(contiguous layer stages) and data-parallel groups over one process per GPU.
 
 Parity: the reference builds its groups in `initialize_neuron_parallel_state`
 (sglang_neuron/parallel/state.py:77-152) with attention-TP, EP-TP and EP groups and group getters
@@ -7,6 +7,11 @@ Parity: the reference builds its groups in `initialize_neuron_parallel_state`
 torch.distributed (one process per GPU); host-side control collectives use a gloo group, as in the
 reference (gloo on the host). EP here spans the same ranks as TP: experts are split in contiguous blocks
 by rank (`ep_group_ranks` rows = EP) and tokens are replicated over the group after attention.
+
+Rank layout: rank = (dp_rank * pp_size + pp_rank) * tp_size + tp_rank. A DP replica (pp_size x tp_size
+ranks) runs one scheduler in lockstep; its replica rank 0 owns request intake. Pipeline stages hold
+contiguous layer blocks (distributed/pipeline.py `StageSpec` in the reference: sglang_neuron/distributed/
+pipeline.py:29); stage s+1's tensor-parallel rank r receives stage s's rank r hidden state.
 """
 from __future__ import annotations
 
@@ -32,10 +37,48 @@ class ParallelState:
     tp_group: Optional[object] = None      # device (NCCL or gloo on CPU) group
     cpu_group: Optional[object] = None     # gloo group for host control
     device: torch.device = torch.device("cpu")
+    pp_size: int = 1
+    pp_rank: int = 0
+    replica_group: Optional[object] = None      # device group of the DP replica (pp_size x tp_size ranks)
+    replica_cpu_group: Optional[object] = None  # gloo group of the DP replica
 
     @property
     def is_first_rank(self) -> bool:
-        return self.tp_rank == 0
+        return self.replica_rank == 0
+
+    @property
+    def replica_size(self) -> int:
+        return self.pp_size * self.tp_size
+
+    @property
+    def replica_rank(self) -> int:
+        return self.pp_rank * self.tp_size + self.tp_rank
+
+    @property
+    def replica_base(self) -> int:
+        """Global rank of this replica's rank 0."""
+        return self.dp_rank * self.replica_size
+
+    @property
+    def is_first_stage(self) -> bool:
+        return self.pp_rank == 0
+
+    @property
+    def is_last_stage(self) -> bool:
+        return self.pp_rank == self.pp_size - 1
+
+    def stage_rank(self, pp_rank: int) -> int:
+        """Global rank of the same tensor-parallel rank in pipeline stage `pp_rank` of this replica."""
+        return self.replica_base + pp_rank * self.tp_size + self.tp_rank
+
+
+def pp_layer_range(num_layers: int, pp_size: int, pp_rank: int):
+    """Contiguous layer block [start, end) of a pipeline stage; earlier stages take the remainder."""
+    if pp_size > num_layers:
+        raise ValueError(f"pp_size {pp_size} exceeds the {num_layers} layers")
+    base, extra = divmod(num_layers, pp_size)
+    start = pp_rank * base + min(pp_rank, extra)
+    return start, start + base + (1 if pp_rank < extra else 0)
 
 
 _STATE = ParallelState()
@@ -69,8 +112,9 @@ def init_process_group_from_env(backend: Optional[str] = None, timeout_s: int = 
 
 
 def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size: int = 1,
-                        device: Optional[torch.device] = None) -> ParallelState:
-    """Build the groups. Ranks are laid out DP-major: rank = dp_rank * tp_size + tp_rank."""
+                        device: Optional[torch.device] = None, pp_size: int = 1) -> ParallelState:
+    """Build the groups. Ranks are laid out DP-major, then PP: rank = (dp_rank * pp_size + pp_rank) * tp_size
+    + tp_rank."""
     ep_size = tp_size if ep_size is None else ep_size
     if ep_size != tp_size:
         raise ValueError("expert parallelism spans the tensor-parallel group here (ep_size must equal tp_size)")
@@ -78,22 +122,34 @@ def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size
         world, rank = dist.get_world_size(), dist.get_rank()
     else:
         world, rank = 1, 0
-    if tp_size * dp_size != world:
-        raise ValueError(f"tp_size {tp_size} x dp_size {dp_size} != world size {world}")
-    dp_rank, tp_rank = divmod(rank, tp_size)
-    tp_group = cpu_group = None
+    if tp_size * pp_size * dp_size != world:
+        raise ValueError(f"tp_size {tp_size} x pp_size {pp_size} x dp_size {dp_size} != world size {world}")
+    dp_rank, rest = divmod(rank, pp_size * tp_size)
+    pp_rank, tp_rank = divmod(rest, tp_size)
+    tp_group = cpu_group = replica_group = replica_cpu_group = None
     if world > 1:
         for d in range(dp_size):
-            ranks = list(range(d * tp_size, (d + 1) * tp_size))
-            g = dist.new_group(ranks)
-            cg = dist.new_group(ranks, backend="gloo")
-            if d == dp_rank:
-                tp_group, cpu_group = g, cg
+            for p_ in range(pp_size):
+                base = (d * pp_size + p_) * tp_size
+                ranks = list(range(base, base + tp_size))
+                g = dist.new_group(ranks)
+                cg = dist.new_group(ranks, backend="gloo")
+                if d == dp_rank and p_ == pp_rank:
+                    tp_group, cpu_group = g, cg
+            if pp_size > 1:
+                ranks = list(range(d * pp_size * tp_size, (d + 1) * pp_size * tp_size))
+                g = dist.new_group(ranks)
+                cg = dist.new_group(ranks, backend="gloo")
+                if d == dp_rank:
+                    replica_group, replica_cpu_group = g, cg
+    if pp_size == 1:
+        replica_group, replica_cpu_group = tp_group, cpu_group
     if device is None:
         device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
     st = ParallelState(world_size=world, rank=rank, tp_size=tp_size, tp_rank=tp_rank, ep_size=ep_size,
                        ep_rank=tp_rank, dp_size=dp_size, dp_rank=dp_rank, tp_group=tp_group,
-                       cpu_group=cpu_group, device=device)
+                       cpu_group=cpu_group, device=device, pp_size=pp_size, pp_rank=pp_rank,
+                       replica_group=replica_group, replica_cpu_group=replica_cpu_group)
     set_state(st)
     return st
 

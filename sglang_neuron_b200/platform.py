@@ -27,8 +27,10 @@ def refuse_unserved(args, spec) -> None:
         raise ValueError(f"{spec.architecture} does not serve speculative algorithm {args.speculative_algorithm!r}")
     if args.tp_size > spec.max_tp:
         raise ValueError(f"tp_size {args.tp_size} exceeds {spec.max_tp} for {spec.architecture}")
-    if args.dp_size < 1 or args.tp_size < 1:
-        raise ValueError("tp_size and dp_size must be >= 1")
+    if args.dp_size < 1 or args.tp_size < 1 or args.pp_size < 1:
+        raise ValueError("tp_size, pp_size and dp_size must be >= 1")
+    if args.pp_size > 1 and args.speculative_algorithm:
+        raise ValueError("speculative decoding is not served with pipeline parallelism")
 
 
 def check_kv_cache(args, spec) -> None:

@@ -22,6 +22,7 @@ class ServerArgs:
     tp_size: int = 1
     ep_size: Optional[int] = None
     dp_size: int = 1
+    pp_size: int = 1
     page_size: int = 16
     kv_cache_dtype: str = "auto"             # auto | bf16 | fp8_e4m3
     context_length: int = 8192

@@ -1,0 +1,81 @@
+"""Pipeline parallelism on CPU ranks (gloo): layers split into contiguous stages, (hidden, residual) sent
+stage to stage, the last stage's sampled ids broadcast to every rank. Greedy tokens of PP=2 and PP=2 x TP=2
+equal the single-rank run, on every rank."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+TINY_QWEN = dict(num_hidden_layers=3, vocab_size=1000, hidden_size=256, intermediate_size=512,
+                 num_attention_heads=4, num_key_value_heads=2, head_dim=64)
+TINY_MOE = dict(num_hidden_layers=3, vocab_size=1000, hidden_size=256, moe_intermediate_size=64, num_experts=8,
+                num_experts_per_tok=2, num_attention_heads=4, num_key_value_heads=2, head_dim=64)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(rank, world, port, base, over, tp, pp, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.parallel.state import destroy_parallel
+    from sglang_neuron_b200.server_args import ServerArgs
+    destroy_parallel()
+    mc.PRESETS["pp-tiny"] = dict(mc.PRESETS[base], **over)
+    eng = Engine(ServerArgs(model="pp-tiny", device="cpu", dtype="float32", tp_size=tp, pp_size=pp,
+                            context_length=256, max_running_requests=4, chunked_prefill_size=32,
+                            random_weight_std=0.05))
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
+    outs = eng.generate(prompts, {"max_new_tokens": 6})
+    q.put((rank, [o["output_ids"] for o in outs]))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _launch(base, over, tp, pp):
+    world = tp * pp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, tp, pp, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+@pytest.mark.parametrize("base,over", [("qwen3-0.6b", TINY_QWEN), ("qwen3-30b-a3b", TINY_MOE)])
+def test_pp2_equals_pp1(base, over):
+    one = _launch(base, over, 1, 1)[0]
+    two = _launch(base, over, 1, 2)
+    assert two[0] == one and two[1] == one
+
+
+@pytest.mark.slow
+def test_pp2_tp2_equals_pp1():
+    one = _launch("qwen3-0.6b", TINY_QWEN, 1, 1)[0]
+    four = _launch("qwen3-0.6b", TINY_QWEN, 2, 2)
+    for r in range(4):
+        assert four[r] == one, f"rank {r}"
+
+
+def test_stage_layer_ranges():
+    from sglang_neuron_b200.parallel.state import pp_layer_range
+    assert [pp_layer_range(36, 4, r) for r in range(4)] == [(0, 9), (9, 18), (18, 27), (27, 36)]
+    assert [pp_layer_range(7, 3, r) for r in range(3)] == [(0, 3), (3, 5), (5, 7)]
+    with pytest.raises(ValueError):
+        pp_layer_range(2, 3, 0)
