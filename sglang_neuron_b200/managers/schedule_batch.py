@@ -49,6 +49,7 @@ class Req:
         self.owned_from = 0                       # pages[owned_from:] belong to the request (not the radix tree)
         self.prefix_node = None                   # radix node pinned while running
         self.prefix_len = 0                       # tokens reused from the prefix cache
+        self.table_pending: List[int] = []        # (slot, index, page) triples of reused pages not yet in the table
         self.kv_len = 0                           # tokens whose KV is written (or being written by launched steps)
         self.scheduled_outputs = 0                # outputs that launched steps will have produced
         self.finished = False

