@@ -46,6 +46,8 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
                torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace,
                bool reduce_partials, int64_t tiled_f);
 void set_pdl(bool on);
+void kv_page_copy(torch::Tensor src_bases, torch::Tensor dst_bases, torch::Tensor src_pages, torch::Tensor dst_pages,
+                  int64_t page_bytes);
 int64_t nvls_flag_bytes();
 void nvls_allreduce(torch::Tensor out, torch::Tensor x, int64_t uc, int64_t mc, int64_t capacity, int64_t rank,
                     int64_t world, int64_t max_ctas, torch::Tensor status);
@@ -100,6 +102,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
   m.def("splitk_allreduce", &splitk_allreduce);
   m.def("set_pdl", &set_pdl);
+  m.def("kv_page_copy", &kv_page_copy);
   m.def("nvls_flag_bytes", &nvls_flag_bytes);
   m.def("nvls_allreduce", &nvls_allreduce);
   m.def("nvls_combine_allreduce", &nvls_combine_allreduce);

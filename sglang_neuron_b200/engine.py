@@ -144,6 +144,8 @@ class Engine:
     def flush_cache(self) -> None:
         self.scheduler.drain()
         if self.scheduler.radix is not None and not self.scheduler.running:
+            if self.scheduler.hicache is not None:
+                self.scheduler.hicache.reset()
             freed = self.scheduler.radix.reset()
             if freed:
                 self.scheduler.alloc.free(list(freed))

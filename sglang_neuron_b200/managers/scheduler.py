@@ -38,6 +38,11 @@ class Scheduler:
         self.P = args.page_size
         self.alloc = make_page_allocator(runner.num_pages, self.P, reserved=1)
         self.radix = None if args.disable_radix_cache else RadixCacheHandle(self.P)
+        self.hicache = None
+        if args.enable_hierarchical_cache and self.radix is not None:
+            from ..mem_cache.hicache import HiCache
+            n_host = args.hicache_host_pages or int(runner.num_pages * args.hicache_ratio)
+            self.hicache = HiCache(runner.kv_pool, self.P, max(1, n_host), runner.device)
         self.waiting: Deque[Req] = collections.deque()
         self.running: List[Req] = []
         self.inflight: Deque[Tuple[StepInput, object, object]] = collections.deque()
@@ -91,6 +96,8 @@ class Scheduler:
         if self.radix is not None:
             freed = self.radix.evict(n - self.alloc.available())
             if freed:
+                if self.hicache is not None:
+                    self.hicache.sync_writes()  # host copies of these pages must land before reuse
                 self.alloc.free(list(freed))
             pages = self.alloc.alloc(n)
             if len(pages) == n:
@@ -119,6 +126,10 @@ class Scheduler:
             if n_pages > 0:
                 dup = self.radix.insert(ids[:n_tok], r.pages[:n_pages])
                 to_free = list(dup) + r.pages[max(n_pages, r.owned_from):]
+                if self.hicache is not None:
+                    # write-through from the tree's own pages (duplicates are freed right below)
+                    _, canon, _ = self.radix.match_prefix(ids[:n_tok])
+                    self.hicache.write_through(ids[:n_tok], list(canon)[:n_pages])
             else:
                 to_free = owned
             if r.prefix_node is not None:
@@ -149,16 +160,27 @@ class Scheduler:
                 break
             self.waiting.popleft()
             r.slot = self.free_slots.pop()
+            if self.radix is not None and node is not None:
+                self.radix.inc_lock(node)
+                r.prefix_node = node
+            tree_pages = len(prefix_pages)  # pages of the device tree: shared, not owned by the request
+            if self.hicache is not None:
+                # pages past the device match that the host tier still holds: load instead of recompute
+                room = (len(ids) - 1) // self.P - tree_pages
+                slots = self.hicache.match(ids, tree_pages, room) if room > 0 else []
+                new = self._alloc_pages(len(slots)) if slots else None
+                if new:
+                    self.hicache.load(slots, new)
+                    prefix_pages = prefix_pages + new
+                    prefix_len = len(prefix_pages) * self.P
+                    self.stats["host_hit_tokens"] = self.stats.get("host_hit_tokens", 0) + len(new) * self.P
             r.pages = prefix_pages
-            r.owned_from = len(prefix_pages)
+            r.owned_from = tree_pages
             # reused pages enter this slot's block-table row with the request's first step
             r.table_pending = [v for j, pg in enumerate(prefix_pages) for v in (r.slot, j, pg)]
             r.prefix_len = prefix_len
             r.kv_len = prefix_len
             r.prefill_target = len(ids)
-            if self.radix is not None and node is not None:
-                self.radix.inc_lock(node)
-                r.prefix_node = node
             self.stats["cache_hit_tokens"] += prefix_len
             self.stats["prompt_tokens"] += len(ids)
             self.running.append(r)
@@ -369,6 +391,8 @@ class Scheduler:
         step = self.schedule()
         if step is not None:
             t0 = time.perf_counter()
+            if self.hicache is not None:
+                self.hicache.wait_loads()
             ids_host, ev = self.runner.run_step(step)
             self.inflight.append((step, ids_host, ev))
             self.stats["steps"] += 1

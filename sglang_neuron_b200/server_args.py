@@ -33,6 +33,9 @@ class ServerArgs:
     max_prefill_tokens: int = 16384
     enable_mixed_chunk: bool = True          # decode rows ride along with prefill chunks
     disable_radix_cache: bool = False
+    enable_hierarchical_cache: bool = False   # host (pinned memory) tier below the device prefix cache
+    hicache_ratio: float = 2.0                # host pages = ratio x device KV pages (when hicache_host_pages is 0)
+    hicache_host_pages: int = 0
     disable_cuda_graph: bool = False
     cuda_graph_max_bs: int = 256
     cuda_graph_bs: Optional[List[int]] = None

@@ -277,3 +277,27 @@ def _gemm_default_path(T, F, K, bias, tiled):
     _close(y1, ref, 3e-2, 1e-2, "gemm_default")
     assert torch.equal(y1, y2)
     assert torch.equal(out, y1)
+
+
+def test_kv_page_copy_device_host_round_trip():
+    """HiCache page copies: device pages -> pinned host slots -> other device pages, every layer buffer in
+    one launch per direction (the kernel addresses pinned host memory directly)."""
+    from sglang_neuron_b200.mem_cache.hicache import HiCache
+    from sglang_neuron_b200.mem_cache.memory_pool import MHATokenToKVPool
+    torch.manual_seed(12)
+    pool = MHATokenToKVPool(3, 40, 16, 2, 64, torch.float8_e4m3fn, DEV)
+    for b in pool.k_buffers + pool.v_buffers:
+        b.copy_(torch.randn(b.shape, device=DEV).to(b.dtype))
+    hc = HiCache(pool, 16, 10, torch.device(DEV))
+    toks = list(range(16 * 5))
+    src = [3, 9, 17, 4, 30]
+    assert hc.write_through(toks, src) == 5
+    hc.sync_writes()
+    slots = hc.match(toks, 1, 4)
+    assert len(slots) == 4
+    dst = [35, 36, 37, 38]
+    hc.load(slots, dst)
+    hc.wait_loads()
+    torch.cuda.synchronize()
+    for b in pool.k_buffers + pool.v_buffers:
+        assert torch.equal(b[dst].view(torch.uint8), b[src[1:]].view(torch.uint8))

@@ -52,3 +52,29 @@ def test_prefix_hit_in_a_different_slot():
         got = eng.generate([b], {"max_new_tokens": 8})[0]["output_ids"]
         assert eng.scheduler.stats["cache_hit_tokens"] >= 64
         assert got == want, f"order {order is a}"
+
+
+def test_host_tier_reload_after_device_eviction():
+    """A small device pool evicts the shared prefix from the device tree; the host tier (write-through at
+    insert) reloads its pages for the next request and the tokens equal the no-cache run."""
+    shared, (a, b) = _prompts()
+    ref = _engine(disable_radix_cache=True)
+    want = ref.generate([b], {"max_new_tokens": 8})[0]["output_ids"]
+    eng = _engine(enable_hierarchical_cache=True, max_total_tokens=16 * 24, max_running_requests=2)
+    eng.generate([a], {"max_new_tokens": 8})
+    g = torch.Generator().manual_seed(13)
+    for _ in range(3):  # unrelated prompts push the shared prefix out of the device tree
+        eng.generate([torch.randint(1, 1000, (150,), generator=g).tolist()], {"max_new_tokens": 4})
+    got = eng.generate([b], {"max_new_tokens": 8})[0]["output_ids"]
+    st = eng.scheduler.stats
+    assert st.get("host_hit_tokens", 0) >= 64, st
+    assert eng.scheduler.hicache.stats["written_pages"] > 0 and eng.scheduler.hicache.stats["loaded_pages"] >= 4
+    assert got == want
+
+
+def test_chain_hashes_prefix_property():
+    from sglang_neuron_b200.mem_cache.hicache import chain_hashes
+    x = list(range(100))
+    h1 = chain_hashes(x, 16, 6)
+    h2 = chain_hashes(x[:64] + [7] * 36, 16, 6)
+    assert h1[:4] == h2[:4] and h1[4] != h2[4] and h1[5] != h2[5]
