@@ -145,7 +145,7 @@ def bench_attn(a):
     seq = torch.full((B,), L, device="cuda", dtype=torch.int32)
     q = torch.randn(B, Hq * D, device="cuda").to(torch.bfloat16)
     sinks = torch.randn(Hq, device="cuda")
-    S = default_num_splits(B, Hkv, L)
+    S = a.splits or default_num_splits(B, Hkv, L)
     sc = DecodeScratch(B, Hq, D, S, "cuda")
     us = timeit(lambda: decode_attention(q, kc, vc, bt, seq, Hq, Hkv, D, P, 0, None, 1.0, 1.0, sinks, S, sc),
                 a.iters, a.warmup)
@@ -173,6 +173,7 @@ def main():
     p.add_argument("--k", type=int, default=2880)
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=1536)
+    p.add_argument("--splits", type=int, default=0)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     a = p.parse_args()
