@@ -111,6 +111,10 @@ class Engine:
                 d["ttft_s"] = r.first_token_time - r.arrival
             if self.tokenizer is not None:
                 d["text"] = self.tokenizer.decode(r.output_ids)
+            if r.params.return_logprob:
+                d["output_token_logprobs"] = [[lp, t] for lp, t in zip(r.output_logprobs, r.output_ids)]
+                if r.params.top_logprobs_num > 0:
+                    d["output_top_logprobs"] = [[[lp, t] for lp, t in row] for row in r.output_top_logprobs]
             out.append(d)
         return out
 

@@ -59,11 +59,15 @@ class EngineLoop:
         st = self.streams.get(req.rid)
         if st is None:
             return
-        new = req.output_ids[req.stream_offset:]
+        off = req.stream_offset
+        new = req.output_ids[off:]
         req.stream_offset = len(req.output_ids)
         item = {"rid": req.rid, "new_ids": list(new), "finished": req.finished,
                 "finish_reason": req.finish_reason, "prompt_tokens": req.prompt_len,
                 "completion_tokens": len(req.output_ids), "cached_tokens": req.prefix_len}
+        if req.params.return_logprob:
+            item["new_logprobs"] = list(req.output_logprobs[off:])
+            item["new_top_logprobs"] = list(req.output_top_logprobs[off:])
         st.loop.call_soon_threadsafe(st.queue.put_nowait, item)
         if req.finished:
             self.streams.pop(req.rid, None)

@@ -33,7 +33,19 @@ def _sampling_from_openai(body: Dict[str, Any]) -> SamplingParams:
         max_new_tokens=int(body.get("max_tokens") or body.get("max_completion_tokens") or 128),
         temperature=float(body.get("temperature", 1.0) if body.get("temperature") is not None else 1.0),
         top_k=int(body.get("top_k") or 0), top_p=float(body.get("top_p") if body.get("top_p") is not None else 1.0),
-        seed=body.get("seed"), stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)))
+        seed=body.get("seed"), stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)),
+        return_logprob=_openai_logprobs(body)[0], top_logprobs_num=_openai_logprobs(body)[1])
+
+
+def _openai_logprobs(body: Dict[str, Any]):
+    """(return_logprob, top-k) of an OpenAI request: completions take `logprobs: int` (top-k), chat takes
+    `logprobs: bool` plus `top_logprobs: int`."""
+    lp = body.get("logprobs")
+    if isinstance(lp, bool):
+        return lp, int(body.get("top_logprobs") or 0) if lp else 0
+    if isinstance(lp, int):
+        return True, lp
+    return False, 0
 
 
 def build_app(engine, loop_holder: Dict[str, Any]):
@@ -140,28 +152,47 @@ def build_app(engine, loop_holder: Dict[str, Any]):
         except (KeyError, ValueError) as e:
             return JSONResponse({"error": str(e)}, status_code=400)
         sp = SamplingParams.from_dict(body.get("sampling_params"))
+        if body.get("return_logprob"):  # SGLang puts these at the request level
+            sp.return_logprob = True
+            sp.top_logprobs_num = int(body.get("top_logprobs_num") or sp.top_logprobs_num or 0)
+
+        def logprob_meta(lps, tops, toks):
+            m = {"output_token_logprobs": [[lp, t, None] for lp, t in zip(lps, toks)]}
+            if sp.top_logprobs_num > 0:
+                m["output_top_logprobs"] = [[[lp, t, None] for lp, t in row] for row in tops]
+            return m
+
         if body.get("stream"):
             async def sse():
                 acc: List[int] = []
+                lps, tops = [], []
                 async for item in run(ids, sp):
                     acc += item["new_ids"]
-                    out = {"text": decode(acc), "output_ids": list(acc),
-                           "meta_info": {"finish_reason": item["finish_reason"],
-                                         "completion_tokens": item["completion_tokens"]}}
+                    lps += item.get("new_logprobs", [])
+                    tops += item.get("new_top_logprobs", [])
+                    meta = {"finish_reason": item["finish_reason"], "completion_tokens": item["completion_tokens"]}
+                    if sp.return_logprob:
+                        meta.update(logprob_meta(lps, tops, acc))
+                    out = {"text": decode(acc), "output_ids": list(acc), "meta_info": meta}
                     yield f"data: {json.dumps(out)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
         acc: List[int] = []
+        lps, tops = [], []
         last = None
         try:
             async for item in run(ids, sp):
                 acc += item["new_ids"]
+                lps += item.get("new_logprobs", [])
+                tops += item.get("new_top_logprobs", [])
                 last = item
         except ValueError as e:
             return JSONResponse({"error": str(e)}, status_code=400)
-        return {"text": decode(acc), "output_ids": acc,
-                "meta_info": {"prompt_tokens": last["prompt_tokens"], "completion_tokens": last["completion_tokens"],
-                              "cached_tokens": last["cached_tokens"], "finish_reason": last["finish_reason"]}}
+        meta = {"prompt_tokens": last["prompt_tokens"], "completion_tokens": last["completion_tokens"],
+                "cached_tokens": last["cached_tokens"], "finish_reason": last["finish_reason"]}
+        if sp.return_logprob:
+            meta.update(logprob_meta(lps, tops, acc))
+        return {"text": decode(acc), "output_ids": acc, "meta_info": meta}
 
     async def _openai(body, ids, chat: bool):
         sp = _sampling_from_openai(body)
@@ -182,13 +213,27 @@ def build_app(engine, loop_holder: Dict[str, Any]):
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
         acc: List[int] = []
+        lps, tops = [], []
         last = None
         async for item in run(ids, sp):
             acc += item["new_ids"]
+            lps += item.get("new_logprobs", [])
+            tops += item.get("new_top_logprobs", [])
             last = item
         text = decode(acc)
         choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": last["finish_reason"]}
                   if chat else {"index": 0, "text": text, "finish_reason": last["finish_reason"], "token_ids": acc})
+        if sp.return_logprob:
+            tok = (lambda t: decode([t]) if engine.tokenizer is not None else str(t))
+            if chat:
+                choice["logprobs"] = {"content": [
+                    {"token": tok(t), "logprob": lp, "bytes": None,
+                     "top_logprobs": [{"token": tok(tt), "logprob": tl} for tl, tt in (tops[i] if i < len(tops) else [])]}
+                    for i, (lp, t) in enumerate(zip(lps, acc))]}
+            else:
+                choice["logprobs"] = {"tokens": [tok(t) for t in acc], "token_logprobs": lps,
+                                      "top_logprobs": [{tok(tt): tl for tl, tt in row} for row in tops] or None,
+                                      "text_offset": None}
         return {"id": cid, "object": obj, "created": created, "model": engine.args.model, "choices": [choice],
                 "usage": {"prompt_tokens": last["prompt_tokens"], "completion_tokens": last["completion_tokens"],
                           "total_tokens": last["prompt_tokens"] + last["completion_tokens"]}}

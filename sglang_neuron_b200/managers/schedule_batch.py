@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import dataclasses
 import time
-from typing import List, Optional
+from typing import List, Optional, Tuple
 
 import numpy as np
 
@@ -24,6 +24,8 @@ class SamplingParams:
     seed: Optional[int] = None
     stop_token_ids: Optional[List[int]] = None
     ignore_eos: bool = False
+    return_logprob: bool = False       # log-probability of every generated token (raw distribution)
+    top_logprobs_num: int = 0          # plus the k most likely tokens at every position
 
     @property
     def needs_filter(self) -> bool:
@@ -50,6 +52,8 @@ class Req:
         self.prefix_node = None                   # radix node pinned while running
         self.prefix_len = 0                       # tokens reused from the prefix cache
         self.table_pending: List[int] = []        # (slot, index, page) triples of reused pages not yet in the table
+        self.output_logprobs: List[float] = []    # per generated token (when params.return_logprob)
+        self.output_top_logprobs: List[List[Tuple[float, int]]] = []
         self.kv_len = 0                           # tokens whose KV is written (or being written by launched steps)
         self.scheduled_outputs = 0                # outputs that launched steps will have produced
         self.finished = False
@@ -108,6 +112,8 @@ class StepInput:
     max_seq_len: int = 0
     needs_topk_topp: bool = False
     relay_first_token: Optional[np.ndarray] = None
+    logprob_k: int = -1                 # >= 0: compute token logprobs (+ top-k) for this step
+    logprob_host: Optional[object] = None  # host view [B, 1 + 2k] filled by the runner
 
     def arrays(self):
         return {

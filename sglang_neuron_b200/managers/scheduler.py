@@ -337,12 +337,14 @@ class Scheduler:
         seeds = np.fromiter((r.seed for r in reqs), dtype=np.int64, count=B)
         slot_idx = np.fromiter((r.slot for r in reqs), dtype=np.int64, count=B)
         needs = any(r.params.needs_filter for r in reqs)
+        lp = [r.params.top_logprobs_num for r in reqs if r.params.return_logprob]
+        logprob_k = max(lp) if lp else -1
         step = StepInput(mode=mode, epoch=self.epoch, reqs=list(reqs), sampled=list(sampled), batch_size=B,
                          num_tokens=len(pos), num_decode=num_decode, input_ids=ids, positions=pos,
                          out_cache_loc=slots, logits_idx=logits_idx, req_idx=slot_idx, seeds=seeds, top_k=top_k,
                          seq_lens=seq, qo_indptr=qo, page_upd=np.asarray(upd, dtype=np.int32), temperature=temp,
                          top_p=top_p, max_extend=max_extend, max_seq_len=int(seq.max()) if B else 0,
-                         needs_topk_topp=needs)
+                         needs_topk_topp=needs, logprob_k=logprob_k)
         self.epoch += 1
         return step
 
@@ -354,12 +356,19 @@ class Scheduler:
         if watch is not None:
             watch.check()
         ids = ids_host.numpy() if hasattr(ids_host, "numpy") else np.asarray(ids_host)
+        lpr = step.logprob_host.numpy() if step.logprob_host is not None else None
         now = time.perf_counter()
         for i, (r, s) in enumerate(zip(step.reqs, step.sampled)):
             if not s or r.finished:
                 continue
             tok = int(ids[i])
             r.output_ids.append(tok)
+            if lpr is not None and r.params.return_logprob:
+                k = r.params.top_logprobs_num
+                K = (lpr.shape[1] - 1) // 2
+                r.output_logprobs.append(float(lpr[i, 0]))
+                if k > 0:
+                    r.output_top_logprobs.append([(float(lpr[i, 1 + j]), int(lpr[i, 1 + K + j])) for j in range(k)])
             if r.first_token_time is None:
                 r.first_token_time = now
             r.token_times.append(now)

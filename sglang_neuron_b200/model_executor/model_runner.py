@@ -185,6 +185,7 @@ class ModelRunner:
                          self.max_reqs + 1)
         self.graph_runner = None
         self.logits_hook = None  # test seam: called with (ForwardBatch, local logits) of eager steps
+        self._logprobs = None
         self.status_watch = None
         if self.cuda:
             from ..ops import gemm as gemm_ops, moe as moe_ops
@@ -274,12 +275,20 @@ class ModelRunner:
 
     def run_step(self, step) -> Tuple[torch.Tensor, Optional[torch.cuda.Event]]:
         """Launch one forward for a host-built StepInput; returns (pinned host ids view, event)."""
-        if step.mode == ForwardMode.DECODE and self.graph_runner is not None and self.graph_runner.can_run(step):
+        if (step.mode == ForwardMode.DECODE and step.logprob_k < 0 and self.graph_runner is not None
+                and self.graph_runner.can_run(step)):
             ids = self.graph_runner.replay(step)
         else:
             ids = self.forward_eager(step)
         if self.status_watch is not None:
             self.status_watch.snapshot(self.io)
+        if step.logprob_k >= 0 and self._logprobs is not None:
+            info = self._logprobs
+            host = torch.empty(info.shape, dtype=torch.float32, pin_memory=self.cuda)
+            host.copy_(info, non_blocking=self.cuda)  # ordered before the readback event
+            self.io.d2h_bytes += info.numel() * 4
+            step.logprob_host = host
+        self._logprobs = None
         return self.io.readback(ids)
 
     def forward_eager(self, step) -> torch.Tensor:
@@ -305,6 +314,7 @@ class ModelRunner:
             max_seq_len=step.max_seq_len, temperature=v["temperature"], seeds=v["seeds"], top_k=v["top_k"],
             top_p=v["top_p"], needs_topk_topp=step.needs_topk_topp)
         fb.extra["num_decode"] = D
+        fb.extra["logprob_k"] = getattr(step, "logprob_k", -1)
         # split count depends only on (rows, kv heads, context length) so eager and captured decode
         # reduce in the same order and produce identical tokens
         kvh = self.model.attention_layers()[0].num_kv_heads
@@ -326,6 +336,11 @@ class ModelRunner:
             ids = torch.empty(B, dtype=torch.int64, device=self.device)
         ids = pp_broadcast_ids(ids.contiguous())
         self.relay.index_copy_(0, req_idx.view(-1), ids.view(-1))
+        k = fb.extra.get("logprob_k", -1)
+        if k >= 0:  # the last stage's logprobs go to every rank of the replica too
+            info = self._logprobs if self._logprobs is not None else torch.empty(
+                B, 1 + 2 * k, dtype=torch.float32, device=self.device)
+            self._logprobs = pp_broadcast_ids(info.contiguous())
         return ids
 
     def forward_model(self, fb: ForwardBatch) -> torch.Tensor:
@@ -380,4 +395,51 @@ class ModelRunner:
                 out.copy_(ids)
                 ids = out
         self.relay.index_copy_(0, req_idx.view(-1), ids.view(-1))
+        k = fb.extra.get("logprob_k", -1) if fb.extra else -1
+        if k >= 0:
+            self._logprobs = self._logprob_info(logits, ids, k)
         return ids
+
+    def _logprob_info(self, logits: torch.Tensor, ids: torch.Tensor, k: int) -> torch.Tensor:
+        """[B, 1 + 2k] fp32: log-probability of each chosen id under the raw (temperature 1) distribution, then
+        the top-k log-probabilities and their ids (as fp32). Vocabulary-sharded logits are merged with one
+        gather of per-shard (max, sum of exp) and of per-shard top-k, and a max-reduce of the chosen logit.
+        Parity: the reference sampler's per-shard logsumexp and exact top-logprobs
+        (sglang_neuron/sampling.py:212-470)."""
+        st = get_state()
+        lg = logits[:, : self.vocab_valid].float()
+        B = lg.shape[0]
+        m = lg.max(dim=-1).values
+        se = torch.exp(lg - m[:, None]).sum(dim=-1)
+        local = ids.view(-1).long() - self.vocab_start
+        own = (local >= 0) & (local < self.vocab_valid)
+        chosen = torch.where(own, lg.gather(1, local.clamp(0, max(self.vocab_valid - 1, 0))[:, None])[:, 0],
+                             torch.full_like(m, float("-inf")))
+        kk = min(k, self.vocab_valid)
+        tv, ti = (lg.topk(kk, dim=-1) if kk > 0 else (lg[:, :0], torch.zeros(B, 0, dtype=torch.long,
+                                                                                  device=lg.device)))
+        ti = ti + self.vocab_start
+        if st.tp_size > 1:
+            import torch.distributed as dist
+            from ..parallel.collectives import tp_all_gather_into
+            pack = torch.cat([m[:, None], se[:, None], chosen[:, None], tv, ti.float()], dim=1).contiguous()
+            g = torch.empty(st.tp_size * B, pack.shape[1], dtype=torch.float32, device=lg.device)
+            tp_all_gather_into(g, pack)
+            g = g.view(st.tp_size, B, -1)
+            M = g[:, :, 0].max(dim=0).values
+            se = (g[:, :, 1] * torch.exp(g[:, :, 0] - M[None])).sum(dim=0)
+            m = M
+            chosen = g[:, :, 2].max(dim=0).values
+            if kk > 0:
+                allv = g[:, :, 3:3 + kk].permute(1, 0, 2).reshape(B, -1)
+                alli = g[:, :, 3 + kk:3 + 2 * kk].permute(1, 0, 2).reshape(B, -1)
+                tv, sel = allv.topk(kk, dim=-1)
+                ti = alli.gather(1, sel)
+            del dist
+        lse = m + torch.log(se)
+        out = torch.zeros(B, 1 + 2 * k, dtype=torch.float32, device=lg.device)
+        out[:, 0] = chosen - lse
+        if kk > 0:
+            out[:, 1:1 + kk] = tv - lse[:, None]
+            out[:, 1 + k:1 + k + kk] = ti.float()
+        return out

@@ -75,3 +75,16 @@ def test_sampling_temperature_is_reproducible():
 def test_smoke_entry():
     from sglang_neuron_b200.smoke import run_smoke
     run_smoke("cuda:0")
+
+
+def test_logprobs_on_gpu_and_graph_tokens_unchanged():
+    """Requests asking for logprobs run their decode steps eagerly (the captured graphs sample only); the
+    greedy tokens equal a run without logprobs, and the chosen token is the top-1 of its own top-k."""
+    prompts = _prompts(3)
+    plain = _engine("gpt-oss-120b", TINY_OSS, "cuda").generate(prompts, {"max_new_tokens": 6})
+    lp = _engine("gpt-oss-120b", TINY_OSS, "cuda").generate(
+        prompts, {"max_new_tokens": 6, "return_logprob": True, "top_logprobs_num": 4})
+    assert [o["output_ids"] for o in plain] == [o["output_ids"] for o in lp]
+    for o in lp:
+        for (l, t), top in zip(o["output_token_logprobs"], o["output_top_logprobs"]):
+            assert top[0][1] == t and abs(top[0][0] - l) < 1e-3 and l <= 0.0
