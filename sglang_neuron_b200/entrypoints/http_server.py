@@ -267,6 +267,8 @@ def main(argv=None):
     ns = p.parse_args(argv)
     args = ServerArgs.from_cli(ns)
     logging.basicConfig(level=getattr(logging, args.log_level.upper(), logging.INFO))
+    from ..process_init import install_clean_exit
+    install_clean_exit()
     from ..engine import Engine
     engine = Engine(args)
     if engine.rank != 0:

@@ -86,7 +86,12 @@ class CudaGraphRunner:
                 self.graphs[bs] = g
         torch.cuda.current_stream(r.device).wait_stream(stream)
         torch.cuda.synchronize(r.device)
-        logger.info("captured %d decode graphs (bs %s)", len(self.graphs), self.bs_list)
+        from ..parallel.contract import assert_graphs_consistent
+        kvh = r.model.attention_layers()[0].num_kv_heads
+        self.digest = assert_graphs_consistent({
+            "bs": self.bs_list, "launches": [self.launches[b] for b in self.bs_list],
+            "splits": [r.backend.splits_for(b, kvh, self.args.context_length) for b in self.bs_list]})
+        logger.info("captured %d decode graphs (bs %s, digest %s)", len(self.graphs), self.bs_list, self.digest)
 
     def _fill_padding(self, start: int, end: int) -> None:
         v = self.views

@@ -158,6 +158,12 @@ class ModelRunner:
             from ..speculative.mtp import MTPDraftHead
             self.draft = MTPDraftHead(self.model, self.dtype, self.device)
         self.load_weights()
+        from ..parallel.contract import assert_fleet_consistent
+        self.fleet_digest = assert_fleet_consistent({
+            "arch": cfg.architecture, "layers": cfg.num_layers, "hidden": cfg.hidden_size,
+            "windows": [cfg.layer_window(i) for i in range(cfg.num_layers)], "tp": st.tp_size, "pp": st.pp_size,
+            "dp": st.dp_size, "page": args.page_size, "kv": str(args.kv_cache_dtype), "dtype": str(self.dtype),
+            "spec": args.speculative_algorithm or ""})
         self.page_size = args.page_size
         self.max_pages_per_req = (args.context_length + self.page_size - 1) // self.page_size + 1
         self.max_reqs = args.max_running_requests

@@ -26,3 +26,18 @@ def init_process(local_rank=None) -> None:
             from .cpu_placement import bind_to_gpu
             bind_to_gpu(lr)
     _DONE[0] = True
+
+
+def install_clean_exit() -> None:
+    """SIGTERM raises SystemExit in the main thread, so `finally` blocks run (CUDA graphs released, process
+    groups destroyed, shared buffers unmapped) instead of the process dying mid-collective.
+    Parity: the reference's runtime_init install_clean_exit (sglang_neuron/model_executor/runtime_init.py:313)."""
+    import signal
+
+    def _handler(signum, frame):
+        raise SystemExit(128 + signum)
+
+    try:
+        signal.signal(signal.SIGTERM, _handler)
+    except ValueError:  # not the main thread: leave the default disposition
+        pass

@@ -108,3 +108,23 @@ def test_hook_registry_resolves_and_refuses_double_replace():
     reg.undo_all()
     assert not sglang_tree.rank_label().startswith("wrapped-")
     assert gp.register() == "sglang_neuron_b200.platform.B200SRTPlatform"
+
+
+def test_contract_digests_and_clean_exit():
+    import os
+    import signal
+    from sglang_neuron_b200.parallel.contract import assert_fleet_consistent, digest
+    from sglang_neuron_b200.process_init import install_clean_exit
+    assert digest({"a": 1, "b": [2, 3]}) == digest({"b": [2, 3], "a": 1})
+    assert digest({"a": 1}) != digest({"a": 2})
+    assert assert_fleet_consistent({"x": 1}) == digest({"x": 1})  # single process: no gather
+    prev = signal.getsignal(signal.SIGTERM)
+    try:
+        install_clean_exit()
+        import pytest
+        with pytest.raises(SystemExit):
+            os.kill(os.getpid(), signal.SIGTERM)
+            import time
+            time.sleep(1)
+    finally:
+        signal.signal(signal.SIGTERM, prev)

@@ -61,3 +61,36 @@ def test_tp2_equals_tp1(base, over):
     two = _tp(base, over, 2)
     assert two[0] == one, "TP=2 rank 0 tokens differ from TP=1"
     assert two[1] == one, "follower rank saw different tokens"
+
+
+def _contract_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from sglang_neuron_b200.parallel.contract import assert_fleet_consistent
+    from sglang_neuron_b200.parallel.state import destroy_parallel, init_process_group_from_env, initialize_parallel
+    destroy_parallel()
+    init_process_group_from_env(backend="gloo", timeout_s=60)
+    initialize_parallel(world, device=torch.device("cpu"))
+    same = assert_fleet_consistent({"model": "x"})
+    try:
+        assert_fleet_consistent({"model": "x", "layers": 2 + rank})
+        q.put((rank, same, "accepted"))
+    except RuntimeError:
+        q.put((rank, same, "refused"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fleet_contract_refuses_mismatched_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_contract_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (d, v)) for r, d, v in (q.get(timeout=120) for _ in ps))
+    for p in ps:
+        p.join(timeout=30)
+    assert res[0][0] == res[1][0]
+    assert res[0][1] == res[1][1] == "refused"
