@@ -25,6 +25,14 @@ from .server_args import ServerArgs
 logger = logging.getLogger(__name__)
 
 
+def trim_at_stop(text: str, stops) -> str:
+    """The text up to the first occurrence of any stop sequence (OpenAI semantics: the stop is not returned)."""
+    if not stops:
+        return text
+    cut = min((i for i in (text.find(s) for s in stops) if i >= 0), default=-1)
+    return text if cut < 0 else text[:cut]
+
+
 class Engine:
     def __init__(self, args: Optional[ServerArgs] = None, **kwargs):
         args = args or ServerArgs(**kwargs)
@@ -62,6 +70,18 @@ class Engine:
             except Exception as e:  # no tokenizer files: token-id mode
                 logger.info("tokenizer unavailable (%s); serving token ids", e)
         self._ids = itertools.count()
+        if self.tokenizer is not None:
+            self.scheduler.stop_checker = self._stop_hit
+
+    def _stop_hit(self, r) -> bool:
+        """A text stop sequence appears in the decoded tail of the output (the tail covers the longest stop
+        sequence: every token decodes to at least one character or none)."""
+        longest = max(len(s) for s in r.params.stop)
+        tail = self.tokenizer.decode(r.output_ids[-(longest + 4):])
+        return any(s in tail for s in r.params.stop)
+
+    def abort(self, rid: str) -> None:
+        self.scheduler.abort(rid)
 
     # ------------------------------------------------------------------------------------------
     def _to_ids(self, prompt) -> List[int]:
@@ -75,6 +95,8 @@ class Engine:
         """Queue one request. On a follower rank (replica rank > 0) nothing is queued locally: requests arrive
         through rank 0's broadcast, and the returned rid is the one rank 0 assigns to the same call."""
         sp = sampling_params if isinstance(sampling_params, SamplingParams) else SamplingParams.from_dict(sampling_params)
+        if sp.stop and self.tokenizer is None:
+            raise ValueError("text stop sequences need a tokenizer; use stop_token_ids")
         rid = rid or f"req-{next(self._ids)}"
         if get_state().replica_rank != 0:
             return rid
@@ -110,7 +132,7 @@ class Engine:
             if r.first_token_time is not None:
                 d["ttft_s"] = r.first_token_time - r.arrival
             if self.tokenizer is not None:
-                d["text"] = self.tokenizer.decode(r.output_ids)
+                d["text"] = trim_at_stop(self.tokenizer.decode(r.output_ids), r.params.stop)
             if r.params.return_logprob:
                 d["output_token_logprobs"] = [[lp, t] for lp, t in zip(r.output_logprobs, r.output_ids)]
                 if r.params.top_logprobs_num > 0:

@@ -49,6 +49,11 @@ class EngineLoop:
         self.wake.set()
         return rid, st
 
+    def abort(self, rid: str) -> None:
+        with self.lock:
+            self.engine.scheduler.abort(rid)
+        self.wake.set()
+
     def shutdown(self) -> None:
         self.stop_flag = True
         self.wake.set()

@@ -9,6 +9,7 @@ in; this build owns that layer because it is a standalone engine.
 """
 import argparse
 import asyncio
+import dataclasses
 import json
 import logging
 import os
@@ -17,6 +18,7 @@ import uuid
 from typing import Any, Dict, List, Optional
 
 from ..managers.schedule_batch import SamplingParams
+from ..engine import trim_at_stop
 from ..server_args import ServerArgs
 
 try:  # FastAPI resolves handler annotations from module globals
@@ -34,7 +36,8 @@ def _sampling_from_openai(body: Dict[str, Any]) -> SamplingParams:
         temperature=float(body.get("temperature", 1.0) if body.get("temperature") is not None else 1.0),
         top_k=int(body.get("top_k") or 0), top_p=float(body.get("top_p") if body.get("top_p") is not None else 1.0),
         seed=body.get("seed"), stop_token_ids=body.get("stop_token_ids"), ignore_eos=bool(body.get("ignore_eos", False)),
-        return_logprob=_openai_logprobs(body)[0], top_logprobs_num=_openai_logprobs(body)[1])
+        return_logprob=_openai_logprobs(body)[0], top_logprobs_num=_openai_logprobs(body)[1],
+        stop=([body["stop"]] if isinstance(body.get("stop"), str) else (body.get("stop") or None)))
 
 
 def _openai_logprobs(body: Dict[str, Any]):
@@ -73,23 +76,32 @@ def build_app(engine, loop_holder: Dict[str, Any]):
             return ""
         return engine.tokenizer.decode(ids)
 
-    async def run(ids: List[int], sp: SamplingParams):
-        rid, st = loop().submit(ids, sp)
+    async def run(ids: List[int], sp: SamplingParams, rid: Optional[str] = None):
+        if sp.stop and engine.tokenizer is None:
+            raise ValueError("text stop sequences need a tokenizer; use stop_token_ids")
+        rid, st = loop().submit(ids, sp, rid)
         metrics.requests_total.inc()
         t0 = time.perf_counter()
         first = True
-        while True:
-            item = await st.queue.get()
-            if "error" in item:
-                raise ValueError(item["error"])
-            if first and item.get("new_ids"):
-                metrics.ttft.observe(time.perf_counter() - t0)
-                first = False
-            metrics.tokens_total.inc(len(item.get("new_ids", [])))
-            yield item
-            if item.get("finished"):
-                metrics.e2e.observe(time.perf_counter() - t0)
-                return
+        done = False
+        try:
+            while True:
+                item = await st.queue.get()
+                if "error" in item:
+                    done = True
+                    raise ValueError(item["error"])
+                if first and item.get("new_ids"):
+                    metrics.ttft.observe(time.perf_counter() - t0)
+                    first = False
+                metrics.tokens_total.inc(len(item.get("new_ids", [])))
+                yield item
+                if item.get("finished"):
+                    done = True
+                    metrics.e2e.observe(time.perf_counter() - t0)
+                    return
+        finally:
+            if not done:  # the client went away (or the handler was cancelled): stop generating
+                loop().abort(rid)
 
     @app.get("/health")
     async def health():
@@ -144,6 +156,12 @@ def build_app(engine, loop_holder: Dict[str, Any]):
         state["profiler"] = None
         return {"trace": path}
 
+    @app.post("/abort_request")
+    async def abort_request(req: Request):
+        body = await req.json()
+        loop().abort(str(body["rid"]))
+        return {"success": True}
+
     @app.post("/generate")
     async def generate(req: Request):
         body = await req.json()
@@ -166,14 +184,14 @@ def build_app(engine, loop_holder: Dict[str, Any]):
             async def sse():
                 acc: List[int] = []
                 lps, tops = [], []
-                async for item in run(ids, sp):
+                async for item in run(ids, sp, body.get("rid")):
                     acc += item["new_ids"]
                     lps += item.get("new_logprobs", [])
                     tops += item.get("new_top_logprobs", [])
                     meta = {"finish_reason": item["finish_reason"], "completion_tokens": item["completion_tokens"]}
                     if sp.return_logprob:
                         meta.update(logprob_meta(lps, tops, acc))
-                    out = {"text": decode(acc), "output_ids": list(acc), "meta_info": meta}
+                    out = {"text": trim_at_stop(decode(acc), sp.stop), "output_ids": list(acc), "meta_info": meta}
                     yield f"data: {json.dumps(out)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
@@ -181,7 +199,7 @@ def build_app(engine, loop_holder: Dict[str, Any]):
         lps, tops = [], []
         last = None
         try:
-            async for item in run(ids, sp):
+            async for item in run(ids, sp, body.get("rid")):
                 acc += item["new_ids"]
                 lps += item.get("new_logprobs", [])
                 tops += item.get("new_top_logprobs", [])
@@ -192,7 +210,7 @@ def build_app(engine, loop_holder: Dict[str, Any]):
                 "cached_tokens": last["cached_tokens"], "finish_reason": last["finish_reason"]}
         if sp.return_logprob:
             meta.update(logprob_meta(lps, tops, acc))
-        return {"text": decode(acc), "output_ids": acc, "meta_info": meta}
+        return {"text": trim_at_stop(decode(acc), sp.stop), "output_ids": acc, "meta_info": meta}
 
     async def _openai(body, ids, chat: bool):
         sp = _sampling_from_openai(body)
@@ -212,31 +230,49 @@ def build_app(engine, loop_holder: Dict[str, Any]):
                                                  "model": engine.args.model, "choices": [choice]}) + "\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
-        acc: List[int] = []
-        lps, tops = [], []
-        last = None
-        async for item in run(ids, sp):
-            acc += item["new_ids"]
-            lps += item.get("new_logprobs", [])
-            tops += item.get("new_top_logprobs", [])
-            last = item
-        text = decode(acc)
-        choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": last["finish_reason"]}
-                  if chat else {"index": 0, "text": text, "finish_reason": last["finish_reason"], "token_ids": acc})
-        if sp.return_logprob:
-            tok = (lambda t: decode([t]) if engine.tokenizer is not None else str(t))
-            if chat:
-                choice["logprobs"] = {"content": [
-                    {"token": tok(t), "logprob": lp, "bytes": None,
-                     "top_logprobs": [{"token": tok(tt), "logprob": tl} for tl, tt in (tops[i] if i < len(tops) else [])]}
-                    for i, (lp, t) in enumerate(zip(lps, acc))]}
-            else:
-                choice["logprobs"] = {"tokens": [tok(t) for t in acc], "token_logprobs": lps,
-                                      "top_logprobs": [{tok(tt): tl for tl, tt in row} for row in tops] or None,
-                                      "text_offset": None}
-        return {"id": cid, "object": obj, "created": created, "model": engine.args.model, "choices": [choice],
-                "usage": {"prompt_tokens": last["prompt_tokens"], "completion_tokens": last["completion_tokens"],
-                          "total_tokens": last["prompt_tokens"] + last["completion_tokens"]}}
+        async def one(index: int, spi: SamplingParams):
+            acc: List[int] = []
+            lps, tops = [], []
+            last = None
+            async for item in run(ids, spi):
+                acc += item["new_ids"]
+                lps += item.get("new_logprobs", [])
+                tops += item.get("new_top_logprobs", [])
+                last = item
+            text = trim_at_stop(decode(acc), spi.stop)
+            choice = ({"index": index, "message": {"role": "assistant", "content": text},
+                       "finish_reason": last["finish_reason"]}
+                      if chat else {"index": index, "text": text, "finish_reason": last["finish_reason"],
+                                    "token_ids": acc})
+            if spi.return_logprob:
+                tok = (lambda t: decode([t]) if engine.tokenizer is not None else str(t))
+                if chat:
+                    choice["logprobs"] = {"content": [
+                        {"token": tok(t), "logprob": lp, "bytes": None,
+                         "top_logprobs": [{"token": tok(tt), "logprob": tl}
+                                          for tl, tt in (tops[i] if i < len(tops) else [])]}
+                        for i, (lp, t) in enumerate(zip(lps, acc))]}
+                else:
+                    choice["logprobs"] = {"tokens": [tok(t) for t in acc], "token_logprobs": lps,
+                                          "top_logprobs": [{tok(tt): tl for tl, tt in row} for row in tops] or None,
+                                          "text_offset": None}
+            return choice, last
+
+        n = max(1, int(body.get("n") or 1))
+        sps = []
+        for i in range(n):  # n samples: distinct seeds (seed + i when a seed is given)
+            spi = dataclasses.replace(sp)
+            if sp.seed is not None:
+                spi.seed = sp.seed + i
+            sps.append(spi)
+        results = await asyncio.gather(*[one(i, spi) for i, spi in enumerate(sps)])
+        choices = [c for c, _ in results]
+        last = results[0][1]
+        completion = sum(l["completion_tokens"] for _, l in results)
+        return {"id": cid, "object": obj, "created": created, "model": engine.args.model, "choices": choices,
+                "usage": {"prompt_tokens": last["prompt_tokens"], "completion_tokens": completion,
+                          "total_tokens": last["prompt_tokens"] + completion}}
+
 
     @app.post("/v1/completions")
     async def completions(req: Request):

@@ -24,6 +24,8 @@ class SamplingParams:
     seed: Optional[int] = None
     stop_token_ids: Optional[List[int]] = None
     ignore_eos: bool = False
+    stop: Optional[List[str]] = None   # text stop sequences (need a tokenizer)
+    n: int = 1                         # samples per prompt (expanded by the API layer)
     return_logprob: bool = False       # log-probability of every generated token (raw distribution)
     top_logprobs_num: int = 0          # plus the k most likely tokens at every position
 
@@ -36,7 +38,10 @@ class SamplingParams:
         if not d:
             return cls()
         known = {f.name for f in dataclasses.fields(cls)}
-        return cls(**{k: v for k, v in d.items() if k in known})
+        sp = cls(**{k: v for k, v in d.items() if k in known})
+        if isinstance(sp.stop, str):
+            sp.stop = [sp.stop]
+        return sp
 
 
 class Req:

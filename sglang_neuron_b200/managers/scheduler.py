@@ -51,6 +51,8 @@ class Scheduler:
         self.overlap = not args.disable_overlap_schedule
         self.eos = set(cfg.eos_token_id or [])
         self.pending_arrivals: List[Req] = []
+        self.pending_aborts: List[str] = []
+        self.stop_checker = None  # callable(req) -> bool: a text stop sequence appeared (set with a tokenizer)
         self.finished_reqs: List[Req] = []
         self.finished_by_rid: Dict[str, Req] = {}
         self.reqs_by_rid: Dict[str, Req] = {}
@@ -71,16 +73,39 @@ class Scheduler:
     def _sync_arrivals(self) -> None:
         st = get_state()
         if st.replica_size > 1:
-            payload = ([(r.rid, r.origin_input_ids, r.params) for r in self.pending_arrivals]
+            payload = (([(r.rid, r.origin_input_ids, r.params) for r in self.pending_arrivals], self.pending_aborts)
                        if st.replica_rank == 0 else None)
             payload = cpu_broadcast_object(payload, src=0)
             if st.replica_rank != 0:
                 self.pending_arrivals = [Req(rid, ids, p, eos_ids=[] if p.ignore_eos else self.eos)
-                                         for rid, ids, p in payload]
+                                         for rid, ids, p in payload[0]]
+                self.pending_aborts = list(payload[1])
         for r in self.pending_arrivals:
             self.reqs_by_rid[r.rid] = r
         self.waiting.extend(self.pending_arrivals)
         self.pending_arrivals = []
+        aborts, self.pending_aborts = self.pending_aborts, []
+        for rid in aborts:
+            self._abort(rid)
+
+    def abort(self, rid: str) -> None:
+        """Abort a request (queued or running) at the next step boundary; every rank applies it at the same
+        point of the request stream."""
+        self.pending_aborts.append(rid)
+
+    def _abort(self, rid: str) -> None:
+        r = self.reqs_by_rid.get(rid)
+        if r is None or r.finished:
+            return
+        if r in self.waiting:
+            self.waiting.remove(r)
+            r.finished, r.finish_reason = True, "abort"
+            self.finished_reqs.append(r)
+            self.finished_by_rid[r.rid] = r
+        else:
+            self._finish(r, "abort")
+        if self.on_token is not None:
+            self.on_token(r)
 
     def has_work(self) -> bool:
         return bool(self.waiting or self.running or self.inflight or self.pending_arrivals)
@@ -377,6 +402,8 @@ class Scheduler:
                 self._finish(r, "stop")
             elif len(r.output_ids) >= r.params.max_new_tokens:
                 self._finish(r, "length")
+            elif r.params.stop and self.stop_checker is not None and self.stop_checker(r):
+                self._finish(r, "stop")
             if self.on_token is not None:
                 self.on_token(r)
         self.alloc.retire(step.epoch)
