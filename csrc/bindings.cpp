@@ -46,6 +46,9 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
                torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace,
                bool reduce_partials, int64_t tiled_f);
 void set_pdl(bool on);
+void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
+                torch::Tensor seq_lens, int64_t page_size, double sm_scale, int64_t num_splits, torch::Tensor o_part,
+                torch::Tensor lse_part);
 void kv_page_copy(torch::Tensor src_bases, torch::Tensor dst_bases, torch::Tensor src_pages, torch::Tensor dst_pages,
                   int64_t page_bytes);
 int64_t nvls_flag_bytes();
@@ -102,6 +105,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
   m.def("splitk_allreduce", &splitk_allreduce);
   m.def("set_pdl", &set_pdl);
+  m.def("mla_decode", &mla_decode);
   m.def("kv_page_copy", &kv_page_copy);
   m.def("nvls_flag_bytes", &nvls_flag_bytes);
   m.def("nvls_allreduce", &nvls_allreduce);

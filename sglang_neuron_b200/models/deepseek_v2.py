@@ -92,8 +92,13 @@ class MLAAttention(nn.Module):
 
 
 class DeepseekV2ForCausalLM(CausalLM):
-    # the latent attention still runs as PyTorch ops with per-request host loops (no CUDA graph yet)
-    graph_capturable = False
+    @property
+    def graph_capturable(self) -> bool:
+        """Decode runs the tensor-core MLA kernel (no host work) when the latent pool is bf16 on a GPU."""
+        a = self.attention_layers()[0]
+        return (self.device.type == "cuda" and a.kv_pool is not None and a.kv_pool.dtype == torch.bfloat16
+                and a.r == 512 and a.rope == 64)
+
     def make_layer(self, i: int) -> DecoderLayer:
         cfg = self.cfg
         attn = MLAAttention(cfg, i, self.dtype, self.device, self.max_pos)

@@ -13,15 +13,35 @@ from ..model_executor.forward_batch import ForwardBatch
 
 
 def mla_write_rows(cache: torch.Tensor, rows: torch.Tensor, slots: torch.Tensor, page_size: int) -> None:
-    keep = slots >= 0
-    s = slots.clamp(min=0)
-    page = s // page_size
-    off = s % page_size
-    vals = rows.to(cache.dtype)
-    if bool(keep.all()):
-        cache[page, 0, off] = vals
-    else:
-        cache[page[keep], 0, off[keep]] = vals[keep]
+    """Write latent rows at their slots; rows with slot < 0 (batch padding) land in the reserved page 0
+    (no host synchronisation: the write is capturable in a CUDA graph)."""
+    s = torch.where(slots >= 0, slots, torch.zeros_like(slots))
+    cache[s // page_size, 0, s % page_size] = rows.to(cache.dtype)
+
+
+def mla_kernel_ok(q: torch.Tensor, cache: torch.Tensor, r: int) -> bool:
+    return (q.is_cuda and cache.dtype == torch.bfloat16 and q.dtype == torch.bfloat16 and r == 512
+            and q.shape[-1] == 576)
+
+
+def mla_num_splits(batch: int, heads: int, max_ctx: int, num_sms: int = 148) -> int:
+    """Context splits so that batch x head groups x splits CTAs fill about two waves (1 CTA of 85 KB smem
+    per SM slot pair), at least 64 tokens per split."""
+    ctas = max(1, batch * ((heads + 15) // 16))
+    return int(max(1, min(2 * num_sms // ctas, (max_ctx + 63) // 64, 16)))
+
+
+def mla_decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
+               page_size: int, scale: float, num_splits: int) -> torch.Tensor:
+    """Tensor-core absorbed-MLA decode (csrc/kernels/mla_decode.cu): q [B, H, 576] -> [B, H, 512]."""
+    from .._ext import kernels
+    B, H, _ = q.shape
+    out = torch.empty(B, H, 512, dtype=q.dtype, device=q.device)
+    S = max(1, int(num_splits))
+    o_part = torch.empty(B * H * S * 512 if S > 1 else 1, dtype=torch.float32, device=q.device)
+    lse = torch.empty(B * H * S if S > 1 else 1, dtype=torch.float32, device=q.device)
+    kernels().mla_decode(out, q.contiguous(), cache, block_table, seq_lens, page_size, scale, S, o_part, lse)
+    return out
 
 
 def _one(q, cache, bt_row, L, q_pos, r, scale, page_size):
@@ -44,6 +64,9 @@ def mla_attention(q: torch.Tensor, cache: torch.Tensor, fb: ForwardBatch, r: int
         out[:D] = mla_attention(q[:D], cache, dec, r, scale, page_size)
         out[D:] = mla_attention(q[D:], cache, ext, r, scale, page_size)
         return out
+    if fb.is_decode and mla_kernel_ok(q, cache, r):
+        splits = fb.decode_splits or mla_num_splits(q.shape[0], q.shape[1], fb.max_seq_len or 4096)
+        return mla_decode(q, cache, fb.block_table, fb.seq_lens, page_size, scale, splits)
     seq = fb.seq_lens.tolist()
     if fb.is_decode:
         for b, L in enumerate(seq):

@@ -88,3 +88,30 @@ def test_logprobs_on_gpu_and_graph_tokens_unchanged():
     for o in lp:
         for (l, t), top in zip(o["output_token_logprobs"], o["output_top_logprobs"]):
             assert top[0][1] == t and abs(top[0][0] - l) < 1e-3 and l <= 0.0
+
+
+TINY_DSV2 = dict(num_hidden_layers=2, vocab_size=2048, hidden_size=512, intermediate_size=1024,
+                 moe_intermediate_size=128, n_routed_experts=8, num_experts_per_tok=2, n_shared_experts=1,
+                 num_attention_heads=16, num_key_value_heads=16)
+
+
+def test_deepseek_mla_graph_equals_eager_and_tracks_cpu():
+    """DeepSeek-V2 decode on the MLA kernel: captured graphs give the eager tokens, and the GPU prefill logits
+    follow the fp32 CPU oracle (MoE with MXFP8 activations, hence the GPT-OSS tolerance; only the first
+    token's logits are compared: later steps would see different greedy tokens)."""
+    prompts = _prompts()
+    a = _engine("deepseek-v2-lite", TINY_DSV2, "cuda", graph=True, kv="bf16")
+    assert a.runner.graph_runner is not None, "MLA decode should be graph-capturable"
+    ga = a.generate(prompts, {"max_new_tokens": 10})
+    b = _engine("deepseek-v2-lite", TINY_DSV2, "cuda", graph=False, kv="bf16").generate(prompts, {"max_new_tokens": 10})
+    assert [o["output_ids"] for o in ga] == [o["output_ids"] for o in b]
+    got = {}
+    for dev in ("cuda", "cpu"):
+        eng = _engine("deepseek-v2-lite", TINY_DSV2, dev, graph=False, kv="bf16" if dev == "cuda" else "auto",
+                      std=0.2)
+        rows = []
+        eng.runner.logits_hook = lambda fb, lg: rows.append(lg[:, :2048].float().cpu())
+        eng.generate(_prompts(3), {"max_new_tokens": 1})
+        got[dev] = torch.cat(rows, 0)
+    rel = (got["cuda"] - got["cpu"]).norm() / got["cpu"].norm()
+    assert rel < 0.2, f"rel {rel}"

@@ -301,3 +301,29 @@ def test_kv_page_copy_device_host_round_trip():
     torch.cuda.synchronize()
     for b in pool.k_buffers + pool.v_buffers:
         assert torch.equal(b[dst].view(torch.uint8), b[src[1:]].view(torch.uint8))
+
+
+@pytest.mark.parametrize("H,ctx,splits,P", [(16, [1, 17, 300, 1000], 1, 16), (16, [64, 129, 5], 4, 16),
+                                            (20, [33, 700], 3, 64), (8, [1000, 2], 2, 16)])
+def test_mla_decode_kernel(H, ctx, splits, P):
+    """Tensor-core absorbed-MLA decode vs the fp32 PyTorch reference (stale/NaN bytes past each request's
+    end are never read)."""
+    from sglang_neuron_b200.ops.mla import _one, mla_decode
+    torch.manual_seed(13)
+    B = len(ctx)
+    max_pages = max((c + P - 1) // P for c in ctx) + 1
+    n_pages = B * max_pages + 2
+    perm = torch.randperm(n_pages - 1)[: B * max_pages] + 1
+    bt = perm.view(B, max_pages).to(torch.int32)
+    cache = (torch.randn(n_pages, 1, P, 576) * 0.5).to(torch.bfloat16)
+    for b, c in enumerate(ctx):  # poison the tail of each request's last page
+        for t in range(c, ((c + P - 1) // P) * P):
+            cache[int(bt[b, t // P]), 0, t % P] = float("nan")
+    q = (torch.randn(B, H, 576) * 0.5).to(torch.bfloat16)
+    scale = 0.0625
+    ref = torch.stack([_one(q[b:b + 1].float(), cache.float(), bt[b], ctx[b], torch.tensor([ctx[b] - 1]), 512,
+                            scale, P)[0] for b in range(B)])
+    out = mla_decode(q.to(DEV), cache.to(DEV), bt.to(DEV), torch.tensor(ctx, dtype=torch.int32, device=DEV), P,
+                     scale, splits)
+    torch.cuda.synchronize()
+    _close(out, ref, 2e-2, 2e-2, "mla_decode")
