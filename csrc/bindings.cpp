@@ -38,7 +38,7 @@ void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torc
 // moe_gemm_sm100.cu
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets, int64_t bn,
-              int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status, int64_t F);
+              int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status, int64_t F, c10::optional<torch::Tensor> qout, c10::optional<torch::Tensor> sfout);
 // activation.cu
 void silu_and_mul(torch::Tensor out, torch::Tensor x);
 // gemm_sm100.cu
@@ -95,7 +95,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_quant_mxfp8", &gather_quant_mxfp8);
   m.def("moe_combine", &moe_combine);
   m.def("gemm_bf16", &gemm_bf16);
-  m.def("moe_gemm", &moe_gemm);
+  m.def("moe_gemm", &moe_gemm, py::arg("out"), py::arg("xq"), py::arg("sfb"), py::arg("w"), py::arg("sfa"),
+        py::arg("bias"), py::arg("seg_offsets"), py::arg("tile_offsets"), py::arg("bn"), py::arg("epi"),
+        py::arg("alpha"), py::arg("limit"), py::arg("num_sms"), py::arg("status"), py::arg("F"),
+        py::arg("qout") = py::none(), py::arg("sfout") = py::none());
   m.def("silu_and_mul", &silu_and_mul);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

@@ -69,6 +69,11 @@ struct MoeParams {
   int KB;                       // ceil(K / 128)
   float alpha, limit;           // clamped SwiGLU parameters
   int* status;
+  // Gated epilogues only: write the activation straight as MXFP8 (the down projection's B operand) instead
+  // of bf16: e4m3 values [R, q_ld] and e8m0 scales in the chunk-atom order (null: bf16 to `out`).
+  uint8_t* qout;
+  uint8_t* sfout;
+  int q_ld, q_KB, q_chunk, q_bn;
 };
 
 SNB_DEVICE void bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -269,22 +274,44 @@ __global__ void __launch_bounds__(192, MoeCfg<BN>::CTAS_PER_SM)
             for (int j = 0; j < CW; ++j) xbuf[(row - 64) * 32 + ((j + row) & 31)] = v[j];
           }
           bar_epi();
-          if (ok && q < 2) {
-            const int jcol = mt * 64 + row;  // activation column
-            if (jcol < p.F / 2) {
+          const bool ok_w = __all_sync(0xffffffffu, ok);  // warp-uniform for the shuffles below
+          if (ok_w && q < 2) {
+            const int jcol = mt * 64 + row;  // activation column; warp q holds MX block 2 mt + q
+            const bool colok = jcol < p.F / 2;
 #pragma unroll
-              for (int j = 0; j < CW; ++j) {
-                float g = v[j];
-                float u = xbuf[row * 32 + ((j + row + 64) & 31)];
-                float a;
-                if constexpr (EPI == EPI_SWIGLU_CLAMP) {
-                  g = fminf(g, p.limit);
-                  u = fminf(fmaxf(u, -p.limit), p.limit);
-                  a = (u + 1.f) * (g * sigmoidf_(g * p.alpha));
-                } else {
-                  a = g * sigmoidf_(g) * u;
+            for (int j = 0; j < CW; ++j) {
+              float g = v[j];
+              float u = xbuf[row * 32 + ((j + row + 64) & 31)];
+              float a;
+              if constexpr (EPI == EPI_SWIGLU_CLAMP) {
+                g = fminf(g, p.limit);
+                u = fminf(fmaxf(u, -p.limit), p.limit);
+                a = (u + 1.f) * (g * sigmoidf_(g * p.alpha));
+              } else {
+                a = g * sigmoidf_(g) * u;
+              }
+              const int rr = r0 + c * 32 + j;
+              if (p.qout == nullptr) {
+                if (colok) p.out[(size_t)rr * p.ldo + jcol] = __float2bfloat16(a);
+              } else {
+                // MXFP8 of the bf16-rounded activation: one e8m0 scale per 32 columns (this warp's lanes)
+                a = colok ? __bfloat162float(__float2bfloat16(a)) : 0.f;
+                float amax = fabsf(a);
+#pragma unroll
+                for (int sh = 16; sh > 0; sh >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, sh));
+                int X = 0;
+                if (amax > 0.f) X = max(-127, min(127, (int)ceilf(log2f(amax / 448.f))));
+                if (colok) p.qout[(size_t)rr * p.q_ld + jcol] = snb::f_to_fp8e4m3(a * exp2f((float)-X));
+                const int tile = rr / p.q_bn, i = rr % p.q_bn;
+                uint8_t* sfrow = p.sfout + (size_t)tile * p.q_KB * p.q_chunk + (i % 32) * 16 + (i / 32) * 4;
+                if (lane == 0) {
+                  const int blk = 2 * mt + q;
+                  sfrow[(blk >> 2) * p.q_chunk + (blk & 3)] = (uint8_t)(X + 127);
                 }
-                p.out[(size_t)(r0 + c * 32 + j) * p.ldo + jcol] = __float2bfloat16(a);
+                if (mt == p.MT - 1 && q == 0 && lane < 4 * p.q_KB - 2 * p.MT) {
+                  const int blk = 2 * p.MT + lane;  // padding blocks past the last column: scale 1
+                  sfrow[(blk >> 2) * p.q_chunk + (blk & 3)] = 127;
+                }
               }
             }
           }
@@ -334,7 +361,7 @@ void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const Moe
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets,
               int64_t bn, int64_t epi, double alpha, double limit, int64_t num_sms, torch::Tensor status,
-              int64_t F) {
+              int64_t F, c10::optional<torch::Tensor> qout, c10::optional<torch::Tensor> sfout) {
   // w: tiled weights [E, MT, KB, 128, bpr] (bpr = 64 bytes of packed fp4 or 128 bytes of fp8 per row of a
   // 128-wide K block), zero-padded past F rows and K columns.
   TORCH_CHECK(w.dim() == 5 && w.size(3) == BM, "moe_gemm: weights must be tiled [E, MT, KB, 128, bytes]");
@@ -368,6 +395,21 @@ void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Ten
   p.alpha = (float)alpha;
   p.limit = (float)limit;
   p.status = status.data_ptr<int>();
+  p.qout = nullptr;
+  p.sfout = nullptr;
+  p.q_ld = p.q_KB = p.q_chunk = p.q_bn = 0;
+  if (qout.has_value()) {
+    TORCH_CHECK(epi != 2 && sfout.has_value(), "moe_gemm: MXFP8 output is for the gated projections");
+    TORCH_CHECK(qout->scalar_type() == at::kFloat8_e4m3fn && qout->is_contiguous() && qout->size(0) == R &&
+                    qout->size(1) == F / 2, "moe_gemm: qout must be [R, F/2] e4m3");
+    p.qout = reinterpret_cast<uint8_t*>(qout->data_ptr());
+    p.sfout = sfout->data_ptr<uint8_t>();
+    p.q_ld = F / 2;
+    p.q_KB = (F / 2 + BK - 1) / BK;
+    p.q_chunk = (int)std::min<int64_t>(bn, 32) * 16;
+    p.q_bn = bn;
+    TORCH_CHECK(sfout->numel() >= (int64_t)(R / bn) * p.q_KB * p.q_chunk, "moe_gemm: sfout size");
+  }
   TORCH_CHECK(sfa.numel() >= (int64_t)E * p.MT * p.KB * SF_SMEM, "moe_gemm: sfa size");
   // One 2D view over all tiles: rows = E*MT*KB*128, each row one 128-value K slice of one weight row.
   CUtensorMap ta = snb_host::make_tmap_2d(w.data_ptr(),
