@@ -30,9 +30,14 @@ def _rand_experts(E, H, I, fp4, bias, seed=0, interleaved=True):
     (300, 8, 2880, 2880, True, "swiglu_clamp", True),
     (40, 16, 2048, 768, False, "silu", False),
     (500, 16, 2048, 768, False, "silu", False),
+    (63, 32, 2880, 2880, True, "swiglu_clamp", True),
+    (41, 16, 2048, 768, False, "silu", False),
+    (301, 8, 2880, 2880, True, "swiglu_clamp", True),
 ])
-def test_fused_moe(T, E, H, I, fp4, act, bias):
+def test_fused_moe(T, E, H, I, fp4, act, bias, monkeypatch):
     from sglang_neuron_b200.ops.moe import fused_moe, fused_moe_ref, topk_route
+    # odd T: the gate/up epilogue writes MXFP8 directly (opt-in path); even T: separate quantise launch
+    monkeypatch.setenv("SGLANG_B200_MOE_FUSED_ACT_QUANT", "1" if T % 2 else "0")
     from sglang_neuron_b200.ops.gemm import check_status
     torch.manual_seed(T)
     ew = _rand_experts(E, H, I, fp4, bias, seed=T, interleaved=fp4)
