@@ -26,7 +26,7 @@ from ..configs.model_config import ModelConfig
 from ..mem_cache.memory_pool import MHATokenToKVPool, MLATokenToKVPool, ReqToPagePool
 from ..models.families import get_model_class
 from ..models.weights import RandomSource, SafetensorsSource, load_model_weights
-from ..ops.sampling import apply_top_k_top_p, sample_tokens
+from ..ops.sampling import sample_tokens
 from ..parallel.collectives import tp_all_gather_into
 from ..parallel.state import get_state
 from ..server_args import ServerArgs
@@ -377,12 +377,27 @@ class ModelRunner:
         B = h_last.shape[0]
         positions = fb.positions.index_select(0, fb.logits_idx) + 1
         if fb.needs_topk_topp:
-            full = logits[:, : self.vocab_valid]
+            # per-shard top-256 candidate pools, one gather, filters + Gumbel-max on the merged pool
+            from ..ops.sampling import sample_filtered
+            merge = None
             if st.tp_size > 1:
-                from ..parallel.collectives import tp_all_gather
-                full = tp_all_gather(full.contiguous(), dim=-1)
-            full = apply_top_k_top_p(full.float(), fb.top_k, fb.top_p)
-            ids = sample_tokens(full, fb.temperature, fb.seeds, positions, out=out)
+                def merge(vals, ids):
+                    from ..parallel.collectives import tp_all_gather_into
+                    n = vals.shape[1]
+                    pack = torch.cat([vals, ids.float()], dim=1).contiguous()
+                    g = torch.empty(st.tp_size * pack.shape[0], pack.shape[1], dtype=torch.float32,
+                                    device=vals.device)
+                    tp_all_gather_into(g, pack)
+                    g = g.view(st.tp_size, pack.shape[0], -1)
+                    av = g[:, :, :n].permute(1, 0, 2).reshape(pack.shape[0], -1)
+                    ai = g[:, :, n:].permute(1, 0, 2).reshape(pack.shape[0], -1)
+                    mv, sel = av.topk(n, dim=-1)
+                    return mv, ai.gather(1, sel).long()
+            ids = sample_filtered(logits, fb.temperature, fb.top_k, fb.top_p, fb.seeds, positions,
+                                  self.vocab_start, self.vocab_valid, merge)
+            if out is not None:
+                out.copy_(ids)
+                ids = out
         elif st.tp_size == 1:
             ids = sample_tokens(logits, fb.temperature, fb.seeds, positions, out=out,
                                 valid_vocab=self.vocab_valid)

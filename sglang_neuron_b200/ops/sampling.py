@@ -81,3 +81,73 @@ def apply_top_k_top_p(logits: torch.Tensor, top_k: torch.Tensor, top_p: torch.Te
     sorted_l = sorted_l.masked_fill(mask, float("-inf"))
     out = torch.empty_like(sorted_l).scatter_(-1, idx, sorted_l)
     return out.to(logits.dtype)
+
+
+# ---- filtered sampling over a candidate pool ---------------------------------------------------------------
+# Parity: the reference's topk_topp mode (sglang_neuron/sampling.py:337 sample_filtered_sharded_logits,
+# sampling_topk.py): every vocabulary shard proposes its top-256 logits, one gather merges them, the filters
+# and the Gumbel-max draw run on the 256-candidate pool. Top-k is exact for k <= 256; top-p is exact whenever
+# the nucleus lies inside the pool.
+
+POOL = 256
+_C1 = 0x9E3779B97F4A7C15
+_C2 = 0xBF58476D1CE4E5B9
+_C3 = 0x94D049BB133111EB
+_C4 = 0x100000001B3
+
+
+def _i64(c: int) -> int:
+    return c - (1 << 64) if c >= (1 << 63) else c
+
+
+def _shr(z: torch.Tensor, s: int) -> torch.Tensor:
+    """Logical right shift of int64 bit patterns."""
+    return (z >> s) & ((1 << (64 - s)) - 1)
+
+
+def _mix64_t(z: torch.Tensor) -> torch.Tensor:
+    z = z + _i64(_C1)
+    z = (z ^ _shr(z, 30)) * _i64(_C2)
+    z = (z ^ _shr(z, 27)) * _i64(_C3)
+    return z ^ _shr(z, 31)
+
+
+def gumbel_noise_ids(seeds: torch.Tensor, positions: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    """Gumbel noise of the listed token ids: the same function of (seed, position, token id) as the device
+    sampler and gumbel_noise_ref. seeds/positions: [B]; ids: [B, N] -> [B, N] fp32."""
+    tok = ids.long()
+    inner = _mix64_t((positions.long()[:, None] * _i64(_C4)) ^ _mix64_t(tok))
+    h = _mix64_t(seeds.long()[:, None] ^ inner)
+    u = (_shr(h, 40).double() + 0.5) / 16777216.0
+    return (-torch.log(-torch.log(u))).float()
+
+
+def sample_filtered(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+                    seeds: torch.Tensor, positions: torch.Tensor, vocab_offset: int = 0, valid_vocab: int = 0,
+                    merge=None, pool: int = POOL) -> torch.Tensor:
+    """Top-k / top-p / temperature sampling of (a shard of) logits [B, V_local]. `merge(vals, ids)` combines
+    the per-shard candidate pools of a vocabulary-sharded head (returns the merged, descending pool).
+    Temperature is applied first; top-k keeps the k best; top-p keeps the smallest prefix of the sorted
+    candidates whose probability reaches p; greedy rows (temperature 0) take the best candidate."""
+    V = valid_vocab if valid_vocab > 0 else logits.shape[1]
+    lf = logits[:, :V].float()
+    kp = min(pool, V)
+    vals, ids = lf.topk(kp, dim=-1)
+    ids = ids + vocab_offset
+    if merge is not None:
+        vals, ids = merge(vals, ids)
+    P = vals.shape[1]
+    t = temperature.float()
+    s = vals / t.clamp(min=1e-6)[:, None]
+    ar = torch.arange(P, device=vals.device)[None, :]
+    k = torch.where(top_k > 0, top_k.long(), torch.full_like(top_k.long(), P))
+    mask = ar >= k[:, None]
+    probs = torch.softmax(s.masked_fill(mask, float("-inf")), dim=-1)
+    cum = probs.cumsum(-1) - probs
+    mask = mask | (cum >= top_p.float()[:, None])
+    mask[:, 0] = False  # the best candidate always survives
+    s = s.masked_fill(mask, float("-inf"))
+    noisy = s + gumbel_noise_ids(seeds, positions, ids)
+    pick = noisy.argmax(dim=-1)
+    chosen = ids.gather(1, pick[:, None])[:, 0]
+    return torch.where(t > 0, chosen, ids[:, 0]).long()

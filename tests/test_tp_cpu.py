@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _run(rank, world, port, base, over, q):
+def _run(rank, world, port, base, over, q, sp=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
                       LOCAL_RANK=str(rank))
     from sglang_neuron_b200.configs import model_config as mc
@@ -35,18 +35,18 @@ def _run(rank, world, port, base, over, q):
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
     # SPMD: every rank makes the same call; rank 0 owns intake and broadcasts, followers step in lockstep
-    outs = eng.generate(prompts, {"max_new_tokens": 6})
+    outs = eng.generate(prompts, sp or {"max_new_tokens": 6})
     q.put((rank, [o["output_ids"] for o in outs]))
     import torch.distributed as dist
     dist.barrier()
     dist.destroy_process_group()
 
 
-def _tp(base, over, world):
+def _tp(base, over, world, sp=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, q, sp)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
@@ -94,3 +94,11 @@ def test_fleet_contract_refuses_mismatched_ranks():
         p.join(timeout=30)
     assert res[0][0] == res[1][0]
     assert res[0][1] == res[1][1] == "refused"
+
+
+def test_tp2_filtered_sampling_equals_tp1():
+    """Top-k/top-p sampling with a seed: the vocabulary-sharded candidate-pool merge gives the TP=1 tokens."""
+    sp = {"max_new_tokens": 6, "temperature": 0.9, "top_k": 20, "top_p": 0.8, "seed": 7}
+    one = _tp("qwen3-0.6b", TINY_QWEN, 1, sp)[0]
+    two = _tp("qwen3-0.6b", TINY_QWEN, 2, sp)
+    assert two[0] == one and two[1] == one
