@@ -153,6 +153,7 @@ class ModelRunner:
         self.dtype = args.torch_dtype() if self.cuda else torch.float32
         cls = get_model_class(cfg.architecture)
         self.model = cls(cfg, self.dtype, self.device, max_pos=args.context_length + 128)
+        self.model.sp_min_tokens = args.sp_min_tokens
         self.draft = None
         if args.speculative_algorithm == "MTP":
             from ..speculative.mtp import MTPDraftHead

@@ -23,12 +23,13 @@ from ..configs.model_config import ModelConfig
 from ..layers.embedding import ParallelLMHead, VocabParallelEmbedding
 from ..layers.linear import (MergedColumnParallelLinear, QKVParallelLinear, ReplicatedLinear,
                              RowParallelLinear)
-from ..model_executor.forward_batch import ForwardBatch
+from ..model_executor.forward_batch import ForwardBatch, ForwardMode
 from ..ops import activation as act_ops
 from ..ops import moe as moe_ops
 from ..ops.norm import fused_add_rmsnorm, rmsnorm
 from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
-from ..parallel.collectives import fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden, tp_all_reduce
+from ..parallel.collectives import (deferred_reduction, fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden,
+                                    sp_all_gather, sp_gather_rows, sp_reduce_scatter, tp_all_reduce)
 from ..parallel.state import get_state, pp_layer_range
 
 
@@ -206,12 +207,22 @@ class DecoderLayer(nn.Module):
         self.self_attn = attn if attn is not None else GQAAttention(cfg, layer_id, dtype, device, max_pos)
         self.mlp = mlp
 
-    def forward(self, h: torch.Tensor, residual: Optional[torch.Tensor], fb: ForwardBatch):
+    def forward(self, h: torch.Tensor, residual: Optional[torch.Tensor], fb: ForwardBatch, sp_rows: int = 0):
+        """sp_rows > 0: sequence-parallel step; h and residual are this rank's [sp_rows, H] block of the
+        token rows, and the layer returns its block of the next hidden state."""
         if residual is None:
             residual = h.clone()
             h = self.input_layernorm(h)
         else:
             h, residual = self.input_layernorm(h, residual)
+        if sp_rows:
+            T = fb.num_tokens
+            with deferred_reduction():
+                part = self.self_attn(sp_all_gather(h)[:T], fb)
+            h, residual = self.post_attention_layernorm(sp_reduce_scatter(part, sp_rows), residual)
+            with deferred_reduction():
+                part = self.mlp(sp_all_gather(h)[:T])
+            return sp_reduce_scatter(part, sp_rows), residual
         h = self.self_attn(h, fb)
         h, residual = self.post_attention_layernorm(h, residual)
         h = self.mlp(h)
@@ -225,6 +236,8 @@ class CausalLM(nn.Module):
 
     def __init__(self, cfg: ModelConfig, dtype=torch.bfloat16, device="cpu", max_pos: Optional[int] = None):
         super().__init__()
+        # prefill steps of at least this many tokens run sequence-parallel between layers (0: never)
+        self.sp_min_tokens = 0
         self.cfg = cfg
         self.dtype = dtype
         self.device = torch.device(device)
@@ -252,9 +265,20 @@ class CausalLM(nn.Module):
             a.kv_pool = pool
             a.backend = backend
 
+    def sp_rows(self, fb: ForwardBatch) -> int:
+        """Rows per TP rank when this step runs sequence-parallel between layers, else 0."""
+        tp = get_state().tp_size
+        if (tp == 1 or self.sp_min_tokens <= 0 or fb.mode != ForwardMode.EXTEND or fb.num_tokens < self.sp_min_tokens
+                or (self.device.type == "cuda" and torch.cuda.is_current_stream_capturing())):
+            return 0
+        return -(-fb.num_tokens // tp)
+
     def forward(self, fb: ForwardBatch) -> Optional[torch.Tensor]:
         """Sampled rows after the final norm (last pipeline stage), or None on earlier stages (their output
         went to the next stage)."""
+        rows = self.sp_rows(fb)
+        if rows:
+            return self._forward_sp(fb, rows)
         if self.first_stage:
             h = self.embed_tokens(fb.input_ids)
             residual = None
@@ -273,6 +297,24 @@ class CausalLM(nn.Module):
         h_last, pre = self.norm(h_last, r_last)
         self.last_prenorm = pre  # h + residual of the sampled rows (consumed by the MTP draft head)
         return h_last
+
+    def _forward_sp(self, fb: ForwardBatch, rows: int) -> Optional[torch.Tensor]:
+        """Sequence-parallel forward: the embedding's vocabulary-shard partials are reduce-scattered, every
+        layer keeps this rank's block of rows, and the sampled rows are gathered before the final norm."""
+        if self.first_stage:
+            with deferred_reduction():
+                e = self.embed_tokens(fb.input_ids)
+            h, residual = sp_reduce_scatter(e, rows), None
+        else:
+            h, residual = pp_recv_hidden(rows, self.cfg.hidden_size, self.dtype, self.device)
+        for layer in self.layers:
+            h, residual = layer(h, residual, fb, sp_rows=rows)
+        if not self.last_stage:
+            pp_send_hidden(h, torch.zeros_like(h) if residual is None else residual)
+            return None
+        pre = sp_gather_rows(h if residual is None else h + residual, fb.logits_idx, rows)
+        self.last_prenorm = pre
+        return self.norm(pre)
 
     def compute_logits(self, h_last: torch.Tensor) -> torch.Tensor:
         return self.lm_head(h_last)

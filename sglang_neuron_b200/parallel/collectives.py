@@ -6,12 +6,15 @@ Parity: the reference's traced collectives (sglang_neuron/parallel/collectives.p
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 
 from .state import get_state
 
 _custom_allreduce = None
+_defer = [0]  # > 0 inside deferred_reduction(): TP reductions are left to the caller
 
 
 def set_custom_allreduce(comm) -> None:
@@ -21,7 +24,7 @@ def set_custom_allreduce(comm) -> None:
 
 def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
     st = get_state()
-    if st.tp_size == 1:
+    if st.tp_size == 1 or _defer[0]:
         return x
     if _custom_allreduce is not None and _custom_allreduce.can_run(x):
         return _custom_allreduce.all_reduce(x)
@@ -32,7 +35,7 @@ def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
 def fused_combine_all_reduce(out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor, w: torch.Tensor) -> bool:
     """MoE combine + TP/EP all-reduce in one NVLink kernel; returns False when that path is unavailable."""
     st = get_state()
-    if st.tp_size == 1 or _custom_allreduce is None or not _custom_allreduce.can_run(out):
+    if st.tp_size == 1 or _defer[0] or _custom_allreduce is None or not _custom_allreduce.can_run(out):
         return False
     _custom_allreduce.combine_all_reduce(out, y, inv_map, w)
     return True
@@ -50,7 +53,7 @@ def fused_gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias):
     IpcAllReduce.gemm_all_reduce, covers one-wave grids but keeps only F/128 CTAs busy, so it loses to the
     split-K form at the shapes measured; it stays available.)"""
     st = get_state()
-    if st.tp_size == 1 or _custom_allreduce is None or not x.is_cuda or x.dtype != torch.bfloat16:
+    if st.tp_size == 1 or _defer[0] or _custom_allreduce is None or not x.is_cuda or x.dtype != torch.bfloat16:
         return None
     from ..ops.gemm import linear, linear_partials, pick_splits
     x2 = x.reshape(-1, x.shape[-1])
@@ -116,6 +119,55 @@ def cpu_barrier() -> None:
     st = get_state()
     if st.replica_size > 1:
         dist.barrier(group=st.replica_cpu_group)
+
+
+# ---- sequence parallelism between layers ----------------------------------------------------------------
+# Prefill steps keep ceil(T / t) rows of the hidden state and residual per TP rank between layers: the norms
+# and residual adds run on 1/t of the rows, an all-gather brings the normalised rows to every rank before
+# attention and the MLP/MoE, and a reduce-scatter replaces the all-reduce after them (same bytes on the wire).
+# Parity: the reference's GPT-OSS prefill graph (sglang_neuron/models/gpt_oss/mxfp4/model_prefill.py:32,111,
+# 131,197) and the sampled-row gather (models/gpt_oss/sequence_parallel.py:23).
+
+@contextlib.contextmanager
+def deferred_reduction():
+    """Inside this block a layer's TP reduction is left to the caller: tp_all_reduce returns the partial sum
+    unchanged and the fused GEMM / MoE-combine all-reduce paths decline, so a sequence-parallel layer can
+    reduce-scatter the partials instead."""
+    _defer[0] += 1
+    try:
+        yield
+    finally:
+        _defer[0] -= 1
+
+
+def sp_reduce_scatter(x: torch.Tensor, rows: int) -> torch.Tensor:
+    """x: [T, H] partial sums (T <= rows * tp); returns this rank's [rows, H] block of the reduced rows."""
+    st = get_state()
+    tp = st.tp_size
+    if x.shape[0] < rows * tp:
+        x = torch.cat([x, x.new_zeros(rows * tp - x.shape[0], *x.shape[1:])])
+    out = torch.empty((rows,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.reduce_scatter_tensor(out, x.contiguous(), group=st.tp_group)
+    return out
+
+
+def sp_all_gather(x: torch.Tensor) -> torch.Tensor:
+    """x: [rows, H] this rank's block; returns [rows * tp, H] (rank-major)."""
+    st = get_state()
+    out = torch.empty((x.shape[0] * st.tp_size,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x.contiguous(), group=st.tp_group)
+    return out
+
+
+def sp_gather_rows(x: torch.Tensor, idx: torch.Tensor, rows: int) -> torch.Tensor:
+    """Rows `idx` (global row ids) of a row-sharded [rows, H] tensor, on every rank: each rank contributes
+    the rows it holds (zeros elsewhere) and one all-reduce of [len(idx), H] merges them."""
+    st = get_state()
+    local = idx - st.tp_rank * rows
+    mine = (local >= 0) & (local < rows)
+    sel = x.index_select(0, local.clamp(0, rows - 1))
+    sel = torch.where(mine.unsqueeze(1), sel, torch.zeros_like(sel))
+    return tp_all_reduce(sel)
 
 
 # ---- pipeline parallelism -------------------------------------------------------------------------------

@@ -23,6 +23,7 @@ class ServerArgs:
     ep_size: Optional[int] = None
     dp_size: int = 1
     pp_size: int = 1
+    sp_min_tokens: int = 512                 # TP > 1: prefill steps of >= this many tokens run sequence-parallel between layers (0: off)
     page_size: int = 16
     kv_cache_dtype: str = "auto"             # auto | bf16 | fp8_e4m3
     context_length: int = 8192

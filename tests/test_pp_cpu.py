@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _run(rank, world, port, base, over, tp, pp, q):
+def _run(rank, world, port, base, over, tp, pp, q, sp_min_tokens=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
                       LOCAL_RANK=str(rank))
     from sglang_neuron_b200.configs import model_config as mc
@@ -33,7 +33,7 @@ def _run(rank, world, port, base, over, tp, pp, q):
     mc.PRESETS["pp-tiny"] = dict(mc.PRESETS[base], **over)
     eng = Engine(ServerArgs(model="pp-tiny", device="cpu", dtype="float32", tp_size=tp, pp_size=pp,
                             context_length=256, max_running_requests=4, chunked_prefill_size=32,
-                            random_weight_std=0.05))
+                            random_weight_std=0.05, sp_min_tokens=sp_min_tokens))
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
     outs = eng.generate(prompts, {"max_new_tokens": 6})
@@ -44,12 +44,13 @@ def _run(rank, world, port, base, over, tp, pp, q):
         dist.destroy_process_group()
 
 
-def _launch(base, over, tp, pp):
+def _launch(base, over, tp, pp, sp_min_tokens=0):
     world = tp * pp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, tp, pp, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, tp, pp, q, sp_min_tokens))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
@@ -66,9 +67,12 @@ def test_pp2_equals_pp1(base, over):
 
 
 @pytest.mark.slow
-def test_pp2_tp2_equals_pp1():
+@pytest.mark.parametrize("sp_min_tokens", [0, 1])
+def test_pp2_tp2_equals_pp1(sp_min_tokens):
+    """sp_min_tokens=1: every prefill step sequence-parallel inside each stage; the stage boundary carries
+    each TP rank's block of rows."""
     one = _launch("qwen3-0.6b", TINY_QWEN, 1, 1)[0]
-    four = _launch("qwen3-0.6b", TINY_QWEN, 2, 2)
+    four = _launch("qwen3-0.6b", TINY_QWEN, 2, 2, sp_min_tokens)
     for r in range(4):
         assert four[r] == one, f"rank {r}"
 

@@ -21,7 +21,7 @@ def _free_port():
     return p
 
 
-def _run(rank, world, port, base, over, q, sp=None):
+def _run(rank, world, port, base, over, q, sp=None, args_over=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
                       LOCAL_RANK=str(rank))
     from sglang_neuron_b200.configs import model_config as mc
@@ -30,23 +30,33 @@ def _run(rank, world, port, base, over, q, sp=None):
     from sglang_neuron_b200.server_args import ServerArgs
     destroy_parallel()
     mc.PRESETS["tp-tiny"] = dict(mc.PRESETS[base], **over)
+    from sglang_neuron_b200.models import common
+    calls = [0]
+    rs = common.sp_reduce_scatter
+
+    def counted(*a, **k):
+        calls[0] += 1
+        return rs(*a, **k)
+
+    common.sp_reduce_scatter = counted
     eng = Engine(ServerArgs(model="tp-tiny", device="cpu", dtype="float32", tp_size=world, context_length=256,
-                            max_running_requests=4, chunked_prefill_size=32, random_weight_std=0.05))
+                            max_running_requests=4, chunked_prefill_size=32, random_weight_std=0.05,
+                            **(args_over or {})))
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
     # SPMD: every rank makes the same call; rank 0 owns intake and broadcasts, followers step in lockstep
     outs = eng.generate(prompts, sp or {"max_new_tokens": 6})
-    q.put((rank, [o["output_ids"] for o in outs]))
+    q.put((rank, [o["output_ids"] for o in outs] + ([calls[0]] if (args_over or {}).get("sp_min_tokens") else [])))
     import torch.distributed as dist
     dist.barrier()
     dist.destroy_process_group()
 
 
-def _tp(base, over, world, sp=None):
+def _tp(base, over, world, sp=None, args_over=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, q, sp)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, base, over, q, sp, args_over)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
@@ -61,6 +71,16 @@ def test_tp2_equals_tp1(base, over):
     two = _tp(base, over, 2)
     assert two[0] == one, "TP=2 rank 0 tokens differ from TP=1"
     assert two[1] == one, "follower rank saw different tokens"
+
+
+@pytest.mark.parametrize("base,over", [("qwen3-0.6b", TINY_QWEN), ("qwen3-30b-a3b", TINY_MOE)])
+def test_tp2_sequence_parallel_prefill_equals_tp1(base, over):
+    """Every prefill step sequence-parallel (sp_min_tokens=1; odd token counts pad the last rank's block):
+    the reduce-scatter / all-gather forward gives the TP=1 tokens."""
+    one = _tp(base, over, 1, args_over={"sp_min_tokens": 0})[0]
+    two = _tp(base, over, 2, args_over={"sp_min_tokens": 1})
+    assert two[0][-1] > 0, "no step ran sequence-parallel"
+    assert two[0][:-1] == one and two[1][:-1] == one
 
 
 def _contract_worker(rank, world, port, q):
