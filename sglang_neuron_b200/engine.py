@@ -36,6 +36,8 @@ def trim_at_stop(text: str, stops) -> str:
 class Engine:
     def __init__(self, args: Optional[ServerArgs] = None, **kwargs):
         args = args or ServerArgs(**kwargs)
+        from .platform import check_hybrid_swa
+        check_hybrid_swa(args)
         if args.device == "cuda" and not torch.cuda.is_available():
             args.device = "cpu"
         self.args = args

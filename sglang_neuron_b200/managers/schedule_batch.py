@@ -57,6 +57,8 @@ class Req:
         self.prefix_node = None                   # radix node pinned while running
         self.prefix_len = 0                       # tokens reused from the prefix cache
         self.table_pending: List[int] = []        # (slot, index, page) triples of reused pages not yet in the table
+        self.swa_pages: List[int] = []            # window-pool page per logical page (0 once released)
+        self.swa_freed = 0                        # swa_pages[:swa_freed] are released
         self.output_logprobs: List[float] = []    # per generated token (when params.return_logprob)
         self.output_top_logprobs: List[List[Tuple[float, int]]] = []
         self.kv_len = 0                           # tokens whose KV is written (or being written by launched steps)
@@ -128,8 +130,9 @@ class StepInput:
             "temperature": self.temperature, "top_p": self.top_p,
         }
 
-    def decode_arrays(self, bs: int, dummy_slot: int):
-        """Arrays padded to a captured bucket of `bs` rows (padding rows point at the dummy slot)."""
+    def decode_arrays(self, bs: int, dummy_slot: int, upd_per_row: int = 1):
+        """Arrays padded to a captured bucket of `bs` rows (padding rows point at the dummy slot); the page
+        update area holds `upd_per_row` triples per row."""
         B = self.batch_size
         pad = bs - B
 
@@ -138,10 +141,10 @@ class StepInput:
                 return a.astype(dt, copy=False)
             return np.concatenate([a.astype(dt, copy=False), np.full(pad, fill, dtype=dt)])
 
-        pu = np.zeros((bs, 3), dtype=np.int32)
+        pu = np.zeros((bs * upd_per_row, 3), dtype=np.int32)
         pu[:, 0] = dummy_slot
         upd = self.page_upd.reshape(-1, 3)
-        # at most one new page per decode row: place each update on its own row
+        # at most one new page (+ its window-pool page) per decode row
         pu[: len(upd)] = upd
         return {
             "req_idx": padded(self.req_idx, dummy_slot, np.int64),

@@ -38,6 +38,11 @@ class Scheduler:
         self.P = args.page_size
         self.alloc = make_page_allocator(runner.num_pages, self.P, reserved=1)
         self.radix = None if args.disable_radix_cache else RadixCacheHandle(self.P)
+        self.swa = None
+        if getattr(runner, "swa_num_pages", 0):
+            from ..mem_cache.hybrid_swa import SwaPageTracker
+            self.swa = SwaPageTracker(make_page_allocator(runner.swa_num_pages, self.P, reserved=1),
+                                      runner.swa_window, self.P)
         self.hicache = None
         if args.enable_hierarchical_cache and self.radix is not None:
             from ..mem_cache.hicache import HiCache
@@ -130,12 +135,23 @@ class Scheduler:
         return None
 
     def _ensure_pages(self, r: Req, upto_tokens: int, upd: List[int]) -> bool:
+        if self.swa is not None:
+            self.swa.trim(r, r.kv_len)
         need = (upto_tokens + self.P - 1) // self.P - len(r.pages)
         if need <= 0:
             return True
+        swa = None
+        if self.swa is not None:
+            swa = self.swa.alloc_for(need)
+            if swa is None:
+                return False
         pages = self._alloc_pages(need)
         if pages is None:
+            if swa:
+                self.swa.undo(swa)
             return False
+        if swa is not None:
+            self.swa.bind(r, pages, swa, upd)
         for p in pages:
             upd += [r.slot, len(r.pages), p]
             r.pages.append(p)
@@ -165,6 +181,8 @@ class Scheduler:
                 self.radix.dec_lock(r.prefix_node)
         if to_free:
             self.alloc.free_after(list(to_free), r.last_step)
+        if self.swa is not None:
+            self.swa.release(r)
         r.pages, r.owned_from, r.prefix_node = [], 0, None
         if r.slot is not None:
             self.free_slots.append(r.slot)
@@ -407,6 +425,8 @@ class Scheduler:
             if self.on_token is not None:
                 self.on_token(r)
         self.alloc.retire(step.epoch)
+        if self.swa is not None:
+            self.swa.retire(step.epoch)
 
     def _finish(self, r: Req, reason: str) -> None:
         r.finished = True

@@ -8,18 +8,21 @@ size themselves from free HBM (180 GB per GPU) instead of a fixed token count.
 """
 from __future__ import annotations
 
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 import torch
 
 
 class MHATokenToKVPool:
     """Per-layer paged K/V: [num_pages, num_kv_heads, page_size, head_dim]. Page 0 is a reserved dummy
-    page that padding rows of a batch point at."""
+    page that padding rows of a batch point at.
+
+    With a hybrid sliding-window layout (`layer_pages`), the sliding layers' buffers have the window pool's
+    page count and `swa` translates block tables and slots into it (mem_cache/hybrid_swa.py)."""
 
     def __init__(self, num_layers: int, num_pages: int, page_size: int, num_kv_heads: int, head_dim: int,
                  dtype: torch.dtype, device, k_scale: float = 1.0, v_scale: float = 1.0,
-                 layer_ids: Optional[List[int]] = None):
+                 layer_ids: Optional[List[int]] = None, layer_pages: Optional[Dict[int, int]] = None):
         self.num_pages = num_pages
         self.page_size = page_size
         self.num_kv_heads = num_kv_heads
@@ -28,9 +31,13 @@ class MHATokenToKVPool:
         self.k_scale = k_scale
         self.v_scale = v_scale
         self.layer_ids = list(range(num_layers)) if layer_ids is None else list(layer_ids)
-        shape = (num_pages, num_kv_heads, page_size, head_dim)
-        self.k_buffers = [torch.zeros(shape, dtype=dtype, device=device) for _ in self.layer_ids]
-        self.v_buffers = [torch.zeros(shape, dtype=dtype, device=device) for _ in self.layer_ids]
+        pages = {lid: (layer_pages or {}).get(lid, num_pages) for lid in self.layer_ids}
+        self.hybrid = layer_pages is not None
+        self.swa = None  # SwaTranslate when hybrid
+        self.k_buffers = [torch.zeros((pages[l], num_kv_heads, page_size, head_dim), dtype=dtype, device=device)
+                          for l in self.layer_ids]
+        self.v_buffers = [torch.zeros((pages[l], num_kv_heads, page_size, head_dim), dtype=dtype, device=device)
+                          for l in self.layer_ids]
         self._index = {lid: i for i, lid in enumerate(self.layer_ids)}
 
     def kv(self, layer_id: int):
@@ -44,6 +51,8 @@ class MHATokenToKVPool:
 
     def copy_pages(self, src: torch.Tensor, dst: torch.Tensor) -> None:
         """Copy whole pages (all layers): used by PD transfer and by copy-on-write of shared pages."""
+        if self.hybrid:
+            raise RuntimeError("whole-page copies are not defined for the hybrid sliding-window pool")
         for k, v in zip(self.k_buffers, self.v_buffers):
             k[dst] = k[src]
             v[dst] = v[src]

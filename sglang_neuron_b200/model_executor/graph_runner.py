@@ -30,9 +30,11 @@ class CudaGraphRunner:
         self.max_bs = self.bs_list[-1]
         from .model_runner import Layout
         mb = self.max_bs
+        # page-update triples per row: a new page, plus its window-pool page under the hybrid SWA layout
+        self.upr = 2 if getattr(runner.kv_pool, "swa", None) is not None else 1
         self.layout = Layout([
             ("req_idx", torch.int64, mb), ("positions", torch.int64, mb), ("out_cache_loc", torch.int64, mb),
-            ("seeds", torch.int64, mb), ("seq_lens", torch.int32, mb), ("page_upd", torch.int32, 3 * mb),
+            ("seeds", torch.int64, mb), ("seq_lens", torch.int32, mb), ("page_upd", torch.int32, 3 * self.upr * mb),
             ("temperature", torch.float32, mb),
         ])
         self.static = torch.zeros(self.layout.nbytes, dtype=torch.uint8, device=runner.device)
@@ -44,7 +46,8 @@ class CudaGraphRunner:
         self.capture_all()
 
     def can_run(self, step) -> bool:
-        return step.batch_size <= self.max_bs and not step.needs_topk_topp
+        return (step.batch_size <= self.max_bs and not step.needs_topk_topp
+                and len(step.page_upd) <= 3 * self.upr * step.batch_size)
 
     def _fb(self, bs: int) -> ForwardBatch:
         v = self.views
@@ -61,7 +64,7 @@ class CudaGraphRunner:
 
     def _body(self, bs: int) -> None:
         r = self.r
-        r.apply_page_updates(self.views["page_upd"][: 3 * bs])
+        r.apply_page_updates(self.views["page_upd"][: 3 * self.upr * bs])
         fb = self._fb(bs)
         h = r.model(fb)
         r.sample(h, fb, self.views["req_idx"][:bs], out=self.out_ids[:bs])
@@ -102,14 +105,14 @@ class CudaGraphRunner:
         v["seq_lens"][start:end] = 0
         v["temperature"][start:end] = 0
         pu = v["page_upd"].view(-1, 3)
-        pu[start:end, 0] = self.r.dummy_req
-        pu[start:end, 1] = 0
-        pu[start:end, 2] = 0
+        pu[start * self.upr:end * self.upr, 0] = self.r.dummy_req
+        pu[start * self.upr:end * self.upr, 1] = 0
+        pu[start * self.upr:end * self.upr, 2] = 0
 
     def replay(self, step) -> torch.Tensor:
         B = step.batch_size
         bs = self.bs_list[bisect.bisect_left(self.bs_list, B)]
-        arrays = step.decode_arrays(bs, self.r.dummy_req)
+        arrays = step.decode_arrays(bs, self.r.dummy_req, self.upr)
         self.r.io.upload(self.layout, arrays, dst=self.static)
         self.graphs[bs].replay()
         _ext.add_launches(self.launches[bs])

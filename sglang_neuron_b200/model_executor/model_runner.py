@@ -236,6 +236,19 @@ class ModelRunner:
         # this pipeline stage's layers (+ the MTP block's one extra layer)
         layer_ids = [a.layer_id for a in attn] + ([cfg.num_layers] if self.draft is not None else [])
         n_layers = len(layer_ids)
+        # hybrid sliding-window layout: sliding layers in a window pool sized by the scheduling bound
+        swa_layers = [a.layer_id for a in attn if getattr(a, "window", 0) > 0] if args.enable_hybrid_swa else []
+        swa_pages, swa_bytes = 0, 0
+        if swa_layers:
+            from ..mem_cache.hybrid_swa import check_window_pool, window_pool_pages
+            win = max(a.window for a in attn if a.layer_id in swa_layers)
+            need = window_pool_pages(self.max_reqs, win, P, args.chunked_prefill_size)
+            swa_pages = args.swa_pool_pages or need
+            check_window_pool(swa_pages, self.max_reqs, win, P, args.chunked_prefill_size)
+            swa_bytes = swa_pages * MHATokenToKVPool.bytes_per_page(len(swa_layers), P, attn[0].num_kv_heads,
+                                                                    cfg.head_dim, self.kv_dtype)
+            n_layers -= len(swa_layers)
+            self.swa_window = win
         if cfg.is_mla:
             per_page = MLATokenToKVPool.bytes_per_page(n_layers, P, cfg.kv_lora_rank, cfg.qk_rope_head_dim,
                                                        self.kv_dtype)
@@ -247,7 +260,7 @@ class ModelRunner:
         elif self.cuda:
             free, total = torch.cuda.mem_get_info(self.device)
             reserve = 6 * (1 << 30) + int(0.04 * total)
-            budget = max(0, int(free * args.mem_fraction_static) - reserve)
+            budget = max(0, int(free * args.mem_fraction_static) - reserve - swa_bytes)
             num_pages = max(2, budget // per_page)
             cap = (self.max_reqs * self.max_pages_per_req) + 1
             num_pages = min(num_pages, max(cap, 2))
@@ -258,10 +271,17 @@ class ModelRunner:
             self.kv_pool = MLATokenToKVPool(n_layers, self.num_pages, P, cfg.kv_lora_rank,
                                             cfg.qk_rope_head_dim, self.kv_dtype, self.device, layer_ids=layer_ids)
         else:
-            self.kv_pool = MHATokenToKVPool(n_layers, self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
-                                            self.kv_dtype, self.device, layer_ids=layer_ids)
+            self.kv_pool = MHATokenToKVPool(len(layer_ids), self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
+                                            self.kv_dtype, self.device, layer_ids=layer_ids,
+                                            layer_pages={l: swa_pages for l in swa_layers} if swa_layers else None)
         logger.info("KV pool: %d pages x %d tokens (%.2f GB, %s)", self.num_pages, P,
                     self.num_pages * per_page / 1e9, self.kv_dtype)
+        self.swa_num_pages = swa_pages
+        if swa_layers:
+            from ..mem_cache.hybrid_swa import SwaTranslate
+            self.kv_pool.swa = SwaTranslate(self.num_pages, P, self.device)
+            logger.info("window pool for %d sliding layers: %d pages (%.2f GB, window %d)", len(swa_layers),
+                        swa_pages, swa_bytes / 1e9, self.swa_window)
 
     # ------------------------------------------------------------------------------------------
     @staticmethod
@@ -278,6 +298,16 @@ class ModelRunner:
         if upd.numel() == 0:
             return
         u = upd.view(-1, 3).long()
+        swa = getattr(self.kv_pool, "swa", None)
+        if swa is not None:
+            # (-1, main page, window page) triples go to the window-page map, the rest to the block table
+            # (map triples are redirected to the dummy row's first entry, which nothing reads)
+            m = swa.apply(u)
+            row = torch.where(m, torch.full_like(u[:, 0], self.dummy_req), u[:, 0])
+            col = torch.where(m, torch.zeros_like(u[:, 1]), u[:, 1])
+            val = torch.where(m, torch.zeros_like(u[:, 2]), u[:, 2])
+            self.req_to_page.table[row, col] = val.to(torch.int32)
+            return
         self.req_to_page.table[u[:, 0], u[:, 1]] = u[:, 2].to(torch.int32)
 
     def run_step(self, step) -> Tuple[torch.Tensor, Optional[torch.cuda.Event]]:

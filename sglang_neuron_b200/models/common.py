@@ -96,6 +96,8 @@ class GQAAttention(nn.Module):
         k = qkv[:, qs:qs + kvs]
         v = qkv[:, qs + kvs:]
         kc, vc = self.kv_cache()
+        if self.window > 0 and self.kv_pool.swa is not None:
+            fb = self.kv_pool.swa.batch(fb)  # block table and write slots in window-pool pages
         rope_qk_norm_kv_write(q, k, v, fb.positions, self.cos_sin, self.num_heads, self.num_kv_heads,
                               self.head_dim, self.cfg.rot_dim, self.cfg.rope_neox,
                               self.q_norm.weight if self.q_norm is not None else None,

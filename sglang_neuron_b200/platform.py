@@ -31,6 +31,19 @@ def refuse_unserved(args, spec) -> None:
         raise ValueError("tp_size, pp_size and dp_size must be >= 1")
     if args.pp_size > 1 and args.speculative_algorithm:
         raise ValueError("speculative decoding is not served with pipeline parallelism")
+    check_hybrid_swa(args)
+
+
+def check_hybrid_swa(args) -> None:
+    if args.enable_hybrid_swa:
+        # the window pool keeps only the pages inside the window: prefix reuse, host tiers and KV hand-off,
+        # which all need a prefix's whole KV, are not served with it
+        if args.enable_hierarchical_cache or args.disaggregation_mode != "null" or args.speculative_algorithm:
+            raise ValueError("the hybrid sliding-window pool is not served with the host KV tier, PD "
+                             "disaggregation or speculative decoding")
+        if not args.disable_radix_cache:
+            logger.info("hybrid sliding-window pool: prefix cache disabled")
+            args.disable_radix_cache = True
 
 
 def check_kv_cache(args, spec) -> None:

@@ -34,6 +34,8 @@ class ServerArgs:
     max_prefill_tokens: int = 16384
     enable_mixed_chunk: bool = True          # decode rows ride along with prefill chunks
     disable_radix_cache: bool = False
+    enable_hybrid_swa: bool = False           # sliding-window layers keep their K/V in a small window pool
+    swa_pool_pages: int = 0                   # window pool pages (0: the sizing bound for max_running_requests)
     enable_hierarchical_cache: bool = False   # host (pinned memory) tier below the device prefix cache
     hicache_ratio: float = 2.0                # host pages = ratio x device KV pages (when hicache_host_pages is 0)
     hicache_host_pages: int = 0

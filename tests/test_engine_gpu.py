@@ -18,14 +18,14 @@ TINY_MOE = dict(num_hidden_layers=2, vocab_size=2048, hidden_size=512, moe_inter
                 num_experts_per_tok=4, num_attention_heads=8, num_key_value_heads=4, head_dim=128)
 
 
-def _engine(base, over, device, graph=True, kv="auto", std=0.05):
+def _engine(base, over, device, graph=True, kv="auto", std=0.05, **kw):
     destroy_parallel()
     name = base + "-gputest"
     mc.PRESETS[name] = dict(mc.PRESETS[base], **over)
     args = ServerArgs(model=name, device=device, dtype="bfloat16" if device == "cuda" else "float32", page_size=16,
                       context_length=512, max_running_requests=8, chunked_prefill_size=48,
                       disable_cuda_graph=not graph, cuda_graph_bs=[1, 2, 4, 8], kv_cache_dtype=kv,
-                      random_weight_std=std, random_gen_device="cpu")
+                      random_weight_std=std, random_gen_device="cpu", **kw)
     return Engine(args)
 
 
@@ -41,6 +41,19 @@ def test_graph_equals_eager(base, over, kv):
     a = _engine(base, over, "cuda", graph=True, kv=kv).generate(prompts, {"max_new_tokens": 12})
     b = _engine(base, over, "cuda", graph=False, kv=kv).generate(prompts, {"max_new_tokens": 12})
     assert [o["output_ids"] for o in a] == [o["output_ids"] for o in b]
+
+
+def test_hybrid_swa_pool_equals_single_pool():
+    """Sliding layers in the window pool (pages reused across requests as they leave the window), decode in
+    CUDA graphs with the translated tables: the same tokens as one pool for all layers."""
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, 2048, (L,), generator=g).tolist() for L in (5, 33, 70, 17, 90, 120, 64, 41)]
+    sp = {"max_new_tokens": 48}
+    one = _engine("gpt-oss-120b", TINY_OSS, "cuda").generate(prompts, sp)
+    eng = _engine("gpt-oss-120b", TINY_OSS, "cuda", enable_hybrid_swa=True)
+    two = eng.generate(prompts, sp)
+    assert eng.runner.swa_num_pages < sum(len(p) + 48 for p in prompts) // 16  # pages had to be reused
+    assert [o["output_ids"] for o in two] == [o["output_ids"] for o in one]
 
 
 @pytest.mark.parametrize("base,over,tol", [("gpt-oss-120b", TINY_OSS, 0.2), ("qwen3-8b", TINY_QWEN, 0.08)])
