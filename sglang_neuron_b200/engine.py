@@ -51,7 +51,8 @@ class Engine:
             device = torch.device("cuda", local)
         else:
             device = torch.device("cpu")
-        st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device, pp_size=args.pp_size)
+        st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device, pp_size=args.pp_size,
+                                 dp_attention=args.enable_dp_attention)
         self.rank = st.rank
         self.custom_ar = None
         if st.tp_size > 1 and device.type == "cuda":
@@ -116,7 +117,13 @@ class Engine:
         if self.args.speculative_algorithm == "MTP":
             return self._generate_spec(prompts, sps)
         handles = [self.submit(p, sp) for p, sp in zip(prompts, sps)]
-        if get_state().replica_rank != 0:
+        if get_state().attn_dp_size > 1:
+            # DP attention: every rank steps until the exchanged state says no group has work left
+            self.scheduler.step()
+            while self.scheduler.has_work():
+                self.scheduler.step()
+            reqs = [self.scheduler.reqs_by_rid[h if isinstance(h, str) else h.rid] for h in handles]
+        elif get_state().replica_rank != 0:
             # follower: step in lockstep until rank 0's matching requests have finished here too
             want = set(handles)
             while not want.issubset(self.scheduler.finished_by_rid):

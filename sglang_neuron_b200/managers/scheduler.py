@@ -64,6 +64,17 @@ class Scheduler:
         self.on_token: Optional[Callable[[Req], None]] = None
         self.stats = collections.Counter()
         self.step_times: List[Tuple[int, float, int, int]] = []
+        # DP attention: this rank's attention group serves every D-th arrival; the others' requests are
+        # mirrored from the per-step exchange (tokens and finish state published by each group's rank 0)
+        st = get_state()
+        self.dp_groups, self.dp_group = st.attn_dp_size, st.attn_dp_rank
+        self.dp_leader = st.tp_rank == 0
+        self._arrival_seq = 0
+        self._remote: Dict[str, Req] = {}
+        self._outbox: List[Tuple] = []
+        self._global_busy = False
+        if self.dp_groups > 1:
+            self.overlap = False  # results are published once per step, right after the step
 
     # ------------------------------------------------------------------------------------------
     # request intake
@@ -87,7 +98,16 @@ class Scheduler:
                 self.pending_aborts = list(payload[1])
         for r in self.pending_arrivals:
             self.reqs_by_rid[r.rid] = r
-        self.waiting.extend(self.pending_arrivals)
+        if self.dp_groups > 1:
+            for r in self.pending_arrivals:
+                g = self._arrival_seq % self.dp_groups
+                self._arrival_seq += 1
+                if g == self.dp_group:
+                    self.waiting.append(r)
+                else:
+                    self._remote[r.rid] = r
+        else:
+            self.waiting.extend(self.pending_arrivals)
         self.pending_arrivals = []
         aborts, self.pending_aborts = self.pending_aborts, []
         for rid in aborts:
@@ -113,7 +133,7 @@ class Scheduler:
             self.on_token(r)
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running or self.inflight or self.pending_arrivals)
+        return bool(self.waiting or self.running or self.inflight or self.pending_arrivals or self._global_busy)
 
     # ------------------------------------------------------------------------------------------
     # page management
@@ -422,6 +442,8 @@ class Scheduler:
                 self._finish(r, "length")
             elif r.params.stop and self.stop_checker is not None and self.stop_checker(r):
                 self._finish(r, "stop")
+            if self.dp_groups > 1 and self.dp_leader:
+                self._outbox.append((r.rid, tok, r.finished, r.finish_reason))
             if self.on_token is not None:
                 self.on_token(r)
         self.alloc.retire(step.epoch)
@@ -444,6 +466,8 @@ class Scheduler:
     def step(self) -> None:
         """One scheduler iteration: admit, launch one forward, and process the previous step's tokens."""
         self._sync_arrivals()
+        if self.dp_groups > 1:
+            return self._step_dp()
         step = self.schedule()
         if step is not None:
             t0 = time.perf_counter()
@@ -457,6 +481,47 @@ class Scheduler:
         keep = 1 if (self.overlap and step is not None) else 0
         while len(self.inflight) > keep:
             self._process(*self.inflight.popleft())
+
+    def _step_dp(self) -> None:
+        """DP attention lockstep: every rank exchanges (rows it will run, busy, tokens published since the last
+        exchange); the step's MoE exchange is sized by the largest group and groups without rows run an idle
+        forward. Parity: the reference's DP-attention lockstep with idle dummies
+        (sglang_neuron/model_executor/graph_runner.py:822-869 `plan_step`, :1639 `run_idle`)."""
+        from ..parallel.collectives import dp_exchange
+        step = self.schedule()
+        n = step.num_tokens if step is not None else 0
+        busy = bool(self.waiting or self.running or self.inflight)
+        info = dp_exchange((n, busy, self._outbox))
+        self._outbox = []
+        for _, _, out in info:
+            for rid, tok, fin, reason in out:
+                r = self._remote.get(rid)
+                if r is None:
+                    continue
+                r.output_ids.append(tok)
+                if r.first_token_time is None:
+                    r.first_token_time = time.perf_counter()
+                if fin:
+                    r.finished, r.finish_reason = True, reason
+                    self.finished_reqs.append(r)
+                    self.finished_by_rid[rid] = r
+                    del self._remote[rid]
+                if self.on_token is not None:
+                    self.on_token(r)
+        rows = max(i[0] for i in info)
+        self._global_busy = rows > 0 or any(i[1] for i in info)
+        if rows == 0:
+            return
+        if step is None:
+            self.runner.run_idle(rows)
+            return
+        step.dp_rows = rows
+        t0 = time.perf_counter()
+        ids_host, ev = self.runner.run_step(step)
+        self.stats["steps"] += 1
+        self.stats["decode_steps" if step.mode == ForwardMode.DECODE else "extend_steps"] += 1
+        self.step_times.append((step.epoch, t0, step.batch_size, step.num_tokens))
+        self._process(step, ids_host, ev)
 
     def run_until_idle(self, max_steps: int = 1 << 62) -> None:
         n = 0

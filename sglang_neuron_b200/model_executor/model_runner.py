@@ -313,7 +313,7 @@ class ModelRunner:
     def run_step(self, step) -> Tuple[torch.Tensor, Optional[torch.cuda.Event]]:
         """Launch one forward for a host-built StepInput; returns (pinned host ids view, event)."""
         if (step.mode == ForwardMode.DECODE and step.logprob_k < 0 and self.graph_runner is not None
-                and self.graph_runner.can_run(step)):
+                and not getattr(step, "dp_rows", 0) and self.graph_runner.can_run(step)):
             ids = self.graph_runner.replay(step)
         else:
             ids = self.forward_eager(step)
@@ -327,6 +327,10 @@ class ModelRunner:
             step.logprob_host = host
         self._logprobs = None
         return self.io.readback(ids)
+
+    def run_idle(self, rows: int) -> None:
+        """DP attention: this attention group has no rows this step; join the other groups' MoE exchanges."""
+        self.model.forward_idle(rows)
 
     def forward_eager(self, step) -> torch.Tensor:
         B, T = step.batch_size, step.num_tokens
@@ -352,6 +356,7 @@ class ModelRunner:
             top_p=v["top_p"], needs_topk_topp=step.needs_topk_topp)
         fb.extra["num_decode"] = D
         fb.extra["logprob_k"] = getattr(step, "logprob_k", -1)
+        fb.extra["dp_rows"] = getattr(step, "dp_rows", 0)  # DP attention: rows per group in the MoE exchange
         # split count depends only on (rows, kv heads, context length) so eager and captured decode
         # reduce in the same order and produce identical tokens
         kvh = self.model.attention_layers()[0].num_kv_heads

@@ -28,8 +28,9 @@ from ..ops import activation as act_ops
 from ..ops import moe as moe_ops
 from ..ops.norm import fused_add_rmsnorm, rmsnorm
 from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
-from ..parallel.collectives import (deferred_reduction, fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden,
-                                    sp_all_gather, sp_gather_rows, sp_reduce_scatter, tp_all_reduce)
+from ..parallel.collectives import (deferred_reduction, dp_gather_rows, dp_scatter_rows, fused_combine_all_reduce,
+                                    pp_recv_hidden, pp_send_hidden, sp_all_gather, sp_gather_rows, sp_reduce_scatter,
+                                    tp_all_reduce)
 from ..parallel.state import get_state, pp_layer_range
 
 
@@ -184,6 +185,21 @@ class MoEBlock(nn.Module):
             out = out + self.shared(x)
         return tp_all_reduce(out)
 
+    def forward_dp(self, x: torch.Tensor, rows: int) -> torch.Tensor:
+        """DP attention: route every group's rows (all-gathered, padded to `rows` per group) through this
+        rank's experts, sum the partials over all ranks and keep this group's rows. Shared experts run on the
+        group's own rows, reduced over the attention group."""
+        n = x.shape[0]
+        xa = dp_gather_rows(x, rows)
+        logits = self.router(xa)
+        w, ids = moe_ops.topk_route(logits, self.top_k, self.route_mode, self.cfg.routed_scaling_factor)
+        part = moe_ops.fused_moe(xa, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
+                                 self.cfg.swiglu_limit, e_lo=self.e_lo)
+        y = dp_scatter_rows(part, rows, n)
+        if self.shared is not None and n > 0:
+            y = y + tp_all_reduce(self.shared(x))
+        return y
+
     # -- weights ------------------------------------------------------------------------------
     def set_experts_from_dense(self, w13: torch.Tensor, w2: torch.Tensor, b13=None, b2=None,
                                interleaved: bool = False):
@@ -217,6 +233,11 @@ class DecoderLayer(nn.Module):
             h = self.input_layernorm(h)
         else:
             h, residual = self.input_layernorm(h, residual)
+        dp_rows = fb.extra.get("dp_rows", 0)
+        if dp_rows and isinstance(self.mlp, MoEBlock):
+            h = self.self_attn(h, fb)
+            h, residual = self.post_attention_layernorm(h, residual)
+            return self.mlp.forward_dp(h, dp_rows), residual
         if sp_rows:
             T = fb.num_tokens
             with deferred_reduction():
@@ -269,8 +290,9 @@ class CausalLM(nn.Module):
 
     def sp_rows(self, fb: ForwardBatch) -> int:
         """Rows per TP rank when this step runs sequence-parallel between layers, else 0."""
-        tp = get_state().tp_size
-        if (tp == 1 or self.sp_min_tokens <= 0 or fb.mode != ForwardMode.EXTEND or fb.num_tokens < self.sp_min_tokens
+        st = get_state()
+        tp = st.tp_size
+        if (tp == 1 or st.attn_dp_size > 1 or self.sp_min_tokens <= 0 or fb.mode != ForwardMode.EXTEND or fb.num_tokens < self.sp_min_tokens
                 or (self.device.type == "cuda" and torch.cuda.is_current_stream_capturing())):
             return 0
         return -(-fb.num_tokens // tp)
@@ -299,6 +321,14 @@ class CausalLM(nn.Module):
         h_last, pre = self.norm(h_last, r_last)
         self.last_prenorm = pre  # h + residual of the sampled rows (consumed by the MTP draft head)
         return h_last
+
+    def forward_idle(self, rows: int) -> None:
+        """DP attention, no requests in this attention group this step: take part in every MoE block's token
+        exchange with zero rows, so the groups that do have rows can run."""
+        x = torch.zeros(0, self.cfg.hidden_size, dtype=self.dtype, device=self.device)
+        for layer in self.layers:
+            if isinstance(layer.mlp, MoEBlock):
+                layer.mlp.forward_dp(x, rows)
 
     def _forward_sp(self, fb: ForwardBatch, rows: int) -> Optional[torch.Tensor]:
         """Sequence-parallel forward: the embedding's vocabulary-shard partials are reduce-scattered, every

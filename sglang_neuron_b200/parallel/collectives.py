@@ -170,6 +170,44 @@ def sp_gather_rows(x: torch.Tensor, idx: torch.Tensor, rows: int) -> torch.Tenso
     return tp_all_reduce(sel)
 
 
+# ---- DP attention: token exchange around the MoE ------------------------------------------------------------
+# Each attention group holds its own requests' rows; the experts are split over every rank. Before a MoE
+# block the groups' rows (padded to the step's largest group, `rows`) are all-gathered so every rank routes
+# every token through its experts; after it the partial outputs are summed over all ranks and each group
+# keeps its own rows (a reduce-scatter when groups are single ranks). Parity: the reference's DP-attention
+# decode (sglang_neuron/models/gpt_oss/mxfp4/model_decode.py:90-98: all-gather over the DP group, experts,
+# wide all-reduce or reduce-scatter).
+
+def dp_gather_rows(x: torch.Tensor, rows: int) -> torch.Tensor:
+    """x: [T_g, H] (T_g <= rows) -> [D * rows, H], group-major, zero padding rows."""
+    st = get_state()
+    if x.shape[0] < rows:
+        x = torch.cat([x, x.new_zeros(rows - x.shape[0], *x.shape[1:])])
+    out = torch.empty((rows * st.attn_dp_size,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x.contiguous(), group=st.dp_cross_group)
+    return out
+
+
+def dp_scatter_rows(part: torch.Tensor, rows: int, n: int) -> torch.Tensor:
+    """part: [D * rows, H] partial sums on every rank -> this group's first n rows of the total."""
+    st = get_state()
+    if st.tp_size == 1:  # one rank per group: a reduce-scatter over all ranks
+        out = torch.empty((rows,) + tuple(part.shape[1:]), dtype=part.dtype, device=part.device)
+        dist.reduce_scatter_tensor(out, part.contiguous(), group=st.moe_group)
+        return out[:n]
+    dist.all_reduce(part, group=st.moe_group)
+    g = st.attn_dp_rank
+    return part[g * rows:g * rows + n]
+
+
+def dp_exchange(obj):
+    """All-gather a host object over every rank of the DP-attention world (the per-step lockstep record)."""
+    st = get_state()
+    out = [None] * st.replica_size
+    dist.all_gather_object(out, obj, group=st.replica_cpu_group)
+    return out
+
+
 # ---- pipeline parallelism -------------------------------------------------------------------------------
 # Stage boundaries move (hidden, residual) of every token from stage s to stage s+1 (same TP rank) with one
 # point-to-point send (NCCL on GPUs, gloo on the CPU tier); the last stage's sampled ids are broadcast to the

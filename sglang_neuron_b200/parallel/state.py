@@ -8,6 +8,12 @@ torch.distributed (one process per GPU); host-side control collectives use a glo
 reference (gloo on the host). EP here spans the same ranks as TP: experts are split in contiguous blocks
 by rank (`ep_group_ranks` rows = EP) and tokens are replicated over the group after attention.
 
+DP attention (`initialize_parallel(..., dp_attention=True)`): the world of T ranks splits into D attention
+groups of T/D ranks; `tp_*` then describe the attention group (QKV/o_proj, dense MLP, vocabulary shards,
+sampling), experts are split over all T ranks (`ep_*`), and tokens cross groups only around the MoE
+(all-gather before, reduce-scatter after, on `moe_group`). Parity: the reference's DP-attention groups
+(sglang_neuron/parallel/groups.py:72 `dp_column_ranks`, parallel/state.py:125-126).
+
 Rank layout: rank = (dp_rank * pp_size + pp_rank) * tp_size + tp_rank. A DP replica (pp_size x tp_size
 ranks) runs one scheduler in lockstep; its replica rank 0 owns request intake. Pipeline stages hold
 contiguous layer blocks (distributed/pipeline.py `StageSpec` in the reference: sglang_neuron/distributed/
@@ -41,6 +47,10 @@ class ParallelState:
     pp_rank: int = 0
     replica_group: Optional[object] = None      # device group of the DP replica (pp_size x tp_size ranks)
     replica_cpu_group: Optional[object] = None  # gloo group of the DP replica
+    attn_dp_size: int = 1                       # DP-attention groups inside the replica (1: off)
+    attn_dp_rank: int = 0
+    moe_group: Optional[object] = None          # device group of all ranks (DP attention: MoE token exchange)
+    dp_cross_group: Optional[object] = None     # ranks with this tp_rank in every attention group
 
     @property
     def is_first_rank(self) -> bool:
@@ -48,11 +58,11 @@ class ParallelState:
 
     @property
     def replica_size(self) -> int:
-        return self.pp_size * self.tp_size
+        return self.pp_size * self.tp_size * self.attn_dp_size
 
     @property
     def replica_rank(self) -> int:
-        return self.pp_rank * self.tp_size + self.tp_rank
+        return (self.pp_rank * self.attn_dp_size + self.attn_dp_rank) * self.tp_size + self.tp_rank
 
     @property
     def replica_base(self) -> int:
@@ -112,9 +122,12 @@ def init_process_group_from_env(backend: Optional[str] = None, timeout_s: int = 
 
 
 def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size: int = 1,
-                        device: Optional[torch.device] = None, pp_size: int = 1) -> ParallelState:
+                        device: Optional[torch.device] = None, pp_size: int = 1,
+                        dp_attention: bool = False) -> ParallelState:
     """Build the groups. Ranks are laid out DP-major, then PP: rank = (dp_rank * pp_size + pp_rank) * tp_size
-    + tp_rank."""
+    + tp_rank. With dp_attention, dp_size attention groups split the tp_size ranks instead (one replica)."""
+    if dp_attention and dp_size > 1:
+        return _initialize_dp_attention(tp_size, ep_size, dp_size, device, pp_size)
     ep_size = tp_size if ep_size is None else ep_size
     if ep_size != tp_size:
         raise ValueError("expert parallelism spans the tensor-parallel group here (ep_size must equal tp_size)")
@@ -150,6 +163,41 @@ def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size
                        ep_rank=tp_rank, dp_size=dp_size, dp_rank=dp_rank, tp_group=tp_group,
                        cpu_group=cpu_group, device=device, pp_size=pp_size, pp_rank=pp_rank,
                        replica_group=replica_group, replica_cpu_group=replica_cpu_group)
+    set_state(st)
+    return st
+
+
+def _initialize_dp_attention(tp_size, ep_size, dp_size, device, pp_size) -> ParallelState:
+    if pp_size != 1:
+        raise ValueError("DP attention is not served with pipeline parallelism")
+    if tp_size % dp_size:
+        raise ValueError(f"dp_size {dp_size} must divide tp_size {tp_size} under DP attention")
+    if ep_size not in (None, tp_size):
+        raise ValueError("under DP attention experts span all tp_size ranks (ep_size must equal tp_size)")
+    world, rank = (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
+    if world != tp_size:
+        raise ValueError(f"tp_size {tp_size} != world size {world}")
+    a = tp_size // dp_size
+    g_rank, tp_rank = divmod(rank, a)
+    tp_group = cpu_group = cross = None
+    for g in range(dp_size):
+        ranks = list(range(g * a, (g + 1) * a))
+        dg, cg = dist.new_group(ranks), dist.new_group(ranks, backend="gloo")
+        if g == g_rank:
+            tp_group, cpu_group = dg, cg
+    for t in range(a):
+        ranks = list(range(t, tp_size, a))
+        xg = dist.new_group(ranks)
+        if t == tp_rank:
+            cross = xg
+    world_group = dist.new_group(list(range(world)))
+    world_cpu = dist.new_group(list(range(world)), backend="gloo")
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    st = ParallelState(world_size=world, rank=rank, tp_size=a, tp_rank=tp_rank, ep_size=tp_size, ep_rank=rank,
+                       dp_size=1, dp_rank=0, tp_group=tp_group, cpu_group=cpu_group, device=device,
+                       replica_group=world_group, replica_cpu_group=world_cpu, attn_dp_size=dp_size,
+                       attn_dp_rank=g_rank, moe_group=world_group, dp_cross_group=cross)
     set_state(st)
     return st
 

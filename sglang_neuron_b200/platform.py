@@ -35,6 +35,12 @@ def refuse_unserved(args, spec) -> None:
 
 
 def check_hybrid_swa(args) -> None:
+    if args.enable_dp_attention and args.dp_size > 1:
+        if args.speculative_algorithm or args.disaggregation_mode != "null" or args.pp_size > 1:
+            raise ValueError("DP attention is not served with speculative decoding, PD disaggregation or "
+                             "pipeline parallelism")
+        if args.tp_size % args.dp_size:
+            raise ValueError(f"dp_size {args.dp_size} must divide tp_size {args.tp_size} under DP attention")
     if args.enable_hybrid_swa:
         # the window pool keeps only the pages inside the window: prefix reuse, host tiers and KV hand-off,
         # which all need a prefix's whole KV, are not served with it

@@ -21,7 +21,8 @@ class ServerArgs:
     device: str = "cuda"
     tp_size: int = 1
     ep_size: Optional[int] = None
-    dp_size: int = 1
+    dp_size: int = 1                         # DP replicas, or attention groups inside TP with enable_dp_attention
+    enable_dp_attention: bool = False        # dp_size attention groups split the tp_size ranks; experts span all
     pp_size: int = 1
     sp_min_tokens: int = 512                 # TP > 1: prefill steps of >= this many tokens run sequence-parallel between layers (0: off)
     page_size: int = 16

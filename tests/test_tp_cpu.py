@@ -39,6 +39,14 @@ def _run(rank, world, port, base, over, q, sp=None, args_over=None):
         return rs(*a, **k)
 
     common.sp_reduce_scatter = counted
+    dp_calls = [0]
+    fdp = common.MoEBlock.forward_dp
+
+    def counted_dp(self, *a, **k):
+        dp_calls[0] += 1
+        return fdp(self, *a, **k)
+
+    common.MoEBlock.forward_dp = counted_dp
     eng = Engine(ServerArgs(model="tp-tiny", device="cpu", dtype="float32", tp_size=world, context_length=256,
                             max_running_requests=4, chunked_prefill_size=32, random_weight_std=0.05,
                             **(args_over or {})))
@@ -46,7 +54,10 @@ def _run(rank, world, port, base, over, q, sp=None, args_over=None):
     prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
     # SPMD: every rank makes the same call; rank 0 owns intake and broadcasts, followers step in lockstep
     outs = eng.generate(prompts, sp or {"max_new_tokens": 6})
-    q.put((rank, [o["output_ids"] for o in outs] + ([calls[0]] if (args_over or {}).get("sp_min_tokens") else [])))
+    if (args_over or {}).get("enable_dp_attention"):
+        q.put((rank, [o["output_ids"] for o in outs], dp_calls[0], eng.scheduler.stats["output_tokens"]))
+    else:
+        q.put((rank, [o["output_ids"] for o in outs] + ([calls[0]] if (args_over or {}).get("sp_min_tokens") else [])))
     import torch.distributed as dist
     dist.barrier()
     dist.destroy_process_group()
@@ -59,7 +70,10 @@ def _tp(base, over, world, sp=None, args_over=None):
     procs = [ctx.Process(target=_run, args=(r, world, port, base, over, q, sp, args_over)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in procs)
+    res = {}
+    for _ in procs:
+        item = q.get(timeout=300)
+        res[item[0]] = item[1] if len(item) == 2 else item[1:]
     for p in procs:
         p.join(timeout=60)
     return res
@@ -81,6 +95,29 @@ def test_tp2_sequence_parallel_prefill_equals_tp1(base, over):
     two = _tp(base, over, 2, args_over={"sp_min_tokens": 1})
     assert two[0][-1] > 0, "no step ran sequence-parallel"
     assert two[0][:-1] == one and two[1][:-1] == one
+
+
+@pytest.mark.parametrize("base,over", [("qwen3-30b-a3b", TINY_MOE), ("qwen3-0.6b", TINY_QWEN)])
+def test_dp_attention_two_groups_equals_tp1(base, over):
+    """Two attention groups of one rank (requests split between them, experts split over both ranks, tokens
+    all-gathered / reduce-scattered around each MoE block, idle forwards once a group runs dry): the tokens
+    of every request equal the single-rank run, on both ranks."""
+    one = _tp(base, over, 1)[0]
+    two = _tp(base, over, 2, args_over={"dp_size": 2, "enable_dp_attention": True})
+    assert two[0][0] == one and two[1][0] == one
+    # each group generated only its own requests' tokens (requests 0 and 2 on group 0, request 1 on group 1)
+    assert two[0][2] == len(one[0]) + len(one[2]) and two[1][2] == len(one[1])
+    if base == "qwen3-30b-a3b":
+        assert two[0][1] > 0 and two[0][1] == two[1][1]  # same number of MoE exchanges (lockstep + idle)
+
+
+@pytest.mark.slow
+def test_dp_attention_groups_of_two_ranks_equals_tp1():
+    """World 4: two attention groups of two TP ranks each; experts over all four ranks."""
+    one = _tp("qwen3-30b-a3b", TINY_MOE, 1)[0]
+    four = _tp("qwen3-30b-a3b", TINY_MOE, 4, args_over={"dp_size": 2, "enable_dp_attention": True})
+    for r in range(4):
+        assert four[r][0] == one, f"rank {r}"
 
 
 def _contract_worker(rank, world, port, q):
