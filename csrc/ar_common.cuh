@@ -102,5 +102,85 @@ SNB_DEVICE void ar_reduce_store(const ARPeers& peers, int half, int world, size_
   }
 }
 
+// Residual add + RMSNorm fused into the reduce step: the CTA owns whole rows [r0, r1) of a [T, H] call.
+// For each row: x = sum of the world's slots (fp32), residual <- x + residual (stored as bf16), and
+// out <- (x + residual) * rsqrt(mean((x + residual)^2) + eps) * weight, from the fp32 sum. This is the
+// add + norm that follows the all-reduce in a decoder layer (the output is the next block's input).
+struct ARNorm {
+  __nv_bfloat16* residual;      // [T, H], updated in place
+  const __nv_bfloat16* weight;  // [H]
+  float eps;
+  int H;
+};
+constexpr int kNormVecs = 2;  // 8-wide vectors per thread per row: H <= kNormVecs * 8 * blockDim.x
+
+SNB_DEVICE void ar_reduce_norm_store(const ARPeers& peers, int half, int world, size_t capacity, int rank,
+                                     __nv_bfloat16* __restrict__ out, const ARNorm& nm, int r0, int r1) {
+  __shared__ float red[32];
+  const int hv = nm.H / 8;
+  for (int t = r0; t < r1; ++t) {
+    float acc[kNormVecs][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormVecs; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c >= hv) continue;
+      const int64_t v = (int64_t)t * hv + c;
+      float r[8];
+      snb::unpack_bf16x8(reinterpret_cast<const uint4*>(nm.residual)[v], r);
+      for (int q = 0; q < world; ++q) {
+        const uint4 u = reinterpret_cast<const uint4*>(ar_slot(peers, rank, half, q, world, capacity))[v];
+        float f[8];
+        snb::unpack_bf16x8(u, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] += f[j];
+      }
+      reinterpret_cast<uint4*>(nm.residual)[v] = snb::pack_bf16x8(r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        acc[i][j] = r[j];
+        ss += r[j] * r[j];
+      }
+    }
+    ss = snb::warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float s2 = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      s2 = snb::warp_sum(s2);
+      if (threadIdx.x == 0) red[0] = s2;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)nm.H + nm.eps);
+    __syncthreads();  // red[0] is rewritten by the next row
+#pragma unroll
+    for (int i = 0; i < kNormVecs; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c >= hv) continue;
+      float w[8];
+      snb::unpack_bf16x8(reinterpret_cast<const uint4*>(nm.weight)[c], w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] *= inv * w[j];
+      reinterpret_cast<uint4*>(out)[(int64_t)t * hv + c] = snb::pack_bf16x8(acc[i]);
+    }
+  }
+}
+
+// Chunk of a call: vectors [v0, v1) of n8 = T * H / 8; with a fused norm the chunk is whole rows.
+SNB_DEVICE void ar_chunk(int64_t nvec, int hv, bool rows, int64_t& v0, int64_t& v1, int& r0, int& r1) {
+  if (rows) {
+    const int T = (int)(nvec / hv);
+    const int per = (T + gridDim.x - 1) / gridDim.x;
+    r0 = min(T, (int)blockIdx.x * per);
+    r1 = min(T, r0 + per);
+    v0 = (int64_t)r0 * hv;
+    v1 = (int64_t)r1 * hv;
+  } else {
+    const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
+    v0 = min(nvec, (int64_t)blockIdx.x * per);
+    v1 = min(nvec, v0 + per);
+    r0 = r1 = 0;
+  }
+}
 
 }  // namespace snb_ar

@@ -62,7 +62,8 @@ void nvls_splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t spl
                            int64_t world, int64_t max_ctas, torch::Tensor status);
 bool get_pdl();
 void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
-                      std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status);
+                      std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status,
+                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps);
 
 void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                          torch::Tensor status, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
@@ -72,10 +73,12 @@ std::tuple<int64_t, py::bytes> symm_alloc(int64_t capacity, int64_t world);
 int64_t symm_open(py::bytes handle);
 void symm_close(int64_t ptr, bool owned);
 void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
-                        int64_t capacity, int64_t num_ctas, torch::Tensor status);
+                        int64_t capacity, int64_t num_ctas, torch::Tensor status,
+                        c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps);
 void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w,
                            std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas,
-                           torch::Tensor status);
+                           torch::Tensor status, c10::optional<torch::Tensor> residual,
+                           c10::optional<torch::Tensor> weight, double eps);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sglang_neuron_b200 sm_100a kernels";
@@ -103,10 +106,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
-  m.def("one_shot_allreduce", &one_shot_allreduce);
-  m.def("moe_combine_allreduce", &moe_combine_allreduce);
+  m.def("one_shot_allreduce", &one_shot_allreduce, py::arg("out"), py::arg("inp"), py::arg("bufs"), py::arg("rank"),
+        py::arg("capacity"), py::arg("num_ctas"), py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
+  m.def("moe_combine_allreduce", &moe_combine_allreduce, py::arg("out"), py::arg("y"), py::arg("inv_map"),
+        py::arg("w"), py::arg("bufs"), py::arg("rank"), py::arg("capacity"), py::arg("num_ctas"), py::arg("status"),
+        py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
-  m.def("splitk_allreduce", &splitk_allreduce);
+  m.def("splitk_allreduce", &splitk_allreduce, py::arg("out"), py::arg("partial"), py::arg("splits"),
+        py::arg("bias"), py::arg("bufs"), py::arg("rank"), py::arg("capacity"), py::arg("num_ctas"),
+        py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
   m.def("set_pdl", &set_pdl);
   m.def("mla_decode", &mla_decode);
   m.def("kv_page_copy", &kv_page_copy);

@@ -27,42 +27,48 @@ namespace {
 
 constexpr int kThreadsAR = 512;
 
+// kNorm: the reduce step also adds the residual and applies RMSNorm (ar_reduce_norm_store); chunks are rows.
+template <bool kNorm>
 __global__ void __launch_bounds__(kThreadsAR) one_shot_allreduce_kernel(
     ARPeers peers, int rank, int world, size_t capacity, const __nv_bfloat16* __restrict__ in,
-    __nv_bfloat16* __restrict__ out, int64_t n, int* status) {
+    __nv_bfloat16* __restrict__ out, int64_t n, ARNorm nm, int* status) {
   snb::pdl_wait();
   snb::pdl_trigger();
   const ARBuf b = ar_layout(peers, rank, world, capacity);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
   const int half = e & 1;
-  const int64_t nvec = n / 8;
-  const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
-  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
+  int64_t v0, v1;
+  int r0, r1;
+  ar_chunk(n / 8, kNorm ? nm.H / 8 : 1, kNorm, v0, v1, r0, r1);
   for (int p = 0; p < world; ++p) {
     uint4* dst = reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity));
     const uint4* src = reinterpret_cast<const uint4*>(in);
     for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
   }
-  if (ar_exchange(peers, b, rank, world, capacity, e, status)) ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) {
+    if constexpr (kNorm) ar_reduce_norm_store(peers, half, world, capacity, rank, out, nm, r0, r1);
+    else ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  }
   ar_finish(b, e);
 }
 
 // MoE combine fused with the expert-parallel all-reduce: each rank forms its partial
 // sum_j w[t,j] * y[inv_map[t*K+j]] over the experts it owns, stores it straight into every peer's slot,
 // and reduces the world's partials for its chunk of tokens. One launch replaces combine + all-reduce.
+template <bool kNorm>
 __global__ void __launch_bounds__(kThreadsAR) moe_combine_allreduce_kernel(
     ARPeers peers, int rank, int world, size_t capacity, const __nv_bfloat16* __restrict__ y, int ys,
     const int32_t* __restrict__ inv_map, const float* __restrict__ w, int K, int T, int H,
-    __nv_bfloat16* __restrict__ out, int* status) {
+    __nv_bfloat16* __restrict__ out, ARNorm nm, int* status) {
   snb::pdl_wait();
   snb::pdl_trigger();
   const ARBuf b = ar_layout(peers, rank, world, capacity);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
   const int half = e & 1;
-  const int64_t nvec = (int64_t)T * H / 8;
-  const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
-  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
   const int hv = H / 8;
+  int64_t v0, v1;
+  int r0, r1;
+  ar_chunk((int64_t)T * hv, hv, kNorm, v0, v1, r0, r1);
   for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
     const int t = (int)(v / hv), c = (int)(v % hv);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -78,25 +84,30 @@ __global__ void __launch_bounds__(kThreadsAR) moe_combine_allreduce_kernel(
     const uint4 packed = snb::pack_bf16x8(acc);
     for (int p = 0; p < world; ++p) reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity))[v] = packed;
   }
-  if (ar_exchange(peers, b, rank, world, capacity, e, status)) ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) {
+    if constexpr (kNorm) ar_reduce_norm_store(peers, half, world, capacity, rank, out, nm, r0, r1);
+    else ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  }
   ar_finish(b, e);
 }
 
 // Split-K GEMM epilogue fused with the all-reduce: sum the S fp32 partial tiles of this rank (+ bias),
 // push the bf16 result into every peer's slot, and reduce the world's copies. Together with the split-K
 // tcgen05 GEMM this makes a row-parallel projection + all-reduce two launches with every SM busy.
+template <bool kNorm>
 __global__ void __launch_bounds__(kThreadsAR) splitk_allreduce_kernel(
     ARPeers peers, int rank, int world, size_t capacity, const float* __restrict__ partial, int splits,
-    const __nv_bfloat16* __restrict__ bias, int T, int F, __nv_bfloat16* __restrict__ out, int* status) {
+    const __nv_bfloat16* __restrict__ bias, int T, int F, __nv_bfloat16* __restrict__ out, ARNorm nm,
+    int* status) {
   snb::pdl_wait();
   snb::pdl_trigger();
   const ARBuf b = ar_layout(peers, rank, world, capacity);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
   const int half = e & 1;
-  const int64_t nvec = (int64_t)T * F / 8;
-  const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
-  const int64_t v0 = blockIdx.x * per, v1 = min(nvec, v0 + per);
   const int fv = F / 8;
+  int64_t v0, v1;
+  int r0, r1;
+  ar_chunk((int64_t)T * fv, fv, kNorm, v0, v1, r0, r1);
   for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
     const int f8 = (int)(v % fv) * 8;
     float acc[8];
@@ -115,7 +126,10 @@ __global__ void __launch_bounds__(kThreadsAR) splitk_allreduce_kernel(
     const uint4 packed = snb::pack_bf16x8(acc);
     for (int p = 0; p < world; ++p) reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity))[v] = packed;
   }
-  if (ar_exchange(peers, b, rank, world, capacity, e, status)) ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) {
+    if constexpr (kNorm) ar_reduce_norm_store(peers, half, world, capacity, rank, out, nm, r0, r1);
+    else ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  }
   ar_finish(b, e);
 }
 
@@ -151,41 +165,67 @@ void symm_close(int64_t ptr, bool owned) {
   else cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
 }
 
+// Optional fused residual add + RMSNorm of a [T, H] call (H = weight size): `out` receives the normalised
+// rows and `residual` is updated in place; the CTA count is then capped at T (one or more rows per CTA).
+static ARNorm make_norm(const c10::optional<torch::Tensor>& residual, const c10::optional<torch::Tensor>& weight,
+                        double eps, int64_t n, int64_t& num_ctas) {
+  ARNorm nm{nullptr, nullptr, (float)eps, 0};
+  if (!residual) return nm;
+  TORCH_CHECK(weight && weight->scalar_type() == at::kBFloat16 && residual->scalar_type() == at::kBFloat16 &&
+              residual->is_contiguous() && weight->is_contiguous(), "fused norm: bf16 contiguous residual/weight");
+  const int64_t H = weight->numel();
+  TORCH_CHECK(H % 8 == 0 && H <= kNormVecs * 8 * kThreadsAR && n % H == 0 && residual->numel() == n,
+              "fused norm: hidden size ", H);
+  nm.residual = (__nv_bfloat16*)residual->data_ptr();
+  nm.weight = (const __nv_bfloat16*)weight->data_ptr();
+  nm.H = (int)H;
+  num_ctas = std::max<int64_t>(1, std::min<int64_t>(num_ctas, n / H));
+  return nm;
+}
+
 void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
-                        int64_t capacity, int64_t num_ctas, torch::Tensor status) {
+                        int64_t capacity, int64_t num_ctas, torch::Tensor status,
+                        c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps) {
   const int world = (int)bufs.size();
   TORCH_CHECK(world >= 1 && world <= kMaxRanks, "one_shot_allreduce: world size");
   TORCH_CHECK(in.scalar_type() == at::kBFloat16 && in.is_contiguous() && out.is_contiguous(), "one_shot_allreduce: bf16");
   const int64_t n = in.numel();
   TORCH_CHECK(n % 8 == 0 && (size_t)n * 2 <= (size_t)capacity, "one_shot_allreduce: size ", n, " over capacity");
   TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "one_shot_allreduce: CTA count");
+  const ARNorm nm = make_norm(residual, weight, eps, n, num_ctas);
   ARPeers peers;
   for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
-  snb::launch_pdl(one_shot_allreduce_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
-      peers, rank, world, capacity, (const __nv_bfloat16*)in.data_ptr(), (__nv_bfloat16*)out.data_ptr(), n,
+  auto kern = residual ? one_shot_allreduce_kernel<true> : one_shot_allreduce_kernel<false>;
+  snb::launch_pdl(kern, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
+      peers, rank, world, capacity, (const __nv_bfloat16*)in.data_ptr(), (__nv_bfloat16*)out.data_ptr(), n, nm,
       status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w,
                            std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas,
-                           torch::Tensor status) {
+                           torch::Tensor status, c10::optional<torch::Tensor> residual,
+                           c10::optional<torch::Tensor> weight, double eps) {
   const int world = (int)bufs.size();
   const int T = out.size(0), H = out.size(1), K = w.size(1);
   TORCH_CHECK(world >= 1 && world <= kMaxRanks && H % 8 == 0, "moe_combine_allreduce: shape");
   TORCH_CHECK((size_t)T * H * 2 <= (size_t)capacity, "moe_combine_allreduce: over capacity");
   TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "moe_combine_allreduce: CTA count");
   if (T == 0) return;
+  const ARNorm nm = make_norm(residual, weight, eps, (int64_t)T * H, num_ctas);
+  TORCH_CHECK(!residual || nm.H == H, "moe_combine_allreduce: norm size");
   ARPeers peers;
   for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
-  snb::launch_pdl(moe_combine_allreduce_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
+  auto kern = residual ? moe_combine_allreduce_kernel<true> : moe_combine_allreduce_kernel<false>;
+  snb::launch_pdl(kern, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
-      w.data_ptr<float>(), K, T, H, (__nv_bfloat16*)out.data_ptr(), status.data_ptr<int>());
+      w.data_ptr<float>(), K, T, H, (__nv_bfloat16*)out.data_ptr(), nm, status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
-                      std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status) {
+                      std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status,
+                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps) {
   const int world = (int)bufs.size();
   const int T = out.size(0), F = out.size(1);
   TORCH_CHECK(F % 8 == 0 && out.is_contiguous() && partial.scalar_type() == at::kFloat, "splitk_allreduce: layout");
@@ -193,11 +233,14 @@ void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, 
   TORCH_CHECK((size_t)T * F * 2 <= (size_t)capacity, "splitk_allreduce: over capacity");
   TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "splitk_allreduce: CTA count");
   if (T == 0) return;
+  const ARNorm nm = make_norm(residual, weight, eps, (int64_t)T * F, num_ctas);
+  TORCH_CHECK(!residual || nm.H == F, "splitk_allreduce: norm size");
   ARPeers peers;
   for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
-  snb::launch_pdl(splitk_allreduce_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
+  auto kern = residual ? splitk_allreduce_kernel<true> : splitk_allreduce_kernel<false>;
+  snb::launch_pdl(kern, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, partial.data_ptr<float>(), splits,
-      bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr, T, F, (__nv_bfloat16*)out.data_ptr(),
+      bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr, T, F, (__nv_bfloat16*)out.data_ptr(), nm,
       status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -172,17 +172,18 @@ class RowParallelLinear(PackedWeight, nn.Module):
         self.weight = _param((out_features, self.in_local), dtype, device)
         self.bias = _param((out_features,), dtype, device) if bias else None
 
-    def forward(self, x):
+    def forward(self, x, norm=None):
+        """norm: an optional parallel.collectives.FusedNorm folded into the all-reduce (see there)."""
         st = get_state()
         # the bias is added once (on rank 0) so the all-reduce sums it exactly once
         b = self.bias if (self.bias is not None and st.tp_rank == 0) else None
         if self.reduce and st.tp_size > 1:
-            y = fused_gemm_all_reduce(x, self.gemm_weight, b)
+            y = fused_gemm_all_reduce(x, self.gemm_weight, b, norm=norm)
             if y is not None:
                 return y
         y = linear(x, self.gemm_weight, b)
         if self.reduce and st.tp_size > 1:
-            y = tp_all_reduce(y)
+            y = tp_all_reduce(y, norm=norm)
         return y
 
     def load(self, w: torch.Tensor, b: Optional[torch.Tensor] = None):

@@ -28,9 +28,9 @@ from ..ops import activation as act_ops
 from ..ops import moe as moe_ops
 from ..ops.norm import fused_add_rmsnorm, rmsnorm
 from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
-from ..parallel.collectives import (deferred_reduction, dp_gather_rows, dp_scatter_rows, fused_combine_all_reduce,
-                                    pp_recv_hidden, pp_send_hidden, sp_all_gather, sp_gather_rows, sp_reduce_scatter,
-                                    tp_all_reduce)
+from ..parallel.collectives import (FusedNorm, deferred_reduction, dp_gather_rows, dp_scatter_rows,
+                                    fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden, sp_all_gather,
+                                    sp_gather_rows, sp_reduce_scatter, tp_all_reduce)
 from ..parallel.state import get_state, pp_layer_range
 
 
@@ -90,7 +90,7 @@ class GQAAttention(nn.Module):
     def kv_cache(self):
         return self.kv_pool.kv(self.layer_id)
 
-    def forward(self, h: torch.Tensor, fb: ForwardBatch) -> torch.Tensor:
+    def forward(self, h: torch.Tensor, fb: ForwardBatch, norm=None) -> torch.Tensor:
         qkv = self.qkv_proj(h)
         qs, kvs = self.qkv_proj.q_size, self.qkv_proj.kv_size
         q = qkv[:, :qs]
@@ -106,7 +106,7 @@ class GQAAttention(nn.Module):
                               kc, vc, fb.out_cache_loc, self.kv_pool.page_size, self.kv_pool.k_scale,
                               self.kv_pool.v_scale)
         o = self.backend.attend(q, self, fb)
-        return self.o_proj(o)
+        return self.o_proj(o, norm=norm)
 
     def load(self, get):
         p = f"model.layers.{self.layer_id}.self_attn."
@@ -130,8 +130,8 @@ class DenseMLP(nn.Module):
         self.gate_up = MergedColumnParallelLinear(hidden, [inter, inter], dtype=dtype, device=device)
         self.down = RowParallelLinear(inter, hidden, reduce=reduce, dtype=dtype, device=device)
 
-    def forward(self, x):
-        return self.down(act_ops.silu_and_mul(self.gate_up(x)))
+    def forward(self, x, norm=None):
+        return self.down(act_ops.silu_and_mul(self.gate_up(x)), norm=norm)
 
     def load(self, get, prefix: str):
         self.gate_up.load_part(0, get(prefix + "gate_proj.weight"))
@@ -165,25 +165,25 @@ class MoEBlock(nn.Module):
         self.device = device
         self.alignment_cache = {}
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, norm=None) -> torch.Tensor:
         logits = self.router(x)
         w, ids = moe_ops.topk_route(logits, self.top_k, self.route_mode, self.cfg.routed_scaling_factor)
         if self.shared is None and x.is_cuda and get_state().tp_size > 1:
-            # combine + expert-parallel all-reduce fused into one NVLink kernel when available
+            # combine + expert-parallel all-reduce (+ the next residual add and norm) in one NVLink kernel
             reduced = [False]
 
             def combine(out, y, inv_map, topk_w):
-                reduced[0] = fused_combine_all_reduce(out, y, inv_map, topk_w)
+                reduced[0] = fused_combine_all_reduce(out, y, inv_map, topk_w, norm=norm)
                 return reduced[0]
 
             out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
                                     self.cfg.swiglu_limit, e_lo=self.e_lo, combine_fn=combine)
-            return out if reduced[0] else tp_all_reduce(out)
+            return out if reduced[0] else tp_all_reduce(out, norm=norm)
         out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
                                 self.cfg.swiglu_limit, e_lo=self.e_lo)
         if self.shared is not None:
             out = out + self.shared(x)
-        return tp_all_reduce(out)
+        return tp_all_reduce(out, norm=norm)
 
     def forward_dp(self, x: torch.Tensor, rows: int) -> torch.Tensor:
         """DP attention: route every group's rows (all-gathered, padded to `rows` per group) through this
@@ -225,10 +225,18 @@ class DecoderLayer(nn.Module):
         self.self_attn = attn if attn is not None else GQAAttention(cfg, layer_id, dtype, device, max_pos)
         self.mlp = mlp
 
-    def forward(self, h: torch.Tensor, residual: Optional[torch.Tensor], fb: ForwardBatch, sp_rows: int = 0):
+    def forward(self, h: torch.Tensor, residual: Optional[torch.Tensor], fb: ForwardBatch, sp_rows: int = 0,
+                next_norm=None):
         """sp_rows > 0: sequence-parallel step; h and residual are this rank's [sp_rows, H] block of the
-        token rows, and the layer returns its block of the next hidden state."""
-        if residual is None:
+        token rows, and the layer returns its block of the next hidden state.
+
+        Under TP the residual add + RMSNorm after each all-reduce is offered to the all-reduce kernel
+        (FusedNorm): the attention output comes back already post-attention-normed, and with `next_norm`
+        (the next layer's input norm) the MLP output comes back as the next layer's normed input, which
+        fb.extra["h_normed"] tells the next layer."""
+        if fb.extra.pop("h_normed", False):
+            pass  # the previous layer's all-reduce applied this layer's input norm (residual already updated)
+        elif residual is None:
             residual = h.clone()
             h = self.input_layernorm(h)
         else:
@@ -246,9 +254,20 @@ class DecoderLayer(nn.Module):
             with deferred_reduction():
                 part = self.mlp(sp_all_gather(h)[:T])
             return sp_reduce_scatter(part, sp_rows), residual
-        h = self.self_attn(h, fb)
-        h, residual = self.post_attention_layernorm(h, residual)
-        h = self.mlp(h)
+        fn = FusedNorm.offer(residual, self.post_attention_layernorm)
+        if fn is None:
+            h = self.self_attn(h, fb)
+            h, residual = self.post_attention_layernorm(h, residual)
+        else:
+            h = self.self_attn(h, fb, norm=fn)
+            if not fn.done:
+                h, residual = self.post_attention_layernorm(h, residual)
+        fn = FusedNorm.offer(residual, next_norm)
+        if fn is None:
+            return self.mlp(h), residual
+        h = self.mlp(h, norm=fn)
+        if fn.done:
+            fb.extra["h_normed"] = True
         return h, residual
 
 
@@ -308,8 +327,12 @@ class CausalLM(nn.Module):
             residual = None
         else:
             h, residual = pp_recv_hidden(fb.num_tokens, self.cfg.hidden_size, self.dtype, self.device)
-        for layer in self.layers:
-            h, residual = layer(h, residual, fb)
+        n = len(self.layers)
+        for i, layer in enumerate(self.layers):
+            # the next layer's input norm rides on this layer's last all-reduce when the kernel can take it
+            nxt = self.layers[i + 1].input_layernorm if i + 1 < n else None
+            h, residual = layer(h, residual, fb, next_norm=nxt)
+        fb.extra.pop("h_normed", None)
         if not self.last_stage:
             if residual is None:
                 residual = torch.zeros_like(h)

@@ -59,7 +59,7 @@ class MLAAttention(nn.Module):
     def kv_cache(self):
         return self.kv_pool.kv(self.layer_id)
 
-    def forward(self, h: torch.Tensor, fb: ForwardBatch) -> torch.Tensor:
+    def forward(self, h: torch.Tensor, fb: ForwardBatch, norm=None) -> torch.Tensor:
         T = h.shape[0]
         q = self.q_proj(h).view(T, self.num_heads, self.nope + self.rope)
         kv_a = self.kv_a_proj(h)
@@ -75,7 +75,7 @@ class MLAAttention(nn.Module):
         qf = torch.cat([q_lat, q_pe], dim=-1)  # [T, H, r + rope]
         o_lat = mla_attention(qf, kc, fb, self.r, self.scaling, self.kv_pool.page_size)  # [T, H, r]
         o = torch.einsum("thr,hvr->thv", o_lat.float(), self.w_uv.float()).to(h.dtype)
-        return self.o_proj(o.reshape(T, self.num_heads * self.vd))
+        return self.o_proj(o.reshape(T, self.num_heads * self.vd), norm=norm)
 
     def load(self, get):
         st = get_state()

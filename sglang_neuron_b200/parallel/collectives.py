@@ -7,6 +7,7 @@ Parity: the reference's traced collectives (sglang_neuron/parallel/collectives.p
 from __future__ import annotations
 
 import contextlib
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -22,29 +23,56 @@ def set_custom_allreduce(comm) -> None:
     _custom_allreduce = comm
 
 
-def tp_all_reduce(x: torch.Tensor) -> torch.Tensor:
+class FusedNorm:
+    """The residual add + RMSNorm that follows a block's all-reduce, offered to the reduction: when the NVLink
+    all-reduce kernel takes it (`done` becomes True) the reduced output comes back normalised and `residual`
+    is updated in place, in the same launch; otherwise the caller applies the norm itself."""
+
+    __slots__ = ("residual", "weight", "eps", "done")
+
+    def __init__(self, residual: torch.Tensor, weight: torch.Tensor, eps: float):
+        self.residual, self.weight, self.eps, self.done = residual, weight, eps, False
+
+    @staticmethod
+    def offer(residual: Optional[torch.Tensor], norm_module) -> Optional["FusedNorm"]:
+        """A FusedNorm when the fused path can apply to rows like `residual`, else None."""
+        st = get_state()
+        ar = _custom_allreduce
+        if (residual is None or norm_module is None or st.tp_size == 1 or _defer[0] or ar is None
+                or not getattr(ar, "supports_norm", False) or not residual.is_cuda
+                or residual.dtype != torch.bfloat16 or not residual.is_contiguous()):
+            return None
+        w = norm_module.weight
+        H = w.numel()
+        if w.dtype != torch.bfloat16 or H % 8 or H > 8192 or residual.shape[-1] != H or residual.numel() * 2 > ar.capacity:
+            return None
+        return FusedNorm(residual, w, norm_module.eps)
+
+
+def tp_all_reduce(x: torch.Tensor, norm: Optional[FusedNorm] = None) -> torch.Tensor:
     st = get_state()
     if st.tp_size == 1 or _defer[0]:
         return x
     if _custom_allreduce is not None and _custom_allreduce.can_run(x):
-        return _custom_allreduce.all_reduce(x)
+        return _custom_allreduce.all_reduce(x, norm=norm)
     dist.all_reduce(x, group=st.tp_group)
     return x
 
 
-def fused_combine_all_reduce(out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor, w: torch.Tensor) -> bool:
+def fused_combine_all_reduce(out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor, w: torch.Tensor,
+                             norm: Optional[FusedNorm] = None) -> bool:
     """MoE combine + TP/EP all-reduce in one NVLink kernel; returns False when that path is unavailable."""
     st = get_state()
     if st.tp_size == 1 or _defer[0] or _custom_allreduce is None or not _custom_allreduce.can_run(out):
         return False
-    _custom_allreduce.combine_all_reduce(out, y, inv_map, w)
+    _custom_allreduce.combine_all_reduce(out, y, inv_map, w, norm=norm)
     return True
 
 
 _num_sms = {}
 
 
-def fused_gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias):
+def fused_gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias, norm: Optional[FusedNorm] = None):
     """Row-parallel GEMM + all-reduce over NVLink, or None when that path does not apply.
 
     Decode-sized GEMMs (split-K > 1) run as two launches: the split-K tcgen05 GEMM writes fp32 partials and
@@ -69,10 +97,10 @@ def fused_gemm_all_reduce(x: torch.Tensor, w: torch.Tensor, bias):
     out = torch.empty(T, F, dtype=x.dtype, device=x.device)
     if splits > 1:
         part = linear_partials(x2, w, splits)
-        _custom_allreduce.splitk_all_reduce(part, splits, T, F, bias, out)
+        _custom_allreduce.splitk_all_reduce(part, splits, T, F, bias, out, norm=norm)
     else:
         y = linear(x2, w, bias, splits=1)
-        _custom_allreduce.all_reduce(y, out)
+        _custom_allreduce.all_reduce(y, out, norm=norm)
     return out.view(*x.shape[:-1], F)
 
 

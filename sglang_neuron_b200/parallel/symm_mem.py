@@ -51,7 +51,9 @@ class NvlsAllReduce:
         return (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.numel() % 8 == 0
                 and x.numel() * 2 <= self.capacity)
 
-    def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    supports_norm = False  # the fused residual + RMSNorm epilogue is on the IPC kernels only
+
+    def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, norm=None) -> torch.Tensor:
         if out is None:
             out = torch.empty_like(x)
         kernels().nvls_allreduce(out, x, self.uc, self.mc, self.capacity, self.rank, self.world, self.max_ctas,
@@ -59,7 +61,7 @@ class NvlsAllReduce:
         return out
 
     def combine_all_reduce(self, out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor,
-                           w: torch.Tensor) -> torch.Tensor:
+                           w: torch.Tensor, norm=None) -> torch.Tensor:
         kernels().nvls_combine_allreduce(out, y, inv_map, w, self.uc, self.mc, self.capacity, self.rank,
                                          self.world, self.max_ctas, self.status)
         return out
@@ -68,7 +70,7 @@ class NvlsAllReduce:
         return False
 
     def splitk_all_reduce(self, partial: torch.Tensor, splits: int, T: int, F: int,
-                          bias: Optional[torch.Tensor], out: torch.Tensor) -> torch.Tensor:
+                          bias: Optional[torch.Tensor], out: torch.Tensor, norm=None) -> torch.Tensor:
         kernels().nvls_splitk_allreduce(out, partial, splits, bias, self.uc, self.mc, self.capacity, self.rank,
                                         self.world, self.max_ctas, self.status)
         return out
@@ -111,20 +113,34 @@ class IpcAllReduce:
         return (x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.numel() % 8 == 0
                 and x.numel() * 2 <= self.capacity)
 
-    def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    supports_norm = True
+
+    @staticmethod
+    def _norm_kw(norm):
+        """Fused residual add + RMSNorm arguments (FusedNorm), marked as applied."""
+        if norm is None:
+            return {}
+        norm.done = True
+        return {"residual": norm.residual, "weight": norm.weight, "eps": norm.eps}
+
+    def all_reduce(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, norm=None) -> torch.Tensor:
+        """norm (parallel.collectives.FusedNorm): out receives rmsnorm(sum + residual) and the residual is
+        updated in place, in the same launch."""
         if out is None:
             out = torch.empty_like(x)
         nvec = x.numel() // 8
         ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))  # ~4 KB per CTA: many SMs drive NVLink
-        kernels().one_shot_allreduce(out, x, self.ptrs, self.rank, self.capacity, ctas, self.status)
+        kernels().one_shot_allreduce(out, x, self.ptrs, self.rank, self.capacity, ctas, self.status,
+                                     **self._norm_kw(norm))
         return out
 
     def combine_all_reduce(self, out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor,
-                           w: torch.Tensor) -> torch.Tensor:
+                           w: torch.Tensor, norm=None) -> torch.Tensor:
         """MoE combine (weighted sum of this rank's expert rows per token) fused with the all-reduce."""
         nvec = out.numel() // 8
         ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))
-        kernels().moe_combine_allreduce(out, y, inv_map, w, self.ptrs, self.rank, self.capacity, ctas, self.status)
+        kernels().moe_combine_allreduce(out, y, inv_map, w, self.ptrs, self.rank, self.capacity, ctas, self.status,
+                                        **self._norm_kw(norm))
         return out
 
     def gemm_can_run(self, T: int, F: int, num_sms: int) -> bool:
@@ -144,11 +160,12 @@ class IpcAllReduce:
         return out
 
     def splitk_all_reduce(self, partial: torch.Tensor, splits: int, T: int, F: int,
-                          bias: Optional[torch.Tensor], out: torch.Tensor) -> torch.Tensor:
+                          bias: Optional[torch.Tensor], out: torch.Tensor, norm=None) -> torch.Tensor:
         """Sum split-K partials (+ bias), all-reduce over the group: one launch after the split-K GEMM."""
         nvec = T * F // 8
         ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))
-        kernels().splitk_allreduce(out, partial, splits, bias, self.ptrs, self.rank, self.capacity, ctas, self.status)
+        kernels().splitk_allreduce(out, partial, splits, bias, self.ptrs, self.rank, self.capacity, ctas, self.status,
+                                   **self._norm_kw(norm))
         return out
 
     def close(self) -> None:

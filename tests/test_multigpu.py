@@ -153,6 +153,88 @@ def _nvls_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
+def _ar_norm_worker(rank, world, port, q):
+    """All-reduce + residual add + RMSNorm in one launch (one-shot, split-K GEMM, MoE combine forms) against
+    NCCL all-reduce + the fp32 add + norm."""
+    _init(rank, world, port)
+    import torch.distributed as dist
+    from sglang_neuron_b200.parallel.collectives import FusedNorm, fused_gemm_all_reduce, set_custom_allreduce
+    from sglang_neuron_b200.parallel.state import initialize_parallel
+    from sglang_neuron_b200.parallel.symm_mem import IpcAllReduce
+    initialize_parallel(world, device=torch.device("cuda", rank))
+    ar = IpcAllReduce(capacity_bytes=4 << 20)
+    set_custom_allreduce(ar)
+    errs = []
+
+    class Norm:
+        def __init__(self, H, g):
+            self.weight = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
+            self.eps = 1e-5
+
+    def ref_norm(s, res, nm):
+        v = s + res.float()
+        return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + nm.eps) * nm.weight.float(), v
+
+    def check(out, res_after, s, res_before, nm):
+        want, v = ref_norm(s, res_before, nm)
+        errs.append(((out.float() - want).abs().max() / want.abs().max()).item())
+        errs.append(((res_after.float() - v).abs().max() / v.abs().max()).item())
+
+    for T, H in [(64, 2880), (1, 2880), (13, 4096), (200, 1024)]:
+        g = torch.Generator(device="cuda").manual_seed(5 * T + rank)
+        gw = torch.Generator(device="cuda").manual_seed(99 + T)  # same weight on every rank
+        nm = Norm(H, gw)
+        x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+        res = torch.randn(T, H, generator=gw, device="cuda").to(torch.bfloat16)
+        s = x.float()
+        dist.all_reduce(s)
+        res0 = res.clone()
+        fn = FusedNorm.offer(res, nm)
+        out = ar.all_reduce(x, norm=fn)
+        torch.cuda.synchronize()
+        assert fn.done
+        check(out, res, s, res0, nm)
+        # split-K GEMM partials + bias + all-reduce + add + norm
+        Kl = 512
+        xa = torch.randn(T, Kl, device="cuda", generator=g).to(torch.bfloat16)
+        wt = (torch.randn(H, Kl, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        s = xa.float() @ wt.float().t()
+        dist.all_reduce(s)
+        res0 = res.clone()
+        fn = FusedNorm.offer(res, nm)
+        out = fused_gemm_all_reduce(xa, wt, None, norm=fn)
+        torch.cuda.synchronize()
+        if out is not None and fn.done:
+            check(out, res, s, res0, nm)
+    # MoE combine + all-reduce + add + norm
+    from sglang_neuron_b200.ops.moe import MoEAlignment, moe_align, moe_combine, topk_route
+    T, H, E = 64, 2880, 16
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    gw = torch.Generator(device="cuda").manual_seed(1234)
+    nm = Norm(H, gw)
+    res = torch.randn(T, H, generator=gw, device="cuda").to(torch.bfloat16)
+    w, ids = topk_route(torch.randn(T, E, device="cuda", generator=g), 4)
+    al = MoEAlignment(T * 4, E // world, 16, "cuda")
+    moe_align(ids, rank * (E // world), E // world, al)
+    y = torch.randn(al.r_max, H, device="cuda", generator=g).to(torch.bfloat16)
+    comb = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    moe_combine(comb, y, al.inv_map, w)
+    s = comb.float()
+    dist.all_reduce(s)
+    res0 = res.clone()
+    fn = FusedNorm.offer(res, nm)
+    out = torch.empty(T, H, device="cuda", dtype=torch.bfloat16)
+    ar.combine_all_reduce(out, y, al.inv_map[: T * 4], w, norm=fn)
+    torch.cuda.synchronize()
+    check(out, res, s, res0, nm)
+    set_custom_allreduce(None)
+    status = int(ar.status[0])
+    ar.close()
+    q.put((rank, errs, status))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def _engine_worker(rank, world, port, q):
     _init(rank, world, port)
     import torch.distributed as dist
@@ -174,11 +256,37 @@ def _engine_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def _spawn(fn, world):
+def _logits_worker(rank, world, port, q, extra):
+    """Prefill logits of one 40-token and one 9-token prompt (max_new_tokens=1) under a layout `extra`."""
+    if world > 1:
+        _init(rank, world, port)
+    import torch.distributed as dist
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.server_args import ServerArgs
+    mc.PRESETS["mg-oss"] = dict(mc.PRESETS["gpt-oss-120b"], num_hidden_layers=2, vocab_size=2048, hidden_size=512,
+                                intermediate_size=256, num_local_experts=8, num_attention_heads=8,
+                                num_key_value_heads=2, head_dim=64, sliding_window=16)
+    eng = Engine(ServerArgs(model="mg-oss", tp_size=extra.pop("tp", world), page_size=16, context_length=256,
+                            max_running_requests=4, chunked_prefill_size=64, disable_cuda_graph=True,
+                            random_weight_std=0.05, random_gen_device="cpu", **extra))
+    rows = []
+    eng.runner.logits_hook = lambda fb, lg: rows.append(lg[:, :2048].float().cpu())
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, 2048, (n,), generator=g).tolist() for n in (40, 9)]
+    eng.generate(prompts, {"max_new_tokens": 1})
+    eng.shutdown()
+    q.put((rank, torch.cat(rows, 0) if rows else None))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _spawn(fn, world, *args):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    ps = [ctx.Process(target=fn, args=(r, world, port, q) + args) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -199,6 +307,14 @@ def test_one_shot_allreduce_matches_nccl():
 
 
 @needs2
+def test_allreduce_with_fused_residual_norm_matches_nccl():
+    res = _spawn(_ar_norm_worker, 2)
+    for rank, (errs, status) in res.items():
+        assert status == 0, f"rank {rank}: bounded wait expired"
+        assert len(errs) >= 12 and max(errs) < 2e-2, f"rank {rank}: {errs}"
+
+
+@needs2
 def test_nvls_allreduce_matches_nccl():
     res = _spawn(_nvls_worker, 2)
     for rank, (errs, status) in res.items():
@@ -213,3 +329,28 @@ def test_tp2_engine_ranks_agree():
     res = _spawn(_engine_worker, 2)
     assert res[0][0] == res[1][0]
     assert all(len(o) == 8 for o in res[0][0])
+
+
+def _rel(a, b):
+    return ((a - b).norm() / b.norm()).item()
+
+
+@needs2
+def test_sequence_parallel_prefill_tracks_all_reduce_prefill():
+    """TP=2 prefill with every step sequence-parallel (NCCL reduce-scatter / all-gather between layers)
+    against the all-reduce layout: same logits up to bf16 summation order."""
+    ar = _spawn(_logits_worker, 2, {"sp_min_tokens": 0})
+    sp = _spawn(_logits_worker, 2, {"sp_min_tokens": 1})
+    for r in (0, 1):
+        assert _rel(sp[r][0], ar[r][0]) < 2e-2
+
+
+@needs2
+def test_dp_attention_prefill_tracks_single_gpu():
+    """Two attention groups of one GPU each (request 0 on GPU 0, request 1 on GPU 1, experts split over
+    both, token rows exchanged around each MoE block) against one GPU running both requests."""
+    one = _spawn(_logits_worker, 1, {"tp": 1})[0][0]
+    dp = _spawn(_logits_worker, 2, {"dp_size": 2, "enable_dp_attention": True})
+    assert dp[0][0].shape[0] == 1 and dp[1][0].shape[0] == 1
+    assert _rel(dp[0][0], one[0:1]) < 2e-2
+    assert _rel(dp[1][0], one[1:2]) < 2e-2
