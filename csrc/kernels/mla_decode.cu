@@ -10,6 +10,11 @@
 // shuffle reductions) and publish P (bf16) and the rescale factor; each warp then owns 128 of the 512 value
 // columns and accumulates P V. Splits write normalised partials + log-sum-exp, merged by a second kernel.
 //
+// Extend (prefill / chunked prefill, `qo_indptr` given): the 16 M rows of a CTA are 16 consecutive
+// (query token, head) pairs of one request (token-major), each with its own causal limit prefix + t + 1;
+// the CTA walks the context up to its last row's limit. One query token per request with all its heads is
+// the decode case, so both share the tile pipeline.
+//
 // Parity: the reference's `paged_absorbed_mla` decode (sglang_neuron/nki/deepseek_mla_decode.py:510:
 // 128-token tiles, online softmax, direct slot addressing) and its torch twin (ops/attention/mla.py:32).
 #include <torch/extension.h>
@@ -28,7 +33,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int SMEM_K = 2 * TT * RSK * 2;           // two stages
 constexpr int SMEM_SP = 4 * 16 * TT * 4;           // partial scores per warp
 constexpr int SMEM_P = 16 * RSP * 2;
-constexpr int SMEM_TOTAL = SMEM_K + SMEM_SP + SMEM_P + 3 * 16 * 4 + kMaxSplitPages * 4;
+constexpr int SMEM_TOTAL = SMEM_K + SMEM_SP + SMEM_P + 4 * 16 * 4 + kMaxSplitPages * 4;
 
 SNB_DEVICE void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -49,7 +54,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     const __nv_bfloat16* __restrict__ q, int q_stride, const __nv_bfloat16* __restrict__ cache,
     const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ seq_lens, int page_size,
     int H, float scale_log2, __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part,
-    float* __restrict__ lse_part, int num_splits) {
+    float* __restrict__ lse_part, int num_splits, const int32_t* __restrict__ qo_indptr) {
   snb::pdl_wait();
   snb::pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem[];
@@ -59,13 +64,25 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   float* alpha_s = reinterpret_cast<float*>(smem + SMEM_K + SMEM_SP + SMEM_P);  // [16]
   float* m_s = alpha_s + 16;
   float* l_s = m_s + 16;
-  int32_t* sbt = reinterpret_cast<int32_t*>(l_s + 16);
+  int32_t* lim_s = reinterpret_cast<int32_t*>(l_s + 16);  // per-row key limit (0: row unused)
+  int32_t* sbt = lim_s + 16;
 
   const int split = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, qd = lane & 3;
   const int h0 = hg * 16;
-  const int hn = min(16, H - h0);
-  const int ctx = seq_lens[b];
+  // rows of this CTA: decode -> heads h0.. of request b's token; extend -> (token, head) pairs h0..
+  const bool ext = qo_indptr != nullptr;
+  const int q0 = ext ? qo_indptr[b] : b;
+  const int nq = ext ? qo_indptr[b + 1] - q0 : 1;
+  const int nrows = ext ? nq * H - h0 : min(16, H - h0);
+  if (nrows <= 0) return;  // extend: this request has fewer rows than the grid's row groups
+  const int hn = min(16, nrows);
+  const int kv_len = seq_lens[b];
+  const int prefix = kv_len - nq;
+  auto row_tok = [&](int row) { return ext ? q0 + (h0 + row) / H : b; };
+  auto row_head = [&](int row) { return ext ? (h0 + row) % H : h0 + row; };
+  auto row_lim = [&](int row) { return row >= hn ? 0 : (ext ? prefix + (h0 + row) / H + 1 : kv_len); };
+  const int ctx = row_lim(hn - 1);  // the last row sees the most keys
   const int per = ((ctx + num_splits - 1) / num_splits + TT - 1) / TT * TT;
   const int s0 = split * per, s1 = min(ctx, s0 + per);
   const int ntiles = s0 < s1 ? (s1 - s0 + TT - 1) / TT : 0;
@@ -76,6 +93,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   if (tid < 16) {
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.f;
+    lim_s[tid] = row_lim(tid);
   }
   __syncthreads();
 
@@ -98,18 +116,23 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     cp_async_commit();
   };
 
-  // Q fragments of this warp's 9 k16 steps (rows = heads h0 + gq, h0 + gq + 8)
+  // Q fragments of this warp's 9 k16 steps (rows gq, gq + 8)
   uint32_t qa[9][4];
   {
-    const __nv_bfloat16* qb = q + (size_t)b * q_stride + (size_t)h0 * DK;
+    const __nv_bfloat16* qr[2];
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+      const int row = gq + rh * 8;
+      qr[rh] = row < hn ? q + (size_t)row_tok(row) * q_stride + (size_t)row_head(row) * DK : nullptr;
+    }
 #pragma unroll
     for (int kk = 0; kk < 9; ++kk) {
       const int k0 = (warp * 9 + kk) * 16;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int row = gq + (r & 1) * 8;
         const int col = k0 + qd * 2 + (r >> 1) * 8;
-        qa[kk][r] = row < hn ? *reinterpret_cast<const uint32_t*>(qb + (size_t)row * DK + col) : 0u;
+        const __nv_bfloat16* p = qr[r & 1];
+        qa[kk][r] = p != nullptr ? *reinterpret_cast<const uint32_t*>(p + col) : 0u;
       }
     }
   }
@@ -148,7 +171,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
         const int col = c4 + j;
         float v = sp[row * TT + col] + sp[(16 + row) * TT + col] + sp[(32 + row) * TT + col] +
                   sp[(48 + row) * TT + col];
-        v = (t0 + col < s1 && row < hn) ? v * scale_log2 : -INFINITY;
+        v = (t0 + col < s1 && t0 + col < lim_s[row]) ? v * scale_log2 : -INFINITY;
         s[j] = v;
         mx = fmaxf(mx, v);
       }
@@ -216,13 +239,14 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     if (row >= hn) continue;
     const float L = l_s[row], M = m_s[row];
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int h = h0 + row;
+    const int h = row_head(row);
+    const int tok = row_tok(row);
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       const int col = warp * 128 + n * 8 + qd * 2;
       const float x0 = o[n][rh * 2] * inv, x1 = o[n][rh * 2 + 1] * inv;
       if (num_splits == 1) {
-        *reinterpret_cast<__nv_bfloat162*>(out + (size_t)b * out_stride + (size_t)h * DV + col) =
+        *reinterpret_cast<__nv_bfloat162*>(out + (size_t)tok * out_stride + (size_t)h * DV + col) =
             __floats2bfloat162_rn(x0, x1);
       } else {
         const size_t pidx = ((size_t)b * H + h) * num_splits + split;
@@ -282,8 +306,39 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
                                  (int)q.stride(0), (const __nv_bfloat16*)cache.data_ptr(),
                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                  seq_lens.data_ptr<int32_t>(), (int)page_size, H, (float)sm_scale * kLog2e,
-                                 (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), op, lp, S));
+                                 (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), op, lp, S,
+                                 (const int32_t*)nullptr));
   if (S > 1)
     C10_CUDA_CHECK(snb::launch_pdl(mla_merge_kernel, B * H, 128, 0, st, (const float*)op, (const float*)lp,
                                    (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), H, S));
+}
+
+// Extend: q [T, H, 576] for the new tokens of B requests (rows qo_indptr[b] .. qo_indptr[b+1]), whose latent
+// rows are already in the cache; seq_lens[b] = prefix + new tokens. out: [T, H, 512].
+void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
+                torch::Tensor seq_lens, torch::Tensor qo_indptr, int64_t max_extend, int64_t page_size,
+                double sm_scale) {
+  const int T = q.size(0), H = q.size(1), B = seq_lens.size(0);
+  if (T == 0 || B == 0) return;
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "mla_extend: bf16");
+  TORCH_CHECK(q.size(2) == DK && cache.size(-1) == DK && q.stride(2) == 1 && q.stride(1) == DK, "mla_extend: q");
+  TORCH_CHECK(out.size(2) == DV && out.stride(1) == DV && out.stride(2) == 1, "mla_extend: out");
+  TORCH_CHECK(cache.is_contiguous() && (reinterpret_cast<uintptr_t>(cache.data_ptr()) % 16) == 0, "mla_extend: cache");
+  TORCH_CHECK(qo_indptr.scalar_type() == at::kInt && qo_indptr.numel() == B + 1, "mla_extend: qo_indptr");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && block_table.scalar_type() == at::kInt, "mla_extend: int32 tables");
+  auto st = at::cuda::getCurrentCUDAStream();
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL));
+    attr = true;
+  }
+  const int64_t groups = (std::max<int64_t>(1, max_extend) * H + 15) / 16;
+  TORCH_CHECK(groups <= 65535, "mla_extend: too many rows per request");
+  dim3 grid(1, (unsigned)groups, B);
+  C10_CUDA_CHECK(snb::launch_pdl(mla_decode_kernel, grid, kThr, SMEM_TOTAL, st, (const __nv_bfloat16*)q.data_ptr(),
+                                 (int)q.stride(0), (const __nv_bfloat16*)cache.data_ptr(),
+                                 block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
+                                 seq_lens.data_ptr<int32_t>(), (int)page_size, H, (float)sm_scale * kLog2e,
+                                 (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), (float*)nullptr,
+                                 (float*)nullptr, 1, qo_indptr.data_ptr<int32_t>()));
 }

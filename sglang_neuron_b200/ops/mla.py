@@ -44,6 +44,17 @@ def mla_decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, 
     return out
 
 
+def mla_extend(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
+               qo_indptr: torch.Tensor, max_extend: int, page_size: int, scale: float) -> torch.Tensor:
+    """Prefill / chunked-prefill absorbed MLA on tensor cores: q [T, H, 576] of the new tokens (their latent
+    rows already written) -> [T, H, 512]; causal within each request's chunk, full over its prefix.
+    Parity: the reference's `prefill_absorbed_mla_cte` (sglang_neuron/nki/deepseek_mla_prefill.py:437)."""
+    out = torch.empty(q.shape[0], q.shape[1], 512, dtype=q.dtype, device=q.device)
+    kernels().mla_extend(out, q.contiguous(), cache, block_table, seq_lens, qo_indptr, int(max_extend), page_size,
+                         scale)
+    return out
+
+
 def _one(q, cache, bt_row, L, q_pos, r, scale, page_size):
     n_pages = (L + page_size - 1) // page_size
     kv = cache[bt_row[:n_pages].long(), 0].reshape(n_pages * page_size, -1)[:L].float()  # [L, r+rope]
@@ -67,6 +78,8 @@ def mla_attention(q: torch.Tensor, cache: torch.Tensor, fb: ForwardBatch, r: int
     if fb.is_decode and mla_kernel_ok(q, cache, r):
         splits = fb.decode_splits or mla_num_splits(q.shape[0], q.shape[1], fb.max_seq_len or 4096)
         return mla_decode(q, cache, fb.block_table, fb.seq_lens, page_size, scale, splits)
+    if not fb.is_decode and mla_kernel_ok(q, cache, r) and fb.qo_indptr is not None and fb.max_extend > 0:
+        return mla_extend(q, cache, fb.block_table, fb.seq_lens, fb.qo_indptr, fb.max_extend, page_size, scale)
     seq = fb.seq_lens.tolist()
     if fb.is_decode:
         for b, L in enumerate(seq):

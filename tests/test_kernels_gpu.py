@@ -327,3 +327,34 @@ def test_mla_decode_kernel(H, ctx, splits, P):
                      scale, splits)
     torch.cuda.synchronize()
     _close(out, ref, 2e-2, 2e-2, "mla_decode")
+
+
+@pytest.mark.parametrize("H,chunks,P", [(16, [(0, 37), (100, 5), (16, 64)], 16), (2, [(0, 130), (33, 1), (7, 40)], 16),
+                                        (4, [(250, 90)], 64)])
+def test_mla_extend_kernel(H, chunks, P):
+    """Absorbed-MLA prefill on tensor cores (rows = (token, head) pairs, per-row causal limits) vs the fp32
+    PyTorch reference, for chunks with and without a cached prefix; NaN poison past each request's end."""
+    from sglang_neuron_b200.ops.mla import _one, mla_extend
+    torch.manual_seed(17)
+    B = len(chunks)
+    lens = [p + n for p, n in chunks]
+    max_pages = max((L + P - 1) // P for L in lens) + 1
+    n_pages = B * max_pages + 2
+    perm = torch.randperm(n_pages - 1)[: B * max_pages] + 1
+    bt = perm.view(B, max_pages).to(torch.int32)
+    cache = (torch.randn(n_pages, 1, P, 576) * 0.5).to(torch.bfloat16)
+    for b, L in enumerate(lens):
+        for t in range(L, ((L + P - 1) // P) * P):
+            cache[int(bt[b, t // P]), 0, t % P] = float("nan")
+    T = sum(n for _, n in chunks)
+    q = (torch.randn(T, H, 576) * 0.5).to(torch.bfloat16)
+    qo = [0]
+    for _, n in chunks:
+        qo.append(qo[-1] + n)
+    scale = 0.0625
+    ref = torch.cat([_one(q[qo[b]:qo[b + 1]].float(), cache.float(), bt[b], lens[b],
+                          torch.arange(chunks[b][0], lens[b]), 512, scale, P) for b in range(B)])
+    out = mla_extend(q.to(DEV), cache.to(DEV), bt.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV),
+                     torch.tensor(qo, dtype=torch.int32, device=DEV), max(n for _, n in chunks), P, scale)
+    torch.cuda.synchronize()
+    _close(out, ref, 2e-2, 2e-2, "mla_extend")
