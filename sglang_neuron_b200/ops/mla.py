@@ -49,6 +49,7 @@ def mla_extend(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, 
     """Prefill / chunked-prefill absorbed MLA on tensor cores: q [T, H, 576] of the new tokens (their latent
     rows already written) -> [T, H, 512]; causal within each request's chunk, full over its prefix.
     Parity: the reference's `prefill_absorbed_mla_cte` (sglang_neuron/nki/deepseek_mla_prefill.py:437)."""
+    from .._ext import kernels
     out = torch.empty(q.shape[0], q.shape[1], 512, dtype=q.dtype, device=q.device)
     kernels().mla_extend(out, q.contiguous(), cache, block_table, seq_lens, qo_indptr, int(max_extend), page_size,
                          scale)
