@@ -7,6 +7,7 @@ Parity: the reference's traced collectives (sglang_neuron/parallel/collectives.p
 from __future__ import annotations
 
 import contextlib
+import os
 from typing import Optional
 
 import torch
@@ -16,6 +17,7 @@ from .state import get_state
 
 _custom_allreduce = None
 _defer = [0]  # > 0 inside deferred_reduction(): TP reductions are left to the caller
+_FUSED_NORM = os.environ.get("SGLANG_B200_FUSED_AR_NORM", "1") != "0"
 
 
 def set_custom_allreduce(comm) -> None:
@@ -38,7 +40,7 @@ class FusedNorm:
         """A FusedNorm when the fused path can apply to rows like `residual`, else None."""
         st = get_state()
         ar = _custom_allreduce
-        if (residual is None or norm_module is None or st.tp_size == 1 or _defer[0] or ar is None
+        if (residual is None or not _FUSED_NORM or norm_module is None or st.tp_size == 1 or _defer[0] or ar is None
                 or not getattr(ar, "supports_norm", False) or not residual.is_cuda
                 or residual.dtype != torch.bfloat16 or not residual.is_contiguous()):
             return None
