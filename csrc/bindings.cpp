@@ -48,7 +48,7 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
 void set_pdl(bool on);
 void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
                 torch::Tensor seq_lens, torch::Tensor qo_indptr, int64_t max_extend, int64_t page_size,
-                double sm_scale);
+                double sm_scale, int64_t dcp_size, int64_t dcp_rank, c10::optional<torch::Tensor> lse_out);
 void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
                 torch::Tensor seq_lens, int64_t page_size, double sm_scale, int64_t num_splits, torch::Tensor o_part,
                 torch::Tensor lse_part);
@@ -120,7 +120,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
   m.def("set_pdl", &set_pdl);
   m.def("mla_decode", &mla_decode);
-  m.def("mla_extend", &mla_extend);
+  m.def("mla_extend", &mla_extend, py::arg("out"), py::arg("q"), py::arg("cache"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("qo_indptr"), py::arg("max_extend"), py::arg("page_size"), py::arg("sm_scale"),
+        py::arg("dcp_size") = 1, py::arg("dcp_rank") = 0, py::arg("lse_out") = py::none());
   m.def("kv_page_copy", &kv_page_copy);
   m.def("nvls_flag_bytes", &nvls_flag_bytes);
   m.def("nvls_allreduce", &nvls_allreduce);

@@ -15,6 +15,11 @@
 // the CTA walks the context up to its last row's limit. One query token per request with all its heads is
 // the decode case, so both share the tile pipeline.
 //
+// Decode context parallelism (dcp_size D > 1): logical page j of a request lives on DCP rank j % D, and the
+// block table given here lists only this rank's pages (local page i = logical page i * D + dcp_rank). Keys
+// are walked in that local order; causal limits are compared against each key's logical position. With
+// `lse_out` the kernel also writes each row's log2-sum-exp, so the D ranks' partials can be merged.
+//
 // Parity: the reference's `paged_absorbed_mla` decode (sglang_neuron/nki/deepseek_mla_decode.py:510:
 // 128-token tiles, online softmax, direct slot addressing) and its torch twin (ops/attention/mla.py:32).
 #include <torch/extension.h>
@@ -54,7 +59,8 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     const __nv_bfloat16* __restrict__ q, int q_stride, const __nv_bfloat16* __restrict__ cache,
     const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ seq_lens, int page_size,
     int H, float scale_log2, __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part,
-    float* __restrict__ lse_part, int num_splits, const int32_t* __restrict__ qo_indptr) {
+    float* __restrict__ lse_part, int num_splits, const int32_t* __restrict__ qo_indptr, int dcp_size, int dcp_rank,
+    float* __restrict__ lse_out) {
   snb::pdl_wait();
   snb::pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem[];
@@ -82,7 +88,17 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   auto row_tok = [&](int row) { return ext ? q0 + (h0 + row) / H : b; };
   auto row_head = [&](int row) { return ext ? (h0 + row) % H : h0 + row; };
   auto row_lim = [&](int row) { return row >= hn ? 0 : (ext ? prefix + (h0 + row) / H + 1 : kv_len); };
-  const int ctx = row_lim(hn - 1);  // the last row sees the most keys
+  // keys of this DCP rank among logical positions [0, lim): whole local pages + the partial last page
+  auto local_count = [&](int lim) {
+    if (dcp_size == 1) return lim;
+    const int full = lim / page_size, rem = lim % page_size;
+    const int nfull = full > dcp_rank ? (full - dcp_rank + dcp_size - 1) / dcp_size : 0;
+    return nfull * page_size + ((rem > 0 && full % dcp_size == dcp_rank) ? rem : 0);
+  };
+  auto logical = [&](int v) {
+    return dcp_size == 1 ? v : ((v / page_size) * dcp_size + dcp_rank) * page_size + v % page_size;
+  };
+  const int ctx = local_count(row_lim(hn - 1));  // the last row sees the most keys
   const int per = ((ctx + num_splits - 1) / num_splits + TT - 1) / TT * TT;
   const int s0 = split * per, s1 = min(ctx, s0 + per);
   const int ntiles = s0 < s1 ? (s1 - s0 + TT - 1) / TT : 0;
@@ -171,7 +187,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
         const int col = c4 + j;
         float v = sp[row * TT + col] + sp[(16 + row) * TT + col] + sp[(32 + row) * TT + col] +
                   sp[(48 + row) * TT + col];
-        v = (t0 + col < s1 && t0 + col < lim_s[row]) ? v * scale_log2 : -INFINITY;
+        v = (t0 + col < s1 && logical(t0 + col) < lim_s[row]) ? v * scale_log2 : -INFINITY;
         s[j] = v;
         mx = fmaxf(mx, v);
       }
@@ -248,6 +264,8 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
       if (num_splits == 1) {
         *reinterpret_cast<__nv_bfloat162*>(out + (size_t)tok * out_stride + (size_t)h * DV + col) =
             __floats2bfloat162_rn(x0, x1);
+        if (lse_out != nullptr && warp == 0 && n == 0 && qd == 0)
+          lse_out[(size_t)tok * H + h] = L > 0.f ? M + log2f(L) : -INFINITY;
       } else {
         const size_t pidx = ((size_t)b * H + h) * num_splits + split;
         o_part[pidx * DV + col] = x0;
@@ -307,7 +325,7 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                  seq_lens.data_ptr<int32_t>(), (int)page_size, H, (float)sm_scale * kLog2e,
                                  (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), op, lp, S,
-                                 (const int32_t*)nullptr));
+                                 (const int32_t*)nullptr, 1, 0, (float*)nullptr));
   if (S > 1)
     C10_CUDA_CHECK(snb::launch_pdl(mla_merge_kernel, B * H, 128, 0, st, (const float*)op, (const float*)lp,
                                    (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), H, S));
@@ -315,9 +333,11 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
 
 // Extend: q [T, H, 576] for the new tokens of B requests (rows qo_indptr[b] .. qo_indptr[b+1]), whose latent
 // rows are already in the cache; seq_lens[b] = prefix + new tokens. out: [T, H, 512].
+// dcp_size > 1: block_table holds this rank's pages only (see the kernel); lse_out [T, H] fp32 receives the
+// rows' log2-sum-exp of the scaled scores (-inf for rows with no local key).
 void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
                 torch::Tensor seq_lens, torch::Tensor qo_indptr, int64_t max_extend, int64_t page_size,
-                double sm_scale) {
+                double sm_scale, int64_t dcp_size, int64_t dcp_rank, c10::optional<torch::Tensor> lse_out) {
   const int T = q.size(0), H = q.size(1), B = seq_lens.size(0);
   if (T == 0 || B == 0) return;
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "mla_extend: bf16");
@@ -332,6 +352,10 @@ void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
     C10_CUDA_CHECK(cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL));
     attr = true;
   }
+  TORCH_CHECK(dcp_size >= 1 && dcp_rank >= 0 && dcp_rank < dcp_size, "mla_extend: dcp rank");
+  if (lse_out)
+    TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->is_contiguous() && lse_out->numel() >= (int64_t)T * H,
+                "mla_extend: lse_out");
   const int64_t groups = (std::max<int64_t>(1, max_extend) * H + 15) / 16;
   TORCH_CHECK(groups <= 65535, "mla_extend: too many rows per request");
   dim3 grid(1, (unsigned)groups, B);
@@ -340,5 +364,6 @@ void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                  seq_lens.data_ptr<int32_t>(), (int)page_size, H, (float)sm_scale * kLog2e,
                                  (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), (float*)nullptr,
-                                 (float*)nullptr, 1, qo_indptr.data_ptr<int32_t>()));
+                                 (float*)nullptr, 1, qo_indptr.data_ptr<int32_t>(), (int)dcp_size, (int)dcp_rank,
+                                 lse_out ? lse_out->data_ptr<float>() : (float*)nullptr));
 }

@@ -51,8 +51,11 @@ class Engine:
             device = torch.device("cuda", local)
         else:
             device = torch.device("cpu")
+        if args.dcp_size > 1 and not self.cfg.is_mla:
+            raise ValueError("decode context parallelism splits the latent (MLA) KV pool; "
+                             f"{self.cfg.architecture} has none")
         st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device, pp_size=args.pp_size,
-                                 dp_attention=args.enable_dp_attention)
+                                 dp_attention=args.enable_dp_attention, dcp_size=args.dcp_size)
         self.rank = st.rank
         self.custom_ar = None
         if st.tp_size > 1 and device.type == "cuda":

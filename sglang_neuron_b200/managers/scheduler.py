@@ -36,7 +36,11 @@ class Scheduler:
         self.cfg = cfg
         self.runner = runner
         self.P = args.page_size
-        self.alloc = make_page_allocator(runner.num_pages, self.P, reserved=1)
+        if get_state().dcp_size > 1:
+            from ..parallel.dcp import DcpPageAllocator
+            self.alloc = DcpPageAllocator(runner.num_pages, self.P, get_state().dcp_size)
+        else:
+            self.alloc = make_page_allocator(runner.num_pages, self.P, reserved=1)
         self.radix = None if args.disable_radix_cache else RadixCacheHandle(self.P)
         self.swa = None
         if getattr(runner, "swa_num_pages", 0):
@@ -137,19 +141,22 @@ class Scheduler:
 
     # ------------------------------------------------------------------------------------------
     # page management
-    def _alloc_pages(self, n: int) -> Optional[List[int]]:
+    def _alloc_pages(self, n: int, start: int = 0) -> Optional[List[int]]:
+        """n pages for a request's logical pages start .. start + n - 1 (the index picks the owner rank under
+        decode context parallelism)."""
         if n <= 0:
             return []
-        pages = self.alloc.alloc(n)
+        dcp = hasattr(self.alloc, "alloc_at")
+        pages = self.alloc.alloc_at(start, n) if dcp else self.alloc.alloc(n)
         if len(pages) == n:
             return list(pages)
         if self.radix is not None:
-            freed = self.radix.evict(n - self.alloc.available())
+            freed = self.radix.evict(max(n - self.alloc.available(), n if dcp else 0))
             if freed:
                 if self.hicache is not None:
                     self.hicache.sync_writes()  # host copies of these pages must land before reuse
                 self.alloc.free(list(freed))
-            pages = self.alloc.alloc(n)
+            pages = self.alloc.alloc_at(start, n) if dcp else self.alloc.alloc(n)
             if len(pages) == n:
                 return list(pages)
         return None
@@ -165,7 +172,7 @@ class Scheduler:
             swa = self.swa.alloc_for(need)
             if swa is None:
                 return False
-        pages = self._alloc_pages(need)
+        pages = self._alloc_pages(need, len(r.pages))
         if pages is None:
             if swa:
                 self.swa.undo(swa)

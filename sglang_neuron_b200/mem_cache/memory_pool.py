@@ -74,6 +74,7 @@ class MLATokenToKVPool:
         self.layer_ids = list(range(num_layers)) if layer_ids is None else list(layer_ids)
         self.buffers = [torch.zeros(shape, dtype=dtype, device=device) for _ in self.layer_ids]
         self._index = {lid: i for i, lid in enumerate(self.layer_ids)}
+        self.dcp = None  # parallel.dcp.DcpView when the context's pages are split over DCP ranks
 
     def kv(self, layer_id: int):
         b = self.buffers[self._index[layer_id]]

@@ -262,14 +262,19 @@ class ModelRunner:
             reserve = 6 * (1 << 30) + int(0.04 * total)
             budget = max(0, int(free * args.mem_fraction_static) - reserve - swa_bytes)
             num_pages = max(2, budget // per_page)
-            cap = (self.max_reqs * self.max_pages_per_req) + 1
+            cap = (self.max_reqs * self.max_pages_per_req) // get_state().dcp_size + self.max_reqs + 2
             num_pages = min(num_pages, max(cap, 2))
         else:
-            num_pages = (self.max_reqs * self.max_pages_per_req) + 1
+            # decode context parallelism: each rank holds 1/dcp of every context (+ a partial page each)
+            D = get_state().dcp_size
+            num_pages = (self.max_reqs * self.max_pages_per_req) // D + (self.max_reqs + 2 if D > 1 else 1)
         self.num_pages = int(num_pages)
         if cfg.is_mla:
             self.kv_pool = MLATokenToKVPool(n_layers, self.num_pages, P, cfg.kv_lora_rank,
                                             cfg.qk_rope_head_dim, self.kv_dtype, self.device, layer_ids=layer_ids)
+            if get_state().dcp_size > 1:
+                from ..parallel.dcp import DcpView
+                self.kv_pool.dcp = DcpView(P)
         else:
             self.kv_pool = MHATokenToKVPool(len(layer_ids), self.num_pages, P, attn[0].num_kv_heads, cfg.head_dim,
                                             self.kv_dtype, self.device, layer_ids=layer_ids,

@@ -69,11 +69,18 @@ class MLAAttention(nn.Module):
         k_pe = apply_rope_ref(k_pe, fb.positions, self.cos_sin, self.rope, False).to(h.dtype)
         latent_row = torch.cat([c, k_pe.view(T, self.rope)], dim=-1)
         kc, _ = self.kv_cache()
-        mla_write_rows(kc, latent_row, fb.out_cache_loc, self.kv_pool.page_size)
+        dcp = getattr(self.kv_pool, "dcp", None)
+        # under decode context parallelism only the owner rank of a token's page stores its row
+        loc = dcp.local(fb)[1] if dcp is not None else fb.out_cache_loc
+        mla_write_rows(kc, latent_row, loc, self.kv_pool.page_size)
         # absorption: q_lat[t,h,:] = q_nope[t,h,:] @ W_UK[h]
         q_lat = torch.einsum("thn,hnr->thr", q[:, :, : self.nope].float(), self.w_uk.float()).to(h.dtype)
         qf = torch.cat([q_lat, q_pe], dim=-1)  # [T, H, r + rope]
-        o_lat = mla_attention(qf, kc, fb, self.r, self.scaling, self.kv_pool.page_size)  # [T, H, r]
+        if dcp is not None:
+            from ..parallel.dcp import dcp_mla_attention
+            o_lat = dcp_mla_attention(qf, kc, fb, self.r, self.scaling, self.kv_pool.page_size, dcp)
+        else:
+            o_lat = mla_attention(qf, kc, fb, self.r, self.scaling, self.kv_pool.page_size)  # [T, H, r]
         o = torch.einsum("thr,hvr->thv", o_lat.float(), self.w_uv.float()).to(h.dtype)
         return self.o_proj(o.reshape(T, self.num_heads * self.vd), norm=norm)
 

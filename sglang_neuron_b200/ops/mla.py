@@ -45,14 +45,17 @@ def mla_decode(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, 
 
 
 def mla_extend(q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
-               qo_indptr: torch.Tensor, max_extend: int, page_size: int, scale: float) -> torch.Tensor:
+               qo_indptr: torch.Tensor, max_extend: int, page_size: int, scale: float, dcp=(1, 0),
+               lse_out=None) -> torch.Tensor:
     """Prefill / chunked-prefill absorbed MLA on tensor cores: q [T, H, 576] of the new tokens (their latent
     rows already written) -> [T, H, 512]; causal within each request's chunk, full over its prefix.
+    dcp = (D, rank): block_table lists this rank's pages of a DCP-interleaved context (parallel/dcp.py);
+    lse_out [T, H] fp32 receives each row's log2-sum-exp.
     Parity: the reference's `prefill_absorbed_mla_cte` (sglang_neuron/nki/deepseek_mla_prefill.py:437)."""
     from .._ext import kernels
     out = torch.empty(q.shape[0], q.shape[1], 512, dtype=q.dtype, device=q.device)
     kernels().mla_extend(out, q.contiguous(), cache, block_table, seq_lens, qo_indptr, int(max_extend), page_size,
-                         scale)
+                         scale, int(dcp[0]), int(dcp[1]), lse_out)
     return out
 
 

@@ -51,6 +51,9 @@ class ParallelState:
     attn_dp_rank: int = 0
     moe_group: Optional[object] = None          # device group of all ranks (DP attention: MoE token exchange)
     dp_cross_group: Optional[object] = None     # ranks with this tp_rank in every attention group
+    dcp_size: int = 1                           # decode context parallelism: ranks sharing one latent KV
+    dcp_rank: int = 0
+    dcp_group: Optional[object] = None          # consecutive TP ranks tp_rank // dcp_size
 
     @property
     def is_first_rank(self) -> bool:
@@ -123,7 +126,7 @@ def init_process_group_from_env(backend: Optional[str] = None, timeout_s: int = 
 
 def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size: int = 1,
                         device: Optional[torch.device] = None, pp_size: int = 1,
-                        dp_attention: bool = False) -> ParallelState:
+                        dp_attention: bool = False, dcp_size: int = 1) -> ParallelState:
     """Build the groups. Ranks are laid out DP-major, then PP: rank = (dp_rank * pp_size + pp_rank) * tp_size
     + tp_rank. With dp_attention, dp_size attention groups split the tp_size ranks instead (one replica)."""
     if dp_attention and dp_size > 1:
@@ -159,10 +162,23 @@ def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size
         replica_group, replica_cpu_group = tp_group, cpu_group
     if device is None:
         device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    dcp_group = None
+    if dcp_size > 1:
+        if tp_size % dcp_size:
+            raise ValueError(f"dcp_size {dcp_size} must divide tp_size {tp_size}")
+        for d in range(dp_size):
+            for p_ in range(pp_size):
+                base = (d * pp_size + p_) * tp_size
+                for k in range(tp_size // dcp_size):
+                    ranks = list(range(base + k * dcp_size, base + (k + 1) * dcp_size))
+                    g = dist.new_group(ranks)
+                    if rank in ranks:
+                        dcp_group = g
     st = ParallelState(world_size=world, rank=rank, tp_size=tp_size, tp_rank=tp_rank, ep_size=ep_size,
                        ep_rank=tp_rank, dp_size=dp_size, dp_rank=dp_rank, tp_group=tp_group,
                        cpu_group=cpu_group, device=device, pp_size=pp_size, pp_rank=pp_rank,
-                       replica_group=replica_group, replica_cpu_group=replica_cpu_group)
+                       replica_group=replica_group, replica_cpu_group=replica_cpu_group,
+                       dcp_size=dcp_size, dcp_rank=tp_rank % dcp_size, dcp_group=dcp_group)
     set_state(st)
     return st
 

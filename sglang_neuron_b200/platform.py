@@ -35,6 +35,11 @@ def refuse_unserved(args, spec) -> None:
 
 
 def check_hybrid_swa(args) -> None:
+    if args.dcp_size > 1:
+        if (args.tp_size % args.dcp_size or args.enable_hierarchical_cache or args.disaggregation_mode != "null"
+                or args.speculative_algorithm or args.pp_size > 1 or args.enable_dp_attention):
+            raise ValueError("dcp_size must divide tp_size, and DCP is not served with the host KV tier, PD "
+                             "disaggregation, speculative decoding, pipeline parallelism or DP attention")
     if args.enable_dp_attention and args.dp_size > 1:
         if args.speculative_algorithm or args.disaggregation_mode != "null" or args.pp_size > 1:
             raise ValueError("DP attention is not served with speculative decoding, PD disaggregation or "

@@ -24,6 +24,7 @@ class ServerArgs:
     dp_size: int = 1                         # DP replicas, or attention groups inside TP with enable_dp_attention
     enable_dp_attention: bool = False        # dp_size attention groups split the tp_size ranks; experts span all
     pp_size: int = 1
+    dcp_size: int = 1                        # decode context parallelism (MLA models): TP ranks splitting each context's pages
     sp_min_tokens: int = 512                 # TP > 1: prefill steps of >= this many tokens run sequence-parallel between layers (0: off)
     page_size: int = 16
     kv_cache_dtype: str = "auto"             # auto | bf16 | fp8_e4m3

@@ -358,3 +358,50 @@ def test_mla_extend_kernel(H, chunks, P):
                      torch.tensor(qo, dtype=torch.int32, device=DEV), max(n for _, n in chunks), P, scale)
     torch.cuda.synchronize()
     _close(out, ref, 2e-2, 2e-2, "mla_extend")
+
+
+@pytest.mark.parametrize("D,H,chunks,P", [(2, 8, [(0, 37), (100, 1), (16, 64)], 16), (4, 4, [(250, 90), (3, 1)], 16)])
+def test_mla_extend_kernel_dcp_partials_merge(D, H, chunks, P):
+    """Decode context parallelism on one GPU: the D ranks' local page sets (logical page j on rank j % D)
+    are attended separately by the kernel with log2-sum-exp outputs; merging the partials gives attention
+    over the whole context (fp32 reference)."""
+    from sglang_neuron_b200.ops.mla import _one, mla_extend
+    from sglang_neuron_b200.parallel.dcp import merge_partials
+    torch.manual_seed(23)
+    B = len(chunks)
+    lens = [p + n for p, n in chunks]
+    n_log = max((L + P - 1) // P for L in lens) + 1
+    full = (torch.randn(B, n_log * P, 576) * 0.5).to(torch.bfloat16)
+    nxt = [1] * D
+    gbt = torch.zeros(B, n_log, dtype=torch.int32)
+    for b in range(B):
+        for j in range(n_log):
+            gbt[b, j] = nxt[j % D] * D + j % D
+            nxt[j % D] += 1
+    n_local = max(nxt) + 1
+    caches = [torch.zeros(n_local, 1, P, 576, dtype=torch.bfloat16) for _ in range(D)]
+    for b in range(B):
+        for t in range(n_log * P):
+            g = int(gbt[b, t // P])
+            caches[g % D][g // D, 0, t % P] = full[b, t] if t < lens[b] else float("nan")
+    T = sum(n for _, n in chunks)
+    q = (torch.randn(T, H, 576) * 0.5).to(torch.bfloat16)
+    qo = [0]
+    for _, n in chunks:
+        qo.append(qo[-1] + n)
+    scale = 0.0625
+    seq = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    qo_t = torch.tensor(qo, dtype=torch.int32, device=DEV)
+    os_, ls_ = [], []
+    for d in range(D):
+        lbt = torch.div(gbt[:, d::D], D, rounding_mode="floor").contiguous().to(DEV)
+        lse = torch.empty(T, H, dtype=torch.float32, device=DEV)
+        os_.append(mla_extend(q.to(DEV), caches[d].to(DEV), lbt, seq, qo_t, max(n for _, n in chunks), P, scale,
+                              dcp=(D, d), lse_out=lse))
+        ls_.append(lse)
+    got = merge_partials(torch.stack(os_), torch.stack(ls_))
+    torch.cuda.synchronize()
+    ref_cache = full.view(B, n_log, 1, P, 576).float()
+    ref = torch.cat([_one(q[qo[b]:qo[b + 1]].float(), ref_cache[b], torch.arange(n_log, dtype=torch.int32), lens[b],
+                          torch.arange(chunks[b][0], lens[b]), 512, scale, P) for b in range(B)])
+    _close(got, ref, 2e-2, 2e-2, "mla_extend dcp")
