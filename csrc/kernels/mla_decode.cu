@@ -344,7 +344,7 @@ void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
   TORCH_CHECK(q.size(2) == DK && cache.size(-1) == DK && q.stride(2) == 1 && q.stride(1) == DK, "mla_extend: q");
   TORCH_CHECK(out.size(2) == DV && out.stride(1) == DV && out.stride(2) == 1, "mla_extend: out");
   TORCH_CHECK(cache.is_contiguous() && (reinterpret_cast<uintptr_t>(cache.data_ptr()) % 16) == 0, "mla_extend: cache");
-  TORCH_CHECK(qo_indptr.scalar_type() == at::kInt && qo_indptr.numel() == B + 1, "mla_extend: qo_indptr");
+  TORCH_CHECK(qo_indptr.scalar_type() == at::kInt && qo_indptr.numel() >= B + 1, "mla_extend: qo_indptr");
   TORCH_CHECK(seq_lens.scalar_type() == at::kInt && block_table.scalar_type() == at::kInt, "mla_extend: int32 tables");
   auto st = at::cuda::getCurrentCUDAStream();
   static bool attr = false;
