@@ -236,8 +236,15 @@ class ModelRunner:
         # this pipeline stage's layers (+ the MTP block's one extra layer)
         layer_ids = [a.layer_id for a in attn] + ([cfg.num_layers] if self.draft is not None else [])
         n_layers = len(layer_ids)
+        # the stage's KV layout, declared before any pool is built and checked to match on every rank
+        from ..mem_cache.kv_spec import declare
+        from ..parallel.contract import assert_fleet_consistent
+        self.kv_spec = declare(cfg, attn, P, self.kv_dtype, args.enable_hybrid_swa, get_state().dcp_size,
+                               extra_layer_ids=[cfg.num_layers] if self.draft is not None else [])
+        if get_state().cpu_group is not None:  # the stage's TP ranks (stages of a pipeline differ by design)
+            assert_fleet_consistent({"kv_spec": self.kv_spec.digest()}, group=get_state().cpu_group)
         # hybrid sliding-window layout: sliding layers in a window pool sized by the scheduling bound
-        swa_layers = [a.layer_id for a in attn if getattr(a, "window", 0) > 0] if args.enable_hybrid_swa else []
+        swa_layers = self.kv_spec.pool_layers("window")
         swa_pages, swa_bytes = 0, 0
         if swa_layers:
             from ..mem_cache.hybrid_swa import check_window_pool, window_pool_pages

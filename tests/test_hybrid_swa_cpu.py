@@ -82,3 +82,24 @@ def test_hybrid_swa_refuses_prefix_reuse_features():
     args = ServerArgs(model="gpt-oss-120b", enable_hybrid_swa=True, enable_hierarchical_cache=True)
     with pytest.raises(ValueError):
         platform.refuse_unserved(args, model_spec("GptOssForCausalLM"))
+
+
+def test_kv_layout_declaration():
+    """The stage's KV layout is declared before pools: sliding layers go to the window pool only with the
+    hybrid layout, latent layers are one 576-wide row, and the digest tells layouts apart."""
+    from sglang_neuron_b200.mem_cache.kv_spec import declare, phase
+
+    class A:
+        def __init__(self, i, w):
+            self.layer_id, self.window, self.num_kv_heads = i, w, 2
+
+    cfg = mc.resolve_model_config("gpt-oss-120b")
+    attn = [A(0, 128), A(1, 0)]
+    plain = declare(cfg, attn, 16, torch.float8_e4m3fn, hybrid_swa=False)
+    hyb = declare(cfg, attn, 16, torch.float8_e4m3fn, hybrid_swa=True)
+    assert plain.pool_layers("window") == [] and hyb.pool_layers("window") == [0] and hyb.max_window == 128
+    assert [l.kind for l in hyb.layers] == ["sliding", "full"]
+    assert plain.digest() != hyb.digest()
+    ds = declare(mc.resolve_model_config("deepseek-v2-lite"), [A(0, 0)], 16, torch.bfloat16, False, dcp_size=2)
+    assert ds.is_latent and ds.layers[0].head_dim == 576 and ds.dcp_size == 2
+    assert phase("aggregated") == "all" and phase("decode") == "decode"
