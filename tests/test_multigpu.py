@@ -276,7 +276,8 @@ def _logits_worker(rank, world, port, q, extra):
     prompts = [torch.randint(0, 2048, (n,), generator=g).tolist() for n in (40, 9)]
     eng.generate(prompts, {"max_new_tokens": 1})
     eng.shutdown()
-    q.put((rank, torch.cat(rows, 0) if rows else None))
+    # by value (numpy): a tensor would be shared through a file descriptor that dies with this process
+    q.put((rank, torch.cat(rows, 0).numpy() if rows else None))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -332,6 +333,7 @@ def test_tp2_engine_ranks_agree():
 
 
 def _rel(a, b):
+    a, b = torch.as_tensor(a), torch.as_tensor(b)
     return ((a - b).norm() / b.norm()).item()
 
 
