@@ -6,6 +6,8 @@ reference implementations (the oracle path of the CPU test tier).
 """
 import importlib
 
+import torch  # noqa: F401  (loads libc10 / libtorch, which the extension links against)
+
 _C = None
 _runtime = None
 _err = None
