@@ -69,3 +69,59 @@ def test_tp2_dcp2_deepseek_equals_tp1():
     one = _tp("deepseek-v2-lite", TINY_DS, 1)[0]
     two = _tp("deepseek-v2-lite", TINY_DS, 2, args_over={"dcp_size": 2})
     assert two[0] == one and two[1] == one
+
+
+def _prefix_worker(rank, world, port, q, dcp):
+    import os
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.parallel.state import destroy_parallel
+    from sglang_neuron_b200.server_args import ServerArgs
+    destroy_parallel()
+    mc.PRESETS["dcp-tiny"] = dict(mc.PRESETS["deepseek-v2-lite"], **TINY_DS)
+    eng = Engine(ServerArgs(model="dcp-tiny", device="cpu", dtype="float32", tp_size=world, dcp_size=dcp,
+                            page_size=4, context_length=256, max_running_requests=4, chunked_prefill_size=16,
+                            random_weight_std=0.05))
+    g = torch.Generator().manual_seed(9)
+    shared = torch.randint(0, 1000, (37,), generator=g).tolist()
+    outs = []
+    for tail in (5, 9, 2):  # one after the other: later prompts hit the first one's cached pages
+        p = shared + torch.randint(0, 1000, (tail,), generator=g).tolist()
+        outs.append(eng.generate([p], {"max_new_tokens": 5})[0])
+    q.put((rank, [o["output_ids"] for o in outs], [o["cached_tokens"] for o in outs]))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _spawn(world, dcp):
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_prefix_worker, args=(r, world, port, q, dcp)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in ps:
+        item = q.get(timeout=300)
+        res[item[0]] = item[1:]
+    for p in ps:
+        p.join(timeout=60)
+    return res
+
+
+def test_dcp_prefix_cache_hits_keep_page_owners():
+    """Prefix-cache hits under DCP reuse cached pages at the same logical indices (same owner rank): the
+    tokens equal the single-rank run and the later prompts do hit."""
+    one = _spawn(1, 1)[0]
+    two = _spawn(2, 2)
+    assert two[0][0] == one[0] and two[1][0] == one[0]
+    assert two[0][1][1] > 0 and two[0][1][2] > 0
