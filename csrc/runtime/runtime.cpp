@@ -10,6 +10,22 @@
 //    reference drives it (ChunkKeyedRadixCache, sglang_neuron/mem_cache/chunk_keyed_tree.py:58, with the
 //    page as its chunk so hits are bit-identical).
 //  * build_page_table_rows: fills padded int32 block-table rows and slot mappings for a batch in one call.
+//  * ShmReduce: element-wise MIN / MAX of a short int64 vector over the ranks of one node through a POSIX
+//    shared-memory segment (no sockets, no pickling). Parity: the reference's NodeShmMin
+//    (sglang_neuron/distributed/node_shm_min.py:68; docs/design/parallelism.md:940-989: spin, then short
+//    naps, and a timeout), which backs its poll reduces.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <cstring>
+#include <chrono>
+#include <string>
+#include <thread>
+
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
@@ -321,6 +337,77 @@ std::vector<int64_t> slots_for_range(const std::vector<int32_t>& pages, int64_t 
   return out;
 }
 
+// Segment: per rank one 64-byte-aligned slot {atomic<uint64> epoch; int64 vals[2][width]}. Call e writes
+// buffer (e & 1) of its own slot, publishes epoch e (release), waits until every slot shows >= e (acquire),
+// and reduces buffer (e & 1) of all slots. Two buffers suffice: a rank can only start call e + 2 after every
+// rank published e + 1, i.e. after every rank finished reading call e.
+class ShmReduce {
+ public:
+  ShmReduce(const std::string& name, int64_t world, int64_t rank, int64_t width, bool create)
+      : name_(name), world_(world), rank_(rank), width_(width) {
+    if (world < 1 || rank < 0 || rank >= world || width < 1 || width > 4096)
+      throw std::invalid_argument("ShmReduce: bad world / rank / width");
+    slot_bytes_ = ((sizeof(uint64_t) + 2 * width * sizeof(int64_t)) + 63) / 64 * 64;
+    bytes_ = slot_bytes_ * world;
+    int fd = shm_open(name.c_str(), create ? (O_CREAT | O_RDWR) : O_RDWR, 0600);
+    if (fd < 0) throw std::runtime_error("ShmReduce: shm_open failed for " + name);
+    if (create && ftruncate(fd, (off_t)bytes_) != 0) {
+      close(fd);
+      throw std::runtime_error("ShmReduce: ftruncate failed");
+    }
+    void* p = mmap(nullptr, bytes_, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) throw std::runtime_error("ShmReduce: mmap failed");
+    base_ = static_cast<uint8_t*>(p);
+    if (create) std::memset(base_, 0, bytes_);
+    owner_ = create;
+  }
+  ~ShmReduce() {
+    if (base_) munmap(base_, bytes_);
+    if (owner_) shm_unlink(name_.c_str());
+  }
+  std::vector<int64_t> reduce(const std::vector<int64_t>& v, bool is_min, double timeout_s) {
+    if ((int64_t)v.size() != width_) throw std::invalid_argument("ShmReduce: vector width");
+    const uint64_t e = ++epoch_;
+    const int buf = (int)(e & 1);
+    int64_t* mine = vals(rank_, buf);
+    for (int64_t i = 0; i < width_; ++i) mine[i] = v[i];
+    epoch_of(rank_)->store(e, std::memory_order_release);
+    const auto t0 = std::chrono::steady_clock::now();
+    std::vector<int64_t> out(v);
+    for (int64_t q = 0; q < world_; ++q) {
+      if (q == rank_) continue;
+      int spins = 0;
+      long nap_ns = 20000;
+      while (epoch_of(q)->load(std::memory_order_acquire) < e) {
+        if (++spins < 64) continue;
+        struct timespec ts{0, nap_ns};  // naps after the first polls: 20 us, doubling up to 1 ms
+        nanosleep(&ts, nullptr);
+        nap_ns = std::min(nap_ns * 2, 1000000L);
+        const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (dt > timeout_s)
+          throw std::runtime_error("ShmReduce: rank " + std::to_string(q) + " did not arrive within the timeout");
+      }
+      const int64_t* other = vals(q, buf);
+      for (int64_t i = 0; i < width_; ++i) out[i] = is_min ? std::min(out[i], other[i]) : std::max(out[i], other[i]);
+    }
+    return out;
+  }
+  int64_t world() const { return world_; }
+
+ private:
+  std::atomic<uint64_t>* epoch_of(int64_t r) { return reinterpret_cast<std::atomic<uint64_t>*>(base_ + r * slot_bytes_); }
+  int64_t* vals(int64_t r, int buf) {
+    return reinterpret_cast<int64_t*>(base_ + r * slot_bytes_ + sizeof(uint64_t)) + buf * width_;
+  }
+  std::string name_;
+  int64_t world_, rank_, width_;
+  size_t slot_bytes_ = 0, bytes_ = 0;
+  uint8_t* base_ = nullptr;
+  bool owner_ = false;
+  uint64_t epoch_ = 0;
+};
+
 PYBIND11_MODULE(_runtime, m) {
   m.doc() = "sglang_neuron_b200 native host runtime";
   py::class_<PageAllocator>(m, "PageAllocator")
@@ -347,4 +434,12 @@ PYBIND11_MODULE(_runtime, m) {
       .def("reset", &RadixCache::reset);
   m.def("build_page_table_rows", &build_page_table_rows);
   m.def("slots_for_range", &slots_for_range);
+  py::class_<ShmReduce>(m, "ShmReduce")
+      .def(py::init<const std::string&, int64_t, int64_t, int64_t, bool>(), py::arg("name"), py::arg("world"),
+           py::arg("rank"), py::arg("width"), py::arg("create"))
+      .def("min", [](ShmReduce& s, const std::vector<int64_t>& v, double t) { return s.reduce(v, true, t); },
+           py::arg("values"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>())
+      .def("max", [](ShmReduce& s, const std::vector<int64_t>& v, double t) { return s.reduce(v, false, t); },
+           py::arg("values"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>())
+      .def("world", &ShmReduce::world);
 }

@@ -48,6 +48,7 @@ if runtime_sources:
             sources=runtime_sources,
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args=["-O3", "-std=c++17"],
+            libraries=["rt"],  # shm_open on older glibc
         )
     )
 

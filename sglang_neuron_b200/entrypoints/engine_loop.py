@@ -15,6 +15,7 @@ import time
 from typing import Dict, List, Optional
 
 from ..managers.schedule_batch import SamplingParams
+from ..parallel.state import get_state
 
 logger = logging.getLogger(__name__)
 
@@ -95,3 +96,7 @@ class EngineLoop:
             else:
                 self.wake.wait(timeout=0.05)
                 self.wake.clear()
+                if get_state().replica_size > 1:
+                    # heartbeat: follower ranks wait inside the step's arrival sync; an idle step every
+                    # 50 ms keeps them from running into the process group's timeout
+                    sched.step()

@@ -79,6 +79,7 @@ class Scheduler:
         self._global_busy = False
         if self.dp_groups > 1:
             self.overlap = False  # results are published once per step, right after the step
+        self._arrival_flag = _make_arrival_flag(st)
 
     # ------------------------------------------------------------------------------------------
     # request intake
@@ -92,6 +93,12 @@ class Scheduler:
 
     def _sync_arrivals(self) -> None:
         st = get_state()
+        if st.replica_size > 1 and self._arrival_flag is not None:
+            # shared-memory MAX of rank 0's arrival + abort count: the object broadcast only when it has some
+            n = len(self.pending_arrivals) + len(self.pending_aborts) if st.replica_rank == 0 else 0
+            if self._arrival_flag.max([n])[0] == 0:
+                self.pending_arrivals, self.pending_aborts = [], []
+                return
         if st.replica_size > 1:
             payload = (([(r.rid, r.origin_input_ids, r.params) for r in self.pending_arrivals], self.pending_aborts)
                        if st.replica_rank == 0 else None)
@@ -536,6 +543,30 @@ class Scheduler:
             self.step()
             n += 1
         self.drain()
+
+
+_flag_seq = [0]
+
+
+def _make_arrival_flag(st):
+    """Node shared-memory MAX over the replica's ranks (the native runtime's ShmReduce), or None when the
+    runtime is not built or the replica spans one rank; gloo stays the fallback."""
+    import os
+    import torch.distributed as dist
+    from .._ext import _runtime
+    if st.replica_size == 1 or _runtime is None or not hasattr(_runtime, "ShmReduce") or not dist.is_initialized():
+        return None
+    _flag_seq[0] += 1  # every rank builds its schedulers in the same order, so the names match
+    name = f"/snb_{os.environ.get('MASTER_PORT', '0')}_{st.replica_base}_{st.replica_size}_{_flag_seq[0]}_arr"
+    # the replica's rank 0 creates (and zeroes) the segment before the others open it
+    flag = None
+    if st.replica_rank == 0:
+        flag = _runtime.ShmReduce(name, st.replica_size, 0, 1, True)
+    dist.barrier(group=st.replica_cpu_group)
+    if st.replica_rank != 0:
+        flag = _runtime.ShmReduce(name, st.replica_size, st.replica_rank, 1, False)
+    dist.barrier(group=st.replica_cpu_group)
+    return flag
 
 
 def _retracted_flag(self) -> bool:

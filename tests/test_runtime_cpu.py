@@ -128,3 +128,40 @@ def test_contract_digests_and_clean_exit():
             time.sleep(1)
     finally:
         signal.signal(signal.SIGTERM, prev)
+
+
+def _shm_worker(r, name, q):
+    import time
+    from sglang_neuron_b200._ext import _runtime as rt
+    time.sleep(0.2)
+    s = rt.ShmReduce(name, 3, r, 2, False)
+    outs = [s.max([r, -r]) for _ in range(300)]
+    q.put((r, outs[-1], s.min([r * 7, 5])))
+
+
+def test_shm_reduce_min_max_over_processes():
+    """Node shared-memory MIN / MAX over three processes, 300 calls in a row (double-buffered epochs), and a
+    clear error when a rank never arrives."""
+    import multiprocessing as mp
+    import os
+    import pytest
+    from sglang_neuron_b200._ext import _runtime as rt
+    if rt is None or not hasattr(rt, "ShmReduce"):
+        pytest.skip("native runtime not built")
+    name = f"/snb_test_{os.getpid()}"
+    s0 = rt.ShmReduce(name, 3, 0, 2, True)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_shm_worker, args=(r, name, q)) for r in (1, 2)]
+    for p in ps:
+        p.start()
+    outs = [s0.max([0, 0]) for _ in range(300)]
+    last_min = s0.min([0, 5])
+    got = dict((r, (a, b)) for r, a, b in (q.get(timeout=60) for _ in ps))
+    for p in ps:
+        p.join(timeout=30)
+    assert outs[-1] == [2, 0] and last_min == [0, 5]
+    assert got[1] == ([2, 0], [0, 5]) and got[2] == ([2, 0], [0, 5])
+    lonely = rt.ShmReduce(name + "_b", 2, 0, 1, True)
+    with pytest.raises(RuntimeError, match="did not arrive"):
+        lonely.max([1], timeout_s=0.2)
