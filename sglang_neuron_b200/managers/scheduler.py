@@ -558,15 +558,24 @@ def _make_arrival_flag(st):
         return None
     _flag_seq[0] += 1  # every rank builds its schedulers in the same order, so the names match
     name = f"/snb_{os.environ.get('MASTER_PORT', '0')}_{st.replica_base}_{st.replica_size}_{_flag_seq[0]}_arr"
-    # the replica's rank 0 creates (and zeroes) the segment before the others open it
+    # the replica's rank 0 creates (and zeroes) the segment before the others open it; every rank must end
+    # up on the same path, so a rank that cannot map the segment sends all of them back to gloo
+    import torch
     flag = None
-    if st.replica_rank == 0:
-        flag = _runtime.ShmReduce(name, st.replica_size, 0, 1, True)
+    try:
+        if st.replica_rank == 0:
+            flag = _runtime.ShmReduce(name, st.replica_size, 0, 1, True)
+    except RuntimeError as e:
+        logger.warning("shared-memory arrival flag unavailable (%s); using gloo", e)
     dist.barrier(group=st.replica_cpu_group)
-    if st.replica_rank != 0:
-        flag = _runtime.ShmReduce(name, st.replica_size, st.replica_rank, 1, False)
-    dist.barrier(group=st.replica_cpu_group)
-    return flag
+    try:
+        if st.replica_rank != 0:
+            flag = _runtime.ShmReduce(name, st.replica_size, st.replica_rank, 1, False)
+    except RuntimeError as e:
+        logger.warning("shared-memory arrival flag unavailable (%s); using gloo", e)
+    ok = torch.tensor([1 if flag is not None else 0], dtype=torch.int32)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=st.replica_cpu_group)
+    return flag if int(ok) == 1 else None
 
 
 def _retracted_flag(self) -> bool:
