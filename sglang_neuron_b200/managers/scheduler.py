@@ -96,7 +96,8 @@ class Scheduler:
         if st.replica_size > 1 and self._arrival_flag is not None:
             # shared-memory MAX of rank 0's arrival + abort count: the object broadcast only when it has some
             n = len(self.pending_arrivals) + len(self.pending_aborts) if st.replica_rank == 0 else 0
-            if self._arrival_flag.max([n])[0] == 0:
+            # (never tighter than a gloo collective: 1800 s, as the reference's node-shm reduce)
+            if self._arrival_flag.max([n], timeout_s=1800.0)[0] == 0:
                 self.pending_arrivals, self.pending_aborts = [], []
                 return
         if st.replica_size > 1:
