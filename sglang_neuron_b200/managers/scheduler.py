@@ -231,7 +231,8 @@ class Scheduler:
             prefix_len, prefix_pages, node = 0, [], None
             if self.radix is not None:
                 matched, pages, node = self.radix.match_prefix(ids[:-1] if len(ids) > 1 else [])
-                prefix_len = (matched // self.P) * self.P
+                grid = self.args.prefill_chunk_grid or self.P  # chunk-keyed reuse: whole grid chunks only
+                prefix_len = (matched // grid) * grid
                 prefix_pages = list(pages)[: prefix_len // self.P]
             need = (len(ids) + 1 + self.P - 1) // self.P - len(prefix_pages)
             if self.alloc.available() + (self.radix.evictable_pages() if self.radix else 0) < need:
@@ -246,6 +247,9 @@ class Scheduler:
                 # pages past the device match that the host tier still holds: load instead of recompute
                 room = (len(ids) - 1) // self.P - tree_pages
                 slots = self.hicache.match(ids, tree_pages, room) if room > 0 else []
+                if slots and self.args.prefill_chunk_grid:  # keep the reused prefix on the chunk grid
+                    gp = self.args.prefill_chunk_grid // self.P
+                    slots = slots[: max(0, ((tree_pages + len(slots)) // gp) * gp - tree_pages)]
                 new = self._alloc_pages(len(slots)) if slots else None
                 if new:
                     self.hicache.load(slots, new)
@@ -329,6 +333,9 @@ class Scheduler:
             if budget <= 0:
                 break
             n = min(r.prefill_target - r.kv_len, budget)
+            G = self.args.prefill_chunk_grid
+            if G:  # chunks end on the request's grid (a prefix hit then replays the same chunks)
+                n = min(n, G - r.kv_len % G)
             if not self._ensure_pages(r, r.kv_len + n, upd):
                 break
             chunks.append((r, n))

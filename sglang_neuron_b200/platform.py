@@ -35,6 +35,9 @@ def refuse_unserved(args, spec) -> None:
 
 
 def check_hybrid_swa(args) -> None:
+    if args.prefill_chunk_grid and (args.prefill_chunk_grid % args.page_size
+                                    or args.prefill_chunk_grid > args.chunked_prefill_size):
+        raise ValueError("prefill_chunk_grid must be a multiple of page_size and at most chunked_prefill_size")
     if args.dcp_size > 1:
         if (args.tp_size % args.dcp_size or args.enable_hierarchical_cache or args.disaggregation_mode != "null"
                 or args.speculative_algorithm or args.pp_size > 1 or args.enable_dp_attention):

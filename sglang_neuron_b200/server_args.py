@@ -36,6 +36,8 @@ class ServerArgs:
     max_prefill_tokens: int = 16384
     enable_mixed_chunk: bool = True          # decode rows ride along with prefill chunks
     disable_radix_cache: bool = False
+    prefill_chunk_grid: int = 0               # >0: prefill chunks end on multiples of this (per request) and prefix
+                                              # hits are rounded down to it, so a hit replays the uncached chunking
     enable_hybrid_swa: bool = False           # sliding-window layers keep their K/V in a small window pool
     swa_pool_pages: int = 0                   # window pool pages (0: the sizing bound for max_running_requests)
     enable_hierarchical_cache: bool = False   # host (pinned memory) tier below the device prefix cache

@@ -78,3 +78,30 @@ def test_chain_hashes_prefix_property():
     h1 = chain_hashes(x, 16, 6)
     h2 = chain_hashes(x[:64] + [7] * 36, 16, 6)
     assert h1[:4] == h2[:4] and h1[4] != h2[4] and h1[5] != h2[5]
+
+
+def test_chunk_grid_prefix_hits_replay_uncached_chunks():
+    """prefill_chunk_grid: chunks end on multiples of the grid and prefix hits are rounded down to it, so a
+    request that hits the cache computes exactly the chunks it would have computed uncached: the greedy
+    tokens equal a cache-less run."""
+    import torch
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.parallel.state import destroy_parallel
+    from sglang_neuron_b200.server_args import ServerArgs
+    mc.PRESETS["pc-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], **TINY)
+    outs = {}
+    for cache in (False, True):
+        destroy_parallel()
+        eng = Engine(ServerArgs(model="pc-tiny", device="cpu", dtype="float32", page_size=4, context_length=256,
+                                max_running_requests=4, chunked_prefill_size=32, prefill_chunk_grid=8,
+                                disable_radix_cache=not cache, random_weight_std=0.05))
+        g = torch.Generator().manual_seed(2)
+        shared = torch.randint(0, 1000, (29,), generator=g).tolist()
+        res, hits = [], []
+        for tail in (3, 11):
+            o = eng.generate([shared + torch.randint(0, 1000, (tail,), generator=g).tolist()], {"max_new_tokens": 4})[0]
+            res.append(o["output_ids"])
+            hits.append(o["cached_tokens"])
+        outs[cache] = (res, hits)
+    assert outs[True][0] == outs[False][0]
+    assert outs[True][1][1] > 0 and outs[True][1][1] % 8 == 0
