@@ -465,7 +465,10 @@ class Scheduler:
             elif r.params.stop and self.stop_checker is not None and self.stop_checker(r):
                 self._finish(r, "stop")
             if self.dp_groups > 1 and self.dp_leader:
-                self._outbox.append((r.rid, tok, r.finished, r.finish_reason))
+                lp = None
+                if lpr is not None and r.params.return_logprob:
+                    lp = (r.output_logprobs[-1], r.output_top_logprobs[-1] if r.params.top_logprobs_num > 0 else None)
+                self._outbox.append((r.rid, tok, r.finished, r.finish_reason, lp))
             if self.on_token is not None:
                 self.on_token(r)
         self.alloc.retire(step.epoch)
@@ -516,11 +519,15 @@ class Scheduler:
         info = dp_exchange((n, busy, self._outbox))
         self._outbox = []
         for _, _, out in info:
-            for rid, tok, fin, reason in out:
+            for rid, tok, fin, reason, lp in out:
                 r = self._remote.get(rid)
                 if r is None:
                     continue
                 r.output_ids.append(tok)
+                if lp is not None:
+                    r.output_logprobs.append(lp[0])
+                    if lp[1] is not None:
+                        r.output_top_logprobs.append(lp[1])
                 if r.first_token_time is None:
                     r.first_token_time = time.perf_counter()
                 if fin:

@@ -47,6 +47,8 @@ def _run(rank, world, port, base, over, q, sp=None, args_over=None):
         return fdp(self, *a, **k)
 
     common.MoEBlock.forward_dp = counted_dp
+    args_over = dict(args_over or {})
+    want_lp = args_over.pop("want_logprobs", False)
     eng = Engine(ServerArgs(model="tp-tiny", device="cpu", dtype="float32", tp_size=world, context_length=256,
                             max_running_requests=4, chunked_prefill_size=32, random_weight_std=0.05,
                             **(args_over or {})))
@@ -54,7 +56,9 @@ def _run(rank, world, port, base, over, q, sp=None, args_over=None):
     prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
     # SPMD: every rank makes the same call; rank 0 owns intake and broadcasts, followers step in lockstep
     outs = eng.generate(prompts, sp or {"max_new_tokens": 6})
-    if (args_over or {}).get("enable_dp_attention"):
+    if want_lp:
+        q.put((rank, [o["output_ids"] for o in outs], [[lp for lp, _ in o["output_token_logprobs"]] for o in outs]))
+    elif (args_over or {}).get("enable_dp_attention"):
         q.put((rank, [o["output_ids"] for o in outs], dp_calls[0], eng.scheduler.stats["output_tokens"]))
     else:
         q.put((rank, [o["output_ids"] for o in outs] + ([calls[0]] if (args_over or {}).get("sp_min_tokens") else [])))
@@ -109,6 +113,21 @@ def test_dp_attention_two_groups_equals_tp1(base, over):
     assert two[0][2] == len(one[0]) + len(one[2]) and two[1][2] == len(one[1])
     if base == "qwen3-30b-a3b":
         assert two[0][1] > 0 and two[0][1] == two[1][1]  # same number of MoE exchanges (lockstep + idle)
+
+
+def test_dp_attention_publishes_logprobs_across_groups():
+    """Logprobs of requests served by the other attention group reach every rank with their tokens."""
+    sp = {"max_new_tokens": 4, "return_logprob": True, "top_logprobs_num": 2}
+    two = _tp("qwen3-30b-a3b", TINY_MOE, 2, sp=sp, args_over={"dp_size": 2, "enable_dp_attention": True,
+                                                              "want_logprobs": True})
+    one = _tp("qwen3-30b-a3b", TINY_MOE, 1, sp=sp, args_over={"want_logprobs": True})
+    ids1, lp1 = one[0]
+    for r in (0, 1):
+        ids, lp = two[r]
+        assert ids == ids1
+        assert len(lp) == 3 and all(len(x) == 4 for x in lp)
+        for a, b in zip(lp, lp1):
+            assert all(abs(u - v) < 1e-3 for u, v in zip(a, b))
 
 
 @pytest.mark.slow
