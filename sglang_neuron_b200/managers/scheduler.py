@@ -79,7 +79,12 @@ class Scheduler:
         self._global_busy = False
         if self.dp_groups > 1:
             self.overlap = False  # results are published once per step, right after the step
-        self._arrival_flag = _make_arrival_flag(st)
+        self._arrival_flag = _make_shm(st, 1, "arr")
+        # optional program fence: ranks check that they launch the same step program (debug; one shared-memory
+        # reduce per step). Parity: the reference's ProgramSwitchFence (model_executor/program_fence.py:69).
+        import os
+        self._fence = (_make_shm(st, 2, "fence") if os.environ.get("SGLANG_B200_STEP_FENCE") == "1"
+                       and self.dp_groups == 1 else None)
 
     # ------------------------------------------------------------------------------------------
     # request intake
@@ -494,6 +499,12 @@ class Scheduler:
         if self.dp_groups > 1:
             return self._step_dp()
         step = self.schedule()
+        if self._fence is not None:
+            key = (hash((int(step.mode), step.batch_size, step.num_tokens, step.max_extend)) & 0x3FFFFFFFFFFF
+                   if step is not None else 0)
+            got = self._fence.max([key, -key], timeout_s=1800.0)
+            if got[0] != -got[1]:
+                raise RuntimeError(f"ranks are about to launch different step programs (epoch {self.epoch})")
         if step is not None:
             t0 = time.perf_counter()
             if self.hicache is not None:
@@ -563,8 +574,8 @@ class Scheduler:
 _flag_seq = [0]
 
 
-def _make_arrival_flag(st):
-    """Node shared-memory MAX over the replica's ranks (the native runtime's ShmReduce), or None when the
+def _make_shm(st, width: int, tag: str):
+    """Node shared-memory MIN/MAX over the replica's ranks (the native runtime's ShmReduce), or None when the
     runtime is not built or the replica spans one rank; gloo stays the fallback."""
     import os
     import torch.distributed as dist
@@ -572,20 +583,20 @@ def _make_arrival_flag(st):
     if st.replica_size == 1 or _runtime is None or not hasattr(_runtime, "ShmReduce") or not dist.is_initialized():
         return None
     _flag_seq[0] += 1  # every rank builds its schedulers in the same order, so the names match
-    name = f"/snb_{os.environ.get('MASTER_PORT', '0')}_{st.replica_base}_{st.replica_size}_{_flag_seq[0]}_arr"
+    name = f"/snb_{os.environ.get('MASTER_PORT', '0')}_{st.replica_base}_{st.replica_size}_{_flag_seq[0]}_{tag}"
     # the replica's rank 0 creates (and zeroes) the segment before the others open it; every rank must end
     # up on the same path, so a rank that cannot map the segment sends all of them back to gloo
     import torch
     flag = None
     try:
         if st.replica_rank == 0:
-            flag = _runtime.ShmReduce(name, st.replica_size, 0, 1, True)
+            flag = _runtime.ShmReduce(name, st.replica_size, 0, width, True)
     except RuntimeError as e:
         logger.warning("shared-memory arrival flag unavailable (%s); using gloo", e)
     dist.barrier(group=st.replica_cpu_group)
     try:
         if st.replica_rank != 0:
-            flag = _runtime.ShmReduce(name, st.replica_size, st.replica_rank, 1, False)
+            flag = _runtime.ShmReduce(name, st.replica_size, st.replica_rank, width, False)
     except RuntimeError as e:
         logger.warning("shared-memory arrival flag unavailable (%s); using gloo", e)
     ok = torch.tensor([1 if flag is not None else 0], dtype=torch.int32)

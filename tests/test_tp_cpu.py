@@ -49,6 +49,7 @@ def _run(rank, world, port, base, over, q, sp=None, args_over=None):
     common.MoEBlock.forward_dp = counted_dp
     args_over = dict(args_over or {})
     want_lp = args_over.pop("want_logprobs", False)
+    os.environ.update(args_over.pop("env", {}))
     eng = Engine(ServerArgs(model="tp-tiny", device="cpu", dtype="float32", tp_size=world, context_length=256,
                             max_running_requests=4, chunked_prefill_size=32, random_weight_std=0.05,
                             **(args_over or {})))
@@ -113,6 +114,14 @@ def test_dp_attention_two_groups_equals_tp1(base, over):
     assert two[0][2] == len(one[0]) + len(one[2]) and two[1][2] == len(one[1])
     if base == "qwen3-30b-a3b":
         assert two[0][1] > 0 and two[0][1] == two[1][1]  # same number of MoE exchanges (lockstep + idle)
+
+
+def test_tp2_with_step_fence_equals_tp1():
+    """SGLANG_B200_STEP_FENCE=1: every step the ranks compare the program they launch through shared memory;
+    matching ranks run on unchanged."""
+    one = _tp("qwen3-0.6b", TINY_QWEN, 1)[0]
+    two = _tp("qwen3-0.6b", TINY_QWEN, 2, args_over={"env": {"SGLANG_B200_STEP_FENCE": "1"}})
+    assert two[0] == one and two[1] == one
 
 
 def test_dp_attention_publishes_logprobs_across_groups():
