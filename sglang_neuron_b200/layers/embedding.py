@@ -34,7 +34,8 @@ class VocabParallelEmbedding(nn.Module):
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
         st = get_state()
         if st.tp_size == 1:
-            return self.weight[ids]
+            # clamped: an id the scheduler refuses may already be the input of the overlapped next step
+            return self.weight[ids.clamp(0, self.weight.shape[0] - 1)]
         local = ids - self.start
         mask = (local >= 0) & (local < (self.end - self.start))
         out = self.weight[local.clamp(0, self.per - 1)] * mask[:, None].to(self.weight.dtype)

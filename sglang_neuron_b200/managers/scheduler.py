@@ -452,6 +452,15 @@ class Scheduler:
             if not s or r.finished:
                 continue
             tok = int(ids[i])
+            if not 0 <= tok < self.cfg.vocab_size:
+                # a corrupted logits row (NaN / inf) must not reach the detokenizer or the relay: refuse the
+                # id and end only this request. Parity: refuse_invalid_token_ids (async_execution.py:237).
+                logger.error("request %s: sampled token id %d outside the vocabulary; request ended", r.rid, tok)
+                self.stats["invalid_token_ids"] += 1
+                self._finish(r, "error: invalid token id")
+                if self.on_token is not None:
+                    self.on_token(r)
+                continue
             r.output_ids.append(tok)
             if lpr is not None and r.params.return_logprob:
                 k = r.params.top_logprobs_num

@@ -165,3 +165,34 @@ def test_shm_reduce_min_max_over_processes():
     lonely = rt.ShmReduce(name + "_b", 2, 0, 1, True)
     with pytest.raises(RuntimeError, match="did not arrive"):
         lonely.max([1], timeout_s=0.2)
+
+
+def test_invalid_sampled_token_id_ends_only_that_request():
+    """A sampled id outside the vocabulary (what a corrupted logits row gives) ends its request with an error
+    reason; the other requests of the batch finish normally."""
+    import torch
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.parallel.state import destroy_parallel
+    from sglang_neuron_b200.server_args import ServerArgs
+    destroy_parallel()
+    mc.PRESETS["inv-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], num_hidden_layers=1, vocab_size=500, hidden_size=128,
+                                  intermediate_size=256, num_attention_heads=2, num_key_value_heads=1, head_dim=64)
+    eng = Engine(ServerArgs(model="inv-tiny", device="cpu", dtype="float32", context_length=128,
+                            max_running_requests=4, random_weight_std=0.05, disable_overlap_schedule=True))
+    calls = [0]
+    sample = eng.runner.sample
+
+    def bad_third_step(*a, **k):
+        ids = sample(*a, **k)
+        calls[0] += 1
+        if calls[0] == 3:
+            ids[0] = 10_000  # the first request of this step gets an impossible id
+        return ids
+
+    eng.runner.sample = bad_third_step
+    outs = eng.generate([[1, 2, 3], [4, 5, 6, 7]], {"max_new_tokens": 6})
+    reasons = sorted(o["finish_reason"] for o in outs)
+    assert reasons == ["error: invalid token id", "length"]
+    assert all(0 <= t < 500 for o in outs for t in o["output_ids"])
+    assert eng.scheduler.stats["invalid_token_ids"] == 1
