@@ -122,11 +122,11 @@ class PDLink:
         if work.completed:
             return True
         if self.stream is None:
-            import datetime
-            try:
-                work.work.wait(datetime.timedelta(milliseconds=20))  # gloo: wait exactly once per message
-            except RuntimeError:  # not yet: the peer has not posted the matching call
-                return False
+            # gloo point-to-point work only completes through wait(), and a wait that times out closes the
+            # pair, so wait without a short limit: the protocol has already posted the matching call (decode
+            # posts its receive before acknowledging; prefill sends only after the acknowledgement), and the
+            # process group's timeout bounds it
+            work.work.wait()
             work.completed = True
             return True
         work.completed = work.work.is_completed()

@@ -25,14 +25,14 @@ def _prompts():
     return [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (21, 40, 9)]
 
 
-def _engine(dp_size):
+def _engine(dp_size, tp_size=1):
     from sglang_neuron_b200.configs import model_config as mc
     from sglang_neuron_b200.engine import Engine
     from sglang_neuron_b200.parallel.state import destroy_parallel
     from sglang_neuron_b200.server_args import ServerArgs
     destroy_parallel()
     mc.PRESETS["pd-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], **TINY)
-    return Engine(ServerArgs(model="pd-tiny", device="cpu", dtype="float32", tp_size=1, dp_size=dp_size,
+    return Engine(ServerArgs(model="pd-tiny", device="cpu", dtype="float32", tp_size=tp_size, dp_size=dp_size,
                              context_length=256, max_running_requests=4, chunked_prefill_size=32,
                              random_weight_std=0.05))
 
@@ -105,3 +105,68 @@ def test_pd_prefill_aborts_when_decode_never_answers():
     res = _run(drop_ack=True)
     assert res[0]["sent"] == 0 and res[0]["aborted"] == ["pd0", "pd1", "pd2"]
     assert res[1] == {}
+
+
+def _worker_tp2(rank, port, q):
+    """World 4: prefill group = ranks 0-1 (TP2), decode group = ranks 2-3 (TP2); every rank of a group makes
+    the same calls (the group's rank 0 owns intake and the store protocol)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE="4", RANK=str(rank),
+                      LOCAL_RANK="0")
+    import time
+    import torch.distributed as dist
+    from sglang_neuron_b200.disaggregation.pd import DecodeSide, PDLink, PrefillSide
+    from sglang_neuron_b200.managers.schedule_batch import SamplingParams
+    eng = _engine(2, tp_size=2)
+    store = dist.distributed_c10d._get_default_store()
+    role = "prefill" if rank < 2 else "decode"
+    link = PDLink(role, 2, store, timeout_s=60.0)
+    result = None
+    if role == "prefill":
+        side = PrefillSide(eng, link)
+        for i, p in enumerate(_prompts()):
+            side.submit(f"pd{i}", p, SamplingParams(max_new_tokens=7))
+        from sglang_neuron_b200.parallel.state import get_state
+        t0 = time.time()
+        while time.time() - t0 < 120:
+            side.step()
+            # the group's ranks stop together (step() is a lockstep call): MIN of their "done" flags
+            done = torch.tensor([int(side.sent == 3 and not side.pending and not side.sending)])
+            dist.all_reduce(done, op=dist.ReduceOp.MIN, group=get_state().cpu_group)
+            if int(done):
+                break
+            time.sleep(0.001)
+        result = {"sent": side.sent, "aborted": sorted(side.aborted)}
+    else:
+        side = DecodeSide(eng, link)
+        t0 = time.time()
+        want = {"pd0", "pd1", "pd2"}
+        from sglang_neuron_b200.parallel.state import get_state
+        while time.time() - t0 < 120:
+            side.step()
+            done = torch.tensor([int(want.issubset(eng.scheduler.finished_by_rid))])
+            dist.all_reduce(done, op=dist.ReduceOp.MIN, group=get_state().cpu_group)
+            if int(done):
+                break
+            time.sleep(0.001)
+        eng.scheduler.drain()
+        result = {rid: eng.scheduler.finished_by_rid[rid].output_ids for rid in sorted(want)
+                  if rid in eng.scheduler.finished_by_rid}
+    q.put((rank, result))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_pd_tp2_groups_match_aggregated():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker_tp2, args=(r, port, q)) for r in range(4)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    ref = _engine(1).generate(_prompts(), {"max_new_tokens": 7})
+    assert res[0]["sent"] == 3 and res[1]["sent"] == 3
+    for r in (2, 3):
+        assert [res[r][f"pd{i}"] for i in range(3)] == [o["output_ids"] for o in ref]
