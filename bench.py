@@ -29,7 +29,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "output tok/s at concurrency 64; p50 TTFT & ITL (GPT-OSS-120B-shape TP8 EP8)"
-BASELINE_VALUE = None  # BASELINE.md publishes no throughput number for this metric
+BASELINE_VALUE = None  # no published reference number exists for this metric
+OUT_DIR = os.environ.get("SNB_BENCH_OUT", os.path.join(ROOT, "bench_out"))  # clock samples, profiler tables
 
 
 def parse():
@@ -71,7 +72,7 @@ def reference_arm(a):
 class ClockSampler:
     def __init__(self, index: int):
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        self.path = os.path.join(OUT_DIR, f"clocks_rank{index}.csv")
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
@@ -116,7 +117,7 @@ class ClockSampler:
 
 def _profile_steps(eng, sched, refill, rank, n, dev):
     """Run n more steps under torch.profiler (CUPTI kernel activity, graph-replayed kernels included) and
-    write the per-kernel device-time table of this rank to gpurun_out/torchprof_rank<r>.txt."""
+    write the per-kernel device-time table of this rank to <SNB_BENCH_OUT>/torchprof_rank<r>.txt."""
     import torch
     from torch.profiler import ProfilerActivity, profile
     torch.cuda.synchronize(dev)
@@ -133,8 +134,8 @@ def _profile_steps(eng, sched, refill, rank, n, dev):
                 sched._process(*sched.inflight.popleft())
         sched.drain()
         torch.cuda.synchronize(dev)
-    os.makedirs("gpurun_out", exist_ok=True)
-    with open(f"gpurun_out/torchprof_rank{rank}.txt", "w") as f:
+    os.makedirs(OUT_DIR, exist_ok=True)
+    with open(os.path.join(OUT_DIR, f"torchprof_rank{rank}.txt"), "w") as f:
         f.write(p.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=90))
 
 
