@@ -38,6 +38,8 @@ from ..parallel.state import get_state
 
 logger = logging.getLogger(__name__)
 
+POLL_WIDTH = 64  # transfers whose state one poll reduce carries (later ones wait for the next poll)
+
 
 @dataclasses.dataclass
 class Header:
@@ -240,6 +242,12 @@ class DecodeSide:
         self.receiving: List[Tuple[Header, object, torch.Tensor, List[int], int, float]] = []
         self.quarantined: List[int] = []
         self.aborted: List[str] = []
+        # poll reduce: the MIN over the group's ranks of each transfer's state (2 received, 1 waiting,
+        # 0 timed out) through node shared memory; None (one rank, or no shared memory) keeps the leader's
+        # decision broadcast over gloo. Parity: the reference's poll reduce over node shm
+        # (sglang_neuron/disaggregation/poll_reduce.py:68-108).
+        from ..managers.scheduler import _make_shm
+        self._poll = _make_shm(get_state(), POLL_WIDTH, "pdpoll")
 
     def poll(self) -> None:
         sched = self.engine.scheduler
@@ -273,15 +281,27 @@ class DecodeSide:
             if self.link.is_leader:
                 self.link.put(f"pd/ready/{h.seq}", "ready")
             self.receiving.append((h, work, buf, pages, sched.epoch, time.time()))
-        # 2. completed receives become running requests (leader decides; followers wait for their own)
+        # 2. completed receives become running requests: every rank's own transfer state, MIN-reduced (or the
+        #    leader decides and followers wait for their own)
         done_seqs: List[int] = []
-        if self.link.is_leader:
+        if self._poll is not None:
+            items = self.receiving[:POLL_WIDTH]
+            now = time.time()
+            states = [2 if self.link.done(work) else (0 if now - t0 > self.link.timeout_s else 1)
+                      for _h, work, _b, _p, _e, t0 in items]
+            red = self._poll.min(states + [2] * (POLL_WIDTH - len(states)), timeout_s=1800.0)
+            for (h, *_rest), s in zip(items, red):
+                if s == 2:
+                    done_seqs.append(h.seq)
+                elif s == 0:
+                    done_seqs.append(-h.seq - 1)  # abort marker
+        elif self.link.is_leader:
             for h, work, buf, pages, _e, t0 in self.receiving:
                 if self.link.done(work):
                     done_seqs.append(h.seq)
                 elif time.time() - t0 > self.link.timeout_s:
                     done_seqs.append(-h.seq - 1)  # abort marker
-        if st.tp_size > 1:
+        if st.tp_size > 1 and self._poll is None:
             from ..parallel.collectives import cpu_broadcast_object
             done_seqs = cpu_broadcast_object(done_seqs, src=0)
         keep = []
