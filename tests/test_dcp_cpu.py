@@ -125,3 +125,24 @@ def test_dcp_prefix_cache_hits_keep_page_owners():
     two = _spawn(2, 2)
     assert two[0][0] == one[0] and two[1][0] == one[0]
     assert two[0][1][1] > 0 and two[0][1][2] > 0
+
+
+def test_dcp_view_local_tables_and_slots(monkeypatch):
+    """Global page g = local * D + owner: rank d's table keeps logical pages d, d + D, ... as local ids, and a
+    write slot survives only on the owner of its page (others get -1)."""
+    from sglang_neuron_b200.model_executor.forward_batch import ForwardBatch, ForwardMode
+    from sglang_neuron_b200.parallel import dcp as dcp_mod
+    from sglang_neuron_b200.parallel.state import ParallelState
+
+    P, D = 4, 2
+    gbt = torch.tensor([[2 * 1 + 0, 2 * 1 + 1, 2 * 2 + 0, 2 * 2 + 1, 0]], dtype=torch.int32)  # logical 0..3 + pad
+    loc = torch.tensor([gbt[0, 2].item() * P + 1, gbt[0, 3].item() * P + 3, -1], dtype=torch.int64)
+    fb = ForwardBatch(mode=ForwardMode.EXTEND, batch_size=1, num_tokens=3, input_ids=torch.zeros(3, dtype=torch.int64),
+                      positions=torch.zeros(3, dtype=torch.int64), out_cache_loc=loc,
+                      seq_lens=torch.tensor([16], dtype=torch.int32), block_table=gbt,
+                      logits_idx=torch.zeros(1, dtype=torch.int64))
+    for d, want_bt, want_loc in [(0, [1, 2, 0], [2 * P + 1, -1, -1]), (1, [1, 2], [-1, 2 * P + 3, -1])]:
+        monkeypatch.setattr(dcp_mod, "get_state", lambda d=d: ParallelState(dcp_size=D, dcp_rank=d))
+        fb.extra.clear()
+        bt, lloc = dcp_mod.DcpView(P).local(fb)
+        assert bt[0].tolist() == want_bt and lloc.tolist() == want_loc
