@@ -52,10 +52,22 @@ if runtime_sources:
         )
     )
 
+# SGLang selects a platform and loads plugins through these entry-point groups: `activate()` claims the process
+# on an sm_100 GPU, `register()` refuses unknown SGLANG_B200_* names and installs the runtime hooks of the
+# exported serving policy. Parity: the reference's pyproject.toml [project.entry-points] (same two groups).
+ENTRY_POINTS = {
+    "sglang.srt.platforms": ["b200 = sglang_neuron_b200:activate"],
+    "sglang.srt.plugins": ["b200_hooks = sglang_neuron_b200.general_plugin:register"],
+}
+
 setup(
     name="sglang_neuron_b200",
     version="0.1.0",
-    packages=["sglang_neuron_b200"],
+    packages=["sglang_neuron_b200"] + ["sglang_neuron_b200." + p for p in (
+        "attention", "benchmarks", "configs", "disaggregation", "entrypoints", "layers", "managers", "mem_cache",
+        "model_executor", "models", "ops", "parallel", "speculative", "utils")],
+    package_data={"sglang_neuron_b200": ["hook_pins.json"]},
+    entry_points=ENTRY_POINTS,
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -36,10 +36,19 @@ def trim_at_stop(text: str, stops) -> str:
 class Engine:
     def __init__(self, args: Optional[ServerArgs] = None, **kwargs):
         args = args or ServerArgs(**kwargs)
+        from . import env_registry, general_plugin, serving_policy
         from .platform import check_hybrid_swa
         check_hybrid_swa(args)
-        if args.device == "cuda" and not torch.cuda.is_available():
+        if args.device == "cuda" and (not torch.cuda.is_available()
+                                      or env_registry.get_bool("SGLANG_B200_CPU_MODE", False)):
             args.device = "cpu"
+        # this launch's serving policy: resolved once, exported, and read back by every part of the rank
+        # (scheduler overlap depth, graph capture, the plugin's runtime hooks)
+        serving_policy.export(serving_policy.resolve(args))
+        general_plugin.register()
+        self.policy = serving_policy.current()
+        if not self.policy.cuda_graph:
+            args.disable_cuda_graph = True
         self.args = args
         overrides = {}
         self.cfg: ModelConfig = resolve_model_config(args.model, **overrides)

@@ -123,6 +123,10 @@ def build_app(engine, loop_holder: Dict[str, Any]):
         d = {k: v for k, v in vars(engine.args).items()}
         d["scheduler_stats"] = dict(engine.scheduler.stats)
         d["kv_pages"] = engine.runner.num_pages
+        from .. import sglang_tree
+        d["parallel"] = sglang_tree.parallel_of()
+        d["rank_label"] = sglang_tree.rank_label()
+        d["serving_policy"] = dataclasses.asdict(engine.policy) if getattr(engine, "policy", None) else None
         return d
 
     @app.get("/v1/models")

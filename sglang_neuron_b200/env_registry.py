@@ -1,7 +1,9 @@
 """Registry of every `SGLANG_B200_*` environment variable, by class; unknown names are refused.
 
 Parity: sglang_neuron/env_registry.py (`refuse_unknown`, :125) keeps one table of the plugin's environment
-names so a typo cannot silently disable a setting. Same rule here for the `SGLANG_B200_` prefix.
+names so a typo cannot silently disable a setting. Same rule here for the `SGLANG_B200_` prefix, and every
+registered name has a reader (tests/test_runtime_cpu.py checks that each name appears in the package or the
+native sources besides this table).
 """
 from __future__ import annotations
 
@@ -14,11 +16,10 @@ PREFIX = "SGLANG_B200_"
 REGISTRY: Dict[str, tuple] = {
     "SGLANG_B200_SERVING_POLICY": ("policy", "JSON serving policy exported by the launching process"),
     "SGLANG_B200_HOST_TRACE": ("trace", "directory for per-rank host-trace TSV files"),
-    "SGLANG_B200_HOST_TRACE_SPANS": ("trace", "comma-separated extra host-trace spans"),
-    "SGLANG_B200_PROFILE_RANKS": ("profile", "ranks that profile from process start"),
-    "SGLANG_B200_PROFILE_SERVE_START": ("profile", "first decode step of a bounded profile window"),
+    "SGLANG_B200_PROFILE_RANKS": ("profile", "comma-separated ranks that take the serve profile window (default: all)"),
+    "SGLANG_B200_PROFILE_SERVE_START": ("profile", "first scheduler step of the bounded serve profile window"),
     "SGLANG_B200_PROFILE_SERVE_STEPS": ("profile", "length of the bounded profile window in steps"),
-    "SGLANG_B200_PROFILE_DIR": ("profile", "output directory of profile windows"),
+    "SGLANG_B200_PROFILE_DIR": ("profile", "output directory of the serve profile window (default profile_out)"),
     "SGLANG_B200_MAX_INFLIGHT_LAUNCHES": ("runtime", "steps launched ahead of result processing (overlap depth)"),
     "SGLANG_B200_SAMPLER": ("runtime", "'device' (default) or 'host' sampling"),
     "SGLANG_B200_DISABLE_FUSED_COLLECTIVES": ("parallel", "use NCCL instead of the NVLink fused kernels"),
@@ -27,13 +28,9 @@ REGISTRY: Dict[str, tuple] = {
     "SGLANG_B200_STEP_FENCE": ("debug", "1: ranks check through shared memory that each step launches the same program"),
     "SGLANG_B200_FUSED_AR_NORM": ("collectives", "residual add + RMSNorm inside the NVLink all-reduce kernels (0 turns it off)"),
     "SGLANG_B200_NVLS": ("parallel", "allow NVLS multimem (0/1)"),
-    "SGLANG_B200_PD_TRANSFER": ("disagg", "KV transfer backend for PD: 'p2p' (default) or 'fake'"),
-    "SGLANG_B200_PD_BOOTSTRAP_PORT": ("disagg", "bootstrap port of a prefill server"),
-    "SGLANG_B200_KERNEL_STATUS_CHECK": ("debug", "read kernel status words after every step (0/1)"),
-    "SGLANG_B200_BUILD_CACHE": ("build", "directory of the digest-keyed kernel build cache"),
-    "SGLANG_B200_CPU_MODE": ("debug", "force the CPU oracle path (torch reference ops)"),
+    "SGLANG_B200_KERNEL_STATUS_CHECK": ("debug", "copy and check the kernels' bounded-wait status words after every step (default 1)"),
+    "SGLANG_B200_CPU_MODE": ("debug", "1: serve on the CPU oracle path (torch reference ops) even with a GPU"),
     "SGLANG_B200_NUMA_BIND": ("placement", "bind each rank's threads to its GPU's NUMA node (0/1)"),
-    "SGLANG_B200_PROGRAM_FENCE_CHECK": ("debug", "all-gather the captured-graph id each step and compare"),
 }
 
 

@@ -57,7 +57,13 @@ class Scheduler:
         self.inflight: Deque[Tuple[StepInput, object, object]] = collections.deque()
         self.free_slots = list(range(runner.max_reqs - 1, -1, -1))
         self.epoch = 0
-        self.overlap = not args.disable_overlap_schedule
+        from .. import serving_policy
+        pol = serving_policy.current()
+        # overlap depth from the launch's serving policy: steps launched before the oldest one is processed
+        self.overlap = (pol.async_execution if pol is not None else not args.disable_overlap_schedule)
+        self.inflight_depth = max(1, pol.max_inflight_launches if pol is not None else 2)
+        if args.disable_overlap_schedule:
+            self.overlap = False
         self.eos = set(cfg.eos_token_id or [])
         self.pending_arrivals: List[Req] = []
         self.pending_aborts: List[str] = []
@@ -85,6 +91,11 @@ class Scheduler:
         import os
         self._fence = (_make_shm(st, 2, "fence") if os.environ.get("SGLANG_B200_STEP_FENCE") == "1"
                        and self.dp_groups == 1 else None)
+        # host timeline (select / launch / result spans per step), one TSV per rank label
+        from .. import sglang_tree
+        from ..utils.host_trace import HostTrace
+        self.trace = HostTrace(args.host_trace_dir or os.environ.get("SGLANG_B200_HOST_TRACE"),
+                               sglang_tree.rank_label())
 
     # ------------------------------------------------------------------------------------------
     # request intake
@@ -255,7 +266,9 @@ class Scheduler:
                 if slots and self.args.prefill_chunk_grid:  # keep the reused prefix on the chunk grid
                     gp = self.args.prefill_chunk_grid // self.P
                     slots = slots[: max(0, ((tree_pages + len(slots)) // gp) * gp - tree_pages)]
-                new = self._alloc_pages(len(slots)) if slots else None
+                # logical pages tree_pages.. onward (the start picks each page's owner under DCP; DCP with the
+                # host tier is refused at launch, so this start only matters if that refusal is lifted)
+                new = self._alloc_pages(len(slots), tree_pages) if slots else None
                 if new:
                     self.hicache.load(slots, new)
                     prefix_pages = prefix_pages + new
@@ -507,7 +520,8 @@ class Scheduler:
         self._sync_arrivals()
         if self.dp_groups > 1:
             return self._step_dp()
-        step = self.schedule()
+        with self.trace.span("select", self.epoch):
+            step = self.schedule()
         if self._fence is not None:
             key = (hash((int(step.mode), step.batch_size, step.num_tokens, step.max_extend)) & 0x3FFFFFFFFFFF
                    if step is not None else 0)
@@ -518,14 +532,17 @@ class Scheduler:
             t0 = time.perf_counter()
             if self.hicache is not None:
                 self.hicache.wait_loads()
-            ids_host, ev = self.runner.run_step(step)
+            with self.trace.span("launch", step.epoch, step.batch_size, step.num_tokens):
+                ids_host, ev = self.runner.run_step(step)
             self.inflight.append((step, ids_host, ev))
             self.stats["steps"] += 1
             self.stats["decode_steps" if step.mode == ForwardMode.DECODE else "extend_steps"] += 1
             self.step_times.append((step.epoch, t0, step.batch_size, step.num_tokens))
-        keep = 1 if (self.overlap and step is not None) else 0
+        keep = self.inflight_depth - 1 if (self.overlap and step is not None) else 0
         while len(self.inflight) > keep:
-            self._process(*self.inflight.popleft())
+            done = self.inflight[0][0]
+            with self.trace.span("result", done.epoch, done.batch_size, done.num_tokens):
+                self._process(*self.inflight.popleft())
 
     def _step_dp(self) -> None:
         """DP attention lockstep: every rank exchanges (rows it will run, busy, tokens published since the last

@@ -194,7 +194,8 @@ class ModelRunner:
         self.logits_hook = None  # test seam: called with (ForwardBatch, local logits) of eager steps
         self._logprobs = None
         self.status_watch = None
-        if self.cuda:
+        from .. import env_registry
+        if self.cuda and env_registry.get_bool("SGLANG_B200_KERNEL_STATUS_CHECK", True):
             from ..ops import gemm as gemm_ops, moe as moe_ops
             from ..parallel import collectives
             srcs = [gemm_ops._status_buf(self.device), moe_ops._status(self.device)]

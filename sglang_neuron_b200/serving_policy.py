@@ -4,6 +4,9 @@ and read (never re-derived) by every rank.
 Parity: sglang_neuron/serving_policy.py (`ServingPolicy` :32, `resolve` :426, `export` :551, `current` :559,
 `set_launch_setting` :534): role, async execution, overlap depth, giga decode, decode result lag, prefix
 cache backend and parallel sizes travel in one frozen object so policy stays out of user flags.
+
+Readers: `Engine` resolves and exports the policy of its launch, then the scheduler takes its overlap depth,
+the model runner its graph capture and the plugin's runtime hooks their sampler from `current()`.
 """
 from __future__ import annotations
 
@@ -30,16 +33,33 @@ class ServingPolicy:
     kv_cache_dtype: str = "auto"
     page_size: int = 16
     speculative: Optional[str] = None
+    sampler: str = "device"               # device | host (SGLANG_B200_SAMPLER)
     launch_settings: Dict[str, str] = dataclasses.field(default_factory=dict)
 
 
-def resolve(args) -> ServingPolicy:
+def resolve(args, environ=os.environ) -> ServingPolicy:
+    """The launch's policy from its arguments and the registered environment switches. A host sampler runs
+    outside CUDA graphs, so it turns graph capture off (recorded as a launch setting)."""
+    from . import env_registry
     role = {"null": "aggregated"}.get(args.disaggregation_mode, args.disaggregation_mode)
-    return ServingPolicy(
-        role=role, async_execution=not args.disable_overlap_schedule, cuda_graph=not args.disable_cuda_graph,
+    sampler = (env_registry.get("SGLANG_B200_SAMPLER", "device", environ) or "device").strip().lower()
+    if sampler not in ("device", "host"):
+        raise ValueError(f"SGLANG_B200_SAMPLER={sampler!r}: expected 'device' or 'host'")
+    depth = int(env_registry.get("SGLANG_B200_MAX_INFLIGHT_LAUNCHES", "2", environ))
+    if depth < 1:
+        raise ValueError("SGLANG_B200_MAX_INFLIGHT_LAUNCHES must be >= 1")
+    async_exec = not args.disable_overlap_schedule and depth > 1
+    pol = ServingPolicy(
+        role=role, async_execution=async_exec, max_inflight_launches=depth if async_exec else 1,
+        cuda_graph=not args.disable_cuda_graph and sampler == "device",
         mixed_chunk=args.enable_mixed_chunk, prefix_cache="none" if args.disable_radix_cache else "radix-page",
         tp_size=args.tp_size, ep_size=args.ep_size or args.tp_size, dp_size=args.dp_size,
-        kv_cache_dtype=args.kv_cache_dtype, page_size=args.page_size, speculative=args.speculative_algorithm)
+        fused_collectives=not env_registry.get_bool("SGLANG_B200_DISABLE_FUSED_COLLECTIVES", False, environ),
+        kv_cache_dtype=args.kv_cache_dtype, page_size=args.page_size, speculative=args.speculative_algorithm,
+        sampler=sampler)
+    if sampler == "host" and not args.disable_cuda_graph:
+        pol = set_launch_setting(pol, "cuda_graph", "off", "the host sampler reads logits on the host each step")
+    return pol
 
 
 def export(policy: ServingPolicy, environ=os.environ) -> str:

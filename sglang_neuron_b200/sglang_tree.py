@@ -2,6 +2,8 @@
 seam tests patch.
 
 Parity: sglang_neuron/sglang_tree.py:17-86 (`parallel_of`, `dp_widths`, `scheduler_batch`, `rank_label`).
+Readers: the server's `/get_server_info` route (parallel layout, rank label) and the host trace (file name per
+rank label).
 """
 from __future__ import annotations
 
@@ -12,7 +14,8 @@ from .parallel.state import get_state
 
 def parallel_of() -> Dict[str, int]:
     st = get_state()
-    return {"tp": st.tp_size, "ep": st.ep_size, "dp": st.dp_size, "pp": 1, "world": st.world_size}
+    return {"tp": st.tp_size, "ep": st.ep_size, "dp": st.dp_size, "pp": st.pp_size, "dcp": st.dcp_size,
+            "attn_dp": st.attn_dp_size, "world": st.world_size}
 
 
 def dp_widths() -> Tuple[int, int]:
@@ -26,4 +29,5 @@ def scheduler_batch(args) -> int:
 
 def rank_label() -> str:
     st = get_state()
-    return f"dp{st.dp_rank}-tp{st.tp_rank}"
+    lab = f"dp{st.dp_rank}-tp{st.tp_rank}"
+    return lab + (f"-pp{st.pp_rank}" if st.pp_size > 1 else "")

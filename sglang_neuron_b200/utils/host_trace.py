@@ -13,7 +13,7 @@ from typing import Optional
 
 
 class HostTrace:
-    def __init__(self, directory: Optional[str], rank: int = 0):
+    def __init__(self, directory: Optional[str], rank="0"):
         self.enabled = bool(directory)
         self.f = None
         self.lock = threading.Lock()

@@ -20,6 +20,7 @@ class ProfileWindow:
         self.num_steps = num_steps
         self.prof = None
         self.steps = 0
+        self.last_path: Optional[str] = None
 
     def start(self) -> None:
         os.makedirs(self.output_dir, exist_ok=True)
@@ -44,6 +45,7 @@ class ProfileWindow:
         path = os.path.join(self.output_dir, f"trace-{int(time.time())}.json")
         self.prof.export_chrome_trace(path)
         self.prof = None
+        self.last_path = path
         return path
 
 
