@@ -17,8 +17,11 @@
 //  * A call needs batch * num_q_heads * num_splits * (head_dim + 1) fp32 values of scratch; larger requests
 //    are rejected with SNB_NOALLOC_ERR_TOO_LARGE before anything is launched.
 //  * Host code cannot use the array's name as a device address. The first call made on a device (with that
-//    device current) looks the address up once with cudaGetSymbolAddress and caches it per device; make that
-//    first call outside any CUDA stream capture.
+//    device current) looks the address up with cudaGetSymbolAddress and caches it together with the
+//    device's current context; a call that finds a different context (after cudaDeviceReset, which reloads
+//    the module) looks it up again. Make the first call on a device outside any CUDA stream capture.
+//  * A CUDA error already pending on the calling thread is reported (SNB_NOALLOC_ERR_PRIOR) and left
+//    pending for its owner; the call then launches nothing.
 //  * All calls share the one array and it keeps whatever the previous call left in it. Nothing in it has to
 //    start at zero: each split writes every value the merge step later reads. Calls whose executions overlap
 //    on the GPU (different streams, or different host threads without ordering) race on the array and must
@@ -31,6 +34,7 @@
 #include <mutex>
 
 #include "../common.cuh"
+#include "../snb_noalloc.h"
 
 namespace {
 
@@ -177,6 +181,23 @@ __global__ void noalloc_merge_kernel(const float* __restrict__ o_part, const flo
 
 std::mutex g_setup_mutex;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
+CUcontext g_scratch_ctx[kMaxDevices] = {nullptr};
+
+// The calling thread's current context, through the runtime's driver entry point (no libcuda link needed).
+CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (Fn) nullptr;
+    return reinterpret_cast<Fn>(p);
+  }();
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
 
 template <int D, typename CacheT>
 int launch_na(int G, dim3 grid, cudaStream_t st, const __nv_bfloat16* q, int qs, const void* kc, const void* vc,
@@ -199,16 +220,8 @@ int launch_na(int G, dim3 grid, cudaStream_t st, const __nv_bfloat16* q, int qs,
 
 }  // namespace
 
-enum {
-  SNB_NOALLOC_OK = 0,
-  SNB_NOALLOC_ERR_ARGS = -1,
-  SNB_NOALLOC_ERR_TOO_LARGE = -2,
-  SNB_NOALLOC_ERR_SYMBOL = -3,
-  SNB_NOALLOC_ERR_LAUNCH = -4,
-};
-
 // Largest scratch request accepted, in fp32 values (batch * num_q_heads * num_splits * (head_dim + 1)).
-extern "C" __attribute__((visibility("default"))) long long snb_decode_attention_noalloc_scratch_capacity() {
+extern "C" __attribute__((visibility("default"))) long long snb_decode_attention_noalloc_scratch_capacity(void) {
   return kNoAllocScratchFloats;
 }
 
@@ -229,15 +242,20 @@ extern "C" __attribute__((visibility("default"))) int snb_decode_attention_noall
   if (batch == 0) return SNB_NOALLOC_OK;
   const long long need = (long long)batch * num_q_heads * num_splits * (head_dim + 1);
   if (need > kNoAllocScratchFloats) return SNB_NOALLOC_ERR_TOO_LARGE;
+  // an error left pending by earlier work belongs to its owner: report it and launch nothing, so the
+  // launch checks below see only this call's launches
+  if (cudaPeekAtLastError() != cudaSuccess) return SNB_NOALLOC_ERR_PRIOR;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SNB_NOALLOC_ERR_SYMBOL;
   float* base = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_scratch_ptr[dev] == nullptr) {
+    const CUcontext ctx = current_context();
+    if (g_scratch_ptr[dev] == nullptr || ctx == nullptr || ctx != g_scratch_ctx[dev]) {
       void* p = nullptr;
       if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return SNB_NOALLOC_ERR_SYMBOL;
       g_scratch_ptr[dev] = static_cast<float*>(p);
+      g_scratch_ctx[dev] = ctx;
     }
     base = g_scratch_ptr[dev];
   }

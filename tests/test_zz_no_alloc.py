@@ -8,15 +8,36 @@ second call reuses the library-resident scratch the first call left behind).
 This file is named so that pytest collects it last.
 """
 import ctypes
-import glob
 import os
+import re
 
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
-PKG = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "sglang_neuron_b200")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "sglang_neuron_b200")
+HEADER = os.path.join(ROOT, "csrc", "snb_noalloc.h")
+
+# C parameter type in the header -> ctypes type used for the call
+_CTYPES = {"void*": ctypes.c_void_p, "const void*": ctypes.c_void_p, "const int32_t*": ctypes.c_void_p,
+           "const float*": ctypes.c_void_p, "cudaStream_t": ctypes.c_void_p, "int": ctypes.c_int,
+           "float": ctypes.c_float}
+
+
+def _header_argtypes():
+    """ctypes argument types read from the prototype in csrc/snb_noalloc.h, so the call below cannot drift
+    from the declared signature."""
+    text = open(HEADER).read()
+    m = re.search(r"int snb_decode_attention_noalloc\(([^)]*)\);", text)
+    assert m, "prototype not found in the header"
+    types = []
+    for p in m.group(1).split(","):
+        p = " ".join(p.split())
+        t = p.rsplit(" ", 1)[0].replace(" *", "*")
+        types.append(_CTYPES[t])
+    return types
 
 
 def _lib():
@@ -24,18 +45,18 @@ def _lib():
     lib = ctypes.CDLL(ext.__file__)
     fn = lib.snb_decode_attention_noalloc
     fn.restype = ctypes.c_int
-    fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
-                   ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
-                   ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
-                   ctypes.c_float, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    fn.argtypes = _header_argtypes()
     cap = lib.snb_decode_attention_noalloc_scratch_capacity
     cap.restype = ctypes.c_longlong
     return fn, cap()
 
 
-def _case(seed, B, Hq, Hkv, D, P, fp8, window, with_sinks):
+def _case(seed, B, Hq, Hkv, D, P, fp8, window, with_sinks, short=False):
     g = torch.Generator().manual_seed(seed)
     ctx = torch.randint(1, 700, (B,), generator=g)
+    if short:  # empty contexts and contexts shorter than the split count: splits with no keys (lse = -inf)
+        ctx[0] = 0
+        ctx[1:3] = torch.tensor([1, 3])
     max_pages = int((ctx.max() + P - 1) // P) + 1
     n_pages = B * max_pages + 2
     perm = torch.randperm(n_pages, generator=g)
@@ -58,9 +79,10 @@ def test_noalloc_matches_decode_attention_two_calls(fp8, window, with_sinks, D, 
     P, S = 16, 4
     ks, vs = (0.9, 1.1) if fp8 else (1.0, 1.0)
     scale = D ** -0.5
+    from sglang_neuron_b200.ops.attention import decode_attention_ref
     for call in range(2):
         B = 6 if call == 0 else 9
-        q, kc, vc, bt, seq, sinks = _case(100 + call, B, Hq, Hkv, D, P, fp8, window, with_sinks)
+        q, kc, vc, bt, seq, sinks = _case(100 + call, B, Hq, Hkv, D, P, fp8, window, with_sinks, short=call == 1)
         assert B * Hq * S * (D + 1) <= capacity
         ref = decode_attention(q, kc, vc, bt, seq, Hq, Hkv, D, P, window, scale, ks, vs, sinks, num_splits=S)
         out = torch.full_like(ref, float("nan"))
@@ -73,6 +95,12 @@ def test_noalloc_matches_decode_attention_two_calls(fp8, window, with_sinks, D, 
         err = (out.float() - ref.float()).abs().max().item()
         tol = 2e-2 + 2e-2 * ref.float().abs().max().item()
         assert err <= tol, f"call {call}: max err {err} > {tol}"
+        # the fp32 PyTorch reference on CPU copies, so a fault shared by both kernels cannot pass
+        cpu = decode_attention_ref(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), seq.cpu(), Hq, Hkv, D, P, window, scale,
+                                   ks, vs, sinks.cpu() if sinks is not None else None)
+        err = (out.float().cpu() - cpu).abs().max().item()
+        tol = 2e-2 + 2e-2 * cpu.abs().max().item()
+        assert err <= tol, f"call {call}: max err vs fp32 reference {err} > {tol}"
 
 
 def test_noalloc_rejects_oversized_request():
