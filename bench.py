@@ -115,27 +115,51 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def _profile_steps(eng, sched, refill, rank, n, dev):
-    """Run n more steps under torch.profiler (CUPTI kernel activity, graph-replayed kernels included) and
-    write the per-kernel device-time table of this rank to <SNB_BENCH_OUT>/torchprof_rank<r>.txt."""
+def _profile_steps(eng, sched, refill, rank, n, dev, mode_filter=None):
+    """Profile steps under torch.profiler (CUPTI kernel activity, graph-replayed kernels included): n
+    consecutive steps, or with mode_filter ("mixed" or "decode") the next single step of that kind. Writes
+    the per-kernel device-time table of this rank to <SNB_BENCH_OUT>/torchprof_rank<r>[_<mode>].txt.
+    Eagerly launched kernels run without programmatic dependent launch here: with it, a kernel is timed from
+    the moment it becomes resident while its predecessor still runs, so durations would overlap."""
     import torch
     from torch.profiler import ProfilerActivity, profile
+
+    from sglang_neuron_b200._ext import kernels
+    kernels().set_pdl(False)
+
+    from sglang_neuron_b200.model_executor.forward_batch import ForwardMode
     torch.cuda.synchronize(dev)
-    with profile(activities=[ProfilerActivity.CUDA]) as p:
-        for _ in range(n):
-            refill()
-            sched._sync_arrivals()
-            step = sched.schedule()
-            if step is None:
-                continue
-            ids_host, ev = eng.runner.run_step(step)
-            sched.inflight.append((step, ids_host, ev))
-            while len(sched.inflight) > 1:
-                sched._process(*sched.inflight.popleft())
-        sched.drain()
-        torch.cuda.synchronize(dev)
+    p = profile(activities=[ProfilerActivity.CUDA])
+    taken, started = 0, False
+    for _ in range(max(n, 1) * 64):
+        if taken >= (1 if mode_filter else n):
+            break
+        refill()
+        sched._sync_arrivals()
+        step = sched.schedule()
+        if step is None:
+            continue
+        kind = "decode" if step.mode == ForwardMode.DECODE else "mixed"
+        hit = mode_filter is None or kind == mode_filter
+        if hit and not started:
+            sched.drain()
+            torch.cuda.synchronize(dev)
+            p.start()
+            started = True
+        ids_host, ev = eng.runner.run_step(step)
+        sched.inflight.append((step, ids_host, ev))
+        taken += int(hit)
+        while len(sched.inflight) > 1:
+            sched._process(*sched.inflight.popleft())
+    sched.drain()
+    torch.cuda.synchronize(dev)
+    if not started:
+        return
+    p.stop()
     os.makedirs(OUT_DIR, exist_ok=True)
-    with open(os.path.join(OUT_DIR, f"torchprof_rank{rank}.txt"), "w") as f:
+    suffix = f"_{mode_filter}" if mode_filter else ""
+    with open(os.path.join(OUT_DIR, f"torchprof_rank{rank}{suffix}.txt"), "w") as f:
+        f.write(f"{taken} profiled step(s)\n")
         f.write(p.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=90))
 
 
@@ -227,13 +251,16 @@ def main():
         torch.cuda.cudart().cudaProfilerStart()
     start_ev.record()
     timed_steps = []
+    step_evs = []  # one event at each step's launch point: consecutive pairs time each step on the device
     for _ in range(a.steps):
         refill()
-        n_before = len(sched.inflight)
         sched._sync_arrivals()
         step = sched.schedule()
         if step is None:
             continue
+        sev = torch.cuda.Event(enable_timing=True)
+        sev.record()
+        step_evs.append(sev)
         ids_host, ev = eng.runner.run_step(step)
         sched.inflight.append((step, ids_host, ev))
         sched.stats["steps"] += 1
@@ -249,15 +276,17 @@ def main():
     wall = time.perf_counter() - wall0
     clk = clocks.stop()
     dev_ms = start_ev.elapsed_time(end_ev)
+    step_ms = [e0.elapsed_time(e1) for e0, e1 in zip(step_evs, step_evs[1:] + [end_ev])]
     delivered = sched.stats["output_tokens"] - delivered0
     launches = _ext.launch_count() - launches0
     n_steps = len(timed_steps)
     h2d = (io.h2d_bytes - h2d0) / max(1, n_steps)
     d2h = (io.d2h_bytes - d2h0) / max(1, n_steps)
     if world > 1:
-        t = torch.tensor([dev_ms, wall], device=dev)
+        t = torch.tensor([dev_ms, wall] + step_ms, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, wall = float(t[0]), float(t[1])
+        step_ms = t[2:].tolist()
     # latency stats from the requests that received tokens in the window
     ttfts, itls = [], []
     for r in sched.finished_reqs + [req(rid) for rid in live if req(rid) is not None]:
@@ -268,6 +297,13 @@ def main():
     value = produced / (dev_ms / 1e3)
     e2e = delivered / wall
     mixed = sum(1 for s in timed_steps if s.mode != ForwardMode.DECODE)
+    dec_ms = [t for s, t in zip(timed_steps, step_ms) if s.mode == ForwardMode.DECODE]
+    mix_ms = [t for s, t in zip(timed_steps, step_ms) if s.mode != ForwardMode.DECODE]
+    step_stats = {"decode_p50_ms": round(statistics.median(dec_ms), 3) if dec_ms else None,
+                  "decode_mean_ms": round(statistics.fmean(dec_ms), 3) if dec_ms else None,
+                  "mixed_ms": [round(t, 3) for t in mix_ms],
+                  "mixed_tokens": [int(s.num_tokens) for s in timed_steps if s.mode != ForwardMode.DECODE],
+                  "how": "CUDA events at each step's launch point, max over ranks"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": a.gpus, "steps": n_steps,
@@ -281,7 +317,9 @@ def main():
                        "l2": "inputs larger than L2 (60+ GB of expert weights streamed per step)",
                        "steps_mixed_prefill": mixed, "cuda_graph": not a.no_graph},
             "p50_ttft_ms": round(statistics.median(ttfts), 2) if ttfts else None,
+            "ttft_samples": len(ttfts),
             "p50_itl_ms": round(statistics.median(itls), 3) if itls else None,
+            "step_device_ms": step_stats,
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h),
                     "how": "host wall clock around the same steps via Engine scheduler/runner (pinned H2D inputs, "
@@ -293,7 +331,8 @@ def main():
         print(json.dumps(line), flush=True)
     if os.environ.get("SNB_TORCH_PROFILE"):
         # attribution only (after the timed region): per-kernel device time of a few more steps, every rank
-        _profile_steps(eng, sched, refill, rank, int(os.environ.get("SNB_TORCH_PROFILE")), dev)
+        _profile_steps(eng, sched, refill, rank, int(os.environ.get("SNB_TORCH_PROFILE")), dev,
+                       os.environ.get("SNB_TORCH_PROFILE_MODE") or None)
     eng.shutdown()
     if world > 1:
         dist.barrier()

@@ -33,7 +33,7 @@ void topk_route(torch::Tensor weights, torch::Tensor ids, torch::Tensor logits, 
 void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, torch::Tensor seg_offsets,
                torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map);
 void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
-                        int64_t bn);
+                        int64_t bn, c10::optional<torch::Tensor> used);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, bool accumulate);
 // moe_gemm_sm100.cu
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
@@ -98,7 +98,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_tokens", &sample_tokens);
   m.def("topk_route", &topk_route);
   m.def("moe_align", &moe_align);
-  m.def("gather_quant_mxfp8", &gather_quant_mxfp8);
+  m.def("gather_quant_mxfp8", &gather_quant_mxfp8, py::arg("q"), py::arg("sf"), py::arg("x"), py::arg("src"),
+        py::arg("bn"), py::arg("used") = py::none());
   m.def("moe_combine", &moe_combine);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("moe_gemm", &moe_gemm, py::arg("out"), py::arg("xq"), py::arg("sfb"), py::arg("w"), py::arg("sfa"),

@@ -173,13 +173,16 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
 
 // One warp per permuted row; each lane quantises whole 32-element blocks.
 // x: [T, H] bf16 (row stride xs). Output q: [R, Kp] e4m3 (Kp = padded row pitch), scales in atom order.
+// `used` (optional, device): the number of rows the expert segments actually occupy (seg_offsets[E_local]);
+// rows past it belong to no tile the grouped GEMM runs, so they are skipped. The grid stays sized for the
+// static capacity R (graph capture), but the work follows the routed row count, which shrinks with EP.
 __global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int xs, const int32_t* __restrict__ src,
                                           int R, int H, int Kp, int BN, uint8_t* __restrict__ q,
-                                          uint8_t* __restrict__ sf) {
+                                          uint8_t* __restrict__ sf, const int32_t* __restrict__ used) {
   snb::pdl_wait();
   snb::pdl_trigger();
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (r >= R) return;
+  if (r >= R || (used != nullptr && r >= *used)) return;
   const int s = src != nullptr ? src[r] : r;
   const int KB = (Kp + 127) / 128;           // 128-wide K blocks
   const int nblk = KB * 4;                    // 32-wide scale blocks incl. padding
@@ -288,7 +291,7 @@ void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, tor
 }
 
 void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
-                        int64_t bn) {
+                        int64_t bn, c10::optional<torch::Tensor> used) {
   const int R = q.size(0), Kp = q.size(1), H = x.size(1);
   if (R == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && H % 32 == 0, "gather_quant: x");
@@ -300,7 +303,8 @@ void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10:
   const int threads = 256, blocks = (R * 32 + threads - 1) / threads;
   snb::launch_pdl(gather_quant_mxfp8_kernel, blocks, threads, 0, st, (const __nv_bfloat16*)x.data_ptr(), x.stride(0),
                                                        src ? src->data_ptr<int32_t>() : nullptr, R, H, Kp, bn,
-                                                       (uint8_t*)q.data_ptr(), (uint8_t*)sf.data_ptr());
+                                                       (uint8_t*)q.data_ptr(), (uint8_t*)sf.data_ptr(),
+                                                       used ? used->data_ptr<int32_t>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -21,6 +21,9 @@ def main():
     p.add_argument("--hidden", type=int, default=2880)
     p.add_argument("--k-local", type=int, default=0)
     p.add_argument("--iters", type=int, default=50)
+    p.add_argument("--graph", action="store_true",
+                   help="time the ops replayed from a CUDA graph (no host launch cost between calls)")
+    p.add_argument("--cta-sweep", action="store_true", help="one-shot all-reduce at several CTA counts")
     a = p.parse_args()
     from ..parallel.state import init_process_group_from_env, initialize_parallel
     from ..parallel.symm_mem import IpcAllReduce
@@ -50,18 +53,47 @@ def main():
         for _ in range(5):
             fn()
         torch.cuda.synchronize()
+        g = None
+        if a.graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(a.iters):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
         dist.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(a.iters):
-            fn()
+        if g is not None:
+            g.replay()
+        else:
+            for _ in range(a.iters):
+                fn()
         e.record()
         torch.cuda.synchronize()
         v = torch.tensor([s.elapsed_time(e) / a.iters * 1e3], device=dev)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        del g
         return round(float(v), 2)
 
-    res = {"world": world, "tokens": T, "hidden": H, "k_local": K,
+    if a.cta_sweep:
+        from ..parallel.collectives import FusedNorm
+        sweep = {}
+        resid = torch.randn(T, H, device=dev).to(torch.bfloat16)
+        nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+
+        class _N:  # stand-in norm module for FusedNorm
+            weight, eps = nw, 1e-5
+
+        for c in (8, 16, 32, 64, 128, 148):
+            ar.max_ctas = c
+            sweep[f"oneshot_ctas{c}_us"] = t_op(lambda: ar.all_reduce(x, out))
+            sweep[f"oneshot_norm_ctas{c}_us"] = t_op(lambda: ar.all_reduce(x, out, norm=FusedNorm(resid, nw, 1e-5)))
+        ar.max_ctas = 64
+        if rank == 0:
+            print(json.dumps({"world": world, "tokens": T, "graph": a.graph, **sweep}), flush=True)
+
+    res = {"world": world, "tokens": T, "hidden": H, "k_local": K, "graph": a.graph,
            "nccl_allreduce_us": t_op(lambda: dist.all_reduce(x)),
            "oneshot_allreduce_us": t_op(lambda: ar.all_reduce(x, out)),
            "combine_then_nccl_us": t_op(lambda: (moe_combine(out, y, al.inv_map, w), dist.all_reduce(out))),

@@ -1,6 +1,7 @@
 """Kernel microbenchmarks with roofline fractions (CUDA-event timed, warm, L2 flushed between iterations).
 
     python -m sglang_neuron_b200.benchmarks.kernels moe --tokens 64        # one GPT-OSS-120B MoE layer
+    python -m sglang_neuron_b200.benchmarks.kernels moe_stages --tokens 1087 --ep 8   # per-stage, one EP rank
     python -m sglang_neuron_b200.benchmarks.kernels gemm --tokens 64 --n 5120 --k 2880
     python -m sglang_neuron_b200.benchmarks.kernels attn --batch 64 --ctx 1536
 
@@ -103,6 +104,59 @@ def bench_moe(a):
                       "tflops": round(flops / (us * 1e-6) / 1e12, 2)}))
 
 
+def bench_moe_stages(a):
+    """Per-stage device time of one MoE layer (routing, alignment, MXFP8 quantise, gate/up GEMM, activation
+    quantise, down GEMM, combine), each timed alone (PDL off, L2 flushed). --ep N keeps 1/N of the experts
+    local, as one rank of EP N sees them."""
+    from .._ext import kernels
+    from ..ops import moe
+    kernels().set_pdl(False)
+    E, H, I, K = a.experts, 2880, 2880, 4
+    El = E // a.ep
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w13 = torch.randint(0, 256, (El, 2 * I, H // 2), device="cuda", dtype=torch.uint8, generator=g)
+    s13 = torch.randint(119, 122, (El, 2 * I, H // 32), device="cuda", dtype=torch.uint8, generator=g)
+    w2 = torch.randint(0, 256, (El, H, I // 2), device="cuda", dtype=torch.uint8, generator=g)
+    s2 = torch.randint(119, 122, (El, H, I // 32), device="cuda", dtype=torch.uint8, generator=g)
+    ew = moe.ExpertWeights(w13, s13, torch.zeros(El, 2 * I, device="cuda", dtype=torch.bfloat16), w2, s2,
+                           torch.zeros(El, H, device="cuda", dtype=torch.bfloat16), H, I, True)
+    T = a.tokens
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    logits = torch.randn(T, E, device="cuda")
+    w, ids = moe.topk_route(logits, K)
+    bn = a.bn or moe.pick_bn(T, K, El)
+    al = moe.MoEAlignment(T * K, El, bn, "cuda")
+    moe.moe_align(ids, 0, El, al)
+    R = al.r_max
+    used = al.seg_offsets[El:El + 1]
+    xq, sfb = moe.gather_quant_mxfp8(x, al.sorted_src, R, bn, used=used)
+    act = torch.empty(R, I, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    st = {
+        "route": lambda: moe.topk_route(logits, K),
+        "align": lambda: moe.moe_align(ids, 0, El, al),
+        "quant_x_all_rows": lambda: moe.gather_quant_mxfp8(x, al.sorted_src, R, bn),
+        "quant_x": lambda: moe.gather_quant_mxfp8(x, al.sorted_src, R, bn, used=used),
+        "gate_up": lambda: moe.moe_gemm(act, xq, sfb, ew.w13, ew.sfa13, ew.b13, al, moe.EPI_SWIGLU_CLAMP, 2 * I),
+        "quant_act": lambda: moe.gather_quant_mxfp8(act, None, R, bn, used=used),
+        "down": lambda: moe.moe_gemm(y, xq[:, :I] if I == H else xq, sfb, ew.w2, ew.sfa2, ew.b2, al, moe.EPI_BIAS, H),
+        "combine": lambda: moe.moe_combine(out, y, al.inv_map, w),
+    }
+    res = {"tokens": T, "experts_local": El, "bn": bn, "rows_capacity": R, "rows_used": int(used.item())}
+    only = set(a.only.split(",")) if a.only else None
+    for k, f in st.items():
+        if only is None or k in only:
+            res[k + "_us"] = round(timeit(f, a.iters, a.warmup), 2)
+    if only is not None:
+        kernels().set_pdl(True)
+        print(json.dumps(res))
+        return
+    res["fused_moe_us"] = round(timeit(lambda: moe.fused_moe(x, w, ids, ew, al=al, bn=bn), a.iters, a.warmup), 2)
+    kernels().set_pdl(True)
+    print(json.dumps(res))
+
+
 def bench_gemm(a):
     from ..ops.gemm import linear
     T, N, K = a.tokens, a.n, a.k
@@ -166,7 +220,10 @@ def bench_attn(a):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["moe", "gemm", "attn"])
+    p.add_argument("which", choices=["moe", "moe_stages", "gemm", "attn"])
+    p.add_argument("--ep", type=int, default=1)
+    p.add_argument("--bn", type=int, default=0, help="moe_stages: force the token tile (16/32/64/128)")
+    p.add_argument("--only", default="", help="moe_stages: comma-separated stages to time")
     p.add_argument("--tokens", type=int, default=64)
     p.add_argument("--experts", type=int, default=128)
     p.add_argument("--n", type=int, default=5120)
@@ -177,7 +234,7 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     a = p.parse_args()
-    {"moe": bench_moe, "gemm": bench_gemm, "attn": bench_attn}[a.which](a)
+    {"moe": bench_moe, "moe_stages": bench_moe_stages, "gemm": bench_gemm, "attn": bench_attn}[a.which](a)
 
 
 if __name__ == "__main__":

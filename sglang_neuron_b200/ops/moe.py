@@ -158,8 +158,10 @@ def sf_atom_offset(row_in_tile: torch.Tensor, kk: torch.Tensor) -> torch.Tensor:
     return (row_in_tile % 32) * 16 + (row_in_tile // 32) * 4 + kk
 
 
-def gather_quant_mxfp8(x: torch.Tensor, src: Optional[torch.Tensor], rows: int, bn: int, kp: int = None):
+def gather_quant_mxfp8(x: torch.Tensor, src: Optional[torch.Tensor], rows: int, bn: int, kp: int = None,
+                       used: Optional[torch.Tensor] = None):
     """Permute rows of x by `src` (-1 = zero row) and quantise to MXFP8 with scales in chunk-atom order.
+    `used` ([1] int32 on the device, the routed row count) lets the kernel skip rows no GEMM tile reads.
     Returns (q [rows, kp] float8_e4m3fn, sf uint8 flat)."""
     H = x.shape[1]
     kp = H if kp is None else kp
@@ -170,7 +172,7 @@ def gather_quant_mxfp8(x: torch.Tensor, src: Optional[torch.Tensor], rows: int, 
         # the kernel writes every scale byte the MMA reads (rows < BN of each chunk, all K blocks); the
         # remaining bytes of a chunk belong to rows the MMA never reads, so no fill is needed
         sf = torch.empty(nsf, dtype=torch.uint8, device=x.device)
-        kernels().gather_quant_mxfp8(q, sf, x, src, bn)
+        kernels().gather_quant_mxfp8(q, sf, x, src, bn, used)
         return q, sf
     sf = torch.full((nsf,), 127, dtype=torch.uint8, device=x.device)
     s = src.long() if src is not None else torch.arange(rows)
@@ -331,7 +333,8 @@ def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew:
         al = MoEAlignment(T * K, E, bn, x.device)
     moe_align(topk_ids, e_lo, E, al)
     R = al.r_max
-    xq, sfb = gather_quant_mxfp8(x, al.sorted_src, R, bn)
+    used = al.seg_offsets[E:E + 1]  # rows the local experts' segments occupy (<= R)
+    xq, sfb = gather_quant_mxfp8(x, al.sorted_src, R, bn, used=used)
     epi = EPI_SWIGLU_CLAMP if activation == "swiglu_clamp" else EPI_SILU
     if _fused_act_quant():
         # the gate/up epilogue quantises its activation to MXFP8 in place of a separate gather-quantise launch
@@ -344,7 +347,7 @@ def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew:
     else:
         act = torch.empty(R, ew.inter, dtype=torch.bfloat16, device=x.device)
         moe_gemm(act, xq, sfb, ew.w13, ew.sfa13, ew.b13, al, epi, 2 * ew.inter, alpha, limit)
-        aq, sfb2 = gather_quant_mxfp8(act, None, R, bn)
+        aq, sfb2 = gather_quant_mxfp8(act, None, R, bn, used=used)
     y = torch.empty(R, H, dtype=torch.bfloat16, device=x.device)
     moe_gemm(y, aq, sfb2, ew.w2, ew.sfa2, ew.b2, al, EPI_BIAS, H)
     if out is None:
