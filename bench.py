@@ -39,6 +39,9 @@ def parse():
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--baseline", default="", choices=["", "nccl"],
+                   help="nccl: this engine with cuBLAS dense GEMMs and NCCL collectives (no fused kernels), the "
+                        "comparison build the repository's baseline tables quote")
     p.add_argument("--model", default="gpt-oss-120b")
     p.add_argument("--concurrency", type=int, default=64)
     p.add_argument("--input-len", type=int, default=1024)
@@ -168,6 +171,8 @@ def main():
     if a.impl == "reference":
         reference_arm(a)
         return
+    if a.baseline:
+        os.environ["SGLANG_B200_BASELINE"] = a.baseline
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -308,7 +313,8 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": a.gpus, "steps": n_steps,
             "warmup": a.warmup, "ms_per_step": round(dev_ms / max(1, n_steps), 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "impl": "ours",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "impl": "baseline-nccl-cublas" if a.baseline else "ours",
             "data": "synthetic token ids (uniform, seeded); random-init weights of the named architecture",
             "config": {"model": "GPT-OSS-120B-shape (36 layers, hidden 2880, 64q/8kv heads x 64, 128 experts top-4, "
                                 "MXFP4 experts, FP8 KV, alternating SWA-128/full, sinks, YaRN)",

@@ -6,6 +6,7 @@
 // then the call epoch counter and a completion ticket. A call reads e = counter + 1 in every CTA, uses half
 // (e & 1), and its last CTA to finish stores the counter.
 #pragma once
+#include <vector>
 #include "common.cuh"
 
 namespace snb_ar {
@@ -15,7 +16,16 @@ constexpr int kMaxCtas = 1024;  // flag slots per rank (CTAs or output tiles of 
 
 struct ARPeers {
   uint8_t* buf[kMaxRanks];  // mapped base of every rank's buffer (mine included)
+  unsigned long long wait_ns;  // budget of each peer-flag wait (a runtime argument: tests make it short)
 };
+
+// Host: the peer table of a call; wait_ns <= 0 takes the default budget SNB_WAIT_NS.
+inline ARPeers make_peers(const std::vector<int64_t>& bufs, int64_t wait_ns) {
+  ARPeers p;
+  for (int i = 0; i < kMaxRanks; ++i) p.buf[i] = i < (int)bufs.size() ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  p.wait_ns = wait_ns > 0 ? (unsigned long long)wait_ns : (unsigned long long)SNB_WAIT_NS;
+  return p;
+}
 
 SNB_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -62,7 +72,7 @@ SNB_DEVICE bool ar_exchange(const ARPeers& peers, const ARBuf& b, int rank, int 
     const uint32_t* fp = b.flags + threadIdx.x * kMaxCtas + blockIdx.x;
     const uint64_t t0 = snb::globaltimer_ns();
     while (ld_acquire_sys(fp) < e) {
-      if (snb::globaltimer_ns() - t0 > SNB_WAIT_NS) {
+      if (snb::globaltimer_ns() - t0 > peers.wait_ns) {
         snb::record_status(status, SNB_ERR_TIMEOUT_PEER);
         ok_s = 0;
         break;

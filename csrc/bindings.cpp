@@ -18,7 +18,8 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
                       int64_t head_dim, int64_t page_size, int64_t window, double sm_scale, double k_scale,
                       double v_scale, c10::optional<torch::Tensor> sinks, int64_t num_splits, torch::Tensor o_part,
-                      torch::Tensor lse_part, c10::optional<torch::Tensor> status);
+                      torch::Tensor lse_part, c10::optional<torch::Tensor> status,
+                      c10::optional<torch::Tensor> merge_counters);
 void extend_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                       torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
                       int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t page_size,
@@ -35,6 +36,12 @@ void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, tor
 void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
                         int64_t bn, c10::optional<torch::Tensor> used);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, bool accumulate);
+// moe_route_fused.cu
+void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::optional<torch::Tensor> bias,
+                     int64_t k, int64_t mode, double scale, int64_t e_lo, int64_t e_local, int64_t bn,
+                     torch::Tensor partial, torch::Tensor w_out, torch::Tensor id_out, torch::Tensor seg_offsets,
+                     torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map, torch::Tensor q,
+                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks);
 // moe_gemm_sm100.cu
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets, int64_t bn,
@@ -66,7 +73,8 @@ void nvls_splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t spl
 bool get_pdl();
 void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
                       std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status,
-                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps);
+                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps,
+                      int64_t wait_ns);
 
 void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                          torch::Tensor status, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
@@ -77,11 +85,12 @@ int64_t symm_open(py::bytes handle);
 void symm_close(int64_t ptr, bool owned);
 void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
                         int64_t capacity, int64_t num_ctas, torch::Tensor status,
-                        c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps);
+                        c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps,
+                        int64_t wait_ns);
 void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w,
                            std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas,
                            torch::Tensor status, c10::optional<torch::Tensor> residual,
-                           c10::optional<torch::Tensor> weight, double eps);
+                           c10::optional<torch::Tensor> weight, double eps, int64_t wait_ns);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sglang_neuron_b200 sm_100a kernels";
@@ -93,7 +102,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_table"), py::arg("seq_lens"), py::arg("num_q_heads"), py::arg("num_kv_heads"),
         py::arg("head_dim"), py::arg("page_size"), py::arg("window"), py::arg("sm_scale"), py::arg("k_scale"),
         py::arg("v_scale"), py::arg("sinks"), py::arg("num_splits"), py::arg("o_part"), py::arg("lse_part"),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("merge_counters") = py::none());
   m.def("extend_attention", &extend_attention);
   m.def("sample_tokens", &sample_tokens);
   m.def("topk_route", &topk_route);
@@ -101,6 +110,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_quant_mxfp8", &gather_quant_mxfp8, py::arg("q"), py::arg("sf"), py::arg("x"), py::arg("src"),
         py::arg("bn"), py::arg("used") = py::none());
   m.def("moe_combine", &moe_combine);
+  m.def("moe_route_fused", &moe_route_fused);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("moe_gemm", &moe_gemm, py::arg("out"), py::arg("xq"), py::arg("sfb"), py::arg("w"), py::arg("sfa"),
         py::arg("bias"), py::arg("seg_offsets"), py::arg("tile_offsets"), py::arg("bn"), py::arg("epi"),
@@ -111,14 +121,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("one_shot_allreduce", &one_shot_allreduce, py::arg("out"), py::arg("inp"), py::arg("bufs"), py::arg("rank"),
-        py::arg("capacity"), py::arg("num_ctas"), py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
+        py::arg("capacity"), py::arg("num_ctas"), py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0,
+        py::arg("wait_ns") = 0);
   m.def("moe_combine_allreduce", &moe_combine_allreduce, py::arg("out"), py::arg("y"), py::arg("inv_map"),
         py::arg("w"), py::arg("bufs"), py::arg("rank"), py::arg("capacity"), py::arg("num_ctas"), py::arg("status"),
-        py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
+        py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0,
+        py::arg("wait_ns") = 0);
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
   m.def("splitk_allreduce", &splitk_allreduce, py::arg("out"), py::arg("partial"), py::arg("splits"),
         py::arg("bias"), py::arg("bufs"), py::arg("rank"), py::arg("capacity"), py::arg("num_ctas"),
-        py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0);
+        py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0,
+        py::arg("wait_ns") = 0);
   m.def("set_pdl", &set_pdl);
   m.def("mla_decode", &mla_decode);
   m.def("mla_extend", &mla_extend, py::arg("out"), py::arg("q"), py::arg("cache"), py::arg("block_table"),

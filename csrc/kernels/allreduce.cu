@@ -185,7 +185,8 @@ static ARNorm make_norm(const c10::optional<torch::Tensor>& residual, const c10:
 
 void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
                         int64_t capacity, int64_t num_ctas, torch::Tensor status,
-                        c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps) {
+                        c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps,
+                        int64_t wait_ns) {
   const int world = (int)bufs.size();
   TORCH_CHECK(world >= 1 && world <= kMaxRanks, "one_shot_allreduce: world size");
   TORCH_CHECK(in.scalar_type() == at::kBFloat16 && in.is_contiguous() && out.is_contiguous(), "one_shot_allreduce: bf16");
@@ -193,8 +194,7 @@ void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t
   TORCH_CHECK(n % 8 == 0 && (size_t)n * 2 <= (size_t)capacity, "one_shot_allreduce: size ", n, " over capacity");
   TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "one_shot_allreduce: CTA count");
   const ARNorm nm = make_norm(residual, weight, eps, n, num_ctas);
-  ARPeers peers;
-  for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  const ARPeers peers = make_peers(bufs, wait_ns);
   auto kern = residual ? one_shot_allreduce_kernel<true> : one_shot_allreduce_kernel<false>;
   snb::launch_pdl(kern, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, (const __nv_bfloat16*)in.data_ptr(), (__nv_bfloat16*)out.data_ptr(), n, nm,
@@ -205,7 +205,7 @@ void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t
 void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w,
                            std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas,
                            torch::Tensor status, c10::optional<torch::Tensor> residual,
-                           c10::optional<torch::Tensor> weight, double eps) {
+                           c10::optional<torch::Tensor> weight, double eps, int64_t wait_ns) {
   const int world = (int)bufs.size();
   const int T = out.size(0), H = out.size(1), K = w.size(1);
   TORCH_CHECK(world >= 1 && world <= kMaxRanks && H % 8 == 0, "moe_combine_allreduce: shape");
@@ -214,8 +214,7 @@ void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv
   if (T == 0) return;
   const ARNorm nm = make_norm(residual, weight, eps, (int64_t)T * H, num_ctas);
   TORCH_CHECK(!residual || nm.H == H, "moe_combine_allreduce: norm size");
-  ARPeers peers;
-  for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  const ARPeers peers = make_peers(bufs, wait_ns);
   auto kern = residual ? moe_combine_allreduce_kernel<true> : moe_combine_allreduce_kernel<false>;
   snb::launch_pdl(kern, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
@@ -225,7 +224,8 @@ void moe_combine_allreduce(torch::Tensor out, torch::Tensor y, torch::Tensor inv
 
 void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, c10::optional<torch::Tensor> bias,
                       std::vector<int64_t> bufs, int64_t rank, int64_t capacity, int64_t num_ctas, torch::Tensor status,
-                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps) {
+                      c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps,
+                      int64_t wait_ns) {
   const int world = (int)bufs.size();
   const int T = out.size(0), F = out.size(1);
   TORCH_CHECK(F % 8 == 0 && out.is_contiguous() && partial.scalar_type() == at::kFloat, "splitk_allreduce: layout");
@@ -235,8 +235,7 @@ void splitk_allreduce(torch::Tensor out, torch::Tensor partial, int64_t splits, 
   if (T == 0) return;
   const ARNorm nm = make_norm(residual, weight, eps, (int64_t)T * F, num_ctas);
   TORCH_CHECK(!residual || nm.H == F, "splitk_allreduce: norm size");
-  ARPeers peers;
-  for (int i = 0; i < kMaxRanks; ++i) peers.buf[i] = i < world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  const ARPeers peers = make_peers(bufs, wait_ns);
   auto kern = residual ? splitk_allreduce_kernel<true> : splitk_allreduce_kernel<false>;
   snb::launch_pdl(kern, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
       peers, rank, world, capacity, partial.data_ptr<float>(), splits,

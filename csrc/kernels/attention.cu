@@ -399,7 +399,8 @@ bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
 bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                           torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
                           int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
-                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status);
+                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status,
+                          int* merge_cnt, float v_scale_out);
 
 bool extend_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                           torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
@@ -414,7 +415,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
                       int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
                       double sm_scale, double k_scale, double v_scale, c10::optional<torch::Tensor> sinks,
                       int64_t num_splits, torch::Tensor o_part, torch::Tensor lse_part,
-                      c10::optional<torch::Tensor> status) {
+                      c10::optional<torch::Tensor> status, c10::optional<torch::Tensor> merge_counters) {
   const int B = q.size(0);
   if (B == 0) return;
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16, "decode_attention: bf16 q/out");
@@ -442,10 +443,17 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   // fp8 cache: bulk-async pipelined tensor-core kernel; else the register-prefetch tensor-core kernel for every
   // GQA group up to 16 heads; the CUDA-core kernel below covers the rest
   int* stp = status ? status->data_ptr<int>() : nullptr;
-  const bool mma_done =
-      (stp != nullptr && decode_attention_fp8(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads,
-                                              num_kv_heads, head_dim, page_size, window, scale, vs, sk, S, op, lp,
-                                              stp)) ||
+  int* mcnt = nullptr;
+  if (merge_counters && S > 1) {
+    TORCH_CHECK(merge_counters->scalar_type() == at::kInt && merge_counters->numel() >= (int64_t)B * num_kv_heads,
+                "decode_attention: merge counters");
+    mcnt = merge_counters->data_ptr<int>();
+  }
+  const bool fp8_done = stp != nullptr && decode_attention_fp8(out, q, k_cache, v_cache, block_table, seq_lens,
+                                                               num_q_heads, num_kv_heads, head_dim, page_size, window,
+                                                               scale, vs, sk, S, op, lp, stp, mcnt, (float)v_scale);
+  const bool merged = fp8_done && mcnt != nullptr;
+  const bool mma_done = fp8_done ||
       decode_attention_mma(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads, num_kv_heads, head_dim,
                            page_size, window, scale, vs, sk, S, op, lp);
   if (!mma_done) {
@@ -470,7 +478,7 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
 #undef SNB_DEC_D
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
-  if (S > 1) {
+  if (S > 1 && !merged) {
     snb::launch_pdl(decode_merge_kernel, B * num_q_heads, 64, 0, st, op, lp, sk, outp, out.stride(0), num_q_heads, head_dim, S,
                                                         (float)v_scale);
     C10_CUDA_KERNEL_LAUNCH_CHECK();

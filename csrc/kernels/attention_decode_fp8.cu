@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_kernel(
     const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ seq_lens, int page_size,
     int Hkv, int G, int window, float scale_log2, float v_scale, const float* __restrict__ sinks,
     __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part, float* __restrict__ lse_part,
-    int num_splits, int* status) {
+    int num_splits, int* status, int* __restrict__ merge_cnt, float v_scale_out) {
   using C = Fp8Cfg<D>;
   constexpr int NT = D / 8;      // n8 tiles of the output (head dim)
   constexpr int KB = D / 4;      // K bytes per thread per token row
@@ -340,16 +340,52 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_kernel(
     for (int i = sh[1]; i < sh[0]; ++i)
       if (!snb::mbar_wait_bounded(&full[i % C::NST], (i / C::NST) & 1, status, SNB_ERR_TIMEOUT_TMA)) break;
   }
+  if (num_splits > 1 && merge_cnt != nullptr) {
+    // Split merge in this launch: the last split CTA of (request, KV head) to finish combines every split's
+    // normalised partial (log2-sum-exp weights, sinks in the denominator) and writes the output rows; it
+    // then re-arms the counter for the next call. Partials are read past L1 (written by other CTAs).
+    __threadfence();
+    __syncthreads();
+    int* cnt = merge_cnt + (size_t)b * Hkv + hk;
+    if (tid == 0) sh[3] = atomicAdd(cnt, 1) == num_splits - 1;
+    __syncthreads();
+    if (sh[3]) {
+      __threadfence();
+      const int Hq = Hkv * G;
+      for (int idx = tid; idx < G * D; idx += kThreads) {
+        const int g = idx / D, d = idx % D, h = hk * G + g;
+        const size_t base = ((size_t)b * Hq + h) * num_splits;
+        float M = -INFINITY;
+        for (int s = 0; s < num_splits; ++s) M = fmaxf(M, __ldcg(lse_part + base + s));
+        const float sk = sinks != nullptr ? sinks[h] * kL2e : -INFINITY;
+        const float Mx = fmaxf(M, sk);
+        float total = (sk == -INFINITY) ? 0.f : exp2f(sk - Mx), acc = 0.f;
+        for (int s = 0; s < num_splits; ++s) {
+          const float l = __ldcg(lse_part + base + s);
+          if (l == -INFINITY) continue;
+          const float f = exp2f(l - Mx);
+          total += f;
+          acc += f * __ldcg(o_part + (base + s) * D + d);
+        }
+        const float r = (M == -INFINITY || total <= 0.f) ? 0.f : acc / total * v_scale_out;
+        out[(size_t)b * out_stride + (size_t)h * D + d] = __float2bfloat16(r);
+      }
+      if (tid == 0) *cnt = 0;
+    }
+  }
 }
 
 }  // namespace
 
 // Same contract as decode_attention_mma() for an fp8 cache; false when not covered (head_dim not 64/128, G > 16,
-// or a page size that is neither a divisor nor a multiple of the 64-token tile).
+// or a page size that is neither a divisor nor a multiple of the 64-token tile). With merge_cnt (zeroed int32
+// per (request, KV head)) and more than one split, the split merge runs inside this launch (v_scale_out is
+// applied there) and no merge kernel follows.
 bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                           torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
                           int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
-                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status) {
+                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status,
+                          int* merge_cnt, float v_scale_out) {
   const int G = num_q_heads / num_kv_heads;
   if (k_cache.scalar_type() != at::kFloat8_e4m3fn || G > 16 || (head_dim != 64 && head_dim != 128)) return false;
   if (!((page_size >= 16 && kTile % page_size == 0) || (page_size >= kTile && page_size % kTile == 0))) return false;
@@ -374,7 +410,8 @@ bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
                                    block_table.data_ptr<int32_t>(), (int)block_table.stride(0),                 \
                                    seq_lens.data_ptr<int32_t>(), (int)page_size, (int)num_kv_heads, G,           \
                                    (int)window, scale_log2, v_scale_final, sinks, (__nv_bfloat16*)out.data_ptr(), \
-                                   (int)out.stride(0), o_part, lse_part, (int)num_splits, status));              \
+                                   (int)out.stride(0), o_part, lse_part, (int)num_splits, status, merge_cnt,     \
+                                   v_scale_out));                                                                \
   }
   if (head_dim == 64) SNB_FP8(64) else SNB_FP8(128)
 #undef SNB_FP8

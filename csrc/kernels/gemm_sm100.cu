@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t* fp = arb.flags + lane * snb_ar::kMaxCtas + tile;
         const uint64_t tw = snb::globaltimer_ns();
         while (snb_ar::ld_acquire_sys(fp) < ar_epoch) {
-          if (snb::globaltimer_ns() - tw > SNB_WAIT_NS) {
+          if (snb::globaltimer_ns() - tw > ar.peers.wait_ns) {
             snb::record_status(status, SNB_ERR_TIMEOUT_PEER);
             ar_ok = 0;
             break;
@@ -533,8 +533,7 @@ void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c1
   ar.world = (int)bufs.size();
   ar.capacity = capacity;
   TORCH_CHECK(ar.world >= 1 && ar.world <= snb_ar::kMaxRanks, "gemm_bf16_allreduce: world size");
-  for (int i = 0; i < snb_ar::kMaxRanks; ++i)
-    ar.peers.buf[i] = i < ar.world ? reinterpret_cast<uint8_t*>(bufs[i]) : nullptr;
+  ar.peers = snb_ar::make_peers(bufs, 0);
   auto st = at::cuda::getCurrentCUDAStream();
   const __nv_bfloat16* bp = bias ? (const __nv_bfloat16*)bias->data_ptr() : nullptr;
   int* sp = status.data_ptr<int>();

@@ -157,6 +157,32 @@ def bench_moe_stages(a):
     print(json.dumps(res))
 
 
+def bench_route(a):
+    """The one-launch MoE routing kernel against router GEMM + top-k + align + quantise (four launches)."""
+    from ..ops import moe
+    from ..ops.gemm import TiledWeight, linear
+    T, E, H, K = a.tokens, a.experts, 2880, 4
+    El = E // a.ep
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    wr = TiledWeight((torch.randn(E, H, device="cuda") * 0.02).to(torch.bfloat16))
+    bias = torch.zeros(E, device="cuda", dtype=torch.bfloat16)
+    bn = moe.pick_bn(T, K, El)
+    al = moe.MoEAlignment(T * K, El, bn, "cuda")
+
+    def sep():
+        w, ids = moe.topk_route(linear(x, wr, bias), K)
+        moe.moe_align(ids, 0, El, al)
+        moe.gather_quant_mxfp8(x, al.sorted_src, al.r_max, bn, used=al.seg_offsets[El:El + 1])
+
+    fused = lambda: moe.fused_route_quant(x, wr, E, bias, K, 0, 1.0, 0, El, bn)  # noqa: E731
+    res = {"tokens": T, "experts": E, "experts_local": El,
+           "fused_us": round(timeit(fused, a.iters, a.warmup), 2), "separate_us": round(timeit(sep, a.iters, a.warmup), 2)}
+    if a.iters > 1:
+        res["fused_in_graph_us"] = round(graph_time([fused] * 8), 2)
+        res["separate_in_graph_us"] = round(graph_time([sep] * 8), 2)
+    print(json.dumps(res))
+
+
 def bench_gemm(a):
     from ..ops.gemm import linear
     T, N, K = a.tokens, a.n, a.k
@@ -220,7 +246,7 @@ def bench_attn(a):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["moe", "moe_stages", "gemm", "attn"])
+    p.add_argument("which", choices=["moe", "moe_stages", "route", "gemm", "attn"])
     p.add_argument("--ep", type=int, default=1)
     p.add_argument("--bn", type=int, default=0, help="moe_stages: force the token tile (16/32/64/128)")
     p.add_argument("--only", default="", help="moe_stages: comma-separated stages to time")
@@ -234,7 +260,8 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     a = p.parse_args()
-    {"moe": bench_moe, "moe_stages": bench_moe_stages, "gemm": bench_gemm, "attn": bench_attn}[a.which](a)
+    {"moe": bench_moe, "moe_stages": bench_moe_stages, "route": bench_route, "gemm": bench_gemm,
+     "attn": bench_attn}[a.which](a)
 
 
 if __name__ == "__main__":

@@ -69,7 +69,8 @@ class Engine:
         self.custom_ar = None
         if st.tp_size > 1 and device.type == "cuda":
             from . import env_registry
-            if not env_registry.get_bool("SGLANG_B200_DISABLE_FUSED_COLLECTIVES", False):
+            from .ops.gemm import cublas_baseline
+            if not env_registry.get_bool("SGLANG_B200_DISABLE_FUSED_COLLECTIVES", False) and not cublas_baseline():
                 from .parallel.collectives import set_custom_allreduce
                 from .parallel.symm_mem import make_tp_allreduce
                 self.custom_ar = make_tp_allreduce()

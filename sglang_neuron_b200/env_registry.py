@@ -24,6 +24,8 @@ REGISTRY: Dict[str, tuple] = {
     "SGLANG_B200_SAMPLER": ("runtime", "'device' (default) or 'host' sampling"),
     "SGLANG_B200_DISABLE_FUSED_COLLECTIVES": ("parallel", "use NCCL instead of the NVLink fused kernels"),
     "SGLANG_B200_MOE_FUSED_ACT_QUANT": ("kernels", "1: gate/up GEMM epilogue writes MXFP8 directly (default: separate quantise)"),
+    "SGLANG_B200_FUSED_ROUTE": ("kernels", "decode-sized MoE routing (router GEMM, top-k, align, quantise) in one launch (0 turns it off)"),
+    "SGLANG_B200_BASELINE": ("bench", "'nccl': comparison build with cuBLAS dense GEMMs and NCCL collectives (no fused kernels)"),
     "SGLANG_B200_PDL": ("kernels", "programmatic dependent launch of the sm_100a kernels (0 turns it off)"),
     "SGLANG_B200_STEP_FENCE": ("debug", "1: ranks check through shared memory that each step launches the same program"),
     "SGLANG_B200_FUSED_AR_NORM": ("collectives", "residual add + RMSNorm inside the NVLink all-reduce kernels (0 turns it off)"),

@@ -33,8 +33,10 @@ class PackedWeight:
         return self._packed if self._packed is not None else self.weight
 
     def pack(self) -> None:
+        from ..ops.gemm import cublas_baseline
         w = self.weight
-        if self._packed is not None or not w.is_cuda or w.dtype != torch.bfloat16 or w.dim() != 2 or not w.numel():
+        if (self._packed is not None or not w.is_cuda or w.dtype != torch.bfloat16 or w.dim() != 2 or not w.numel()
+                or cublas_baseline()):  # the cuBLAS comparison build keeps nn.Linear weights
             return
         self._packed = TiledWeight(w.data)
         self.weight = nn.Parameter(torch.empty(0, dtype=w.dtype, device=w.device), requires_grad=False)

@@ -32,6 +32,10 @@ from ..parallel.collectives import (FusedNorm, deferred_reduction, dp_gather_row
                                     fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden, sp_all_gather,
                                     sp_gather_rows, sp_reduce_scatter, tp_all_reduce)
 from ..parallel.state import get_state, pp_layer_range
+from .. import env_registry
+
+# decode-sized MoE routing in one launch (SGLANG_B200_FUSED_ROUTE=0: router GEMM, top-k, align, quantise)
+_FUSED_ROUTE = env_registry.get_bool("SGLANG_B200_FUSED_ROUTE", False)
 
 
 class RMSNorm(nn.Module):
@@ -165,9 +169,24 @@ class MoEBlock(nn.Module):
         self.device = device
         self.alignment_cache = {}
 
-    def forward(self, x: torch.Tensor, norm=None) -> torch.Tensor:
+    def route(self, x: torch.Tensor):
+        """(topk_w, topk_ids, routed): decode-sized CUDA batches take the one-launch routing kernel (router
+        GEMM, top-k, alignment and MXFP8 quantise), whose `routed` result fused_moe consumes directly."""
+        E = self.cfg.num_experts
+        if (x.is_cuda and _FUSED_ROUTE and self.router._packed is not None and 0 < x.shape[0]
+                and x.shape[0] * E <= moe_ops.ROUTE_FUSED_MAX_LOGITS and x.shape[1] % 64 == 0
+                and x.stride(1) == 1 and (x.stride(0) * 2) % 16 == 0 and x.data_ptr() % 16 == 0):
+            bn = moe_ops.pick_bn(x.shape[0], self.top_k, self.e_local)
+            w, ids, al, xq, sfb = moe_ops.fused_route_quant(
+                x, self.router._packed, E, self.router.bias, self.top_k, self.route_mode,
+                self.cfg.routed_scaling_factor, self.e_lo, self.e_local, bn)
+            return w, ids, (al, xq, sfb)
         logits = self.router(x)
         w, ids = moe_ops.topk_route(logits, self.top_k, self.route_mode, self.cfg.routed_scaling_factor)
+        return w, ids, None
+
+    def forward(self, x: torch.Tensor, norm=None) -> torch.Tensor:
+        w, ids, routed = self.route(x)
         if self.shared is None and x.is_cuda and get_state().tp_size > 1:
             # combine + expert-parallel all-reduce (+ the next residual add and norm) in one NVLink kernel
             reduced = [False]
@@ -177,10 +196,10 @@ class MoEBlock(nn.Module):
                 return reduced[0]
 
             out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
-                                    self.cfg.swiglu_limit, e_lo=self.e_lo, combine_fn=combine)
+                                    self.cfg.swiglu_limit, e_lo=self.e_lo, combine_fn=combine, routed=routed)
             return out if reduced[0] else tp_all_reduce(out, norm=norm)
         out = moe_ops.fused_moe(x, w, ids, self.experts, self.activation, self.cfg.swiglu_alpha,
-                                self.cfg.swiglu_limit, e_lo=self.e_lo)
+                                self.cfg.swiglu_limit, e_lo=self.e_lo, routed=routed)
         if self.shared is not None:
             out = out + self.shared(x)
         return tp_all_reduce(out, norm=norm)

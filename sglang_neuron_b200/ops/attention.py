@@ -100,6 +100,8 @@ class DecodeScratch:
         self.max_splits = max_splits
         self.o = torch.empty(max_batch * num_q_heads * max_splits * head_dim, dtype=torch.float32, device=device)
         self.lse = torch.empty(max_batch * num_q_heads * max_splits, dtype=torch.float32, device=device)
+        # arrival counters of the in-kernel split merge (FP8 kernel): zero between calls, re-armed by the kernel
+        self.merge_cnt = torch.zeros(max_batch * num_q_heads, dtype=torch.int32, device=device)
 
 
 def decode_attention(q, k_cache, v_cache, block_table, seq_lens, num_q_heads, num_kv_heads, head_dim,
@@ -117,17 +119,18 @@ def decode_attention(q, k_cache, v_cache, block_table, seq_lens, num_q_heads, nu
     B = q.shape[0]
     if out is None:
         out = torch.empty(B, num_q_heads * head_dim, dtype=q.dtype, device=q.device)
+    cnt = None
     if num_splits > 1:
         if scratch is None:
             scratch = DecodeScratch(B, num_q_heads, head_dim, num_splits, q.device)
         assert num_splits <= scratch.max_splits
-        o_part, lse_part = scratch.o, scratch.lse
+        o_part, lse_part, cnt = scratch.o, scratch.lse, scratch.merge_cnt
     else:
         o_part = lse_part = torch.empty(0, dtype=torch.float32, device=q.device)
     from .gemm import _status_buf
     kernels().decode_attention(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads, num_kv_heads,
                                head_dim, page_size, window, sm_scale, k_scale, v_scale, sinks, num_splits,
-                               o_part, lse_part, _status_buf(q.device))
+                               o_part, lse_part, _status_buf(q.device), cnt)
     return out
 
 

@@ -81,10 +81,20 @@ def pick_splits(T: int, F: int, K: int, num_sms: int = 148) -> int:
     return int(max(1, min(num_sms // ctas, nk // 2, 16)))
 
 
+def cublas_baseline() -> bool:
+    """SGLANG_B200_BASELINE=nccl: the comparison build - dense GEMMs through cuBLAS (torch.matmul) and every
+    collective through NCCL, the rest of the engine unchanged."""
+    from .. import env_registry
+    return (env_registry.get("SGLANG_B200_BASELINE", "") or "").strip().lower() == "nccl"
+
+
+_CUBLAS = cublas_baseline()
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, out=None,
            bn: int = 0, splits: Optional[int] = None) -> torch.Tensor:
     """y = x @ w.T (+ bias). x: [..., K], w: [F, K] tensor or TiledWeight."""
-    if not x.is_cuda or x.dtype != torch.bfloat16:
+    if not x.is_cuda or x.dtype != torch.bfloat16 or (_CUBLAS and not isinstance(w, TiledWeight)):
         if isinstance(w, TiledWeight):
             w = w.untiled()
         y = torch.nn.functional.linear(x, w, bias)

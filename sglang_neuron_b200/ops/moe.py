@@ -305,36 +305,71 @@ def _fused_act_quant() -> bool:
 
 
 def pick_bn(num_tokens: int, top_k: int, num_experts: int) -> int:
+    """Token tile of the grouped GEMM. Tiles of up to 32 tokens run two CTAs per SM and keep the weight stream
+    near the HBM roofline; 64- and 128-token tiles run one CTA per SM whose epilogue (128 x BN accumulators
+    through named barriers) cannot keep up (ncu on the 1087-token GPT-OSS layer: 27 % of DRAM bandwidth,
+    barrier stalls first). Measured per layer at 1087 tokens: gate/up 333 us with 32-token tiles against 532
+    (64) and 991 (128); at 16 local experts 65 us against 84 and 141. Larger token counts re-read each weight
+    tile once per 32-token tile, from L2 (neighbouring CTAs take neighbouring tiles of the same expert)."""
     per_expert = num_tokens * top_k / max(1, num_experts)
-    if per_expert <= 12:
-        return 16
-    if per_expert <= 24:
-        return 32
-    if per_expert <= 56:
-        return 64
-    return 128
+    return 16 if per_expert <= 12 else 32
+
+
+ROUTE_FUSED_MAX_LOGITS = 16384  # T * E the one-launch routing kernel stages in shared memory
+_route_sync = {}
+
+
+def fused_route_quant(x: torch.Tensor, router_w, num_experts: int, bias: Optional[torch.Tensor], k: int,
+                      mode: int, scale: float, e_lo: int, e_local: int, bn: int):
+    """Router GEMM + top-k + expert alignment + MXFP8 gather-quantise in one launch (decode-sized T).
+    router_w: the router weight as ops.gemm.TiledWeight. Returns (topk_w, topk_ids, MoEAlignment, xq, sfb),
+    the values topk_route(linear(x, router_w, bias)), moe_align and gather_quant_mxfp8 produce."""
+    T, H = x.shape
+    dev = x.device
+    w = torch.empty(T, k, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+    al = MoEAlignment(T * k, e_local, bn, dev)
+    R = al.r_max
+    xq = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
+    sfb = torch.empty((R // bn) * ((H + 127) // 128) * sf_chunk_bytes(bn), dtype=torch.uint8, device=dev)
+    kc = max(1, (H + 319) // 320)  # ~320-wide K chunks: E/16 x kc CTAs
+    partial = torch.empty(kc * T * num_experts, dtype=torch.float32, device=dev)
+    key = (dev.type, dev.index)
+    if key not in _route_sync:
+        _route_sync[key] = torch.zeros(2, dtype=torch.int32, device=dev)
+    kernels().moe_route_fused(x, router_w.data, num_experts, bias, k, mode, scale, e_lo, e_local, bn, partial, w,
+                              ids, al.seg_offsets, al.tile_offsets, al.sorted_src, al.inv_map, xq, sfb,
+                              _route_sync[key], _status(dev), kc)
+    return w, ids, al, xq, sfb
 
 
 def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew: ExpertWeights,
               activation: str = "swiglu_clamp", alpha: float = 1.702, limit: float = 7.0,
               e_lo: int = 0, bn: int = 0, al: Optional[MoEAlignment] = None, out=None,
-              combine_fn=None) -> torch.Tensor:
+              combine_fn=None, routed=None) -> torch.Tensor:
     """sum_j w[t,j] * expert_{id[t,j]}(x[t]) over the experts owned here ([e_lo, e_lo + E_local)).
     `combine_fn(out, y, inv_map, w) -> bool` may replace the final combine (e.g. with the combine fused into
-    the expert-parallel all-reduce); it returns False to fall back to the local combine."""
+    the expert-parallel all-reduce); it returns False to fall back to the local combine.
+    `routed` = (MoEAlignment, xq, sfb) from fused_route_quant: alignment and quantisation are done."""
     T, H = x.shape
     K = topk_ids.shape[1]
     if not x.is_cuda:
         return fused_moe_ref(x, topk_w, topk_ids, ew, activation, alpha, limit, e_lo, out=out)
     E = ew.num_experts
-    if bn <= 0:
-        bn = pick_bn(T, K, E)
-    if al is None or al.bn != bn:
-        al = MoEAlignment(T * K, E, bn, x.device)
-    moe_align(topk_ids, e_lo, E, al)
-    R = al.r_max
-    used = al.seg_offsets[E:E + 1]  # rows the local experts' segments occupy (<= R)
-    xq, sfb = gather_quant_mxfp8(x, al.sorted_src, R, bn, used=used)
+    if routed is not None:
+        al, xq, sfb = routed
+        bn = al.bn
+        R = al.r_max
+        used = al.seg_offsets[E:E + 1]
+    else:
+        if bn <= 0:
+            bn = pick_bn(T, K, E)
+        if al is None or al.bn != bn:
+            al = MoEAlignment(T * K, E, bn, x.device)
+        moe_align(topk_ids, e_lo, E, al)
+        R = al.r_max
+        used = al.seg_offsets[E:E + 1]  # rows the local experts' segments occupy (<= R)
+        xq, sfb = gather_quant_mxfp8(x, al.sorted_src, R, bn, used=used)
     epi = EPI_SWIGLU_CLAMP if activation == "swiglu_clamp" else EPI_SILU
     if _fused_act_quant():
         # the gate/up epilogue quantises its activation to MXFP8 in place of a separate gather-quantise launch

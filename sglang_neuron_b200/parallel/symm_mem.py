@@ -94,14 +94,27 @@ def make_tp_allreduce(capacity_bytes: int = 8 << 20):
 
 
 class IpcAllReduce:
-    def __init__(self, capacity_bytes: int = 8 << 20, max_ctas: int = 64):
-        st = get_state()
-        self.rank, self.world = st.tp_rank, st.tp_size
+    """`wait_ns`: budget of every peer-flag wait in these kernels (0: the compiled default of 2 s). A wait that
+    runs out records SNB_ERR_TIMEOUT_PEER in `status`, skips the reduce and returns; the engine raises at the
+    next step boundary."""
+
+    def __init__(self, capacity_bytes: int = 8 << 20, max_ctas: int = 64, wait_ns: int = 0, ptrs=None):
         self.capacity = capacity_bytes
         self.max_ctas = max_ctas
+        self.wait_ns = wait_ns
         k = kernels()
+        if ptrs is not None:
+            # a caller-built peer table (tests: every slot a buffer of this GPU, rank 0)
+            self.rank, self.world, self.own = 0, len(ptrs), ptrs[0]
+            self.ptrs = list(ptrs)
+            self._owned = set(range(len(ptrs)))
+            self.status = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", torch.cuda.current_device()))
+            return
+        st = get_state()
+        self.rank, self.world = st.tp_rank, st.tp_size
         ptr, handle = k.symm_alloc(capacity_bytes, self.world)
         self.own = ptr
+        self._owned = {self.rank}
         handles: List = [None] * self.world
         dist.all_gather_object(handles, (self.rank, handle), group=st.cpu_group)
         self.ptrs = [0] * self.world
@@ -131,7 +144,7 @@ class IpcAllReduce:
         nvec = x.numel() // 8
         ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))  # ~4 KB per CTA: many SMs drive NVLink
         kernels().one_shot_allreduce(out, x, self.ptrs, self.rank, self.capacity, ctas, self.status,
-                                     **self._norm_kw(norm))
+                                     wait_ns=self.wait_ns, **self._norm_kw(norm))
         return out
 
     def combine_all_reduce(self, out: torch.Tensor, y: torch.Tensor, inv_map: torch.Tensor,
@@ -140,7 +153,7 @@ class IpcAllReduce:
         nvec = out.numel() // 8
         ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))
         kernels().moe_combine_allreduce(out, y, inv_map, w, self.ptrs, self.rank, self.capacity, ctas, self.status,
-                                        **self._norm_kw(norm))
+                                        wait_ns=self.wait_ns, **self._norm_kw(norm))
         return out
 
     def gemm_can_run(self, T: int, F: int, num_sms: int) -> bool:
@@ -165,12 +178,12 @@ class IpcAllReduce:
         nvec = T * F // 8
         ctas = max(1, min(self.max_ctas, (nvec + 255) // 256))
         kernels().splitk_allreduce(out, partial, splits, bias, self.ptrs, self.rank, self.capacity, ctas, self.status,
-                                   **self._norm_kw(norm))
+                                   wait_ns=self.wait_ns, **self._norm_kw(norm))
         return out
 
     def close(self) -> None:
         k = kernels()
         for r, p in enumerate(self.ptrs):
             if p:
-                k.symm_close(p, r == self.rank)
+                k.symm_close(p, r in self._owned)
         self.ptrs = []

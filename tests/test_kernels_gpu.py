@@ -405,3 +405,106 @@ def test_mla_extend_kernel_dcp_partials_merge(D, H, chunks, P):
     ref = torch.cat([_one(q[qo[b]:qo[b + 1]].float(), ref_cache[b], torch.arange(n_log, dtype=torch.int32), lens[b],
                           torch.arange(chunks[b][0], lens[b]), 512, scale, P) for b in range(B)])
     _close(got, ref, 2e-2, 2e-2, "mla_extend dcp")
+
+
+@pytest.mark.parametrize("T,E,K,mode,El,e_lo", [(64, 128, 4, 0, 128, 0), (37, 128, 4, 0, 16, 32),
+                                                 (96, 64, 6, 1, 64, 0), (5, 128, 4, 0, 128, 0),
+                                                 (128, 128, 4, 0, 16, 112)])
+def test_fused_route_matches_separate_launches(T, E, K, mode, El, e_lo):
+    """The one-launch routing kernel against the fp32 router logits and the separate align/quantise ops."""
+    from sglang_neuron_b200.ops import moe
+    from sglang_neuron_b200.ops.gemm import TiledWeight
+    torch.manual_seed(T + E)
+    H = 2880
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    wr = (torch.randn(E, H, device=DEV) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(E, device=DEV) * 0.1).to(torch.bfloat16)
+    scale = 1.0 if mode == 0 else 2.5
+    bn = moe.pick_bn(T, K, El)
+    w, ids, al, xq, sfb = moe.fused_route_quant(x, TiledWeight(wr), E, bias, K, mode, scale, e_lo, El, bn)
+    torch.cuda.synchronize()
+    assert int(moe._status(x.device)[0]) == 0
+    # selection: the fp32 logits of the chosen experts are the top-k (up to bf16 rounding of near ties)
+    lf = (x.float() @ wr.float().t() + bias.float()).cpu()
+    top = lf.topk(K, dim=-1).values
+    got = lf.gather(1, ids.long().cpu())
+    assert (got.sort(dim=-1, descending=True).values - top).abs().max().item() <= 0.02
+    lb = lf.to(torch.bfloat16).float()  # the kernel rounds its logits to bf16 like the router GEMM's output
+    if mode == 0:
+        w_ref = torch.softmax(lb.gather(1, ids.long().cpu()), dim=-1) * scale
+    else:
+        w_ref = torch.softmax(lb, dim=-1).gather(1, ids.long().cpu()) * scale
+    _close(w.cpu(), w_ref, 2e-2, 2e-2, "routing weights")
+    # alignment: segments as moe_align lays them out for the same ids, every entry mapped back to its token
+    al2 = moe.MoEAlignment(T * K, El, bn, DEV)
+    moe.moe_align(ids, e_lo, El, al2)
+    assert torch.equal(al.seg_offsets, al2.seg_offsets) and torch.equal(al.tile_offsets, al2.tile_offsets)
+    used = int(al.seg_offsets[El])
+    inv = al.inv_map[: T * K].cpu()
+    src = al.sorted_src.cpu()
+    for i in range(T * K):
+        e = int(ids.view(-1)[i]) - e_lo
+        if 0 <= e < El:
+            assert int(src[int(inv[i])]) == i // K
+        else:
+            assert int(inv[i]) == -1
+    assert int((src[:used] >= 0).sum()) == int((inv >= 0).sum())
+    # quantised rows: byte-identical to the separate quantise kernel over the same permutation
+    q2, sf2 = moe.gather_quant_mxfp8(x, al.sorted_src, al.r_max, bn, used=al.seg_offsets[El:El + 1])
+    torch.cuda.synchronize()
+    assert torch.equal(xq[:used].view(torch.uint8), q2[:used].view(torch.uint8))
+    # scale bytes the MMA reads: (row i of each BN tile, 32-block kk) of every K block of the used tiles
+    KB = (H + 127) // 128
+    i = torch.arange(bn).repeat_interleave(4)
+    kk = torch.arange(4).repeat(bn)
+    offs = moe.sf_atom_offset(i, kk)
+    idx = torch.cat([(c * moe.sf_chunk_bytes(bn)) + offs for c in range((used // bn) * KB)]).to(DEV)
+    assert torch.equal(sfb[idx], sf2[idx])
+
+
+def test_decode_attention_merge_counters_rearm():
+    """FP8 split-K decode with the in-kernel merge: one scratch (counters included) over several calls and
+    batch sizes, each output against the fp32 reference."""
+    from sglang_neuron_b200.ops.attention import DecodeScratch, decode_attention, decode_attention_ref
+    torch.manual_seed(21)
+    D, Hq, Hkv, P, S = 64, 64, 8, 16, 4
+    sc = DecodeScratch(8, Hq, D, S, DEV)
+    for call, ctx in enumerate([[5, 700, 64], [1000, 3, 77, 129, 512, 2, 16, 300], [40]]):
+        B = len(ctx)
+        kc, vc, bt = _make_paged(B, ctx, Hkv, D, P, torch.float8_e4m3fn)
+        q = torch.randn(B, Hq * D, dtype=torch.bfloat16)
+        sk = torch.randn(Hq)
+        seq = torch.tensor(ctx, dtype=torch.int32)
+        ref = decode_attention_ref(q.float(), kc, vc, bt, seq, Hq, Hkv, D, P, 0, None, 0.9, 1.2, sk)
+        out = decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), seq.to(DEV), Hq, Hkv, D, P, 0, None,
+                               0.9, 1.2, sk.to(DEV), num_splits=S, scratch=sc)
+        _close(out, ref, 2e-2, 2e-2, f"decode call {call}")
+        assert int(sc.merge_cnt.abs().sum()) == 0, "merge counters must be re-armed"
+
+
+def test_allreduce_peer_wait_runs_out_with_status():
+    """A world-of-2 all-reduce whose second rank never publishes (its slot is a buffer of this GPU that nobody
+    writes a flag into): the bounded peer wait runs out after its short budget, the kernel records
+    SNB_ERR_TIMEOUT_PEER and returns, and the context stays usable. No GPU fault is involved."""
+    import time
+    from sglang_neuron_b200._ext import kernels
+    from sglang_neuron_b200.parallel.symm_mem import IpcAllReduce
+    k = kernels()
+    cap = 1 << 20
+    p0, _ = k.symm_alloc(cap, 2)
+    p1, _ = k.symm_alloc(cap, 2)
+    ar = IpcAllReduce(cap, ptrs=[p0, p1], wait_ns=50_000_000)  # 50 ms instead of the 2 s default
+    try:
+        x = torch.randn(64 * 2880, device=DEV).to(torch.bfloat16)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ar.all_reduce(x)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        assert int(ar.status[0]) == 4, "expected SNB_ERR_TIMEOUT_PEER"
+        assert dt < 1.0, f"the wait took {dt:.3f} s, not its 50 ms budget"
+        # the context is still usable
+        assert torch.isfinite((x.float() * 2).sum()).item()
+    finally:
+        torch.cuda.synchronize()
+        ar.close()
