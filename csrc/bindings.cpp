@@ -36,12 +36,19 @@ void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, tor
 void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
                         int64_t bn, c10::optional<torch::Tensor> used);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, bool accumulate);
+// mla_rope.cu
+void mla_rope_latent(torch::Tensor kv_a, torch::Tensor q, int64_t H, int64_t nope, int64_t r, int64_t rope,
+                     torch::Tensor norm_w, double eps, torch::Tensor positions, torch::Tensor cos_sin, bool neox,
+                     torch::Tensor cache, torch::Tensor slots, int64_t page_size, torch::Tensor qf);
+// sampling_topk.cu
+void topk_pool(torch::Tensor logits, int64_t V, int64_t K, int64_t vocab_offset, torch::Tensor vals, torch::Tensor ids);
 // moe_route_fused.cu
 void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::optional<torch::Tensor> bias,
                      int64_t k, int64_t mode, double scale, int64_t e_lo, int64_t e_local, int64_t bn,
                      torch::Tensor partial, torch::Tensor w_out, torch::Tensor id_out, torch::Tensor seg_offsets,
                      torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map, torch::Tensor q,
-                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks);
+                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks,
+                     c10::optional<torch::Tensor> dbg);
 // moe_gemm_sm100.cu
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets, int64_t bn,
@@ -52,6 +59,8 @@ void silu_and_mul(torch::Tensor out, torch::Tensor x);
 void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                torch::Tensor status, int64_t bn, int64_t splits, c10::optional<torch::Tensor> workspace,
                bool reduce_partials, int64_t tiled_f);
+void gemm_bf16_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, int64_t tiled_f, torch::Tensor status,
+                       int64_t group_k, int64_t x_rows, int64_t x_stride, int64_t o_rows, int64_t o_stride);
 void set_pdl(bool on);
 void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
                 torch::Tensor seq_lens, torch::Tensor qo_indptr, int64_t max_extend, int64_t page_size,
@@ -61,6 +70,9 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
                 torch::Tensor lse_part);
 void kv_page_copy(torch::Tensor src_bases, torch::Tensor dst_bases, torch::Tensor src_pages, torch::Tensor dst_pages,
                   int64_t page_bytes);
+void kv_page_slice_copy(torch::Tensor src_bases, torch::Tensor dst_bases, torch::Tensor src_pages,
+                        torch::Tensor dst_pages, int64_t src_page_bytes, int64_t dst_page_bytes, int64_t src_off,
+                        int64_t dst_off, int64_t nbytes);
 int64_t nvls_flag_bytes();
 void nvls_allreduce(torch::Tensor out, torch::Tensor x, int64_t uc, int64_t mc, int64_t capacity, int64_t rank,
                     int64_t world, int64_t max_ctas, torch::Tensor status);
@@ -110,8 +122,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_quant_mxfp8", &gather_quant_mxfp8, py::arg("q"), py::arg("sf"), py::arg("x"), py::arg("src"),
         py::arg("bn"), py::arg("used") = py::none());
   m.def("moe_combine", &moe_combine);
-  m.def("moe_route_fused", &moe_route_fused);
+  m.def("topk_pool", &topk_pool);
+  m.def("mla_rope_latent", &mla_rope_latent);
+  m.def("moe_route_fused", &moe_route_fused, py::arg("x"), py::arg("w_tiled"), py::arg("E"), py::arg("bias"),
+        py::arg("k"), py::arg("mode"), py::arg("scale"), py::arg("e_lo"), py::arg("e_local"), py::arg("bn"),
+        py::arg("partial"), py::arg("w_out"), py::arg("id_out"), py::arg("seg_offsets"), py::arg("tile_offsets"),
+        py::arg("sorted_src"), py::arg("inv_map"), py::arg("q"), py::arg("sf"), py::arg("sync"), py::arg("status"),
+        py::arg("k_chunks"), py::arg("dbg") = py::none());
   m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_bf16_grouped", &gemm_bf16_grouped);
   m.def("moe_gemm", &moe_gemm, py::arg("out"), py::arg("xq"), py::arg("sfb"), py::arg("w"), py::arg("sfa"),
         py::arg("bias"), py::arg("seg_offsets"), py::arg("tile_offsets"), py::arg("bn"), py::arg("epi"),
         py::arg("alpha"), py::arg("limit"), py::arg("num_sms"), py::arg("status"), py::arg("F"),
@@ -138,6 +157,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("seq_lens"), py::arg("qo_indptr"), py::arg("max_extend"), py::arg("page_size"), py::arg("sm_scale"),
         py::arg("dcp_size") = 1, py::arg("dcp_rank") = 0, py::arg("lse_out") = py::none());
   m.def("kv_page_copy", &kv_page_copy);
+  m.def("kv_page_slice_copy", &kv_page_slice_copy);
   m.def("nvls_flag_bytes", &nvls_flag_bytes);
   m.def("nvls_allreduce", &nvls_allreduce);
   m.def("nvls_combine_allreduce", &nvls_combine_allreduce);

@@ -52,12 +52,24 @@ struct GemmAR {
 
 SNB_DEVICE void bar_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Grouped (per-head) mode: output rows f of group g = f / x_rows contract over x columns
+// [g * x_stride, g * x_stride + K) (each head multiplies its own slice of x), and output column f lands at
+// (f / o_rows) * o_stride + f % o_rows of `out` (a head's block inside a wider row). x_rows = 0: plain GEMM.
+// DeepSeek-V2's absorbed attention uses it: q_nope . W_UK and o_latent . W_UV for every head in one launch.
+struct GemmGroup {
+  int x_rows, x_stride, o_rows, o_stride;
+};
+
+SNB_DEVICE int group_col(const GemmGroup& g, int f) {
+  return g.o_rows ? (f / g.o_rows) * g.o_stride + f % g.o_rows : f;
+}
+
 template <int BN, bool AR>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                      __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ bias, int F, int T,
                      int K, int ldo, int* status, float* __restrict__ partial, const GemmAR ar, int cluster_reduce,
-                     int w_tiled) {
+                     int w_tiled, const GemmGroup grp) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -118,6 +130,7 @@ __global__ void __launch_bounds__(192, 1)
         load_w(kb, kb);
       }
       snb::pdl_wait();
+      const int xoff = grp.x_rows ? (f0 / grp.x_rows) * grp.x_stride : 0;
       int issued = npre;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % C::STAGES;
@@ -128,7 +141,7 @@ __global__ void __launch_bounds__(192, 1)
           load_w(s, kb);
           issued = kb + 1;
         }
-        snb::tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], (kb0 + kb) * BK, t0);
+        snb::tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], (kb0 + kb) * BK + xoff, t0);
       }
       loads[0] = issued;
     }
@@ -223,7 +236,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < ncol; ++j) {
               const int t = t0 + c * 32 + j;
-              if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(__uint_as_float(r[j]) + bf);
+              if (t < T) out[(size_t)t * ldo + group_col(grp, f)] = __float2bfloat16(__uint_as_float(r[j]) + bf);
             }
           }
         }
@@ -340,11 +353,11 @@ __global__ void __launch_bounds__(192, 1)
           acc.w += v.w;
         }
         if (f < F) {
-          const int t = t0 + g * 4;
-          if (t < T) out[(size_t)t * ldo + f] = __float2bfloat16(acc.x);
-          if (t + 1 < T) out[(size_t)(t + 1) * ldo + f] = __float2bfloat16(acc.y);
-          if (t + 2 < T) out[(size_t)(t + 2) * ldo + f] = __float2bfloat16(acc.z);
-          if (t + 3 < T) out[(size_t)(t + 3) * ldo + f] = __float2bfloat16(acc.w);
+          const int t = t0 + g * 4, oc = group_col(grp, f);
+          if (t < T) out[(size_t)t * ldo + oc] = __float2bfloat16(acc.x);
+          if (t + 1 < T) out[(size_t)(t + 1) * ldo + oc] = __float2bfloat16(acc.y);
+          if (t + 2 < T) out[(size_t)(t + 2) * ldo + oc] = __float2bfloat16(acc.z);
+          if (t + 3 < T) out[(size_t)(t + 3) * ldo + oc] = __float2bfloat16(acc.w);
         }
       }
     }
@@ -422,16 +435,17 @@ int pick_cluster_splits(int tiles, int nk, int num_sms) {
 template <int BN, bool AR = false>
 void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::Tensor& w,
                  const __nv_bfloat16* bias, int* status, cudaStream_t st, int splits, float* partial,
-                 const GemmAR& ar = GemmAR{}, bool reduce_partials = true, int num_sms = 148, int tiled_f = 0) {
+                 const GemmAR& ar = GemmAR{}, bool reduce_partials = true, int num_sms = 148, int tiled_f = 0,
+                 const GemmGroup grp = GemmGroup{0, 0, 0, 0}, int group_k = 0) {
   using C = GemmCfg<BN>;
-  const int T = x.size(0), K = x.size(1), F = tiled_f ? tiled_f : w.size(0);
+  const int T = x.size(0), K = grp.x_rows ? group_k : (int)x.size(1), F = tiled_f ? tiled_f : w.size(0);
   const int wt = tiled_f ? 1 : 0;
   CUtensorMap tw = tiled_f ? snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, BK, w.size(0),
                                                     BK * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)
                            : snb_host::make_tmap_2d(w.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, F,
                                                     w.stride(0) * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tx = snb_host::make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, T, x.stride(0) * 2, BK,
-                                          BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tx = snb_host::make_tmap_2d(x.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x.size(1), T,
+                                          x.stride(0) * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(
@@ -447,15 +461,15 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
     if constexpr (!AR) S = pick_cluster_splits<BN>(tiles_f * tiles_t, (K + BK - 1) / BK, num_sms);
     if (S > 1) {
       C10_CUDA_CHECK(snb::launch_pdl_cluster(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, S), 192, C::SMEM, st,
-                                             S, tw, tx, op, bias, F, T, K, ldo, status, nullptr, ar, 1, wt));
+                                             S, tw, tx, op, bias, F, T, K, ldo, status, nullptr, ar, 1, wt, grp));
     } else {
       C10_CUDA_CHECK(snb::launch_pdl(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, 1), 192, C::SMEM, st, tw, tx,
-                                     op, bias, F, T, K, ldo, status, nullptr, ar, 0, wt));
+                                     op, bias, F, T, K, ldo, status, nullptr, ar, 0, wt, grp));
     }
     return;
   }
   C10_CUDA_CHECK(snb::launch_pdl(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, splits), 192, C::SMEM, st, tw, tx,
-                                 op, bias, F, T, K, ldo, status, splits > 1 ? partial : nullptr, ar, 0, wt));
+                                 op, bias, F, T, K, ldo, status, splits > 1 ? partial : nullptr, ar, 0, wt, grp));
   if (splits > 1 && reduce_partials) {
     const int n = T * F;
     C10_CUDA_CHECK(snb::launch_pdl(splitk_reduce_kernel, (n + 255) / 256, 256, 0, st, partial, bias, op, T, F, ldo,
@@ -509,6 +523,35 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
     case 128: launch_gemm<128>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
     case 256: launch_gemm<256>(out, x, w, bp, sp, st, splits, part, GemmAR{}, reduce_partials, sms, tiled_f); break;
     default: TORCH_CHECK(false, "gemm_bf16: bn must be 16/32/64/128/256");
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Grouped (per-head) GEMM, see GemmGroup: out[t, oc(f)] = sum_k x[t, (f / x_rows) * x_stride + k] * w[f, k]
+// for k < group_k. w: tiled [tiled_f, group_k] weight; x_rows and o_rows multiples of 128, group_k of 64.
+void gemm_bf16_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, int64_t tiled_f, torch::Tensor status,
+                       int64_t group_k, int64_t x_rows, int64_t x_stride, int64_t o_rows, int64_t o_stride) {
+  const int T = x.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16,
+              "gemm_bf16_grouped: bf16");
+  TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1 && w.is_contiguous(), "gemm_bf16_grouped: inner stride");
+  TORCH_CHECK(group_k % BK == 0 && x_rows % BM == 0 && x_rows > 0 && (o_rows == 0 || o_rows % BM == 0) &&
+                  tiled_f % x_rows == 0 && x_stride % 8 == 0, "gemm_bf16_grouped: group shape");
+  TORCH_CHECK((tiled_f / x_rows - 1) * x_stride + group_k <= x.size(1), "gemm_bf16_grouped: x too narrow");
+  const int64_t ntf = (tiled_f + BM - 1) / BM, nk = group_k / BK;
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == BK && w.size(0) == ntf * nk * BM, "gemm_bf16_grouped: tiled weight");
+  const GemmGroup grp{(int)x_rows, (int)x_stride, (int)o_rows, (int)o_stride};
+  auto st = at::cuda::getCurrentCUDAStream();
+  int* sp = status.data_ptr<int>();
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  const int bn = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  switch (bn) {
+    case 16: launch_gemm<16>(out, x, w, nullptr, sp, st, 0, nullptr, GemmAR{}, true, sms, tiled_f, grp, group_k); break;
+    case 32: launch_gemm<32>(out, x, w, nullptr, sp, st, 0, nullptr, GemmAR{}, true, sms, tiled_f, grp, group_k); break;
+    case 64: launch_gemm<64>(out, x, w, nullptr, sp, st, 0, nullptr, GemmAR{}, true, sms, tiled_f, grp, group_k); break;
+    case 128: launch_gemm<128>(out, x, w, nullptr, sp, st, 0, nullptr, GemmAR{}, true, sms, tiled_f, grp, group_k); break;
+    default: launch_gemm<256>(out, x, w, nullptr, sp, st, 0, nullptr, GemmAR{}, true, sms, tiled_f, grp, group_k); break;
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -53,6 +53,7 @@ struct RouteArgs {
   int Kp;
   uint32_t* sync;          // [0] arrival ticket, [1] epoch
   int* status;
+  unsigned long long* dbg;  // DEBUG timestamps
 };
 
 SNB_DEVICE void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -140,6 +141,7 @@ SNB_DEVICE void phase2(const RouteArgs& a, float* lg, int32_t* sid, int32_t* cnt
     }
   }
   __syncthreads();
+  if (a.dbg && tid == 0) a.dbg[gridDim.x * 4 + 1] = snb::globaltimer_ns();
   // top-k: one warp per token (ties -> smallest expert id)
   for (int t = warp; t < a.T; t += kWarps) {
     const float* row = lg + (size_t)t * a.E;
@@ -200,6 +202,7 @@ SNB_DEVICE void phase2(const RouteArgs& a, float* lg, int32_t* sid, int32_t* cnt
     }
   }
   __syncthreads();
+  if (a.dbg && tid == 0) a.dbg[gridDim.x * 4 + 2] = snb::globaltimer_ns();
   // counting sort of the entries owned here into BN-padded segments
   const int N = a.T * a.K, El = a.E_local;
   int32_t* off = cnt + El;
@@ -293,8 +296,10 @@ __global__ void __launch_bounds__(kThreads) moe_route_fused_kernel(const RouteAr
   const int eg = blockIdx.x % eg_count, kc = blockIdx.x / eg_count;
   snb::pdl_wait();  // x is the previous kernel's output; the previous call's epoch store is complete
   if (threadIdx.x == 0) epoch_s = *reinterpret_cast<volatile uint32_t*>(&a.sync[1]) + 1;
+  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 0] = snb::globaltimer_ns();
   phase1(a, eg, kc);
   __syncthreads();
+  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 1] = snb::globaltimer_ns();
   if (threadIdx.x == 0) {
     __threadfence();
     last_s = atomicAdd(&a.sync[0], 1u) == gridDim.x - 1;
@@ -310,6 +315,7 @@ __global__ void __launch_bounds__(kThreads) moe_route_fused_kernel(const RouteAr
     int32_t* cnt = sid + a.T * a.K;
     phase2(a, lg, sid, cnt);
     __syncthreads();
+    if (a.dbg && threadIdx.x == 0) a.dbg[gridDim.x * 4 + 0] = snb::globaltimer_ns();
     if (threadIdx.x == 0) {
       a.sync[0] = 0;
       __threadfence();
@@ -329,6 +335,7 @@ __global__ void __launch_bounds__(kThreads) moe_route_fused_kernel(const RouteAr
     }
   }
   __syncthreads();
+  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 2] = snb::globaltimer_ns();
   if (last_s < 0) return;
   const int used = *reinterpret_cast<volatile int32_t*>(&a.seg_offsets[a.E_local]);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -336,6 +343,8 @@ __global__ void __launch_bounds__(kThreads) moe_route_fused_kernel(const RouteAr
     const int s = reinterpret_cast<volatile int32_t*>(a.sorted_src)[r];
     quant_row(a, r, s, lane);
   }
+  __syncthreads();
+  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 3] = snb::globaltimer_ns();
 }
 
 }  // namespace
@@ -346,7 +355,8 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::opt
                      int64_t k, int64_t mode, double scale, int64_t e_lo, int64_t e_local, int64_t bn,
                      torch::Tensor partial, torch::Tensor w_out, torch::Tensor id_out, torch::Tensor seg_offsets,
                      torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map, torch::Tensor q,
-                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks) {
+                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks,
+                     c10::optional<torch::Tensor> dbg) {
   const int T = x.size(0), H = x.size(1);
   if (T == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && H % 64 == 0, "moe_route_fused: x");
@@ -390,6 +400,7 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::opt
   a.Kp = Kp;
   a.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int32_t>());
   a.status = status.data_ptr<int>();
+  a.dbg = dbg ? reinterpret_cast<unsigned long long*>(dbg->data_ptr<int64_t>()) : nullptr;
   const int grid = (int)((E + kEGroup - 1) / kEGroup * k_chunks);
   const size_t smem = (size_t)T * E * 4 + (size_t)T * k * 4 + (3 * e_local + 1) * 4;
   static bool attr_set = false;

@@ -1,7 +1,15 @@
 """Disaggregated prefill/decode on one box: a prefill TP group and a decode TP group inside one process
-world, KV pages moved rank-to-rank (prefill tp_rank i -> decode tp_rank i, same head shard) by P2P copies
-over NVLink (NCCL send/recv on a dedicated stream; gloo on the CPU tier), with the control plane on the
-process group's store.
+world, with the control plane on the process group's store.
+
+Data plane on GPUs (P2P): every decode rank exports its KV pool buffers over CUDA IPC once; a prefill rank
+maps them and, when a request's destination pages are known, one copy kernel writes the request's pages of
+every layer straight from its own pool into the decode pool's pages over NVLink (plain 16-byte peer stores,
+no staging on either side). Head-major slicing: each rank's pool holds a contiguous range of KV heads, and a
+page's heads are contiguous, so a prefill rank copies exactly the overlap of its head range with each decode
+rank's (any TP sizes on the two sides; a head held by several prefill ranks is sent by the lowest of them).
+Settle-then-ack: a prefill rank posts pd/done/<seq>/<src>/<dst> only after its copy kernel completed, and a
+decode rank admits the request once every done key it expects exists. On the CPU tier the data plane is
+gloo send/recv of a packed buffer.
 
 Parity: the reference's PD path (sglang_neuron/disaggregation/*, sglang_patches/nixl_*, pd_*): the decode
 side pre-allocates pages and publishes where the KV must land (TransferInfo), the prefill side writes the
@@ -87,6 +95,89 @@ class Transfer:
         self.completed = False
 
 
+class DoneKeys:
+    """A P2P transfer as the decode side sees it: complete once every expected done key is in the store."""
+
+    __slots__ = ("keys", "completed")
+
+    def __init__(self, keys: List[str]):
+        self.keys = keys
+        self.completed = False
+
+
+def _pool_buffers(pool) -> List[torch.Tensor]:
+    """Every layer buffer of a pool, in a fixed order (MHA: K buffers then V buffers; MLA: latent buffers)."""
+    if hasattr(pool, "k_buffers"):
+        return list(pool.k_buffers) + list(pool.v_buffers)
+    return list(pool.buffers)
+
+
+def pool_geometry(pool, head_start: int) -> Dict:
+    """Page and head-slice sizes of a pool: [pages, heads, page, D] for MHA (a head's slice of a page is
+    contiguous), [pages, page, width] for MLA (one 'head')."""
+    b0 = _pool_buffers(pool)[0]
+    page_bytes = b0[0].numel() * b0.element_size()
+    heads = b0.shape[1] if hasattr(pool, "k_buffers") else 1
+    return {"page_bytes": page_bytes, "heads": heads, "head_start": head_start, "head_bytes": page_bytes // heads,
+            "buffers": len(_pool_buffers(pool))}
+
+
+def export_pool(pool, head_start: int) -> Dict:
+    """IPC handles of the pool's buffers (allocation handle + byte offset of the buffer inside it)."""
+    out = []
+    for b in _pool_buffers(pool):
+        info = b.untyped_storage()._share_cuda_()
+        handle, off = info[1], info[3]
+        out.append((bytes(handle), int(off) + b.storage_offset() * b.element_size()))
+    return {"bufs": out, **pool_geometry(pool, head_start)}
+
+
+def slice_plan(src_geo: List[Dict], dst_geo: List[Dict]) -> List[Tuple[int, int, int, int, int]]:
+    """(src rank, dst rank, src byte offset, dst byte offset, bytes) per page for every overlap of a source
+    rank's head range with a destination rank's; each head comes from the lowest source rank holding it."""
+    plan = []
+    for j, d in enumerate(dst_geo):
+        d0, d1 = d["head_start"], d["head_start"] + d["heads"]
+        covered = set()
+        for i, s_ in enumerate(src_geo):
+            s0, s1 = s_["head_start"], s_["head_start"] + s_["heads"]
+            lo, hi = max(s0, d0), min(s1, d1)
+            heads = [h for h in range(lo, hi) if h not in covered]
+            if not heads:
+                continue
+            if s_["head_bytes"] != d["head_bytes"]:
+                raise ValueError("PD: prefill and decode pools differ in page size, head dim or KV dtype")
+            lo, hi = heads[0], heads[-1] + 1
+            covered.update(range(lo, hi))
+            plan.append((i, j, (lo - s0) * s_["head_bytes"], (lo - d0) * d["head_bytes"], (hi - lo) * d["head_bytes"]))
+        if covered != set(range(d0, d1)):
+            raise ValueError(f"PD: decode rank {j} heads {d0}..{d1} not all held by the prefill group")
+    return plan
+
+
+class PeerPools:
+    """The decode group's pools mapped into this prefill rank (one IPC open per allocation)."""
+
+    def __init__(self, metas: List[Dict], device):
+        from .._ext import kernels
+        self.k = kernels()
+        self.opened: Dict[bytes, int] = {}
+        self.geo = metas
+        self.bases = []
+        for m in metas:
+            ptrs = []
+            for handle, off in m["bufs"]:
+                if handle not in self.opened:
+                    self.opened[handle] = self.k.symm_open(handle)
+                ptrs.append(self.opened[handle] + off)
+            self.bases.append(torch.tensor(ptrs, dtype=torch.int64, device=device))
+
+    def close(self) -> None:
+        for p in self.opened.values():
+            self.k.symm_close(p, False)
+        self.opened = {}
+
+
 class PDLink:
     """Store-based control plane + rank-to-rank data plane between the two groups."""
 
@@ -97,9 +188,19 @@ class PDLink:
         self.store = store
         self.timeout_s = timeout_s
         self.peer = (st.tp_rank + tp_size) if role == "prefill" else st.tp_rank
+        self.tp_rank = st.tp_rank
         self.is_leader = st.tp_rank == 0
         self.device = st.device
         self.stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
+        self.p2p = self.device.type == "cuda"  # CUDA IPC page copies; gloo send/recv on the CPU tier
+
+    def wait_keys(self, keys: List[str], timeout_s: float = 600.0) -> None:
+        t0 = time.time()
+        while not self.store.check(keys):
+            if time.time() - t0 > timeout_s:
+                raise TimeoutError(f"PD: store keys {keys} never appeared")
+            time.sleep(0.001)
+
 
     def put(self, key: str, obj) -> None:
         self.store.set(key, pickle.dumps(obj))
@@ -123,6 +224,9 @@ class PDLink:
         completes through wait(), which on the CPU tier blocks until the matching peer call arrived."""
         if work.completed:
             return True
+        if isinstance(work, DoneKeys):
+            work.completed = self.store.check(work.keys)
+            return work.completed
         if self.stream is None:
             # gloo point-to-point work only completes through wait(), and a wait that times out closes the
             # pair, so wait without a short limit: the protocol has already posted the matching call (decode
@@ -136,6 +240,8 @@ class PDLink:
 
     def finish(self, work) -> None:
         """Block until a transfer that done() reported (or is about to report) completed."""
+        if isinstance(work, DoneKeys):
+            return
         if self.stream is None:
             while not self.done(work):
                 pass
@@ -151,6 +257,11 @@ class PDLink:
         return Transfer(work)
 
 
+def _head_start(engine) -> int:
+    a = engine.runner.model.attention_layers()[0]
+    return int(getattr(getattr(a, "qkv_proj", None), "kv_head_start", 0))
+
+
 class PrefillSide:
     """Wraps a prefill-role Engine: every request is prefilled (first token only) and handed to decode."""
 
@@ -163,9 +274,49 @@ class PrefillSide:
         self.aborted: List[str] = []
         self.sent = 0
         self.user_params: Dict[str, SamplingParams] = {}
+        self.on_send = None  # test seam: called with (rid, pages) when a request's pages are handed off
         sched = engine.scheduler
         self._orig_finish = sched._finish
         sched._finish = self._on_finish  # keep pages of finished prefills until their KV left
+        self.peers: Optional[PeerPools] = None
+        self.plan: List[Tuple[int, int, int, int, int]] = []
+        if link.p2p:
+            pool = engine.runner.kv_pool
+            self.geo = pool_geometry(pool, _head_start(engine))
+            link.put(f"pd/pgeo/{link.tp_rank}", self.geo)
+            self.src_bases = torch.tensor([b.data_ptr() for b in _pool_buffers(pool)], dtype=torch.int64,
+                                          device=link.device)
+
+    def _ensure_peers(self) -> None:
+        """Map the decode group's pools (once every decode rank exported them) and keep this rank's rows of the
+        head-slice plan."""
+        if self.peers is not None:
+            return
+        link = self.link
+        n_dec, n_pre = link.tp, link.tp
+        link.wait_keys([f"pd/ipc/{j}" for j in range(n_dec)] + [f"pd/pgeo/{i}" for i in range(n_pre)])
+        metas = [link.get(f"pd/ipc/{j}") for j in range(n_dec)]
+        pgeo = [link.get(f"pd/pgeo/{i}") for i in range(n_pre)]
+        self.plan = [p for p in slice_plan(pgeo, metas) if p[0] == link.tp_rank]
+        self.peers = PeerPools(metas, link.device)
+
+    def _send_p2p(self, seq: int, pages: List[int], dst_pages: List[int]):
+        """One copy launch per destination rank on the transfer stream; returns (event, done keys)."""
+        from .._ext import kernels
+        self._ensure_peers()
+        link = self.link
+        src = torch.tensor(pages, dtype=torch.int32, device=link.device)
+        dst = torch.tensor(dst_pages, dtype=torch.int32, device=link.device)
+        link.stream.wait_stream(torch.cuda.current_stream(link.device))
+        keys = []
+        with torch.cuda.stream(link.stream):
+            for i, j, so, do, nb in self.plan:
+                kernels().kv_page_slice_copy(self.src_bases, self.peers.bases[j], src, dst, self.geo["page_bytes"],
+                                             self.peers.geo[j]["page_bytes"], so, do, nb)
+                keys.append(f"pd/done/{seq}/{i}/{j}")
+            ev = torch.cuda.Event()
+            ev.record(link.stream)
+        return ev, keys, (src, dst)
 
     def submit(self, rid: str, prompt: List[int], params: SamplingParams):
         self.user_params[rid] = params  # the decode side serves the request with these
@@ -203,9 +354,16 @@ class PrefillSide:
             if self.link.has(key):
                 status = self.link.get(key)
                 del self.pending[seq]
-                if status != "ready":
+                ok = status == "ready" or (isinstance(status, tuple) and status[0] == "ready")
+                if not ok:
                     self._release(r)
                     self.aborted.append(r.rid)
+                    continue
+                if self.on_send is not None:
+                    self.on_send(r.rid, pages)
+                if self.link.p2p:
+                    ev, keys, keep = self._send_p2p(seq, pages, list(status[1]))
+                    self.sending.append((seq, (ev, keys), keep, r))
                     continue
                 idx = torch.tensor(pages, dtype=torch.long, device=self.link.device)
                 buf = gather_pages(self.engine.runner.kv_pool, idx)
@@ -220,7 +378,16 @@ class PrefillSide:
                     self.link.put(f"pd/abort/{seq}", "prefill-timeout")
         still = []
         for seq, work, buf, r in self.sending:
-            if self.link.done(work):
+            if isinstance(work, tuple):  # P2P: settle (copy kernel complete), then acknowledge, then free
+                ev, keys = work
+                if ev.query():
+                    for k in keys:
+                        self.link.put(k, "ok")
+                    self._release(r)
+                    self.sent += 1
+                else:
+                    still.append((seq, work, buf, r))
+            elif self.link.done(work):
                 self._release(r)
                 self.sent += 1
             else:
@@ -248,6 +415,19 @@ class DecodeSide:
         # (sglang_neuron/disaggregation/poll_reduce.py:68-108).
         from ..managers.scheduler import _make_shm
         self._poll = _make_shm(get_state(), POLL_WIDTH, "pdpoll")
+        self._expect: Optional[List[Tuple[int, int]]] = None  # (src rank, dst rank) rows feeding this rank
+        self.on_admit = None  # test seam: called with (header, pages) when a request's KV has landed
+        if link.p2p:
+            link.put(f"pd/ipc/{link.tp_rank}", export_pool(engine.runner.kv_pool, _head_start(engine)))
+
+    def _done_keys(self, seq: int) -> List[str]:
+        if self._expect is None:
+            link = self.link
+            link.wait_keys([f"pd/ipc/{j}" for j in range(link.tp)] + [f"pd/pgeo/{i}" for i in range(link.tp)])
+            metas = [link.get(f"pd/ipc/{j}") for j in range(link.tp)]
+            pgeo = [link.get(f"pd/pgeo/{i}") for i in range(link.tp)]
+            self._expect = [(i, j) for i, j, *_ in slice_plan(pgeo, metas) if j == link.tp_rank]
+        return [f"pd/done/{seq}/{i}/{j}" for i, j in self._expect]
 
     def poll(self) -> None:
         sched = self.engine.scheduler
@@ -275,11 +455,17 @@ class DecodeSide:
                     self.link.put(f"pd/ready/{h.seq}", "refused: no KV pages")
                 self.aborted.append(h.rid)
                 continue
-            buf = torch.empty(page_buffer_shape(self.engine.runner.kv_pool, h.n_pages),
-                              dtype=self.engine.runner.kv_pool.dtype, device=self.link.device)
-            work = self.link.recv(buf)
-            if self.link.is_leader:
-                self.link.put(f"pd/ready/{h.seq}", "ready")
+            if self.link.p2p:
+                # the prefill ranks write straight into these pages; they are identical on every decode rank
+                work, buf = DoneKeys(self._done_keys(h.seq)), None
+                if self.link.is_leader:
+                    self.link.put(f"pd/ready/{h.seq}", ("ready", list(pages)))
+            else:
+                buf = torch.empty(page_buffer_shape(self.engine.runner.kv_pool, h.n_pages),
+                                  dtype=self.engine.runner.kv_pool.dtype, device=self.link.device)
+                work = self.link.recv(buf)
+                if self.link.is_leader:
+                    self.link.put(f"pd/ready/{h.seq}", "ready")
             self.receiving.append((h, work, buf, pages, sched.epoch, time.time()))
         # 2. completed receives become running requests: every rank's own transfer state, MIN-reduced (or the
         #    leader decides and followers wait for their own)
@@ -320,10 +506,13 @@ class DecodeSide:
     def _admit(self, h: Header, buf: torch.Tensor, pages: List[int]) -> None:
         sched = self.engine.scheduler
         runner = self.engine.runner
-        idx = torch.tensor(pages, dtype=torch.long, device=self.link.device)
-        if self.link.stream is not None:
-            torch.cuda.current_stream(self.link.device).wait_stream(self.link.stream)
-        scatter_pages(runner.kv_pool, idx, buf)
+        if buf is not None:  # packed transfer (CPU tier); P2P copies already landed in the pages
+            idx = torch.tensor(pages, dtype=torch.long, device=self.link.device)
+            if self.link.stream is not None:
+                torch.cuda.current_stream(self.link.device).wait_stream(self.link.stream)
+            scatter_pages(runner.kv_pool, idx, buf)
+        if self.on_admit is not None:
+            self.on_admit(h, pages)
         r = Req(h.rid, h.prompt, h.params, eos_ids=[] if h.params.ignore_eos else sched.eos)
         r.slot = sched.free_slots.pop()
         r.pages = list(pages)

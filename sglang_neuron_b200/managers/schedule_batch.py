@@ -154,4 +154,6 @@ class StepInput:
             "seq_lens": padded(self.seq_lens, 0, np.int32),
             "page_upd": pu.reshape(-1),
             "temperature": padded(self.temperature, 0.0, np.float32),
+            "top_k": padded(self.top_k, 0, np.int64),
+            "top_p": padded(self.top_p, 1.0, np.float32),
         }

@@ -1,4 +1,5 @@
-"""CUDA-graph capture of decode steps for every batch-size bucket at startup.
+"""CUDA-graph capture of decode steps for every batch-size bucket at startup, with the plain (greedy /
+temperature) sampler and with the filtered (top-k / top-p) sampler.
 
 Parity: the reference compiles every prefill and decode shape at warm-up (NeuronModelRuntime.warmup_all,
 sglang_neuron/model_executor/graph_runner.py:692-757; BucketConfig decode batch buckets :149-253) and its
@@ -35,19 +36,22 @@ class CudaGraphRunner:
         self.layout = Layout([
             ("req_idx", torch.int64, mb), ("positions", torch.int64, mb), ("out_cache_loc", torch.int64, mb),
             ("seeds", torch.int64, mb), ("seq_lens", torch.int32, mb), ("page_upd", torch.int32, 3 * self.upr * mb),
-            ("temperature", torch.float32, mb),
+            ("temperature", torch.float32, mb), ("top_k", torch.int64, mb), ("top_p", torch.float32, mb),
         ])
         self.static = torch.zeros(self.layout.nbytes, dtype=torch.uint8, device=runner.device)
         self.views = self.layout.views(self.static)
         self.out_ids = torch.zeros(mb, dtype=torch.int64, device=runner.device)
         self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self.launches: Dict[int, int] = {}
+        # the same buckets with the filtered (top-k / top-p) sampler: radix-select candidate pools per vocab
+        # shard, one gather, filters and Gumbel-max on the pool, all on the device
+        self.graphs_f: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.launches_f: Dict[int, int] = {}
         self.pool = None
         self.capture_all()
 
     def can_run(self, step) -> bool:
-        return (step.batch_size <= self.max_bs and not step.needs_topk_topp
-                and len(step.page_upd) <= 3 * self.upr * step.batch_size)
+        return step.batch_size <= self.max_bs and len(step.page_upd) <= 3 * self.upr * step.batch_size
 
     def _fb(self, bs: int) -> ForwardBatch:
         v = self.views
@@ -62,10 +66,14 @@ class CudaGraphRunner:
                             logits_idx=torch.arange(bs, device=r.device), temperature=v["temperature"][:bs],
                             seeds=v["seeds"][:bs], decode_splits=splits, max_seq_len=self.args.context_length)
 
-    def _body(self, bs: int) -> None:
+    def _body(self, bs: int, filtered: bool = False) -> None:
         r = self.r
         r.apply_page_updates(self.views["page_upd"][: 3 * self.upr * bs])
         fb = self._fb(bs)
+        if filtered:
+            fb.top_k = self.views["top_k"][:bs]
+            fb.top_p = self.views["top_p"][:bs]
+            fb.needs_topk_topp = True
         h = r.model(fb)
         r.sample(h, fb, self.views["req_idx"][:bs], out=self.out_ids[:bs])
 
@@ -77,22 +85,25 @@ class CudaGraphRunner:
         stream.wait_stream(torch.cuda.current_stream(r.device))
         with torch.cuda.stream(stream):
             for bs in reversed(self.bs_list):
-                for _ in range(2):  # warm-up (allocator, lazy init) outside the graph
-                    self._body(bs)
-                g = torch.cuda.CUDAGraph()
-                n0 = _ext.launch_count()
-                with torch.cuda.graph(g, pool=self.pool, stream=stream):
-                    self._body(bs)
-                self.launches[bs] = _ext.launch_count() - n0
-                if self.pool is None:
-                    self.pool = g.pool()
-                self.graphs[bs] = g
+                for filtered, graphs, launches in ((False, self.graphs, self.launches),
+                                                   (True, self.graphs_f, self.launches_f)):
+                    for _ in range(2):  # warm-up (allocator, lazy init) outside the graph
+                        self._body(bs, filtered)
+                    g = torch.cuda.CUDAGraph()
+                    n0 = _ext.launch_count()
+                    with torch.cuda.graph(g, pool=self.pool, stream=stream):
+                        self._body(bs, filtered)
+                    launches[bs] = _ext.launch_count() - n0
+                    if self.pool is None:
+                        self.pool = g.pool()
+                    graphs[bs] = g
         torch.cuda.current_stream(r.device).wait_stream(stream)
         torch.cuda.synchronize(r.device)
         from ..parallel.contract import assert_graphs_consistent
         kvh = r.model.attention_layers()[0].num_kv_heads
         self.digest = assert_graphs_consistent({
             "bs": self.bs_list, "launches": [self.launches[b] for b in self.bs_list],
+            "launches_filtered": [self.launches_f[b] for b in self.bs_list],
             "splits": [r.backend.splits_for(b, kvh, self.args.context_length) for b in self.bs_list]})
         logger.info("captured %d decode graphs (bs %s, digest %s)", len(self.graphs), self.bs_list, self.digest)
 
@@ -104,6 +115,8 @@ class CudaGraphRunner:
         v["seeds"][start:end] = 0
         v["seq_lens"][start:end] = 0
         v["temperature"][start:end] = 0
+        v["top_k"][start:end] = 0
+        v["top_p"][start:end] = 1.0
         pu = v["page_upd"].view(-1, 3)
         pu[start * self.upr:end * self.upr, 0] = self.r.dummy_req
         pu[start * self.upr:end * self.upr, 1] = 0
@@ -114,6 +127,10 @@ class CudaGraphRunner:
         bs = self.bs_list[bisect.bisect_left(self.bs_list, B)]
         arrays = step.decode_arrays(bs, self.r.dummy_req, self.upr)
         self.r.io.upload(self.layout, arrays, dst=self.static)
-        self.graphs[bs].replay()
-        _ext.add_launches(self.launches[bs])
+        if step.needs_topk_topp:
+            self.graphs_f[bs].replay()
+            _ext.add_launches(self.launches_f[bs])
+        else:
+            self.graphs[bs].replay()
+            _ext.add_launches(self.launches[bs])
         return self.out_ids[:B]

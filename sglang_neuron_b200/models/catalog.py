@@ -37,7 +37,8 @@ MODELS: Dict[str, ModelSpec] = {
                                    sinks=True),
     "DeepseekV2ForCausalLM": ModelSpec("DeepseekV2ForCausalLM", "deepseek_v2", kv_dtypes=("bf16",),
                                        expert_format="mxfp8", attention="mla", spec_algorithms=("MTP",),
-                                       cuda_graph=False, notes="latent attention runs as PyTorch ops"),
+                                       cuda_graph=True, notes="absorbed MLA on sm_100a kernels; decode CUDA-graph "
+                                       "captured with the bf16 latent pool"),
 }
 
 REFUSED: Dict[str, str] = {

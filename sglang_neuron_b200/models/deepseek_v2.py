@@ -3,7 +3,9 @@ shared experts and a dense first layer.
 
 Parity: sglang_neuron/models/deepseek_v2/model.py. `_project` (:101) builds q, the compact latent row
 [kv_a_layernorm(c) || rope(k_pe)] (576 wide for V2-Lite) and q_nope . W_UK (the absorption); `_output` (:113)
-multiplies the attended latent by W_UV, then o_proj and one all-reduce. The shared experts' TP partial is
+multiplies the attended latent by W_UV, then o_proj and one all-reduce. On the GPU the latent row and the
+query rope are one kernel (csrc/kernels/mla_rope.cu) and both absorptions are grouped tcgen05 GEMMs (every
+head in one launch); the CPU tier keeps the PyTorch form as the oracle. The shared experts' TP partial is
 summed with the routed partials in one all-reduce (:158-190). YaRN with mscale (config.py:56-80).
 """
 from __future__ import annotations
@@ -52,6 +54,7 @@ class MLAAttention(nn.Module):
         self.cos_sin = RotaryCache.get(cfg, device, max_pos)
         self.kv_pool = None
         self.backend = None
+        self._uk = self._uv = None  # tiled absorption weights (CUDA, set at load)
 
     def sinks_f32(self):
         return None
@@ -59,7 +62,45 @@ class MLAAttention(nn.Module):
     def kv_cache(self):
         return self.kv_pool.kv(self.layer_id)
 
+    def _native(self, h: torch.Tensor) -> bool:
+        kc = self.kv_pool.kv(self.layer_id)[0] if self.kv_pool is not None else None
+        return (h.is_cuda and h.dtype == torch.bfloat16 and self._uk is not None and kc is not None
+                and kc.dtype == torch.bfloat16 and self.rope % 2 == 0 and self.cos_sin.shape[1] == self.rope)
+
+    def _forward_native(self, h: torch.Tensor, fb: ForwardBatch, norm=None) -> torch.Tensor:
+        """Every step of the absorbed attention on sm_100a kernels: the latent row (norm + rope) and rope(q_pe)
+        in one kernel, q_nope . W_UK and o_latent . W_UV as grouped tcgen05 GEMMs (one launch each, all heads),
+        written straight into the query rows / the o_proj input."""
+        from .._ext import kernels
+        from ..ops.gemm import _status_buf
+        T, H = h.shape[0], self.num_heads
+        q = self.q_proj(h)                     # [T, H * (nope + rope)]
+        kv_a = self.kv_a_proj(h)               # [T, r + rope]
+        kc, _ = self.kv_cache()
+        dcp = getattr(self.kv_pool, "dcp", None)
+        loc = dcp.local(fb)[1] if dcp is not None else fb.out_cache_loc
+        qf = torch.empty(T, H * (self.r + self.rope), dtype=h.dtype, device=h.device)
+        k = kernels()
+        k.mla_rope_latent(kv_a, q, H, self.nope, self.r, self.rope, self.kv_a_layernorm.weight,
+                          self.kv_a_layernorm.eps, fb.positions, self.cos_sin, bool(self.cfg.rope_neox), kc, loc,
+                          self.kv_pool.page_size, qf)
+        st = _status_buf(h.device)
+        k.gemm_bf16_grouped(qf, q, self._uk.data, H * self.r, st, self.nope, self.r, self.nope + self.rope, self.r,
+                            self.r + self.rope)
+        qf = qf.view(T, H, self.r + self.rope)
+        if dcp is not None:
+            from ..parallel.dcp import dcp_mla_attention
+            o_lat = dcp_mla_attention(qf, kc, fb, self.r, self.scaling, self.kv_pool.page_size, dcp)
+        else:
+            o_lat = mla_attention(qf, kc, fb, self.r, self.scaling, self.kv_pool.page_size)  # [T, H, r]
+        o = torch.empty(T, H * self.vd, dtype=h.dtype, device=h.device)
+        k.gemm_bf16_grouped(o, o_lat.reshape(T, H * self.r), self._uv.data, H * self.vd, st, self.r, self.vd, self.r,
+                            0, 0)
+        return self.o_proj(o, norm=norm)
+
     def forward(self, h: torch.Tensor, fb: ForwardBatch, norm=None) -> torch.Tensor:
+        if self._native(h):
+            return self._forward_native(h, fb, norm)
         T = h.shape[0]
         q = self.q_proj(h).view(T, self.num_heads, self.nope + self.rope)
         kv_a = self.kv_a_proj(h)
@@ -96,6 +137,12 @@ class MLAAttention(nn.Module):
         self.w_uk.data.copy_(kv_b[:, : self.nope])
         self.w_uv.data.copy_(kv_b[:, self.nope:])
         self.o_proj.load(get(p + "o_proj.weight"))
+        if self.w_uk.is_cuda and self.w_uk.dtype == torch.bfloat16:
+            # the grouped GEMMs' weights: W_UK^T rows (head, latent col) over nope, W_UV rows (head, v) over r
+            from ..ops.gemm import TiledWeight
+            H = self.num_heads
+            self._uk = TiledWeight(self.w_uk.data.transpose(1, 2).reshape(H * self.r, self.nope).contiguous())
+            self._uv = TiledWeight(self.w_uv.data.reshape(H * self.vd, self.r).contiguous())
 
 
 class DeepseekV2ForCausalLM(CausalLM):

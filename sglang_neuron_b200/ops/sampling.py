@@ -130,10 +130,16 @@ def sample_filtered(logits: torch.Tensor, temperature: torch.Tensor, top_k: torc
     Temperature is applied first; top-k keeps the k best; top-p keeps the smallest prefix of the sorted
     candidates whose probability reaches p; greedy rows (temperature 0) take the best candidate."""
     V = valid_vocab if valid_vocab > 0 else logits.shape[1]
-    lf = logits[:, :V].float()
     kp = min(pool, V)
-    vals, ids = lf.topk(kp, dim=-1)
-    ids = ids + vocab_offset
+    if logits.is_cuda:
+        # radix-select kernel: the row's top-kp (value descending, index ascending), no full-vocabulary sort
+        vals = torch.empty(logits.shape[0], kp, dtype=torch.float32, device=logits.device)
+        ids = torch.empty(logits.shape[0], kp, dtype=torch.int64, device=logits.device)
+        kernels().topk_pool(logits, V, kp, vocab_offset, vals, ids)
+    else:
+        lf = logits[:, :V].float()
+        vals, ids = lf.topk(kp, dim=-1)
+        ids = ids + vocab_offset
     if merge is not None:
         vals, ids = merge(vals, ids)
     P = vals.shape[1]

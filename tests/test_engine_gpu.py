@@ -143,3 +143,15 @@ def test_filtered_sampling_on_gpu_is_seeded_and_inside_top_k():
     assert [o["output_ids"] for o in a] == [o["output_ids"] for o in b]
     top5 = torch.cat(rows, 0).topk(5, dim=-1).indices
     assert top5.shape[0] > 0
+
+
+def test_filtered_sampling_graph_equals_eager():
+    """top-k / top-p decode steps replay their own CUDA graphs (radix-select pools, filters, Gumbel-max on
+    the device): the same tokens as the eager path for the same seeds."""
+    prompts = _prompts()
+    sp = {"max_new_tokens": 10, "temperature": 0.8, "top_k": 20, "top_p": 0.9, "seed": 5}
+    eng = _engine("gpt-oss-120b", TINY_OSS, "cuda", graph=True, kv="fp8_e4m3")
+    assert eng.runner.graph_runner is not None and eng.runner.graph_runner.graphs_f
+    a = eng.generate(prompts, sp)
+    b = _engine("gpt-oss-120b", TINY_OSS, "cuda", graph=False, kv="fp8_e4m3").generate(prompts, sp)
+    assert [o["output_ids"] for o in a] == [o["output_ids"] for o in b]

@@ -508,3 +508,25 @@ def test_allreduce_peer_wait_runs_out_with_status():
     finally:
         torch.cuda.synchronize()
         ar.close()
+
+
+@pytest.mark.parametrize("B,V,K,dt,ties", [(64, 201088, 256, torch.bfloat16, False), (3, 25136, 256, torch.bfloat16, True),
+                                            (5, 1000, 40, torch.float32, False), (2, 100, 256, torch.float32, False),
+                                            (7, 151936, 1, torch.bfloat16, True)])
+def test_topk_pool_radix_select(B, V, K, dt, ties):
+    """The radix-select candidate pool against a stable descending sort (value desc, index asc), including
+    heavy ties and rows shorter than the pool."""
+    from sglang_neuron_b200._ext import kernels
+    torch.manual_seed(V + K)
+    x = torch.randn(B, V + 3) * 4
+    if ties:
+        x = x.round()  # few distinct values: the K-th value is shared by many entries
+    x = x.to(dt)
+    kk = min(K, V)
+    vals = torch.empty(B, kk, dtype=torch.float32, device=DEV)
+    ids = torch.empty(B, kk, dtype=torch.int64, device=DEV)
+    kernels().topk_pool(x.to(DEV), V, kk, 7, vals, ids)
+    torch.cuda.synchronize()
+    ref_v, ref_i = x[:, :V].float().sort(dim=-1, descending=True, stable=True)
+    assert torch.equal(vals.cpu(), ref_v[:, :kk])
+    assert torch.equal(ids.cpu(), ref_i[:, :kk] + 7)

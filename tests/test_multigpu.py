@@ -356,3 +356,94 @@ def test_dp_attention_prefill_tracks_single_gpu():
     assert dp[0][0].shape[0] == 1 and dp[1][0].shape[0] == 1
     assert _rel(dp[0][0], one[0:1]) < 2e-2
     assert _rel(dp[1][0], one[1:2]) < 2e-2
+
+
+PD_TINY = dict(num_hidden_layers=2, vocab_size=1000, hidden_size=256, intermediate_size=512,
+               num_attention_heads=4, num_key_value_heads=2, head_dim=64)
+
+
+def _pd_engine(dp_size):
+    from sglang_neuron_b200.configs import model_config as mc
+    from sglang_neuron_b200.engine import Engine
+    from sglang_neuron_b200.server_args import ServerArgs
+    mc.PRESETS["pd-gpu-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], **PD_TINY)
+    return Engine(ServerArgs(model="pd-gpu-tiny", load_format="random", device="cuda", dp_size=dp_size,
+                             context_length=256, max_running_requests=4, chunked_prefill_size=64,
+                             random_weight_std=0.05, disable_cuda_graph=True, mem_fraction_static=0.3,
+                             max_total_tokens=4096))
+
+
+def _pd_prompts():
+    g = torch.Generator().manual_seed(9)
+    return [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (21, 40, 9)]
+
+
+def _page_sums(pool, pages):
+    """Per (buffer, page) byte sums of the given pages of every layer buffer (exact, order-free)."""
+    from sglang_neuron_b200.disaggregation.pd import _pool_buffers
+    idx = torch.tensor(pages, dtype=torch.long, device=_pool_buffers(pool)[0].device)
+    return [b.index_select(0, idx).view(len(pages), -1).view(torch.uint8).long().sum(1).tolist()
+            for b in _pool_buffers(pool)]
+
+
+def _pd_worker(rank, world, port, q):
+    """GPU 0 prefills (its own DP replica), GPU 1 decodes; KV pages move by the P2P copy kernel."""
+    _init(rank, world, port)
+    import time
+    import torch.distributed as dist
+    from sglang_neuron_b200.disaggregation.pd import DecodeSide, PDLink, PrefillSide
+    from sglang_neuron_b200.managers.schedule_batch import SamplingParams
+    eng = _pd_engine(2)
+    store = dist.distributed_c10d._get_default_store()
+    role = "prefill" if rank == 0 else "decode"
+    link = PDLink(role, 1, store, timeout_s=60.0)
+    assert link.p2p
+    sums = {}
+    P = eng.runner.page_size
+    if role == "prefill":
+        side = PrefillSide(eng, link)
+        side.on_send = lambda rid, pages: sums.__setitem__(rid, _page_sums(eng.runner.kv_pool, pages))
+        for i, p in enumerate(_pd_prompts()):
+            side.submit(f"pd{i}", p, SamplingParams(max_new_tokens=7))
+        t0 = time.time()
+        while (eng.scheduler.has_work() or side.pending or side.sending) and time.time() - t0 < 120:
+            side.step()
+            time.sleep(0.001)
+        result = {"sent": side.sent, "aborted": sorted(side.aborted), "sums": sums}
+    else:
+        side = DecodeSide(eng, link)
+        side.on_admit = lambda h, pages: sums.__setitem__(h.rid, _page_sums(eng.runner.kv_pool, pages))
+        t0 = time.time()
+        want = {"pd0", "pd1", "pd2"}
+        while time.time() - t0 < 120:
+            side.step()
+            if want.issubset(eng.scheduler.finished_by_rid):
+                break
+            time.sleep(0.001)
+        eng.scheduler.drain()
+        result = {"tokens": {rid: eng.scheduler.finished_by_rid[rid].output_ids for rid in sorted(want)
+                             if rid in eng.scheduler.finished_by_rid}, "sums": sums, "P": P}
+    torch.cuda.synchronize()
+    q.put((rank, result))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _pd_ref_worker(rank, world, port, q):
+    _init(rank, world, port)
+    eng = _pd_engine(1)
+    out = eng.generate(_pd_prompts(), {"max_new_tokens": 7})
+    q.put((rank, [o["output_ids"] for o in out]))
+
+
+@needs2
+def test_pd_p2p_pages_land_exactly_and_tokens_match_aggregated():
+    """Prefill on GPU 0, decode on GPU 1: the P2P copy kernel writes every page of every layer into the decode
+    pool (byte sums equal page for page), and the decoded tokens equal a one-GPU aggregated engine's."""
+    res = _spawn(_pd_worker, 2)
+    pre, dec = res[0][0], res[1][0]
+    assert pre["sent"] == 3 and pre["aborted"] == []
+    for rid, s in pre["sums"].items():
+        assert dec["sums"][rid] == s, f"{rid}: pages differ after the P2P copy"
+    ref = _spawn(_pd_ref_worker, 1)[0][0]
+    assert [dec["tokens"][f"pd{i}"] for i in range(3)] == ref

@@ -170,3 +170,25 @@ def test_pd_tp2_groups_match_aggregated():
     assert res[0]["sent"] == 3 and res[1]["sent"] == 3
     for r in (2, 3):
         assert [res[r][f"pd{i}"] for i in range(3)] == [o["output_ids"] for o in ref]
+
+
+def test_head_major_slice_plan_across_tp_sizes():
+    """Prefill TP8 (1 KV head each) -> decode TP4 (2 heads each): decode rank j takes head 2j from prefill rank 2j
+    and head 2j+1 from rank 2j+1, each a contiguous slice of the page; replicated heads come from the lowest
+    holder; a decode head nobody holds is refused."""
+    from sglang_neuron_b200.disaggregation.pd import slice_plan
+    hb = 16 * 64  # page_size x head_dim bytes (fp8)
+    pre = [{"head_start": i, "heads": 1, "head_bytes": hb} for i in range(8)]
+    dec = [{"head_start": 2 * j, "heads": 2, "head_bytes": hb} for j in range(4)]
+    plan = slice_plan(pre, dec)
+    assert sorted(plan) == sorted([(2 * j + h, j, 0, h * hb, hb) for j in range(4) for h in range(2)])
+    # decode TP8 from prefill TP4: each decode rank takes the half of one prefill rank's page
+    plan = slice_plan(dec, pre)
+    assert sorted(plan) == sorted([(i // 2, i, (i % 2) * hb, 0, hb) for i in range(8)])
+    # equal TP: whole pages rank to rank
+    assert slice_plan(dec, dec) == [(j, j, 0, 0, 2 * hb) for j in range(4)]
+    # TP16 over 8 heads (replicated: ranks 2h and 2h+1 both hold head h) -> decode TP8: the lower holder sends
+    rep = [{"head_start": r // 2, "heads": 1, "head_bytes": hb} for r in range(16)]
+    assert sorted(slice_plan(rep, pre)) == sorted([(2 * i, i, 0, 0, hb) for i in range(8)])
+    with pytest.raises(ValueError):
+        slice_plan(pre[:4], dec)
