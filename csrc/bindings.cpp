@@ -34,7 +34,7 @@ void topk_route(torch::Tensor weights, torch::Tensor ids, torch::Tensor logits, 
 void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, torch::Tensor seg_offsets,
                torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map);
 void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
-                        int64_t bn, c10::optional<torch::Tensor> used);
+                        int64_t bn, c10::optional<torch::Tensor> used, c10::optional<torch::Tensor> skip);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torch::Tensor w, bool accumulate);
 // mla_rope.cu
 void mla_rope_latent(torch::Tensor kv_a, torch::Tensor q, int64_t H, int64_t nope, int64_t r, int64_t rope,
@@ -47,8 +47,7 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::opt
                      int64_t k, int64_t mode, double scale, int64_t e_lo, int64_t e_local, int64_t bn,
                      torch::Tensor partial, torch::Tensor w_out, torch::Tensor id_out, torch::Tensor seg_offsets,
                      torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map, torch::Tensor q,
-                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks,
-                     c10::optional<torch::Tensor> dbg);
+                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks);
 // moe_gemm_sm100.cu
 void moe_gemm(torch::Tensor out, torch::Tensor xq, torch::Tensor sfb, torch::Tensor w, torch::Tensor sfa,
               c10::optional<torch::Tensor> bias, torch::Tensor seg_offsets, torch::Tensor tile_offsets, int64_t bn,
@@ -120,7 +119,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_route", &topk_route);
   m.def("moe_align", &moe_align);
   m.def("gather_quant_mxfp8", &gather_quant_mxfp8, py::arg("q"), py::arg("sf"), py::arg("x"), py::arg("src"),
-        py::arg("bn"), py::arg("used") = py::none());
+        py::arg("bn"), py::arg("used") = py::none(), py::arg("skip") = py::none());
   m.def("moe_combine", &moe_combine);
   m.def("topk_pool", &topk_pool);
   m.def("mla_rope_latent", &mla_rope_latent);
@@ -128,7 +127,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k"), py::arg("mode"), py::arg("scale"), py::arg("e_lo"), py::arg("e_local"), py::arg("bn"),
         py::arg("partial"), py::arg("w_out"), py::arg("id_out"), py::arg("seg_offsets"), py::arg("tile_offsets"),
         py::arg("sorted_src"), py::arg("inv_map"), py::arg("q"), py::arg("sf"), py::arg("sync"), py::arg("status"),
-        py::arg("k_chunks"), py::arg("dbg") = py::none());
+        py::arg("k_chunks"));
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_bf16_grouped", &gemm_bf16_grouped);
   m.def("moe_gemm", &moe_gemm, py::arg("out"), py::arg("xq"), py::arg("sfb"), py::arg("w"), py::arg("sfa"),

@@ -178,12 +178,18 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
 // static capacity R (graph capture), but the work follows the routed row count, which shrinks with EP.
 __global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int xs, const int32_t* __restrict__ src,
                                           int R, int H, int Kp, int BN, uint8_t* __restrict__ q,
-                                          uint8_t* __restrict__ sf, const int32_t* __restrict__ used) {
+                                          uint8_t* __restrict__ sf, const int32_t* __restrict__ used,
+                                          const int32_t* __restrict__ skip) {
   snb::pdl_wait();
   snb::pdl_trigger();
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (r >= R || (used != nullptr && r >= *used)) return;
+  if (skip != nullptr && skip[r] < 0) return;  // a padding row of the permutation (see below)
   const int s = src != nullptr ? src[r] : r;
+  // Padding rows of a segment (src < 0) are left as they are: row n of a tile's output depends only on
+  // activation row n and its scales, and the combine never reads a padding row, so whatever they hold only
+  // ever reaches outputs nobody reads. (At decode most rows are padding: 16-row tiles for 1-3 tokens.)
+  if (s < 0) return;
   const int KB = (Kp + 127) / 128;           // 128-wide K blocks
   const int nblk = KB * 4;                    // 32-wide scale blocks incl. padding
   const int chunk_bytes = min(BN, 32) * 16;
@@ -291,7 +297,7 @@ void moe_align(torch::Tensor ids, int64_t e_lo, int64_t e_local, int64_t bn, tor
 }
 
 void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10::optional<torch::Tensor> src,
-                        int64_t bn, c10::optional<torch::Tensor> used) {
+                        int64_t bn, c10::optional<torch::Tensor> used, c10::optional<torch::Tensor> skip) {
   const int R = q.size(0), Kp = q.size(1), H = x.size(1);
   if (R == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && H % 32 == 0, "gather_quant: x");
@@ -304,7 +310,8 @@ void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10:
   snb::launch_pdl(gather_quant_mxfp8_kernel, blocks, threads, 0, st, (const __nv_bfloat16*)x.data_ptr(), x.stride(0),
                                                        src ? src->data_ptr<int32_t>() : nullptr, R, H, Kp, bn,
                                                        (uint8_t*)q.data_ptr(), (uint8_t*)sf.data_ptr(),
-                                                       used ? used->data_ptr<int32_t>() : nullptr);
+                                                       used ? used->data_ptr<int32_t>() : nullptr,
+                                                       skip ? skip->data_ptr<int32_t>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -3,19 +3,20 @@
 //
 // The separate path takes four launches per MoE layer (router GEMM, top-k, alignment, quantise); at a few
 // dozen tokens each of them is a few microseconds of launch and tail latency around well under a microsecond
-// of work. Here one grid does all of it:
+// of work. Here one grid of co-resident CTAs does all of it, with two grid-wide barriers:
 //   phase 1, every CTA: a [T x 16-expert] block of router logits over one K chunk, on tensor cores
 //            (mma.sync m16n8k16 bf16 -> fp32; the router weight is read in the GEMM's tiled layout), written
 //            as an fp32 partial;
-//   phase 2, the last CTA to finish phase 1 (arrival ticket): sums the K-chunk partials, adds the bias and
-//            rounds to bf16 (the logits the separate router GEMM would produce), selects the top-k experts of
-//            every token, and sorts the (token, slot) entries of the experts owned here by expert into
-//            BN-padded segments (sorted_src, inv_map, seg_offsets, tile_offsets);
-//   phase 3, every CTA, once the last CTA published phase 2 (epoch flag): quantises the routed rows to MXFP8
-//            (e4m3 values, e8m0 scale per 32, scales in the tcgen05 scale-atom order), zero rows for padding.
-// Each CTA triggers the dependent launch only after it has passed the arrival ticket, i.e. once every CTA of
-// the grid is resident, so a programmatically launched successor can never take the SMs a late CTA needs.
-// Every wait is bounded (SNB_WAIT_NS); a timeout records SNB_ERR_TIMEOUT_PEER and the CTA returns.
+//   phase 2, one warp per token: the K-chunk partials of its logits summed (all loads in flight at once),
+//            bias added, rounded to bf16 (the logits the separate router GEMM produces), top-k selected;
+//   phase 3, every CTA: the same deterministic, stable counting sort of the (token, slot) entries of the
+//            experts owned here (CTA 0 publishes it for the GEMM and the combine), then its share of the routed
+//            rows quantised to MXFP8 (e4m3, e8m0 scale per 32, scales in the tcgen05 atom order).
+// Every phase spreads over the whole grid: an earlier design that ran the reduction, top-k and sort in the
+// last CTA alone measured 110 us against 21 us for the four launches (timestamps per phase: the single-CTA
+// part took 92 us). Each CTA triggers the dependent launch only after the first barrier, i.e. once every CTA
+// of the grid is resident, so a programmatically launched successor never takes the SMs a late CTA needs.
+// Every barrier wait is bounded (SNB_WAIT_NS); a timeout records SNB_ERR_TIMEOUT_PEER and the CTA returns.
 //
 // Parity: the reference's router + top-k inside its decode MoE kernel (sglang_neuron/ops/moe/moe_block_tkg.py:
 // 19-128) and its token -> block mapping (ops/moe/moe_blockwise.py:24-130).
@@ -28,7 +29,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kEGroup = 16;        // experts per CTA (two n8 tiles)
-constexpr int kMaxLogits = 16384;  // T * E staged in shared memory by the last CTA (64 KB)
+constexpr int kMaxLogits = 16384;  // T * E of a decode-sized call (partials [k_chunks, T, E])
 constexpr int kMaxK = 16;
 
 struct RouteArgs {
@@ -51,9 +52,8 @@ struct RouteArgs {
   uint8_t* q;              // [R_max, Kp] e4m3
   uint8_t* sf;             // scale atoms
   int Kp;
-  uint32_t* sync;          // [0] arrival ticket, [1] epoch
+  uint32_t* sync;          // grid barrier: [0] arrival counter, [1] generation
   int* status;
-  unsigned long long* dbg;  // DEBUG timestamps
 };
 
 SNB_DEVICE void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -113,134 +113,165 @@ SNB_DEVICE void phase1(const RouteArgs& a, int eg, int kc) {
   }
 }
 
-// Last CTA: logits, top-k, counting sort. Shared memory: logits [T*E] fp32, then ids [T*K], then counters.
-SNB_DEVICE void phase2(const RouteArgs& a, float* lg, int32_t* sid, int32_t* cnt) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int TE = a.T * a.E;
-  {
-    // sum of the K-chunk partials: each thread keeps its (up to 64) logits in registers and issues one K
-    // chunk's loads for all of them at once, so the reduction costs k_chunks L2 round trips, not T*E/256 x that
-    constexpr int kJ = kMaxLogits / kThreads;
-    float acc[kJ];
-#pragma unroll
-    for (int j = 0; j < kJ; ++j) acc[j] = 0.f;
-    for (int kc = 0; kc < a.k_chunks; ++kc) {
-      const float* p = a.partial + (size_t)kc * TE + tid;
-#pragma unroll
-      for (int j = 0; j < kJ; ++j)
-        if (tid + j * kThreads < TE) acc[j] += __ldcg(p + j * kThreads);
-    }
-#pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-      const int i = tid + j * kThreads;
-      if (i < TE) {
-        float s = acc[j];
-        if (a.bias != nullptr) s += __bfloat162float(a.bias[i % a.E]);
-        lg[i] = __bfloat162float(__float2bfloat16(s));  // the bf16 logits of the separate router GEMM
+// Grid-wide barrier over the co-resident CTAs of this launch: arrival counter sync[0], generation sync[1]
+// (the last CTA to arrive resets the counter and advances the generation). Bounded: on timeout the CTA records
+// SNB_ERR_TIMEOUT_PEER and the caller returns.
+SNB_DEVICE bool grid_barrier(uint32_t* sync, int* status) {
+  __shared__ int ok_s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ok_s = 1;
+    __threadfence();
+    const uint32_t gen = *reinterpret_cast<volatile uint32_t*>(&sync[1]);
+    if (atomicAdd(&sync[0], 1u) == gridDim.x - 1) {
+      sync[0] = 0;
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&sync[1]), "r"(gen + 1u) : "memory");
+    } else {
+      const uint64_t t0 = snb::globaltimer_ns();
+      for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&sync[1]) : "memory");
+        if (v != gen) break;
+        if (snb::globaltimer_ns() - t0 > SNB_WAIT_NS) {
+          snb::record_status(status, SNB_ERR_TIMEOUT_PEER);
+          ok_s = 0;
+          break;
+        }
       }
     }
   }
   __syncthreads();
-  if (a.dbg && tid == 0) a.dbg[gridDim.x * 4 + 1] = snb::globaltimer_ns();
-  // top-k: one warp per token (ties -> smallest expert id)
-  for (int t = warp; t < a.T; t += kWarps) {
-    const float* row = lg + (size_t)t * a.E;
-    float v[8];
-    float mx = -INFINITY;
+  return ok_s != 0;
+}
+
+// Phase 2, one warp per token: lane l holds experts l, l+32, l+64, l+96 (E <= 128 here) or 8 per lane for
+// E <= 256; the K-chunk partials of all of them are loaded together, summed with the bias and rounded to bf16
+// (the logits the separate router GEMM produces), then the top-k selection runs on registers.
+SNB_DEVICE void phase2_token(const RouteArgs& a, int t, int lane) {
+  const int TE = a.T * a.E;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  for (int kc = 0; kc < a.k_chunks; ++kc) {
+    const float* p = a.partial + (size_t)kc * TE + (size_t)t * a.E;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = lane + 32 * i;
-      v[i] = e < a.E ? row[e] : -INFINITY;
-      mx = fmaxf(mx, v[i]);
-    }
-    mx = snb::warp_max(mx);
-    float denom_all = 0.f;
-    if (a.mode == 1) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) denom_all += (v[i] == -INFINITY) ? 0.f : __expf(v[i] - mx);
-      denom_all = snb::warp_sum(denom_all);
-    }
-    float sel_v[kMaxK];
-    int sel_i[kMaxK];
-    for (int j = 0; j < a.K; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int e = lane + 32 * i;
-        if (v[i] > bv || (v[i] == bv && e < bi)) {
-          bv = v[i];
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      sel_v[j] = bv;
-      sel_i[j] = bi;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i == bi) v[i] = -INFINITY;
-    }
-    if (lane == 0) {
-      float s = 0.f;
-      if (a.mode == 0)
-        for (int j = 0; j < a.K; ++j) s += __expf(sel_v[j] - sel_v[0]);
-      for (int j = 0; j < a.K; ++j) {
-        const float wj = a.mode == 0 ? __expf(sel_v[j] - sel_v[0]) / s * a.scale
-                                     : __expf(sel_v[j] - mx) / denom_all * a.scale;
-        a.w_out[(size_t)t * a.K + j] = wj;
-        a.id_out[(size_t)t * a.K + j] = sel_i[j];
-        sid[t * a.K + j] = sel_i[j];
-      }
+      if (e < a.E) v[i] += __ldcg(p + e);
     }
   }
-  __syncthreads();
-  if (a.dbg && tid == 0) a.dbg[gridDim.x * 4 + 2] = snb::globaltimer_ns();
-  // counting sort of the entries owned here into BN-padded segments
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    if (e < a.E) {
+      float s = v[i];
+      if (a.bias != nullptr) s += __bfloat162float(a.bias[e]);
+      v[i] = __bfloat162float(__float2bfloat16(s));
+    } else {
+      v[i] = -INFINITY;
+    }
+    mx = fmaxf(mx, v[i]);
+  }
+  mx = snb::warp_max(mx);
+  float denom_all = 0.f;
+  if (a.mode == 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) denom_all += (v[i] == -INFINITY) ? 0.f : __expf(v[i] - mx);
+    denom_all = snb::warp_sum(denom_all);
+  }
+  // top-k by repeated warp argmax (ties -> smallest expert id); lane j keeps the j-th pick
+  float my_v = -INFINITY, first = -INFINITY;
+  int my_i = 0;
+  for (int j = 0; j < a.K; ++j) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (v[i] > bv || (v[i] == bv && e < bi)) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (j == 0) first = bv;
+    if (lane == j) {
+      my_v = bv;
+      my_i = bi;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i == bi) v[i] = -INFINITY;
+  }
+  float s = 0.f;
+  if (a.mode == 0) s = snb::warp_sum(lane < a.K ? __expf(my_v - first) : 0.f);
+  if (lane < a.K) {
+    const float wj = a.mode == 0 ? __expf(my_v - first) / s * a.scale : __expf(my_v - mx) / denom_all * a.scale;
+    a.w_out[(size_t)t * a.K + lane] = wj;
+    a.id_out[(size_t)t * a.K + lane] = my_i;
+  }
+}
+
+// Phase 3, every CTA: the same deterministic counting sort of the (token, slot) entries of the experts owned
+// here (stable: entries of one expert in flat-index order), in shared memory. CTA 0 publishes it for the
+// grouped GEMM and the combine; every CTA then quantises its share of the rows from its own copy.
+SNB_DEVICE void phase3_sort(const RouteArgs& a, int32_t* sid, int32_t* spos, int32_t* cnt, int32_t* off) {
+  const int tid = threadIdx.x;
   const int N = a.T * a.K, El = a.E_local;
-  int32_t* off = cnt + El;
-  int32_t* cur = off + El + 1;
-  for (int e = tid; e < El; e += kThreads) cnt[e] = cur[e] = 0;
+  for (int i = tid; i < N; i += kThreads) sid[i] = __ldcg(a.id_out + i) - a.e_lo;
+  for (int e = tid; e < El; e += kThreads) cnt[e] = 0;
   __syncthreads();
   for (int i = tid; i < N; i += kThreads) {
-    const int e = sid[i] - a.e_lo;
+    const int e = sid[i];
     if (e >= 0 && e < El) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (tid == 0) {
-    int rows = 0, tiles = 0;
-    for (int e = 0; e < El; ++e) {
-      off[e] = rows;
-      a.seg_offsets[e] = rows;
-      a.tile_offsets[e] = tiles;
-      const int padded = (cnt[e] + a.BN - 1) / a.BN * a.BN;
-      rows += padded;
-      tiles += padded / a.BN;
+  if (tid < 32) {  // exclusive scan of the BN-padded segment sizes (warp 0)
+    const int per = (El + 31) / 32;
+    int rows = 0;
+    for (int j = 0; j < per; ++j) {
+      const int e = tid * per + j;
+      if (e < El) rows += (cnt[e] + a.BN - 1) / a.BN * a.BN;
     }
-    off[El] = rows;
-    a.seg_offsets[El] = rows;
-    a.tile_offsets[El] = tiles;
+    int inc = rows;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int r = __shfl_up_sync(0xffffffffu, inc, o);
+      if (tid >= o) inc += r;
+    }
+    int acc = inc - rows;
+    for (int j = 0; j < per; ++j) {
+      const int e = tid * per + j;
+      if (e < El) {
+        off[e] = acc;
+        acc += (cnt[e] + a.BN - 1) / a.BN * a.BN;
+      }
+    }
+    if (tid == 31) off[El] = inc;
   }
   __syncthreads();
-  for (int r = tid; r < off[El]; r += kThreads) a.sorted_src[r] = -1;
-  __syncthreads();
+  // stable position: the entry's segment start + earlier entries (flat index) of the same expert
   for (int i = tid; i < N; i += kThreads) {
-    const int e = sid[i] - a.e_lo;
+    const int e = sid[i];
+    int p = -1;
     if (e >= 0 && e < El) {
-      const int p = off[e] + atomicAdd(&cur[e], 1);
-      a.sorted_src[p] = i / a.K;
-      a.inv_map[i] = p;
-    } else {
-      a.inv_map[i] = -1;
+      int r = 0;
+      for (int i2 = 0; i2 < i; ++i2) r += sid[i2] == e;
+      p = off[e] + r;
     }
+    spos[i] = p;
   }
+  __syncthreads();
 }
 
 // MXFP8 quantise of permuted row r (one warp; each lane whole 32-element blocks), as gather_quant_mxfp8.
@@ -289,62 +320,41 @@ SNB_DEVICE void quant_row(const RouteArgs& a, int r, int s, int lane) {
 }
 
 __global__ void __launch_bounds__(kThreads) moe_route_fused_kernel(const RouteArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ int last_s;
-  __shared__ uint32_t epoch_s;
+  extern __shared__ __align__(16) int32_t smem_i[];
   const int eg_count = (a.E + kEGroup - 1) / kEGroup;
   const int eg = blockIdx.x % eg_count, kc = blockIdx.x / eg_count;
-  snb::pdl_wait();  // x is the previous kernel's output; the previous call's epoch store is complete
-  if (threadIdx.x == 0) epoch_s = *reinterpret_cast<volatile uint32_t*>(&a.sync[1]) + 1;
-  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 0] = snb::globaltimer_ns();
-  phase1(a, eg, kc);
-  __syncthreads();
-  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 1] = snb::globaltimer_ns();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    last_s = atomicAdd(&a.sync[0], 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  // every CTA has arrived at the ticket (hence is resident) before any of them lets the next kernel launch
-  snb::pdl_trigger();
-  const uint32_t e = epoch_s;
-  if (last_s) {
-    __threadfence();
-    float* lg = reinterpret_cast<float*>(smem);
-    int32_t* sid = reinterpret_cast<int32_t*>(lg + a.T * a.E);
-    int32_t* cnt = sid + a.T * a.K;
-    phase2(a, lg, sid, cnt);
-    __syncthreads();
-    if (a.dbg && threadIdx.x == 0) a.dbg[gridDim.x * 4 + 0] = snb::globaltimer_ns();
-    if (threadIdx.x == 0) {
-      a.sync[0] = 0;
-      __threadfence();
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&a.sync[1]), "r"(e) : "memory");
-    }
-  } else if (threadIdx.x == 0) {
-    const uint64_t t0 = snb::globaltimer_ns();
-    for (;;) {
-      uint32_t v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&a.sync[1]) : "memory");
-      if ((int32_t)(v - e) >= 0) break;
-      if (snb::globaltimer_ns() - t0 > SNB_WAIT_NS) {
-        snb::record_status(a.status, SNB_ERR_TIMEOUT_PEER);
-        last_s = -1;
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 2] = snb::globaltimer_ns();
-  if (last_s < 0) return;
-  const int used = *reinterpret_cast<volatile int32_t*>(&a.seg_offsets[a.E_local]);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = blockIdx.x * kWarps + warp; r < used; r += gridDim.x * kWarps) {
-    const int s = reinterpret_cast<volatile int32_t*>(a.sorted_src)[r];
-    quant_row(a, r, s, lane);
-  }
+  snb::pdl_wait();  // x is the previous kernel's output
+  phase1(a, eg, kc);
+  if (!grid_barrier(a.sync, a.status)) return;
+  // every CTA is resident (it passed the barrier) before any of them lets the next kernel launch
+  snb::pdl_trigger();
+  for (int t = blockIdx.x * kWarps + warp; t < a.T; t += gridDim.x * kWarps) phase2_token(a, t, lane);
+  if (!grid_barrier(a.sync, a.status)) return;
+  const int N = a.T * a.K, El = a.E_local;
+  int32_t* sid = smem_i;
+  int32_t* spos = sid + N;
+  int32_t* cnt = spos + N;
+  int32_t* off = cnt + El;
+  int32_t* src = off + El + 1;  // sorted_src of the used rows
+  phase3_sort(a, sid, spos, cnt, off);
+  const int used = off[El];
+  for (int r = threadIdx.x; r < used; r += kThreads) src[r] = -1;
   __syncthreads();
-  if (a.dbg && threadIdx.x == 0) a.dbg[blockIdx.x * 4 + 3] = snb::globaltimer_ns();
+  for (int i = threadIdx.x; i < N; i += kThreads)
+    if (spos[i] >= 0) src[spos[i]] = i / a.K;
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e <= El; e += kThreads) {
+      a.seg_offsets[e] = off[e];
+      a.tile_offsets[e] = off[e] / a.BN;
+    }
+    for (int r = threadIdx.x; r < used; r += kThreads) a.sorted_src[r] = src[r];
+    for (int i = threadIdx.x; i < N; i += kThreads) a.inv_map[i] = spos[i];
+  }
+  // padding rows (src < 0) are skipped: the grouped GEMM's output rows for them are never read
+  for (int r = blockIdx.x * kWarps + warp; r < used; r += gridDim.x * kWarps)
+    if (src[r] >= 0) quant_row(a, r, src[r], lane);
 }
 
 }  // namespace
@@ -355,14 +365,13 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::opt
                      int64_t k, int64_t mode, double scale, int64_t e_lo, int64_t e_local, int64_t bn,
                      torch::Tensor partial, torch::Tensor w_out, torch::Tensor id_out, torch::Tensor seg_offsets,
                      torch::Tensor tile_offsets, torch::Tensor sorted_src, torch::Tensor inv_map, torch::Tensor q,
-                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks,
-                     c10::optional<torch::Tensor> dbg) {
+                     torch::Tensor sf, torch::Tensor sync, torch::Tensor status, int64_t k_chunks) {
   const int T = x.size(0), H = x.size(1);
   if (T == 0) return;
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && H % 64 == 0, "moe_route_fused: x");
   TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
               "moe_route_fused: x rows must be 16-byte aligned");
-  TORCH_CHECK(E <= 256 && k <= kMaxK && k <= E && T * E <= kMaxLogits, "moe_route_fused: T*E or k too large");
+  TORCH_CHECK(E <= 256 && k <= kMaxK && k <= 32 && k <= E && T * E <= kMaxLogits, "moe_route_fused: T*E or k too large");
   const int nk = (H + 63) / 64;
   TORCH_CHECK(w_tiled.scalar_type() == at::kBFloat16 && w_tiled.numel() == ((E + 127) / 128) * nk * 128 * 64,
               "moe_route_fused: tiled router weight shape");
@@ -400,15 +409,10 @@ void moe_route_fused(torch::Tensor x, torch::Tensor w_tiled, int64_t E, c10::opt
   a.Kp = Kp;
   a.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int32_t>());
   a.status = status.data_ptr<int>();
-  a.dbg = dbg ? reinterpret_cast<unsigned long long*>(dbg->data_ptr<int64_t>()) : nullptr;
   const int grid = (int)((E + kEGroup - 1) / kEGroup * k_chunks);
-  const size_t smem = (size_t)T * E * 4 + (size_t)T * k * 4 + (3 * e_local + 1) * 4;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(moe_route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    attr_set = true;
-  }
-  TORCH_CHECK(smem <= 96 * 1024, "moe_route_fused: shared memory");
+  // shared memory: ids and stable positions of the T*k entries, counts and offsets, the used rows' sources
+  const size_t smem = ((size_t)2 * T * k + 2 * e_local + 1 + (size_t)T * k + (size_t)e_local * bn) * 4;
+  TORCH_CHECK(smem <= 48 * 1024, "moe_route_fused: shared memory");
   snb::launch_pdl(moe_route_fused_kernel, grid, kThreads, smem, at::cuda::getCurrentCUDAStream(), a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

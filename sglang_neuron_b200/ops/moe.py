@@ -159,10 +159,11 @@ def sf_atom_offset(row_in_tile: torch.Tensor, kk: torch.Tensor) -> torch.Tensor:
 
 
 def gather_quant_mxfp8(x: torch.Tensor, src: Optional[torch.Tensor], rows: int, bn: int, kp: int = None,
-                       used: Optional[torch.Tensor] = None):
+                       used: Optional[torch.Tensor] = None, skip: Optional[torch.Tensor] = None):
     """Permute rows of x by `src` (-1 = zero row) and quantise to MXFP8 with scales in chunk-atom order.
     `used` ([1] int32 on the device, the routed row count) lets the kernel skip rows no GEMM tile reads.
-    Returns (q [rows, kp] float8_e4m3fn, sf uint8 flat)."""
+    Padding rows (src < 0, or skip[r] < 0 when rows are already in permuted order) are left untouched on the
+    GPU: their GEMM output rows are never read. Returns (q [rows, kp] float8_e4m3fn, sf uint8 flat)."""
     H = x.shape[1]
     kp = H if kp is None else kp
     KB = (kp + 127) // 128
@@ -172,7 +173,7 @@ def gather_quant_mxfp8(x: torch.Tensor, src: Optional[torch.Tensor], rows: int, 
         # the kernel writes every scale byte the MMA reads (rows < BN of each chunk, all K blocks); the
         # remaining bytes of a chunk belong to rows the MMA never reads, so no fill is needed
         sf = torch.empty(nsf, dtype=torch.uint8, device=x.device)
-        kernels().gather_quant_mxfp8(q, sf, x, src, bn, used)
+        kernels().gather_quant_mxfp8(q, sf, x, src, bn, used, skip)
         return q, sf
     sf = torch.full((nsf,), 127, dtype=torch.uint8, device=x.device)
     s = src.long() if src is not None else torch.arange(rows)
@@ -382,7 +383,7 @@ def fused_moe(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, ew:
     else:
         act = torch.empty(R, ew.inter, dtype=torch.bfloat16, device=x.device)
         moe_gemm(act, xq, sfb, ew.w13, ew.sfa13, ew.b13, al, epi, 2 * ew.inter, alpha, limit)
-        aq, sfb2 = gather_quant_mxfp8(act, None, R, bn, used=used)
+        aq, sfb2 = gather_quant_mxfp8(act, None, R, bn, used=used, skip=al.sorted_src)
     y = torch.empty(R, H, dtype=torch.bfloat16, device=x.device)
     moe_gemm(y, aq, sfb2, ew.w2, ew.sfa2, ew.b2, al, EPI_BIAS, H)
     if out is None:

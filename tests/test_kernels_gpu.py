@@ -213,9 +213,13 @@ def test_gather_quant_mxfp8(bn):
     i = torch.arange(bn).repeat_interleave(4)
     kk = torch.arange(4).repeat(bn)
     offs = sf_atom_offset(i, kk)
-    idx = torch.cat([(c * sf_chunk_bytes(bn)) + offs for c in range((rows // bn) * KB)])
-    assert torch.equal(sf.cpu()[idx], sf_ref[idx])
-    assert (q.cpu().float() - q_ref.float()).abs().max().item() <= 1e-6 * 0 + 32.0 * 0.07
+    # rows with a source (padding rows, src < 0, are left untouched: no GEMM output of theirs is read)
+    ok_rows = torch.nonzero(src >= 0).flatten()
+    tile, ii = ok_rows // bn, ok_rows % bn
+    sel = torch.cat([(((tile * KB + kb) * sf_chunk_bytes(bn)) + sf_atom_offset(ii, torch.tensor(kk)))
+                     for kb in range(KB) for kk in range(4)])
+    assert torch.equal(sf.cpu()[sel], sf_ref[sel])
+    assert (q.cpu()[ok_rows].float() - q_ref[ok_rows].float()).abs().max().item() <= 32.0 * 0.07
 
 
 @pytest.mark.parametrize("T,F,K,bias,splits", [(1, 2880, 2880, True, None), (16, 5120, 2880, False, None),
@@ -452,13 +456,13 @@ def test_fused_route_matches_separate_launches(T, E, K, mode, El, e_lo):
     # quantised rows: byte-identical to the separate quantise kernel over the same permutation
     q2, sf2 = moe.gather_quant_mxfp8(x, al.sorted_src, al.r_max, bn, used=al.seg_offsets[El:El + 1])
     torch.cuda.synchronize()
-    assert torch.equal(xq[:used].view(torch.uint8), q2[:used].view(torch.uint8))
-    # scale bytes the MMA reads: (row i of each BN tile, 32-block kk) of every K block of the used tiles
+    ok_rows = torch.nonzero(src[:used] >= 0).flatten()  # padding rows are left untouched by both kernels
+    assert torch.equal(xq[:used].view(torch.uint8)[ok_rows.to(DEV)], q2[:used].view(torch.uint8)[ok_rows.to(DEV)])
+    # scale bytes the MMA reads for those rows: (row i of its BN tile, 32-block kk) of every K block
     KB = (H + 127) // 128
-    i = torch.arange(bn).repeat_interleave(4)
-    kk = torch.arange(4).repeat(bn)
-    offs = moe.sf_atom_offset(i, kk)
-    idx = torch.cat([(c * moe.sf_chunk_bytes(bn)) + offs for c in range((used // bn) * KB)]).to(DEV)
+    tile, ii = ok_rows // bn, ok_rows % bn
+    idx = torch.cat([(((tile * KB + kb) * moe.sf_chunk_bytes(bn)) + moe.sf_atom_offset(ii, torch.tensor(kk)))
+                     for kb in range(KB) for kk in range(4)]).to(DEV)
     assert torch.equal(sfb[idx], sf2[idx])
 
 
