@@ -94,6 +94,10 @@ void gemm_bf16_allreduce(torch::Tensor out, torch::Tensor x, torch::Tensor w, c1
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t capacity, int64_t world);
 int64_t symm_open(py::bytes handle);
 void symm_close(int64_t ptr, bool owned);
+void sp_allgather(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
+                  int64_t num_ctas, torch::Tensor status, int64_t wait_ns);
+void sp_reducescatter(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
+                      int64_t num_ctas, torch::Tensor status, int64_t wait_ns);
 void one_shot_allreduce(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank,
                         int64_t capacity, int64_t num_ctas, torch::Tensor status,
                         c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> weight, double eps,
@@ -146,6 +150,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0,
         py::arg("wait_ns") = 0);
   m.def("gemm_bf16_allreduce", &gemm_bf16_allreduce);
+  m.def("sp_allgather", &sp_allgather);
+  m.def("sp_reducescatter", &sp_reducescatter);
   m.def("splitk_allreduce", &splitk_allreduce, py::arg("out"), py::arg("partial"), py::arg("splits"),
         py::arg("bias"), py::arg("bufs"), py::arg("rank"), py::arg("capacity"), py::arg("num_ctas"),
         py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0,

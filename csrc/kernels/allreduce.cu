@@ -133,7 +133,95 @@ __global__ void __launch_bounds__(kThreadsAR) splitk_allreduce_kernel(
   ar_finish(b, e);
 }
 
+// Sequence-parallel all-gather over NVLink: rank r's block [n8 vectors] goes into slot r of every rank's
+// buffer (peer stores, CTA c owns chunk c of the block), then each rank copies every slot's chunk c into the
+// rank-major output. One launch, no NCCL; the bytes each rank sends are the block times the world.
+__global__ void __launch_bounds__(kThreadsAR) sp_allgather_kernel(ARPeers peers, int rank, int world, size_t capacity,
+                                                                 const __nv_bfloat16* __restrict__ in,
+                                                                 __nv_bfloat16* __restrict__ out, int64_t n8,
+                                                                 int* status) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
+  const ARBuf b = ar_layout(peers, rank, world, capacity);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
+  const int half = e & 1;
+  int64_t v0, v1;
+  int r0, r1;
+  ar_chunk(n8, 1, false, v0, v1, r0, r1);
+  const uint4* src = reinterpret_cast<const uint4*>(in);
+  for (int p = 0; p < world; ++p) {
+    uint4* dst = reinterpret_cast<uint4*>(ar_slot(peers, p, half, rank, world, capacity));
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
+  }
+  if (ar_exchange(peers, b, rank, world, capacity, e, status)) {
+    for (int q = 0; q < world; ++q) {
+      const uint4* s = reinterpret_cast<const uint4*>(ar_slot(peers, rank, half, q, world, capacity));
+      uint4* o = reinterpret_cast<uint4*>(out) + (int64_t)q * n8;
+      for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) o[v] = s[v];
+    }
+  }
+  ar_finish(b, e);
+}
+
+// Sequence-parallel reduce-scatter over NVLink: `in` holds world blocks of n8 vectors (partial sums of every
+// row); block j goes into slot `rank` of rank j's buffer, then each rank sums the world slots of its own
+// block (fp32, rank order) into out. The bytes each rank sends are (world - 1) / world of its partials.
+__global__ void __launch_bounds__(kThreadsAR) sp_reducescatter_kernel(ARPeers peers, int rank, int world,
+                                                                     size_t capacity,
+                                                                     const __nv_bfloat16* __restrict__ in,
+                                                                     __nv_bfloat16* __restrict__ out, int64_t n8,
+                                                                     int* status) {
+  snb::pdl_wait();
+  snb::pdl_trigger();
+  const ARBuf b = ar_layout(peers, rank, world, capacity);
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(b.counter) + 1;
+  const int half = e & 1;
+  int64_t v0, v1;
+  int r0, r1;
+  ar_chunk(n8, 1, false, v0, v1, r0, r1);
+  for (int j = 0; j < world; ++j) {
+    const uint4* src = reinterpret_cast<const uint4*>(in) + (int64_t)j * n8;
+    uint4* dst = reinterpret_cast<uint4*>(ar_slot(peers, j, half, rank, world, capacity));
+    for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) dst[v] = src[v];
+  }
+  if (ar_exchange(peers, b, rank, world, capacity, e, status))
+    ar_reduce_store(peers, half, world, capacity, rank, out, v0, v1);
+  ar_finish(b, e);
+}
+
 }  // namespace
+
+void sp_allgather(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
+                  int64_t num_ctas, torch::Tensor status, int64_t wait_ns) {
+  const int world = (int)bufs.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "sp_allgather: world size");
+  TORCH_CHECK(in.scalar_type() == at::kBFloat16 && in.is_contiguous() && out.is_contiguous(), "sp_allgather: bf16");
+  const int64_t n = in.numel();
+  TORCH_CHECK(n % 8 == 0 && out.numel() == n * world && (size_t)n * 2 <= (size_t)capacity, "sp_allgather: sizes");
+  TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "sp_allgather: CTA count");
+  if (n == 0) return;
+  const ARPeers peers = make_peers(bufs, wait_ns);
+  C10_CUDA_CHECK(snb::launch_pdl(sp_allgather_kernel, num_ctas, kThreadsAR, 0, at::cuda::getCurrentCUDAStream(),
+                                 peers, (int)rank, world, (size_t)capacity, (const __nv_bfloat16*)in.data_ptr(),
+                                 (__nv_bfloat16*)out.data_ptr(), n / 8, status.data_ptr<int>()));
+}
+
+void sp_reducescatter(torch::Tensor out, torch::Tensor in, std::vector<int64_t> bufs, int64_t rank, int64_t capacity,
+                      int64_t num_ctas, torch::Tensor status, int64_t wait_ns) {
+  const int world = (int)bufs.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "sp_reducescatter: world size");
+  TORCH_CHECK(in.scalar_type() == at::kBFloat16 && in.is_contiguous() && out.is_contiguous(),
+              "sp_reducescatter: bf16");
+  const int64_t n = out.numel();
+  TORCH_CHECK(n % 8 == 0 && in.numel() == n * world && (size_t)n * 2 <= (size_t)capacity, "sp_reducescatter: sizes");
+  TORCH_CHECK(num_ctas >= 1 && num_ctas <= kMaxCtas, "sp_reducescatter: CTA count");
+  if (n == 0) return;
+  const ARPeers peers = make_peers(bufs, wait_ns);
+  C10_CUDA_CHECK(snb::launch_pdl(sp_reducescatter_kernel, num_ctas, kThreadsAR, 0,
+                                 at::cuda::getCurrentCUDAStream(), peers, (int)rank, world, (size_t)capacity,
+                                 (const __nv_bfloat16*)in.data_ptr(), (__nv_bfloat16*)out.data_ptr(), n / 8,
+                                 status.data_ptr<int>()));
+}
 
 // --- IPC plumbing -----------------------------------------------------------------------------------
 // Allocate the communicator buffer (cudaMalloc: IPC needs whole allocations, not caching-allocator blocks)

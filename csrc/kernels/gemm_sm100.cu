@@ -17,18 +17,22 @@
 #include "../tma_host.h"
 #include "../ar_common.cuh"
 #include <algorithm>
+#include <cstdlib>
 
 namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // bf16 elements per 128-byte swizzled row
 
-template <int BN>
+// OCC = CTAs per SM: 1 (a ~200 KB ring) or 2 (two ~100 KB rings: decode-sized GEMMs split K over up to
+// twice as many CTAs, so more SMs stream the weights at once).
+template <int BN, int OCC = 1>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int BUDGET = OCC == 2 ? 100 * 1024 : 200 * 1024;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
   static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -64,13 +68,13 @@ SNB_DEVICE int group_col(const GemmGroup& g, int f) {
   return g.o_rows ? (f / g.o_rows) * g.o_stride + f % g.o_rows : f;
 }
 
-template <int BN, bool AR>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, bool AR, int OCC = 1>
+__global__ void __launch_bounds__(192, OCC)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                      __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ bias, int F, int T,
                      int K, int ldo, int* status, float* __restrict__ partial, const GemmAR ar, int cluster_reduce,
                      int w_tiled, const GemmGroup grp) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, OCC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -386,9 +390,9 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const __
 
 // Largest split count (<= 8, the portable cluster size) whose reduce-scatter slots
 // (S x 128 rows x rs floats) fit in the ring.
-template <int BN>
+template <int BN, int OCC = 1>
 int max_cluster_splits() {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, OCC>;
   int best = 1;
   for (int S = 2; S <= 8; ++S) {
     const int ng = BN / 4, maxg = (ng + S - 1) / S;
@@ -400,11 +404,11 @@ int max_cluster_splits() {
 
 // Split count for the in-cluster reduction: as many K splits as keep every tile's cluster co-resident in
 // one wave (checked with the occupancy calculator once per shape class).
-template <int BN>
+template <int BN, int OCC = 1>
 int pick_cluster_splits(int tiles, int nk, int num_sms) {
-  using C = GemmCfg<BN>;
-  if (tiles * 2 > num_sms) return 1;
-  int S = std::min({max_cluster_splits<BN>(), num_sms / tiles, nk});
+  using C = GemmCfg<BN, OCC>;
+  if (tiles * 2 > num_sms * OCC) return 1;
+  int S = std::min({max_cluster_splits<BN, OCC>(), num_sms * OCC / tiles, nk});
   static int max_clusters[9] = {0};
   while (S > 1) {
     if (max_clusters[S] == 0) {
@@ -420,7 +424,7 @@ int pick_cluster_splits(int tiles, int nk, int num_sms) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_kernel<BN, false>, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_kernel<BN, false, OCC>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = -1;
       }
@@ -459,6 +463,27 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
     // default: split K inside a thread-block cluster when the tiles alone leave SMs idle
     int S = 1;
     if constexpr (!AR) S = pick_cluster_splits<BN>(tiles_f * tiles_t, (K + BK - 1) / BK, num_sms);
+    if constexpr (!AR && BN <= 64) {
+      // two CTAs per SM when that splits K over more SMs than one CTA per SM can
+      using C2 = GemmCfg<BN, 2>;
+      const int S2 = pick_cluster_splits<BN, 2>(tiles_f * tiles_t, (K + BK - 1) / BK, num_sms);
+      static const bool use2 = [] {
+        const char* e = std::getenv("SGLANG_B200_GEMM_2CTA");
+        return !(e != nullptr && e[0] == '0');
+      }();
+      if (use2 && S2 > S) {
+        static bool attr2 = false;
+        if (!attr2) {
+          C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN, false, 2>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C2::SMEM));
+          attr2 = true;
+        }
+        C10_CUDA_CHECK(snb::launch_pdl_cluster(gemm_bf16_kernel<BN, false, 2>, dim3(tiles_f, tiles_t, S2), 192,
+                                               C2::SMEM, st, S2, tw, tx, op, bias, F, T, K, ldo, status, nullptr, ar,
+                                               1, wt, grp));
+        return;
+      }
+    }
     if (S > 1) {
       C10_CUDA_CHECK(snb::launch_pdl_cluster(gemm_bf16_kernel<BN, AR>, dim3(tiles_f, tiles_t, S), 192, C::SMEM, st,
                                              S, tw, tx, op, bias, F, T, K, ldo, status, nullptr, ar, 1, wt, grp));

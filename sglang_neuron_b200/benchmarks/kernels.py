@@ -202,6 +202,11 @@ def bench_gemm(a):
         us = graph_time([lambda i=i: linear(x, ws[i], out=outs[i % 2]) for i in range(n)])
         res["us_in_graph"] = round(us, 2)
         res["copies"] = n
+        # cuBLAS on the same shapes (row-major weights, the plain library GEMM), for comparison
+        wr = [w.untiled().contiguous() for w in ws]
+        res["us_cublas_in_graph"] = round(graph_time([lambda i=i: torch.matmul(x, wr[i].t(), out=outs[i % 2])
+                                                      for i in range(n)]), 2)
+        del wr
     if a.iters > 1:  # grid-per-tile kernel with split-K partials + reduce launch, for comparison
         sp = pick_splits(T, N, K, torch.cuda.get_device_properties(0).multi_processor_count)
         res["us_grid_splitk"] = round(timeit(lambda: linear(x, w, splits=sp), a.iters, a.warmup), 2)

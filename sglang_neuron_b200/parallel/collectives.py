@@ -177,14 +177,25 @@ def sp_reduce_scatter(x: torch.Tensor, rows: int) -> torch.Tensor:
     if x.shape[0] < rows * tp:
         x = torch.cat([x, x.new_zeros(rows * tp - x.shape[0], *x.shape[1:])])
     out = torch.empty((rows,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    if _sp_native(out):
+        return _custom_allreduce.reduce_scatter(x.contiguous(), out)
     dist.reduce_scatter_tensor(out, x.contiguous(), group=st.tp_group)
     return out
+
+
+def _sp_native(block: torch.Tensor) -> bool:
+    """The NVLink all-gather / reduce-scatter kernels take bf16 blocks that fit one buffer slot."""
+    ar = _custom_allreduce
+    return (ar is not None and getattr(ar, "supports_sp", False) and block.is_cuda
+            and block.dtype == torch.bfloat16 and block.numel() % 8 == 0 and block.numel() * 2 <= ar.capacity)
 
 
 def sp_all_gather(x: torch.Tensor) -> torch.Tensor:
     """x: [rows, H] this rank's block; returns [rows * tp, H] (rank-major)."""
     st = get_state()
     out = torch.empty((x.shape[0] * st.tp_size,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    if _sp_native(x):
+        return _custom_allreduce.all_gather(x.contiguous(), out)
     dist.all_gather_into_tensor(out, x.contiguous(), group=st.tp_group)
     return out
 

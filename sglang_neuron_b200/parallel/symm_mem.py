@@ -156,6 +156,25 @@ class IpcAllReduce:
                                         wait_ns=self.wait_ns, **self._norm_kw(norm))
         return out
 
+    supports_sp = True
+
+    def _sp_ctas(self, nvec: int) -> int:
+        return max(1, min(148, (nvec + 511) // 512))
+
+    def all_gather(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Sequence-parallel all-gather of this rank's [rows, H] block into out [world * rows, H] (rank-major),
+        one NVLink launch."""
+        kernels().sp_allgather(out, x, self.ptrs, self.rank, self.capacity, self._sp_ctas(x.numel() // 8),
+                               self.status, self.wait_ns)
+        return out
+
+    def reduce_scatter(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Sequence-parallel reduce-scatter: x [world * rows, H] partial sums -> out [rows, H], this rank's
+        block of the sums, one NVLink launch."""
+        kernels().sp_reducescatter(out, x, self.ptrs, self.rank, self.capacity, self._sp_ctas(out.numel() // 8),
+                                   self.status, self.wait_ns)
+        return out
+
     def gemm_can_run(self, T: int, F: int, num_sms: int) -> bool:
         bn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
         tiles = ((F + 127) // 128) * ((T + bn - 1) // bn)

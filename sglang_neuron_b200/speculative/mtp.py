@@ -97,8 +97,9 @@ class SpecState:
 
 
 class MTPWorker:
-    """Drives prefill + speculative decode steps for a batch of requests through the model runner
-    (host-synchronous, eager). Used by Engine when speculative_algorithm == "MTP"."""
+    """Drives prefill + speculative decode steps for a batch of requests through the model runner (eager;
+    acceptance on the device, two host reads per verify step). Used by Engine when speculative_algorithm ==
+    "MTP"."""
 
     def __init__(self, engine, num_draft: int = 3):
         self.eng = engine
@@ -149,25 +150,28 @@ class MTPWorker:
         logits = model.compute_logits(h)
         return logits, model.last_prenorm
 
-    def _draft_chain(self, reqs, first_tok: torch.Tensor, first_h: torch.Tensor, start_pos: List[int]) -> List[List[int]]:
-        """k draft tokens per request: step 1 consumes (first_tok, first_h) at start_pos, later steps the
-        draft's own outputs."""
+    def _draft_chain(self, reqs, first_tok: torch.Tensor, first_h: torch.Tensor, start_pos: List[int],
+                     steps: Optional[int] = None) -> torch.Tensor:
+        """`steps` (default k) draft tokens per request, kept on the device: step 1 consumes (first_tok,
+        first_h) at start_pos, later steps the draft's own outputs. Returns [B, steps] int64 on the device."""
         head = self.runner.draft
-        drafts = [[] for _ in reqs]
+        steps = self.k if steps is None else steps
+        out = []
         tok, h = first_tok, first_h
         pos = list(start_pos)
-        for _ in range(self.k):
+        for _ in range(steps):
             for i, req in enumerate(reqs):
                 self._ensure_pages(req, pos[i] + 1)
             slots = [self._slots(req, [pos[i]])[0] for i, req in enumerate(reqs)]
             fb = self._fb([0] * len(reqs), pos, slots, [(req, 1) for req in reqs])
             logits, pre = head(tok, h, fb)
-            nxt = logits[:, : self.runner.vocab_valid].float().argmax(-1)
-            for i, t in enumerate(nxt.tolist()):
-                drafts[i].append(int(t))
-            tok, h = nxt, pre
+            tok = logits[:, : self.runner.vocab_valid].float().argmax(-1)
+            out.append(tok)
+            h = pre
             pos = [p + 1 for p in pos]
-        return drafts
+        if not out:
+            return torch.zeros(len(reqs), 0, dtype=torch.long, device=self.runner.device)
+        return torch.stack(out, dim=1)
 
     # -- public ------------------------------------------------------------------------------------
     def prefill(self, reqs) -> None:
@@ -202,13 +206,16 @@ class MTPWorker:
             last_h.append(pre[end])
         drafts = self._draft_chain([r for r, _ in rows],
                                    torch.tensor(firsts, device=self.runner.device), torch.stack(last_h),
-                                   [r.prompt_len for r, _ in rows])
+                                   [r.prompt_len for r, _ in rows]).tolist()  # one read for every draft
         for (req, _), d in zip(rows, drafts):
             req.spec_drafts = d
 
     def step(self, reqs) -> None:
-        """One verify + accept + re-draft step for requests in decode phase."""
+        """One verify + accept + re-draft step for requests in decode phase. Acceptance runs on the device (the
+        drafts against the target's greedy tokens, the accepted length as a cumulative product of matches); the
+        host reads the target's tokens and the accepted lengths once, and the new drafts once."""
         k = self.k
+        dev = self.runner.device
         ids, pos, slots, rows = [], [], [], []
         for req in reqs:
             p = req.kv_len
@@ -220,15 +227,16 @@ class MTPWorker:
             rows.append((req, k + 1))
         fb = self._fb(ids, pos, slots, rows)
         logits, pre = self._target(fb)
-        greedy = logits[:, : self.runner.vocab_valid].float().argmax(-1).tolist()
+        B = len(reqs)
+        greedy = logits[:, : self.runner.vocab_valid].float().argmax(-1).view(B, k + 1)
+        drafts = fb.input_ids.view(B, k + 1)[:, 1:]
+        n_acc = (drafts == greedy[:, :k]).long().cumprod(dim=1).sum(dim=1)  # accepted drafts per request
+        host = torch.cat([greedy, n_acc[:, None]], dim=1).tolist()      # the one read of this verify step
         self.stats["verify_steps"] += 1
         # accept
-        mtp_ids, mtp_h, mtp_pos, mtp_slots, mtp_rows = [], [], [], [], []
+        mtp_ids, mtp_rows_h, mtp_pos, mtp_slots, mtp_rows = [], [], [], [], []
         for i, req in enumerate(reqs):
-            g = greedy[i * (k + 1):(i + 1) * (k + 1)]
-            n = 0
-            while n < k and req.spec_drafts[n] == g[n]:
-                n += 1
+            g, n = host[i][: k + 1], int(host[i][k + 1])
             self.stats["drafted"] += k
             self.stats["accepted"] += n
             new = g[: n + 1]
@@ -241,39 +249,31 @@ class MTPWorker:
             # paired with the target hidden of row j (position p+j)
             for j in range(len(new)):
                 mtp_ids.append(new[j])
-                mtp_h.append(pre[i * (k + 1) + j])
+                mtp_rows_h.append(i * (k + 1) + j)
                 mtp_pos.append(p + 1 + j)
             mtp_slots += self._slots(req, range(p + 1, p + 1 + len(new)))
             mtp_rows.append((req, len(new)))
         keep = [(r, n) for r, n in mtp_rows if len(r.output_ids) < r.params.max_new_tokens]
         fb2 = self._fb(mtp_ids, mtp_pos, mtp_slots, mtp_rows)
-        d_logits, d_pre = self.runner.draft(torch.tensor(mtp_ids, device=self.runner.device), torch.stack(mtp_h), fb2)
+        h_rows = pre.index_select(0, torch.tensor(mtp_rows_h, dtype=torch.long, device=dev))
+        d_logits, d_pre = self.runner.draft(fb2.input_ids, h_rows, fb2)
         if not keep:
             return
         ends = np.cumsum([n for _, n in mtp_rows]) - 1
-        first, first_h, starts, live = [], [], [], []
+        live_idx, starts, live = [], [], []
         for (req, n), e in zip(mtp_rows, ends):
             if len(req.output_ids) >= req.params.max_new_tokens:
                 continue
-            first.append(int(d_logits[int(e), : self.runner.vocab_valid].float().argmax()))
-            first_h.append(d_pre[int(e)])
+            live_idx.append(int(e))
             starts.append(req.kv_len + 1)
             live.append(req)
-        # the first draft came from the catch-up pass; chain the remaining k-1
-        if self.k > 1:
-            rest = self._draft_chain_from(live, first, torch.stack(first_h), starts)
-        else:
-            rest = [[] for _ in live]
-        for req, f, r in zip(live, first, rest):
-            req.spec_drafts = [f] + r
-
-    def _draft_chain_from(self, reqs, first: List[int], h: torch.Tensor, start_pos: List[int]) -> List[List[int]]:
-        saved = self.k
-        self.k = saved - 1
-        try:
-            return self._draft_chain(reqs, torch.tensor(first, device=self.runner.device), h, start_pos)
-        finally:
-            self.k = saved
+        sel = torch.tensor(live_idx, dtype=torch.long, device=dev)
+        first = d_logits.index_select(0, sel)[:, : self.runner.vocab_valid].float().argmax(-1)
+        # the first draft came from the catch-up pass; chain the remaining k-1 on the device
+        rest = self._draft_chain(live, first, d_pre.index_select(0, sel), starts, steps=self.k - 1)
+        new_drafts = torch.cat([first[:, None], rest], dim=1).tolist()  # the one read of the new drafts
+        for req, d in zip(live, new_drafts):
+            req.spec_drafts = d
 
     def generate(self, reqs) -> None:
         self.prefill(reqs)

@@ -447,3 +447,45 @@ def test_pd_p2p_pages_land_exactly_and_tokens_match_aggregated():
         assert dec["sums"][rid] == s, f"{rid}: pages differ after the P2P copy"
     ref = _spawn(_pd_ref_worker, 1)[0][0]
     assert [dec["tokens"][f"pd{i}"] for i in range(3)] == ref
+
+
+def _sp_worker(rank, world, port, q):
+    _init(rank, world, port)
+    import torch.distributed as dist
+    from sglang_neuron_b200.parallel.state import initialize_parallel
+    from sglang_neuron_b200.parallel.symm_mem import IpcAllReduce
+    initialize_parallel(world, device=torch.device("cuda", rank))
+    ar = IpcAllReduce(capacity_bytes=8 << 20)
+    errs = []
+    for rows, H in [(136, 2880), (1, 2880), (512, 4096), (37, 1024)]:
+        g = torch.Generator(device="cuda").manual_seed(rows + rank)
+        blk = torch.randn(rows, H, generator=g, device="cuda").to(torch.bfloat16)
+        ref = torch.empty(rows * world, H, dtype=torch.bfloat16, device="cuda")
+        dist.all_gather_into_tensor(ref, blk)
+        out = torch.empty_like(ref)
+        for _ in range(2):
+            ar.all_gather(blk, out)
+        torch.cuda.synchronize()
+        errs.append(float((out.float() - ref.float()).abs().max()))  # exact copy: 0
+        part = torch.randn(rows * world, H, generator=g, device="cuda").to(torch.bfloat16)
+        ref_rs = torch.empty(rows, H, dtype=torch.float32, device="cuda")
+        dist.reduce_scatter_tensor(ref_rs, part.float())
+        got = torch.empty(rows, H, dtype=torch.bfloat16, device="cuda")
+        for _ in range(2):
+            ar.reduce_scatter(part, got)
+        torch.cuda.synchronize()
+        errs.append(((got.float() - ref_rs).abs().max() / ref_rs.abs().max()).item())
+    q.put((rank, errs, int(ar.status[0])))
+    ar.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@needs2
+def test_sp_allgather_reducescatter_match_nccl():
+    """The sequence-parallel NVLink all-gather (exact) and reduce-scatter (bf16 sum) against NCCL."""
+    res = _spawn(_sp_worker, 2)
+    for rank, (errs, status) in res.items():
+        assert status == 0, f"rank {rank}: bounded wait expired"
+        assert all(e == 0.0 for e in errs[0::2]), f"rank {rank}: all-gather {errs[0::2]}"
+        assert max(errs[1::2]) < 1e-2, f"rank {rank}: reduce-scatter {errs[1::2]}"
