@@ -81,7 +81,12 @@ _NP = {torch.int64: np.int64, torch.int32: np.int32, torch.float32: np.float32}
 
 
 class StepIO:
-    """Packs host arrays into one pinned buffer and uploads them with one copy; reads sampled ids back."""
+    """Packs host arrays into one pinned buffer and uploads them with one copy; reads sampled ids back.
+
+    Two streams: the host->device copy of a step's inputs runs on a copy stream into a device staging slot
+    (so its PCIe latency overlaps the step still running on the compute stream), and the compute stream takes
+    the bytes from there with one device-to-device copy after waiting on the copy's event. Parity: the
+    reference's device_io copy queue and pinned upload ring (sglang_neuron/backend/device_io.py:150-413)."""
 
     def __init__(self, device, max_bytes: int, max_batch: int):
         self.device = torch.device(device)
@@ -90,6 +95,9 @@ class StepIO:
         self.down = PinnedRing(max_batch * 8, 8, self.cuda)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        self.copy_stream = torch.cuda.Stream(device=self.device) if self.cuda else None
+        self.stage = ([torch.empty(max_bytes, dtype=torch.uint8, device=self.device) for _ in range(4)]
+                      if self.cuda else None)
 
     def upload(self, layout: Layout, arrays: Dict[str, np.ndarray], dst: Optional[torch.Tensor] = None):
         slot, host = self.up.acquire()
@@ -100,16 +108,26 @@ class StepIO:
             v.numpy()[:n] = arr
         if dst is None:
             dst = torch.empty(layout.nbytes, dtype=torch.uint8, device=self.device)
-        dst[:layout.nbytes].copy_(host[:layout.nbytes], non_blocking=self.cuda)
-        self.h2d_bytes += layout.nbytes
         if self.cuda:
+            cur = torch.cuda.current_stream(self.device)
+            stage = self.stage[slot]
+            with torch.cuda.stream(self.copy_stream):
+                stage[:layout.nbytes].copy_(host[:layout.nbytes], non_blocking=True)
+                arrived = torch.cuda.Event()
+                arrived.record(self.copy_stream)
+            cur.wait_event(arrived)
+            dst[:layout.nbytes].copy_(stage[:layout.nbytes], non_blocking=True)
             ev = torch.cuda.Event()
-            ev.record()
-            self.up.mark(slot, ev)
+            ev.record(cur)
+            self.up.mark(slot, ev)  # host slot and staging slot are free once the device copy ran
+        else:
+            dst[:layout.nbytes].copy_(host[:layout.nbytes])
+        self.h2d_bytes += layout.nbytes
         return layout.views(dst[:layout.nbytes])
 
     def readback(self, ids: torch.Tensor):
-        """Async copy of [B] int64 ids into a pinned slot; returns (host view, event)."""
+        """Async copy of [B] int64 ids into a pinned slot; returns (host view, event). It stays on the compute
+        stream: the ids of a replayed graph live in the graph's static output, which the next replay rewrites."""
         slot, host = self.down.acquire()
         n = ids.numel()
         hv = host[: n * 8].view(torch.int64)
