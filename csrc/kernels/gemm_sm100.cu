@@ -466,18 +466,18 @@ void launch_gemm(const torch::Tensor& out, const torch::Tensor& x, const torch::
     if constexpr (!AR && BN <= 64) {
       // two CTAs per SM when that splits K over more SMs than one CTA per SM can
       using C2 = GemmCfg<BN, 2>;
-      const int S2 = pick_cluster_splits<BN, 2>(tiles_f * tiles_t, (K + BK - 1) / BK, num_sms);
       static const bool use2 = [] {
         const char* e = std::getenv("SGLANG_B200_GEMM_2CTA");
         return !(e != nullptr && e[0] == '0');
       }();
+      static bool attr2 = false;
+      if (use2 && !attr2) {  // before the occupancy query, which needs the shared-memory size allowed
+        C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN, false, 2>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, C2::SMEM));
+        attr2 = true;
+      }
+      const int S2 = use2 ? pick_cluster_splits<BN, 2>(tiles_f * tiles_t, (K + BK - 1) / BK, num_sms) : 1;
       if (use2 && S2 > S) {
-        static bool attr2 = false;
-        if (!attr2) {
-          C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN, false, 2>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C2::SMEM));
-          attr2 = true;
-        }
         C10_CUDA_CHECK(snb::launch_pdl_cluster(gemm_bf16_kernel<BN, false, 2>, dim3(tiles_f, tiles_t, S2), 192,
                                                C2::SMEM, st, S2, tw, tx, op, bias, F, T, K, ldo, status, nullptr, ar,
                                                1, wt, grp));

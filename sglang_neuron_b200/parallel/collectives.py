@@ -183,10 +183,14 @@ def sp_reduce_scatter(x: torch.Tensor, rows: int) -> torch.Tensor:
     return out
 
 
+_SP_NVLINK = os.environ.get("SGLANG_B200_SP_NVLINK", "0") == "1"
+
+
 def _sp_native(block: torch.Tensor) -> bool:
-    """The NVLink all-gather / reduce-scatter kernels take bf16 blocks that fit one buffer slot."""
+    """The NVLink all-gather / reduce-scatter kernels take bf16 blocks that fit one buffer slot
+    (SGLANG_B200_SP_NVLINK=1; NCCL otherwise)."""
     ar = _custom_allreduce
-    return (ar is not None and getattr(ar, "supports_sp", False) and block.is_cuda
+    return (_SP_NVLINK and ar is not None and getattr(ar, "supports_sp", False) and block.is_cuda
             and block.dtype == torch.bfloat16 and block.numel() % 8 == 0 and block.numel() * 2 <= ar.capacity)
 
 

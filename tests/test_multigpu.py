@@ -450,6 +450,7 @@ def test_pd_p2p_pages_land_exactly_and_tokens_match_aggregated():
 
 
 def _sp_worker(rank, world, port, q):
+    os.environ["SGLANG_B200_SP_NVLINK"] = "1"
     _init(rank, world, port)
     import torch.distributed as dist
     from sglang_neuron_b200.parallel.state import initialize_parallel
