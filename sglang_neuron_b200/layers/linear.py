@@ -38,13 +38,17 @@ class PackedWeight:
         if (self._packed is not None or not w.is_cuda or w.dtype != torch.bfloat16 or w.dim() != 2 or not w.numel()
                 or cublas_baseline()):  # the cuBLAS comparison build keeps nn.Linear weights
             return
-        self._packed = TiledWeight(w.data)
-        self.weight = nn.Parameter(torch.empty(0, dtype=w.dtype, device=w.device), requires_grad=False)
+        from ..ops.gemm import plain_gemm_backend
+        keep = plain_gemm_backend() == "cublas"  # plain GEMMs read the nn.Linear copy through cuBLAS
+        self._packed = TiledWeight(w.data, keep_rowmajor=keep)
+        if not keep:
+            self.weight = nn.Parameter(torch.empty(0, dtype=w.dtype, device=w.device), requires_grad=False)
 
     def unpack(self) -> None:
         """Back to a row-major parameter (before loading new weights into a packed layer)."""
         if self._packed is not None:
-            self.weight = nn.Parameter(self._packed.untiled().contiguous(), requires_grad=False)
+            if self._packed.rowmajor is None:
+                self.weight = nn.Parameter(self._packed.untiled().contiguous(), requires_grad=False)
             self._packed = None
 
 

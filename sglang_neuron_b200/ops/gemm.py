@@ -35,10 +35,11 @@ class TiledWeight:
     16 KB block, `data` = [ceil(F/128) * ceil(K/64) * 128, 64] (tile (f, k) at rows ((f * nk) + k) * 128),
     zero padded. One TMA box then reads one contiguous DRAM stream instead of 128 strided 128-byte rows."""
 
-    __slots__ = ("data", "F", "K")
+    __slots__ = ("data", "F", "K", "rowmajor")
 
-    def __init__(self, w: torch.Tensor):
+    def __init__(self, w: torch.Tensor, keep_rowmajor: bool = False):
         F, K = w.shape
+        self.rowmajor = w if keep_rowmajor else None  # the nn.Linear copy, for plain GEMMs through cuBLAS
         ntf, nk = (F + 127) // 128, (K + 63) // 64
         pad = torch.zeros(ntf * 128, nk * 64, dtype=w.dtype, device=w.device)
         pad[:F, :K] = w
@@ -91,10 +92,31 @@ def cublas_baseline() -> bool:
 _CUBLAS = cublas_baseline()
 
 
+def plain_gemm_backend() -> str:
+    """Where a plain dense GEMM (no fused collective, no grouped layout) runs: "cublas" (default) or "tcgen05"
+    (SGLANG_B200_DENSE_GEMM). Measured in CUDA graphs on a B200, cuBLAS is ahead of this package's tcgen05
+    kernel on every dense shape of the served models (e.g. 64 x 5120 x 2880: 7.8 us against 13.4 us; the
+    1087-token Qwen3-8B mixed step: 23.3 ms against 33.5 ms), so plain library GEMMs go to the library and the
+    tcgen05 kernel serves the fused forms: split-K partials feeding the NVLink all-reduce, the GEMM with the
+    all-reduce in its epilogue, the per-head grouped GEMMs of absorbed MLA."""
+    from .. import env_registry
+    v = (env_registry.get("SGLANG_B200_DENSE_GEMM", "cublas") or "cublas").strip().lower()
+    if v not in ("cublas", "tcgen05"):
+        raise ValueError(f"SGLANG_B200_DENSE_GEMM={v!r}: expected 'cublas' or 'tcgen05'")
+    return v
+
+
+_PLAIN_CUBLAS = plain_gemm_backend() == "cublas"
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, out=None,
            bn: int = 0, splits: Optional[int] = None) -> torch.Tensor:
     """y = x @ w.T (+ bias). x: [..., K], w: [F, K] tensor or TiledWeight."""
-    if not x.is_cuda or x.dtype != torch.bfloat16 or (_CUBLAS and not isinstance(w, TiledWeight)):
+    cublas = _CUBLAS and not isinstance(w, TiledWeight)
+    if (x.is_cuda and x.dtype == torch.bfloat16 and _PLAIN_CUBLAS and splits is None and bn == 0
+            and isinstance(w, TiledWeight) and w.rowmajor is not None):
+        w, cublas = w.rowmajor, True  # a layer's plain GEMM: the library path (see plain_gemm_backend)
+    if not x.is_cuda or x.dtype != torch.bfloat16 or cublas:
         if isinstance(w, TiledWeight):
             w = w.untiled()
         y = torch.nn.functional.linear(x, w, bias)
