@@ -127,8 +127,14 @@ def export_pool(pool, head_start: int) -> Dict:
     out = []
     for b in _pool_buffers(pool):
         info = b.untyped_storage()._share_cuda_()
-        handle, off = info[1], info[3]
-        out.append((bytes(handle), int(off) + b.storage_offset() * b.element_size()))
+        handle, off = bytes(info[1]), info[3]
+        # the caching allocator prefixes the 64-byte cudaIpcMemHandle with its segment kind ('c': cudaMalloc);
+        # expandable (virtual-memory) segments have no IPC handle of this kind
+        if len(handle) == 65:
+            if handle[:1] != b"c":
+                raise RuntimeError("PD P2P needs cudaMalloc-backed KV pools (expandable segments are not shareable)")
+            handle = handle[1:]
+        out.append((handle, int(off) + b.storage_offset() * b.element_size()))
     return {"bufs": out, **pool_geometry(pool, head_start)}
 
 

@@ -201,7 +201,10 @@ class Engine:
     def shutdown(self) -> None:
         self.scheduler.drain()
         if self.runner.graph_runner is not None:
+            # every captured graph (the filtered-sampler ones hold NCCL calls under TP) goes before the process
+            # group, or its destruction waits on them
             self.runner.graph_runner.graphs.clear()
+            self.runner.graph_runner.graphs_f.clear()
         if self.custom_ar is not None:
             from .parallel.collectives import set_custom_allreduce
             torch.cuda.synchronize()
