@@ -29,6 +29,7 @@ REGISTRY: Dict[str, tuple] = {
     "SGLANG_B200_GEMM_2CTA": ("kernels", "decode-sized bf16 GEMMs may run two CTAs per SM to split K over more SMs (0 turns it off)"),
     "SGLANG_B200_SP_NVLINK": ("collectives", "1: sequence-parallel all-gather / reduce-scatter through the NVLink kernels instead of NCCL"),
     "SGLANG_B200_DENSE_GEMM": ("kernels", "plain dense GEMMs: 'cublas' (default, measured faster) or 'tcgen05' (this package's kernel)"),
+    "SGLANG_B200_STEP_TIMER": ("profile", "per-step device time from CUDA events around each step (default 1; /metrics p50 by step kind)"),
     "SGLANG_B200_PDL": ("kernels", "programmatic dependent launch of the sm_100a kernels (0 turns it off)"),
     "SGLANG_B200_STEP_FENCE": ("debug", "1: ranks check through shared memory that each step launches the same program"),
     "SGLANG_B200_FUSED_AR_NORM": ("collectives", "residual add + RMSNorm inside the NVLink all-reduce kernels (0 turns it off)"),

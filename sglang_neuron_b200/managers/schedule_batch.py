@@ -121,6 +121,7 @@ class StepInput:
     relay_first_token: Optional[np.ndarray] = None
     logprob_k: int = -1                 # >= 0: compute token logprobs (+ top-k) for this step
     logprob_host: Optional[object] = None  # host view [B, 1 + 2k] filled by the runner
+    device_events: Optional[tuple] = None  # (start, end) CUDA timing events of the step's device work
 
     def arrays(self):
         return {

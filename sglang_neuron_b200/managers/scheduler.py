@@ -74,6 +74,8 @@ class Scheduler:
         self.on_token: Optional[Callable[[Req], None]] = None
         self.stats = collections.Counter()
         self.step_times: List[Tuple[int, float, int, int]] = []
+        # device time of recent steps: (0 decode / 1 prefill or mixed, ms), from the runner's step timer
+        self.device_ms: Deque[Tuple[int, float]] = collections.deque(maxlen=2048)
         # DP attention: this rank's attention group serves every D-th arrival; the others' requests are
         # mirrored from the per-step exchange (tokens and finish state published by each group's rank 0)
         st = get_state()
@@ -455,6 +457,10 @@ class Scheduler:
     def _process(self, step: StepInput, ids_host, event) -> None:
         if event is not None:
             event.synchronize()
+        ev = getattr(step, "device_events", None)
+        if ev is not None:  # per-step device time (the readback event above completed after it)
+            ev[1].synchronize()
+            self.device_ms.append((int(step.mode != ForwardMode.DECODE), ev[0].elapsed_time(ev[1])))
         watch = getattr(self.runner, "status_watch", None)
         if watch is not None:
             watch.check()

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import logging
 import math
+import os
 from typing import Dict, List, Optional, Tuple
 
 import numpy as np
@@ -35,6 +36,7 @@ from .forward_batch import ForwardBatch, ForwardMode
 logger = logging.getLogger(__name__)
 
 _ALIGN = 16
+_STEP_TIMER = os.environ.get("SGLANG_B200_STEP_TIMER", "1") != "0"
 
 
 class PinnedRing:
@@ -342,7 +344,21 @@ class ModelRunner:
         self.req_to_page.table[u[:, 0], u[:, 1]] = u[:, 2].to(torch.int32)
 
     def run_step(self, step) -> Tuple[torch.Tensor, Optional[torch.cuda.Event]]:
-        """Launch one forward for a host-built StepInput; returns (pinned host ids view, event)."""
+        """Launch one forward for a host-built StepInput; returns (pinned host ids view, event). With the step
+        timer on (default on GPUs, SGLANG_B200_STEP_TIMER=0 turns it off) the step carries a pair of timing
+        events around its device work; the scheduler reads the elapsed time once the step's results arrive."""
+        t0 = None
+        if self.cuda and _STEP_TIMER:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+        out = self._run_step(step)
+        if t0 is not None:
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record()
+            step.device_events = (t0, t1)
+        return out
+
+    def _run_step(self, step) -> Tuple[torch.Tensor, Optional[torch.cuda.Event]]:
         if (step.mode == ForwardMode.DECODE and step.logprob_k < 0 and self.graph_runner is not None
                 and not getattr(step, "dp_rows", 0) and self.graph_runner.can_run(step)):
             ids = self.graph_runner.replay(step)

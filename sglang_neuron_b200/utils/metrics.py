@@ -26,6 +26,8 @@ class Metrics:
         self.free_pages = Gauge("snb_kv_free_pages", "free KV pages", registry=r)
         self.cache_hit = Gauge("snb_cache_hit_rate", "prefix-cache hit rate (tokens)", registry=r)
         self.steps = Gauge("snb_scheduler_steps", "scheduler steps", registry=r)
+        self.step_ms = Gauge("snb_step_device_ms_p50", "median device time of recent steps (ms)", ["kind"],
+                             registry=r)
 
     def update_from(self, engine) -> None:
         s = engine.scheduler
@@ -35,6 +37,9 @@ class Metrics:
         pt = s.stats.get("prompt_tokens", 0)
         self.cache_hit.set(s.stats.get("cache_hit_tokens", 0) / pt if pt else 0.0)
         self.steps.set(s.stats.get("steps", 0))
+        for kind, name in ((0, "decode"), (1, "prefill_or_mixed")):
+            v = sorted(ms for k, ms in list(getattr(s, "device_ms", [])) if k == kind)
+            self.step_ms.labels(kind=name).set(v[len(v) // 2] if v else 0.0)
 
     def render(self) -> str:
         return generate_latest(self.registry).decode()
