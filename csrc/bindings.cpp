@@ -12,7 +12,7 @@ void rope_qk_norm_kv_write(torch::Tensor q, torch::Tensor k, torch::Tensor v, to
                            int64_t rot_dim, bool neox, c10::optional<torch::Tensor> q_norm_w,
                            c10::optional<torch::Tensor> k_norm_w, double norm_eps, torch::Tensor k_cache,
                            torch::Tensor v_cache, torch::Tensor slots, int64_t page_size, double k_scale,
-                           double v_scale);
+                           double v_scale, c10::optional<torch::Tensor> status);
 // attention.cu
 void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                       torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
@@ -112,7 +112,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_out", &rmsnorm_out);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("head_rmsnorm_", &head_rmsnorm_);
-  m.def("rope_qk_norm_kv_write", &rope_qk_norm_kv_write);
+  m.def("rope_qk_norm_kv_write", &rope_qk_norm_kv_write, py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("positions"), py::arg("cos_sin"), py::arg("num_q_heads"), py::arg("num_kv_heads"),
+        py::arg("head_dim"), py::arg("rot_dim"), py::arg("neox"), py::arg("q_norm_w"), py::arg("k_norm_w"),
+        py::arg("norm_eps"), py::arg("k_cache"), py::arg("v_cache"), py::arg("slots"), py::arg("page_size"),
+        py::arg("k_scale"), py::arg("v_scale"), py::arg("status") = py::none());
   m.def("decode_attention", &decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_table"), py::arg("seq_lens"), py::arg("num_q_heads"), py::arg("num_kv_heads"),
         py::arg("head_dim"), py::arg("page_size"), py::arg("window"), py::arg("sm_scale"), py::arg("k_scale"),

@@ -24,7 +24,7 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
                                const T* __restrict__ k_norm_w, float norm_eps,
                                CacheT* __restrict__ k_cache, CacheT* __restrict__ v_cache,
                                const int64_t* __restrict__ slots, int page_size, float inv_k_scale,
-                               float inv_v_scale, int T_tokens) {
+                               float inv_v_scale, int T_tokens, int64_t num_pages, int* status) {
   snb::pdl_wait();
   snb::pdl_trigger();
   __shared__ float rowbuf[kWarps][256];
@@ -36,7 +36,13 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
   const int h = row % heads_per_tok;
   const int per = D / 32;
   float vals[8];
-  const int64_t slot = slots != nullptr ? slots[t] : -1;
+  int64_t slot = slots != nullptr ? slots[t] : -1;
+  if (slot >= 0 && slot / page_size >= num_pages) {
+    // a slot past the pool: recorded (SNB_ERR_BOUNDS, the slot in status[1]) and not written
+    if (status != nullptr && (threadIdx.x & 31) == 0 && atomicCAS(status, 0, SNB_ERR_BOUNDS) == 0)
+      status[1] = (int)(slot & 0x7fffffff);
+    slot = -1;
+  }
 
   if (h >= Hq + Hkv) {  // V row: copy into the cache only
     if (slot < 0 || v_cache == nullptr) return;
@@ -128,12 +134,14 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
 
 // q: [T, Hq*D] view, k/v: [T, Hkv*D] views (row strides arbitrary, unit inner stride).
 // k_cache/v_cache: [pages, Hkv, page_size, D] bf16 or float8_e4m3fn, or empty tensors to skip the write.
+// A slot whose page is past the pool is not written; it is recorded in `status` (SNB_ERR_BOUNDS, slot in [1]).
 void rope_qk_norm_kv_write(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor positions,
                            torch::Tensor cos_sin, int64_t num_q_heads, int64_t num_kv_heads,
                            int64_t head_dim, int64_t rot_dim, bool neox,
                            c10::optional<torch::Tensor> q_norm_w, c10::optional<torch::Tensor> k_norm_w,
                            double norm_eps, torch::Tensor k_cache, torch::Tensor v_cache,
-                           torch::Tensor slots, int64_t page_size, double k_scale, double v_scale) {
+                           torch::Tensor slots, int64_t page_size, double k_scale, double v_scale,
+                           c10::optional<torch::Tensor> status) {
   const int T = q.size(0);
   if (T == 0) return;
   TORCH_CHECK(q.stride(-1) == 1 && k.stride(-1) == 1 && v.stride(-1) == 1, "rope_kv: inner stride");
@@ -152,7 +160,8 @@ void rope_qk_norm_kv_write(torch::Tensor q, torch::Tensor k, torch::Tensor v, to
       cos_sin.data_ptr<float>(), q_norm_w ? (const T_*)q_norm_w->data_ptr() : nullptr,              \
       k_norm_w ? (const T_*)k_norm_w->data_ptr() : nullptr, (float)norm_eps,                        \
       write ? (C_*)k_cache.data_ptr() : nullptr, write ? (C_*)v_cache.data_ptr() : nullptr,         \
-      slots.data_ptr<int64_t>(), page_size, iks, ivs, T)
+      slots.data_ptr<int64_t>(), page_size, iks, ivs, T, write ? (int64_t)k_cache.size(0) : (int64_t)0,  \
+      status ? status->data_ptr<int>() : nullptr)
   if (q.scalar_type() == at::kBFloat16) {
     if (!write || k_cache.scalar_type() == at::kBFloat16) {
       SNB_ROPE_LAUNCH(__nv_bfloat16, __nv_bfloat16);

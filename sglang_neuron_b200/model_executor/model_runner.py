@@ -160,7 +160,8 @@ class KernelStatusWatch:
     def check(self) -> None:
         if bool(self.host.any()):
             codes = self.host.view(-1, 4)[:, 0].tolist()
-            raise RuntimeError(f"an sm_100a kernel reported a bounded-wait timeout (status codes {codes})")
+            raise RuntimeError(f"an sm_100a kernel reported an error status {codes} (1-4: a bounded wait ran out, "
+                               "5: an index past its buffer was skipped, 6: a static capacity was exceeded)")
 
 
 class ModelRunner:

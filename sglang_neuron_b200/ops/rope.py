@@ -5,6 +5,7 @@ from typing import Optional
 import torch
 
 from .._ext import kernels
+from .gemm import _status_buf
 
 
 def _yarn_find_correction_dim(num_rotations, dim, base, max_pos):
@@ -128,7 +129,7 @@ def rope_qk_norm_kv_write(q, k, v, positions, cos_sin, num_q_heads, num_kv_heads
             q, k, v, positions, cos_sin, num_q_heads, num_kv_heads, head_dim, rot_dim, neox, q_norm_w, k_norm_w,
             norm_eps, k_cache if k_cache is not None else empty, v_cache if v_cache is not None else empty,
             slots if slots is not None else torch.full((T,), -1, dtype=torch.long, device=q.device),
-            page_size, k_scale, v_scale)
+            page_size, k_scale, v_scale, status=_status_buf(q.device))
         return
     from .norm import rmsnorm_ref
     qv = q.reshape(T, num_q_heads, head_dim)

@@ -534,3 +534,29 @@ def test_topk_pool_radix_select(B, V, K, dt, ties):
     ref_v, ref_i = x[:, :V].float().sort(dim=-1, descending=True, stable=True)
     assert torch.equal(vals.cpu(), ref_v[:, :kk])
     assert torch.equal(ids.cpu(), ref_i[:, :kk] + 7)
+
+
+def test_rope_kv_write_skips_slot_past_pool_with_bounds_status():
+    """A KV slot whose page lies past the pool is not written: the kernel records SNB_ERR_BOUNDS (5) with the
+    slot, the other rows land normally. The check is always compiled in, so no fault is involved."""
+    from sglang_neuron_b200.ops.gemm import _status_buf
+    from sglang_neuron_b200.ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
+    T, Hq, Hkv, D, P, pages = 3, 4, 2, 64, 16, 4
+    q = torch.randn(T, Hq * D, device=DEV).to(torch.bfloat16)
+    k = torch.randn(T, Hkv * D, device=DEV).to(torch.bfloat16)
+    v = torch.randn(T, Hkv * D, device=DEV).to(torch.bfloat16)
+    kc = torch.zeros(pages + 1, Hkv, P, D, device=DEV, dtype=torch.bfloat16)  # one guard page past the pool
+    vc = torch.zeros_like(kc)
+    pos = torch.tensor([0, 1, 2], device=DEV)
+    cs = build_cos_sin_cache(D, 64, 10000.0, None, DEV)
+    slots = torch.tensor([5, pages * P + 3, 17], device=DEV)  # the middle slot is in the guard page
+    st = _status_buf(q.device)
+    st.zero_()
+    rope_qk_norm_kv_write(q, k, v, pos, cs, Hq, Hkv, D, D, True, k_cache=kc[:pages], v_cache=vc[:pages],
+                          slots=slots, page_size=P)
+    torch.cuda.synchronize()
+    code, where = int(st[0]), int(st[1])
+    st.zero_()
+    assert code == 5 and where == pages * P + 3
+    assert kc[pages].abs().sum().item() == 0 and vc[pages].abs().sum().item() == 0  # guard page untouched
+    assert vc[0, :, 5].abs().sum().item() > 0 and vc[1, :, 1].abs().sum().item() > 0  # the others landed
