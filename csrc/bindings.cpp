@@ -61,6 +61,7 @@ void gemm_bf16(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optiona
 void gemm_bf16_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, int64_t tiled_f, torch::Tensor status,
                        int64_t group_k, int64_t x_rows, int64_t x_stride, int64_t o_rows, int64_t o_stride);
 void set_pdl(bool on);
+void set_decode_fp8_variant(int64_t v);
 void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_table,
                 torch::Tensor seq_lens, torch::Tensor qo_indptr, int64_t max_extend, int64_t page_size,
                 double sm_scale, int64_t dcp_size, int64_t dcp_rank, c10::optional<torch::Tensor> lse_out);
@@ -161,6 +162,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status"), py::arg("residual") = py::none(), py::arg("weight") = py::none(), py::arg("eps") = 0.0,
         py::arg("wait_ns") = 0);
   m.def("set_pdl", &set_pdl);
+  m.def("set_decode_fp8_variant", &set_decode_fp8_variant, py::arg("variant"));
   m.def("mla_decode", &mla_decode);
   m.def("mla_extend", &mla_extend, py::arg("out"), py::arg("q"), py::arg("cache"), py::arg("block_table"),
         py::arg("seq_lens"), py::arg("qo_indptr"), py::arg("max_extend"), py::arg("page_size"), py::arg("sm_scale"),

@@ -52,10 +52,33 @@ SNB_DEVICE void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// two e4m3 bytes (low byte -> low half) -> f16x2
-SNB_DEVICE uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two_bytes & 0xffffu), __NV_E4M3);
-  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+// e4m3 byte pairs -> f16x2 (lower byte -> lower half): bytes 0-1 or bytes 2-3 of a 32-bit word, one cvt each
+SNB_DEVICE uint32_t e4m3x2_to_f16x2(uint32_t w) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\t}" : "=r"(r) : "r"(w));
+  return r;
+}
+
+SNB_DEVICE uint32_t e4m3x2_hi_to_f16x2(uint32_t w) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, h;\n\t}" : "=r"(r) : "r"(w));
+  return r;
+}
+
+// 2^x on the special-function unit (inputs here are <= 0 or -inf; -inf gives +0)
+SNB_DEVICE float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// 16-byte global -> shared copy (L2 only), and an arrival on `bar` once this thread's copies have landed
+SNB_DEVICE void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+SNB_DEVICE void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(snb::smem_u32(bar)) : "memory");
 }
 
 SNB_DEVICE uint32_t f32x2_to_f16x2(float lo, float hi) {
@@ -68,6 +91,84 @@ SNB_DEVICE void bulk_load_nohint(uint32_t dst, const void* src, uint32_t bytes, 
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
+}
+
+// CTA epilogue shared by both FP8 kernels: combine the compute warps' (max, sum, O) over shared memory and write
+// the output rows (one split) or this split's normalised partial and log2-sum-exp; the producer lane waits
+// (bounded) for copies a stopped CTA still has in flight; with merge counters the last split CTA of a
+// (request, KV head) merges every split. red_m / red_l are [warp][16 heads], obuf is fp32 [warp][16 heads][D].
+template <int D>
+SNB_DEVICE void decode_fp8_finish(int warp, int tid, int lane, int b, int hk, int split, int Hkv, int G,
+                                  int num_splits, const float* __restrict__ sinks, float v_scale,
+                                  __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part,
+                                  float* __restrict__ lse_part, const float* red_m, const float* red_l,
+                                  const float* obuf, int* sh, uint64_t* full, int nst, int* status,
+                                  int* __restrict__ merge_cnt, float v_scale_out) {
+  if (warp < kCWarps) {
+    const int Hq = Hkv * G;
+    for (int idx = tid; idx < G * D; idx += kCWarps * 32) {
+      const int g = idx / D, d = idx % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) M = fmaxf(M, red_m[w * 16 + g]);
+      float L = 0.f, acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) {
+        if (red_m[w * 16 + g] == -INFINITY) continue;
+        const float f = exp2f(red_m[w * 16 + g] - M);
+        L += red_l[w * 16 + g] * f;
+        acc += obuf[(w * 16 + g) * D + d] * f;
+      }
+      const int h = hk * G + g;
+      if (num_splits == 1) {
+        float denom = L;
+        if (sinks != nullptr) denom = (M == -INFINITY) ? 1.f : L + exp2f(sinks[h] * kL2e - M);
+        out[(size_t)b * out_stride + (size_t)h * D + d] =
+            __float2bfloat16(denom > 0.f ? acc / denom * v_scale : 0.f);
+      } else {
+        const size_t pidx = ((size_t)b * Hq + h) * num_splits + split;
+        o_part[pidx * D + d] = L > 0.f ? acc / L : 0.f;
+        if (d == 0) lse_part[pidx] = L > 0.f ? M + log2f(L) : -INFINITY;
+      }
+    }
+  } else if (lane == 0) {
+    // a CTA that stopped early still waits (bounded) for the copies it issued before its memory goes away
+    for (int i = sh[1]; i < sh[0]; ++i)
+      if (!snb::mbar_wait_bounded(&full[i % nst], (i / nst) & 1, status, SNB_ERR_TIMEOUT_TMA)) break;
+  }
+  if (num_splits > 1 && merge_cnt != nullptr) {
+    // Split merge in this launch: the last split CTA of (request, KV head) to finish combines every split's
+    // normalised partial (log2-sum-exp weights, sinks in the denominator) and writes the output rows; it
+    // then re-arms the counter for the next call. Partials are read past L1 (written by other CTAs).
+    __threadfence();
+    __syncthreads();
+    int* cnt = merge_cnt + (size_t)b * Hkv + hk;
+    if (tid == 0) sh[3] = atomicAdd(cnt, 1) == num_splits - 1;
+    __syncthreads();
+    if (sh[3]) {
+      __threadfence();
+      const int Hq = Hkv * G;
+      for (int idx = tid; idx < G * D; idx += kThreads) {
+        const int g = idx / D, d = idx % D, h = hk * G + g;
+        const size_t base = ((size_t)b * Hq + h) * num_splits;
+        float M = -INFINITY;
+        for (int s = 0; s < num_splits; ++s) M = fmaxf(M, __ldcg(lse_part + base + s));
+        const float sk = sinks != nullptr ? sinks[h] * kL2e : -INFINITY;
+        const float Mx = fmaxf(M, sk);
+        float total = (sk == -INFINITY) ? 0.f : exp2f(sk - Mx), acc = 0.f;
+        for (int s = 0; s < num_splits; ++s) {
+          const float l = __ldcg(lse_part + base + s);
+          if (l == -INFINITY) continue;
+          const float f = exp2f(l - Mx);
+          total += f;
+          acc += f * __ldcg(o_part + (base + s) * D + d);
+        }
+        const float r = (M == -INFINITY || total <= 0.f) ? 0.f : acc / total * v_scale_out;
+        out[(size_t)b * out_stride + (size_t)h * D + d] = __float2bfloat16(r);
+      }
+      if (tid == 0) *cnt = 0;
+    }
+  }
 }
 
 template <int D>
@@ -224,7 +325,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_kernel(
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t w4 = kw[nt][ks];
-          mma_f16_16816(sc[nt], qa[ks], e4m3x2_to_f16x2(w4), e4m3x2_to_f16x2(w4 >> 16));
+          mma_f16_16816(sc[nt], qa[ks], e4m3x2_to_f16x2(w4), e4m3x2_hi_to_f16x2(w4));
         }
       }
       // ---- online softmax over rows gq / gq + 8; column j of n-tile nt is token (j>>1) + 4*(2nt + (j&1))
@@ -307,75 +408,382 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_kernel(
     }
   }
   __syncthreads();
-  if (warp < kCWarps) {
-    const int Hq = Hkv * G;
-    const float* obuf = reinterpret_cast<const float*>(ring);
-    for (int idx = tid; idx < G * D; idx += kCWarps * 32) {
-      const int g = idx / D, d = idx % D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kCWarps; ++w) M = fmaxf(M, red_m[w * 16 + g]);
-      float L = 0.f, acc = 0.f;
-#pragma unroll
-      for (int w = 0; w < kCWarps; ++w) {
-        if (red_m[w * 16 + g] == -INFINITY) continue;
-        const float f = exp2f(red_m[w * 16 + g] - M);
-        L += red_l[w * 16 + g] * f;
-        acc += obuf[(w * 16 + g) * D + d] * f;
-      }
-      const int h = hk * G + g;
-      if (num_splits == 1) {
-        float denom = L;
-        if (sinks != nullptr) denom = (M == -INFINITY) ? 1.f : L + exp2f(sinks[h] * kL2e - M);
-        out[(size_t)b * out_stride + (size_t)h * D + d] =
-            __float2bfloat16(denom > 0.f ? acc / denom * v_scale : 0.f);
+  decode_fp8_finish<D>(warp, tid, lane, b, hk, split, Hkv, G, num_splits, sinks, v_scale, out, out_stride, o_part,
+                       lse_part, red_m, red_l, reinterpret_cast<const float*>(ring), sh, full, C::NST, status,
+                       merge_cnt, v_scale_out);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Token-major variant: S^T = K Q^T and O^T = V^T P^T, so the MMA's M dimension is tokens (S^T) and head dims
+// (O^T) and its N dimension is the G query heads (8 per n-tile, NG n-tiles). No MMA row is padding for
+// G = 8, a thread holds four scores of two heads per 16 tokens (the row-sum stays a per-thread partial until the
+// end), the scale is folded into Q, and O is rescaled only when some running max moved. P^T leaves the
+// accumulator layout as the B operand of the second MMA through one `movmatrix.trans` per 8x8 block.
+// CTA = one (split, KV head, request); 4 compute warps take 32 tokens each of a 128-token stage.
+//
+// Index maps (all bijections, chosen so every shared-memory fetch is a contiguous 8/16-byte load):
+//   * contraction index of S^T (head dim): step ks, column kk = 2qq + e + 8h -> dim qq*(D/4) + 4ks + 2h + e;
+//   * row r = r3 r2 r1 r0 (bits) of a 16-token block -> token 8r3 + 4r0 + 2r2 + r1, so the k-rows a thread
+//     owns in O^T = V^T P^T (2qd, 2qd+1, 2qd+8, 2qd+9) are tokens qd, qd+4, qd+8, qd+12;
+//   * O^T row (m-tile mt, row 8h + g) -> head dim g*(D/8) + 2mt + h.
+template <int D, int NG>
+struct Fp8TokCfg {
+  static constexpr int TILE = 128;                      // tokens per stage
+  static constexpr int NST = D == 64 ? 3 : 2;           // ring stages
+  static constexpr int STAGE = 2 * TILE * D;            // K tile then V tile, fp8
+  static constexpr int MERGE = kCWarps * 16 * D * 4;    // fp32 [warp][16 heads][D], reuses the ring
+  static constexpr int RING = NST * STAGE > MERGE ? NST * STAGE : MERGE;
+  static constexpr int SMEM = RING + 2 * NST * 8 + kCWarps * 16 * 2 * 4 + 64 + kMaxSplitPages * 4;
+};
+
+SNB_DEVICE uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+
+SNB_DEVICE int tok_of_row(int r) {  // row r of a 16-token block -> token offset
+  return ((r >> 3) & 1) * 8 + (r & 1) * 4 + ((r >> 2) & 1) * 2 + ((r >> 1) & 1);
+}
+
+template <int D, int NG, bool BULK>
+__global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
+    const __nv_bfloat16* __restrict__ q, int q_stride, const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
+    const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ seq_lens, int page_size,
+    int Hkv, int G, int window, float scale_log2, float v_scale, const float* __restrict__ sinks,
+    __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part, float* __restrict__ lse_part,
+    int num_splits, int* status, int* __restrict__ merge_cnt, float v_scale_out) {
+  using C = Fp8TokCfg<D, NG>;
+  constexpr int TILE = C::TILE;
+  constexpr int KS = D / 16;     // contraction steps of S^T = m-tiles of O^T
+  constexpr int KB = D / 4;      // K bytes per thread per token row
+  constexpr int VB = D / 8;      // V bytes per thread per token row
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING);
+  uint64_t* empty = full + C::NST;
+  float* red_m = reinterpret_cast<float*>(empty + C::NST);  // [warp][16 heads]
+  float* red_l = red_m + kCWarps * 16;
+  int* sh = reinterpret_cast<int*>(red_l + kCWarps * 16);   // [0] issued, [1] consumed, [3] merge flag
+  int32_t* sbt = sh + 16;                                    // this split's block-table entries
+
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < C::NST; ++s) {
+      snb::mbar_init(&full[s], BULK ? 1 : 32);  // bulk: one expect-tx arrival; cp.async: one per producer lane
+      snb::mbar_init(&empty[s], kCWarps);
+    }
+    sh[0] = sh[1] = sh[2] = 0;
+    snb::fence_mbar_init();
+  }
+  __syncthreads();
+  snb::pdl_wait();
+  snb::pdl_trigger();
+
+  const int ctx = seq_lens[b];
+  const int lo = (window > 0 && ctx > window) ? ctx - window : 0;  // first attended token
+  const int base = (lo / TILE) * TILE;
+  const int per = ((ctx - base + num_splits - 1) / num_splits + TILE - 1) / TILE * TILE;
+  const int s0 = base + split * per;
+  const int s1 = min(ctx, s0 + per);
+  const int ntiles = s0 < s1 ? (s1 - s0 + TILE - 1) / TILE : 0;
+  const int32_t* bt = block_table + (size_t)b * bt_stride;
+  const int seg = page_size < TILE ? page_size : TILE;  // tokens per bulk copy
+  const int pg0 = s0 / page_size;
+  const int npg = s0 < s1 ? (s1 - 1) / page_size - pg0 + 1 : 0;
+  for (int i = tid; i < min(npg, kMaxSplitPages); i += kThreads) sbt[i] = bt[pg0 + i];
+  __syncthreads();
+
+  if (warp == kCWarps) {
+    // ---------------- producer: whole page segments of K and V into the ring, either as bulk copies (one
+    // segment per lane, completion counted in bytes on the stage barrier) or as 16-byte cp.async by all 32
+    // lanes (each lane arrives on the stage barrier once its copies have landed). Addressing is division-free
+    // for pages of at most one stage: s0 is a multiple of the stage and the stage a multiple of the page.
+    const int nseg = TILE / seg;
+    const size_t pstride = (size_t)Hkv * page_size * D, hoff = (size_t)hk * page_size * D;
+    auto seg_offset = [&](int k, int i) -> size_t {  // byte offset of segment i of stage k in the cache
+      int pi, inpage = 0;
+      if (page_size <= TILE) {
+        pi = k * nseg + i;
       } else {
-        const size_t pidx = ((size_t)b * Hq + h) * num_splits + split;
-        o_part[pidx * D + d] = L > 0.f ? acc / L : 0.f;
-        if (d == 0) lse_part[pidx] = L > 0.f ? M + log2f(L) : -INFINITY;
+        const int ta = s0 + k * TILE;
+        pi = ta / page_size - pg0;
+        inpage = ta - (pg0 + pi) * page_size;
       }
-    }
-  } else if (lane == 0) {
-    // a CTA that stopped early still waits (bounded) for the copies it issued before its memory goes away
-    for (int i = sh[1]; i < sh[0]; ++i)
-      if (!snb::mbar_wait_bounded(&full[i % C::NST], (i / C::NST) & 1, status, SNB_ERR_TIMEOUT_TMA)) break;
-  }
-  if (num_splits > 1 && merge_cnt != nullptr) {
-    // Split merge in this launch: the last split CTA of (request, KV head) to finish combines every split's
-    // normalised partial (log2-sum-exp weights, sinks in the denominator) and writes the output rows; it
-    // then re-arms the counter for the next call. Partials are read past L1 (written by other CTAs).
-    __threadfence();
-    __syncthreads();
-    int* cnt = merge_cnt + (size_t)b * Hkv + hk;
-    if (tid == 0) sh[3] = atomicAdd(cnt, 1) == num_splits - 1;
-    __syncthreads();
-    if (sh[3]) {
-      __threadfence();
-      const int Hq = Hkv * G;
-      for (int idx = tid; idx < G * D; idx += kThreads) {
-        const int g = idx / D, d = idx % D, h = hk * G + g;
-        const size_t base = ((size_t)b * Hq + h) * num_splits;
-        float M = -INFINITY;
-        for (int s = 0; s < num_splits; ++s) M = fmaxf(M, __ldcg(lse_part + base + s));
-        const float sk = sinks != nullptr ? sinks[h] * kL2e : -INFINITY;
-        const float Mx = fmaxf(M, sk);
-        float total = (sk == -INFINITY) ? 0.f : exp2f(sk - Mx), acc = 0.f;
-        for (int s = 0; s < num_splits; ++s) {
-          const float l = __ldcg(lse_part + base + s);
-          if (l == -INFINITY) continue;
-          const float f = exp2f(l - Mx);
-          total += f;
-          acc += f * __ldcg(o_part + (base + s) * D + d);
+      const int32_t page = pi < kMaxSplitPages ? sbt[pi] : bt[pg0 + pi];
+      return (size_t)page * pstride + hoff + (size_t)inpage * D;
+    };
+    int k = 0;
+    for (; k < ntiles; ++k) {
+      const int s = k % C::NST;
+      bool ok = true;
+      if (k >= C::NST) {
+        if (lane == 0) ok = snb::mbar_wait_bounded(&empty[s], ((k / C::NST) & 1) ^ 1, status, SNB_ERR_TIMEOUT_TMA);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+      if (!ok) break;
+      const int t0 = s0 + k * TILE;
+      const uint32_t kd = snb::smem_u32(ring + s * C::STAGE), vd = kd + TILE * D;
+      if constexpr (BULK) {
+        const int ta = t0 + lane * seg;
+        const bool valid = lane < nseg && ta + seg > lo && ta < s1;
+        const uint32_t nvalid = __popc(__ballot_sync(0xffffffffu, valid));
+        if (lane == 0) snb::mbar_arrive_expect_tx(&full[s], nvalid * 2u * seg * D);
+        __syncwarp();
+        if (valid) {
+          const size_t off = seg_offset(k, lane);
+          bulk_load_nohint(kd + lane * seg * D, kc + off, seg * D, snb::smem_u32(&full[s]));
+          bulk_load_nohint(vd + lane * seg * D, vc + off, seg * D, snb::smem_u32(&full[s]));
         }
-        const float r = (M == -INFINITY || total <= 0.f) ? 0.f : acc / total * v_scale_out;
-        out[(size_t)b * out_stride + (size_t)h * D + d] = __float2bfloat16(r);
+      } else {
+        for (int i = 0; i < nseg; ++i) {
+          const int ta = t0 + i * seg;
+          if (!(ta + seg > lo && ta < s1)) continue;
+          const size_t off = seg_offset(k, i);
+          for (int c = lane * 16; c < seg * D; c += 32 * 16) {
+            cp_async16(kd + i * seg * D + c, kc + off + c);
+            cp_async16(vd + i * seg * D + c, vc + off + c);
+          }
+        }
+        cp_async_arrive_noinc(&full[s]);
       }
-      if (tid == 0) *cnt = 0;
     }
+    if (lane == 0) sh[0] = k;
+    if constexpr (!BULK) asm volatile("cp.async.wait_all;" ::: "memory");
+  } else {
+    // ---------------- compute warps
+    const int gq = lane >> 2, qd = lane & 3;
+    // Q^T fragments (B operand of S^T): head ng*8 + gq, dims qd*KB + 4ks + {0,1} and {2,3}, pre-scaled by
+    // scale * log2(e) (f16 keeps 11 mantissa bits, more than the bf16 input has)
+    uint32_t qb[NG][KS][2];
+    {
+      const __nv_bfloat16* qh = q + (size_t)b * q_stride + (size_t)hk * G * D;
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng) {
+        const int h = ng * 8 + gq;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            if (h < G) {
+              const __nv_bfloat162 v =
+                  *reinterpret_cast<const __nv_bfloat162*>(qh + (size_t)h * D + qd * KB + ks * 4 + e * 2);
+              qb[ng][ks][e] = f32x2_to_f16x2(__bfloat162float(v.x) * scale_log2, __bfloat162float(v.y) * scale_log2);
+            } else {
+              qb[ng][ks][e] = 0u;
+            }
+          }
+        }
+      }
+    }
+    float o[KS][NG][4];
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng) o[mt][ng][0] = o[mt][ng][1] = o[mt][ng][2] = o[mt][ng][3] = 0.f;
+    // running max per head column (2qd, 2qd+1 of each n-tile; equal across the 8 lanes of a column) and the
+    // thread's partial row sums (reduced over those lanes at the end)
+    float m_r[NG][2], l_r[NG][2];
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng) m_r[ng][0] = m_r[ng][1] = -INFINITY, l_r[ng][0] = l_r[ng][1] = 0.f;
+    const int krow0 = tok_of_row(gq), krow1 = krow0 + 8;  // tokens of S^T rows gq, gq + 8
+    int k = 0;
+    for (; k < ntiles; ++k) {
+      const int s = k % C::NST;
+      if (!snb::mbar_wait_bounded(&full[s], (k / C::NST) & 1, status, SNB_ERR_TIMEOUT_MMA)) {
+        sh[2] = 1;
+        break;
+      }
+      const uint8_t* kt = ring + s * C::STAGE + warp * 32 * D;
+      const uint8_t* vt = ring + s * C::STAGE + TILE * D + warp * 32 * D;
+      const int tw = s0 + k * TILE + warp * 32;  // first token of this warp's 32
+      const bool whole = tw >= lo && tw + 32 <= s1;
+      // K rows krow0 / krow1 of both 16-token blocks: KB bytes at qd*KB
+      uint32_t kw[2][2][KB / 4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int i = 0; i < KB / 16; ++i) {
+            const uint4 a = *reinterpret_cast<const uint4*>(kt + (u * 16 + (r ? krow1 : krow0)) * D + qd * KB + i * 16);
+            kw[u][r][i * 4] = a.x;
+            kw[u][r][i * 4 + 1] = a.y;
+            kw[u][r][i * 4 + 2] = a.z;
+            kw[u][r][i * 4 + 3] = a.w;
+          }
+      // V rows qd + 4i of both blocks: VB bytes at gq*VB; tokens outside [lo, s1) zeroed (stale page bytes)
+      uint32_t vw[2][4][VB / 4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = u * 16 + qd + 4 * i;
+          const uint8_t* src = vt + row * D + gq * VB;
+          const bool ok = whole || (tw + row >= lo && tw + row < s1);
+          if constexpr (VB == 8) {
+            const uint2 v = *reinterpret_cast<const uint2*>(src);
+            vw[u][i][0] = ok ? v.x : 0u;
+            vw[u][i][1] = ok ? v.y : 0u;
+          } else {
+            const uint4 v = *reinterpret_cast<const uint4*>(src);
+            vw[u][i][0] = ok ? v.x : 0u;
+            vw[u][i][1] = ok ? v.y : 0u;
+            vw[u][i][2] = ok ? v.z : 0u;
+            vw[u][i][3] = ok ? v.w : 0u;
+          }
+        }
+      __syncwarp();
+      if (lane == 0) snb::mbar_arrive(&empty[s]);  // this warp's bytes of the stage are in registers
+      // ---- S^T = K Q^T: sc[u][ng] rows (krow0, krow1) x heads (2qd, 2qd+1), already in log2 units
+      float sc[2][NG][4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) {
+          sc[u][ng][0] = sc[u][ng][1] = sc[u][ng][2] = sc[u][ng][3] = 0.f;
+#pragma unroll
+          for (int ks = 0; ks < KS; ++ks) {
+            const uint32_t w0 = kw[u][0][ks], w1 = kw[u][1][ks];
+            const uint32_t a[4] = {e4m3x2_to_f16x2(w0), e4m3x2_to_f16x2(w1), e4m3x2_hi_to_f16x2(w0),
+                                   e4m3x2_hi_to_f16x2(w1)};
+            mma_f16_16816(sc[u][ng], a, qb[ng][ks][0], qb[ng][ks][1]);
+          }
+        }
+      if (!whole) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int t0 = tw + u * 16 + krow0, t1 = t0 + 8;
+          const bool ok0 = t0 >= lo && t0 < s1, ok1 = t1 >= lo && t1 < s1;
+#pragma unroll
+          for (int ng = 0; ng < NG; ++ng) {
+            if (!ok0) sc[u][ng][0] = sc[u][ng][1] = -INFINITY;
+            if (!ok1) sc[u][ng][2] = sc[u][ng][3] = -INFINITY;
+          }
+        }
+      }
+      // ---- online softmax per head column over the warp's 32 tokens
+      bool moved = false;
+      float alpha[NG][2];
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float mx = fmaxf(fmaxf(sc[0][ng][j], sc[0][ng][2 + j]), fmaxf(sc[1][ng][j], sc[1][ng][2 + j]));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mn = fmaxf(m_r[ng][j], mx);
+          alpha[ng][j] = (mn == m_r[ng][j]) ? 1.f : ex2_approx(m_r[ng][j] - mn);
+          moved |= mn != m_r[ng][j];
+          m_r[ng][j] = mn;
+          l_r[ng][j] *= alpha[ng][j];
+        }
+      // P^T as the B operand of O^T = V^T P^T: pack a row's two head columns, transpose each 8x8 block
+      uint32_t pb[2][NG][2];
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng) {
+        const float r0 = m_r[ng][0] == -INFINITY ? 0.f : m_r[ng][0];
+        const float r1 = m_r[ng][1] == -INFINITY ? 0.f : m_r[ng][1];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float p0 = ex2_approx(sc[u][ng][0] - r0), p1 = ex2_approx(sc[u][ng][1] - r1);
+          const float p2 = ex2_approx(sc[u][ng][2] - r0), p3 = ex2_approx(sc[u][ng][3] - r1);
+          l_r[ng][0] += p0 + p2;
+          l_r[ng][1] += p1 + p3;
+          pb[u][ng][0] = movmatrix_trans(f32x2_to_f16x2(p0, p1));
+          pb[u][ng][1] = movmatrix_trans(f32x2_to_f16x2(p2, p3));
+        }
+      }
+      if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+          for (int ng = 0; ng < NG; ++ng) {
+            o[mt][ng][0] *= alpha[ng][0];
+            o[mt][ng][1] *= alpha[ng][1];
+            o[mt][ng][2] *= alpha[ng][0];
+            o[mt][ng][3] *= alpha[ng][1];
+          }
+      }
+      // ---- O^T += V^T P^T: A rows are head dims (byte 2mt + h of the thread's V slice), k = tokens
+      // qd, qd+4 | qd+8, qd+12 of each 16-token block; one byte permute gathers both dims of a token pair
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        const int w = mt >> 1;
+        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint32_t p01 = __byte_perm(vw[u][0][w], vw[u][1][w], sel);
+          const uint32_t p23 = __byte_perm(vw[u][2][w], vw[u][3][w], sel);
+          const uint32_t a[4] = {e4m3x2_to_f16x2(p01), e4m3x2_hi_to_f16x2(p01), e4m3x2_to_f16x2(p23),
+                                 e4m3x2_hi_to_f16x2(p23)};
+#pragma unroll
+          for (int ng = 0; ng < NG; ++ng) mma_f16_16816(o[mt][ng], a, pb[u][ng][0], pb[u][ng][1]);
+        }
+      }
+    }
+    if (warp == 0 && lane == 0) sh[1] = k;
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        l_r[ng][j] += __shfl_xor_sync(0xffffffffu, l_r[ng][j], 4);
+        l_r[ng][j] += __shfl_xor_sync(0xffffffffu, l_r[ng][j], 8);
+        l_r[ng][j] += __shfl_xor_sync(0xffffffffu, l_r[ng][j], 16);
+      }
+    // ---- per-warp state to shared memory for the merge (after every compute warp left the ring)
+    __syncwarp();
+    asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+    float* obuf = reinterpret_cast<float*>(ring);
+    if (gq == 0) {
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          red_m[warp * 16 + ng * 8 + 2 * qd + j] = m_r[ng][j];
+          red_l[warp * 16 + ng * 8 + 2 * qd + j] = l_r[ng][j];
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = ng * 8 + 2 * qd + (e & 1), d = gq * VB + 2 * mt + (e >> 1);
+          obuf[(warp * 16 + h) * D + d] = o[mt][ng][e];
+        }
   }
+  __syncthreads();
+  decode_fp8_finish<D>(warp, tid, lane, b, hk, split, Hkv, G, num_splits, sinks, v_scale, out, out_stride, o_part,
+                       lse_part, red_m, red_l, reinterpret_cast<const float*>(ring), sh, full, C::NST, status,
+                       merge_cnt, v_scale_out);
 }
 
 }  // namespace
+
+// Opt a kernel into its dynamic shared memory once (one static per kernel) and return the size.
+template <typename Cfg, auto Kern>
+static int fp8_smem_attr() {
+  static bool done = false;
+  if (!done) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    done = true;
+  }
+  return Cfg::SMEM;
+}
+
+// Which FP8 kernel serves a call: 1 (default) the token-major kernel fed by bulk copies, 2 the token-major kernel
+// fed by 16-byte cp.async, 0 the head-major kernel (variants 1 and 2 fall back to it for page sizes that do not
+// tile 128 tokens). Tests and the attention microbenchmark compare them.
+static int g_fp8_decode_variant = 1;
+
+void set_decode_fp8_variant(int64_t v) {
+  TORCH_CHECK(v >= 0 && v <= 2, "set_decode_fp8_variant: 0 (head-major), 1 or 2 (token-major)");
+  g_fp8_decode_variant = (int)v;
+}
 
 // Same contract as decode_attention_mma() for an fp8 cache; false when not covered (head_dim not 64/128, G > 16,
 // or a page size that is neither a divisor nor a multiple of the 64-token tile). With merge_cnt (zeroed int32
@@ -395,25 +803,35 @@ bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
   const int B = q.size(0);
   auto st = at::cuda::getCurrentCUDAStream();
   dim3 grid(num_splits, num_kv_heads, B);
-#define SNB_FP8(DD)                                                                                              \
-  {                                                                                                              \
-    using C = Fp8Cfg<DD>;                                                                                        \
-    static bool attr = false;                                                                                    \
-    if (!attr) {                                                                                                 \
-      C10_CUDA_CHECK(cudaFuncSetAttribute(decode_attn_fp8_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                          C::SMEM));                                                             \
-      attr = true;                                                                                               \
-    }                                                                                                            \
-    C10_CUDA_CHECK(snb::launch_pdl(decode_attn_fp8_kernel<DD>, grid, kThreads, C::SMEM, st,                      \
-                                   (const __nv_bfloat16*)q.data_ptr(), (int)q.stride(0),                         \
-                                   (const uint8_t*)k_cache.data_ptr(), (const uint8_t*)v_cache.data_ptr(),       \
-                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0),                 \
-                                   seq_lens.data_ptr<int32_t>(), (int)page_size, (int)num_kv_heads, G,           \
-                                   (int)window, scale_log2, v_scale_final, sinks, (__nv_bfloat16*)out.data_ptr(), \
-                                   (int)out.stride(0), o_part, lse_part, (int)num_splits, status, merge_cnt,     \
-                                   v_scale_out));                                                                \
+  constexpr int kTok = Fp8TokCfg<64, 1>::TILE;
+  const bool tok = g_fp8_decode_variant != 0 &&
+                   ((page_size >= 16 && kTok % page_size == 0) || (page_size >= kTok && page_size % kTok == 0));
+  auto launch = [&](auto kernel, int smem) {
+    C10_CUDA_CHECK(snb::launch_pdl(kernel, grid, kThreads, smem, st, (const __nv_bfloat16*)q.data_ptr(),
+                                   (int)q.stride(0), (const uint8_t*)k_cache.data_ptr(),
+                                   (const uint8_t*)v_cache.data_ptr(), block_table.data_ptr<int32_t>(),
+                                   (int)block_table.stride(0), seq_lens.data_ptr<int32_t>(), (int)page_size,
+                                   (int)num_kv_heads, G, (int)window, scale_log2, v_scale_final, sinks,
+                                   (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), o_part, lse_part,
+                                   (int)num_splits, status, merge_cnt, v_scale_out));
+  };
+  const bool bulk = g_fp8_decode_variant == 1;
+#define SNB_TOK(DD, NGG, BB) launch(decode_attn_fp8_tok_kernel<DD, NGG, BB>, \
+                                    fp8_smem_attr<Fp8TokCfg<DD, NGG>, decode_attn_fp8_tok_kernel<DD, NGG, BB>>())
+  if (tok) {
+    const int ng = G <= 8 ? 1 : 2;
+    if (head_dim == 64) {
+      if (ng == 1) { if (bulk) SNB_TOK(64, 1, true); else SNB_TOK(64, 1, false); }
+      else { if (bulk) SNB_TOK(64, 2, true); else SNB_TOK(64, 2, false); }
+    } else {
+      if (ng == 1) { if (bulk) SNB_TOK(128, 1, true); else SNB_TOK(128, 1, false); }
+      else { if (bulk) SNB_TOK(128, 2, true); else SNB_TOK(128, 2, false); }
+    }
+  } else if (head_dim == 64) {
+    launch(decode_attn_fp8_kernel<64>, fp8_smem_attr<Fp8Cfg<64>, decode_attn_fp8_kernel<64>>());
+  } else {
+    launch(decode_attn_fp8_kernel<128>, fp8_smem_attr<Fp8Cfg<128>, decode_attn_fp8_kernel<128>>());
   }
-  if (head_dim == 64) SNB_FP8(64) else SNB_FP8(128)
-#undef SNB_FP8
+#undef SNB_TOK
   return true;
 }

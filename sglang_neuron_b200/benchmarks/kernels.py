@@ -221,7 +221,7 @@ def bench_gemm(a):
 
 def bench_attn(a):
     from ..ops.attention import DecodeScratch, decode_attention, default_num_splits
-    B, L, P, Hq, Hkv, D = a.batch, a.ctx, 16, 64, 8, 64
+    B, L, P, Hq, Hkv, D = a.batch, a.ctx, a.page, a.hq, a.hkv, 64
     pages_per = (L + P - 1) // P
     n_pages = B * pages_per + 1
     kc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(torch.float8_e4m3fn)
@@ -232,9 +232,13 @@ def bench_attn(a):
     sinks = torch.randn(Hq, device="cuda")
     S = a.splits or default_num_splits(B, Hkv, L)
     sc = DecodeScratch(B, Hq, D, S, "cuda")
+    from .._ext import kernels
+    kernels().set_decode_fp8_variant(a.variant)
     us = timeit(lambda: decode_attention(q, kc, vc, bt, seq, Hq, Hkv, D, P, 0, None, 1.0, 1.0, sinks, S, sc),
                 a.iters, a.warmup)
     res = {"kernel": "decode_attention (paged GQA, fp8 KV, sinks)", "batch": B, "ctx": L, "splits": S,
+           "heads": f"{Hq}/{Hkv}", "page": P,
+           "variant": ["head-major", "token-major bulk", "token-major cp.async"][a.variant],
            "us_single_cold": round(us, 2)}
     if a.iters > 1:  # back to back in a CUDA graph over KV copies that together exceed L2
         n = max(2, (512 << 20) // (2 * kc.numel()) + 1)
@@ -262,6 +266,10 @@ def main():
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=1536)
     p.add_argument("--splits", type=int, default=0)
+    p.add_argument("--hq", type=int, default=64)
+    p.add_argument("--hkv", type=int, default=8)
+    p.add_argument("--page", type=int, default=16)
+    p.add_argument("--variant", type=int, default=1, help="attn: FP8 kernel, 0 head-major, 1 token-major (bulk copies), 2 token-major (cp.async)")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     a = p.parse_args()

@@ -84,8 +84,8 @@ def extend_attention_ref(q, k_cache, v_cache, block_table, qo_indptr, kv_lens, n
 
 def default_num_splits(batch: int, num_kv_heads: int, max_ctx: int, num_sms: int = 148) -> int:
     """Flash-decoding split count: as many context splits as keep (batch x kv heads x splits) CTAs within one
-    resident wave (4 CTAs per SM), at least 128 tokens per split. Measured at 64 x 8 x 1536 (fp8 KV): one
-    split 54.9 us, two 60.8 us, four 67.7 us, eight 81.1 us: beyond one wave the extra CTAs and the merge cost
+    resident wave (4 CTAs per SM), at least 128 tokens per split. Measured at 64 x 8 x 1536 (fp8 KV, token-major
+    kernel, in a CUDA graph): one split 23.5 us, two 41.9 us: beyond one wave the extra CTAs and the merge cost
     more than they hide."""
     ctas = max(1, batch * num_kv_heads)
     want = max(1, (4 * num_sms) // ctas)
