@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
   (void)total;
 }
 
-// One warp per permuted row; each lane quantises whole 32-element blocks.
+// One thread per (permuted row, 32-element block): consecutive threads take consecutive blocks of a row, so a
+// row's loads and stores coalesce and every block of a decode batch is in flight at once.
 // x: [T, H] bf16 (row stride xs). Output q: [R, Kp] e4m3 (Kp = padded row pitch), scales in atom order.
 // `used` (optional, device): the number of rows the expert segments actually occupy (seg_offsets[E_local]);
 // rows past it belong to no tile the grouped GEMM runs, so they are skipped. The grid stays sized for the
@@ -182,7 +183,10 @@ __global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, i
                                           const int32_t* __restrict__ skip) {
   snb::pdl_wait();
   snb::pdl_trigger();
-  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int KB = (Kp + 127) / 128;           // 128-wide K blocks
+  const int nblk = KB * 4;                    // 32-wide scale blocks incl. padding
+  const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = (int)(item / nblk), blk = (int)(item % nblk);
   if (r >= R || (used != nullptr && r >= *used)) return;
   if (skip != nullptr && skip[r] < 0) return;  // a padding row of the permutation (see below)
   const int s = src != nullptr ? src[r] : r;
@@ -190,56 +194,66 @@ __global__ void gather_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, i
   // activation row n and its scales, and the combine never reads a padding row, so whatever they hold only
   // ever reaches outputs nobody reads. (At decode most rows are padding: 16-row tiles for 1-3 tokens.)
   if (s < 0) return;
-  const int KB = (Kp + 127) / 128;           // 128-wide K blocks
-  const int nblk = KB * 4;                    // 32-wide scale blocks incl. padding
   const int chunk_bytes = min(BN, 32) * 16;
   const int tile = r / BN, i = r % BN;
   uint8_t* qrow = q + (size_t)r * Kp;
-  for (int blk = lane; blk < nblk; blk += 32) {
-    const int k0 = blk * 32;
-    uint8_t e8 = 127;
-    if (s >= 0 && k0 < H) {
-      float f[32];
-      const __nv_bfloat16* xr = x + (size_t)s * xs + k0;
-      float amax = 0.f;
+  const int k0 = blk * 32;
+  uint8_t e8 = 127;
+  if (k0 < H) {
+    const __nv_bfloat16* xr = x + (size_t)s * xs + k0;
+    uint4 raw[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t8[8];
-        snb::unpack_bf16x8(reinterpret_cast<const uint4*>(xr)[c], t8);
+    for (int c = 0; c < 4; ++c) raw[c] = reinterpret_cast<const uint4*>(xr)[c];
+    float f[32];
+    float amax = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          f[c * 8 + j] = t8[j];
-          amax = fmaxf(amax, fabsf(t8[j]));
-        }
+    for (int c = 0; c < 4; ++c) {
+      float t8[8];
+      snb::unpack_bf16x8(raw[c], t8);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        f[c * 8 + j] = t8[j];
+        amax = fmaxf(amax, fabsf(t8[j]));
       }
-      int X = 0;
-      if (amax > 0.f) {
-        X = (int)ceilf(log2f(amax / 448.f));
-        X = max(-127, min(127, X));
-      }
-      e8 = (uint8_t)(X + 127);
-      const float inv = exp2f((float)-X);
-      uint8_t ob[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) ob[j] = snb::f_to_fp8e4m3(f[j] * inv);
-      reinterpret_cast<uint4*>(qrow + k0)[0] = *reinterpret_cast<uint4*>(ob);
-      reinterpret_cast<uint4*>(qrow + k0)[1] = *reinterpret_cast<uint4*>(ob + 16);
-    } else if (k0 < Kp) {
-      reinterpret_cast<uint4*>(qrow + k0)[0] = make_uint4(0, 0, 0, 0);
-      reinterpret_cast<uint4*>(qrow + k0)[1] = make_uint4(0, 0, 0, 0);
     }
-    const int kb = blk >> 2, kk = blk & 3;
-    sf[((size_t)tile * KB + kb) * chunk_bytes + (i % 32) * 16 + (i / 32) * 4 + kk] = e8;
+    int X = 0;
+    if (amax > 0.f) {
+      X = (int)ceilf(log2f(amax / 448.f));
+      X = max(-127, min(127, X));
+    }
+    e8 = (uint8_t)(X + 127);
+    const float inv = exp2f((float)-X);
+    uint8_t ob[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) ob[j] = snb::f_to_fp8e4m3(f[j] * inv);
+    reinterpret_cast<uint4*>(qrow + k0)[0] = *reinterpret_cast<uint4*>(ob);
+    reinterpret_cast<uint4*>(qrow + k0)[1] = *reinterpret_cast<uint4*>(ob + 16);
+  } else if (k0 < Kp) {
+    reinterpret_cast<uint4*>(qrow + k0)[0] = make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(qrow + k0)[1] = make_uint4(0, 0, 0, 0);
   }
+  const int kb = blk >> 2, kk = blk & 3;
+  sf[((size_t)tile * KB + kb) * chunk_bytes + (i % 32) * 16 + (i / 32) * 4 + kk] = e8;
 }
 
-// out[t] = sum_j w[t, j] * y[inv_map[t*K + j]]  (+ out[t] if accumulate). One CTA per token.
+// out[t] = sum_j w[t, j] * y[inv_map[t*K + j]]  (+ out[t] if accumulate). One CTA per token, one 8-element chunk
+// per thread: the token's K row ids and weights are staged in shared memory first, then every row's chunk is
+// requested before any is summed (independent loads, one round trip instead of 2K).
+constexpr int kMaxCombineK = 16;
+
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ys, const int32_t* __restrict__ inv_map,
                                    const float* __restrict__ w, int K, int H, __nv_bfloat16* __restrict__ out,
                                    int os, bool accumulate) {
   snb::pdl_wait();
   snb::pdl_trigger();
+  __shared__ int rows[kMaxCombineK];
+  __shared__ float wts[kMaxCombineK];
   const int t = blockIdx.x;
+  if (threadIdx.x < K) {
+    rows[threadIdx.x] = inv_map[t * K + threadIdx.x];
+    wts[threadIdx.x] = w[t * K + threadIdx.x];
+  }
+  __syncthreads();
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
     float acc[8];
     if (accumulate) {
@@ -248,14 +262,24 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ys, 
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     }
-    for (int j = 0; j < K; ++j) {
-      const int r = inv_map[t * K + j];
-      if (r < 0) continue;
-      const float wj = w[t * K + j];
-      float f[8];
-      snb::unpack_bf16x8(reinterpret_cast<const uint4*>(y + (size_t)r * ys)[c], f);
+    for (int j0 = 0; j0 < K; j0 += 4) {
+      uint4 v[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += wj * f[i];
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u;
+        const int r = j < K ? rows[j] : -1;
+        v[u] = r >= 0 ? reinterpret_cast<const uint4*>(y + (size_t)r * ys)[c] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u;
+        if (j >= K || rows[j] < 0) continue;
+        float f[8];
+        snb::unpack_bf16x8(v[u], f);
+        const float wj = wts[j];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += wj * f[i];
+      }
     }
     reinterpret_cast<uint4*>(out + (size_t)t * os)[c] = snb::pack_bf16x8(acc);
   }
@@ -306,7 +330,8 @@ void gather_quant_mxfp8(torch::Tensor q, torch::Tensor sf, torch::Tensor x, c10:
   const int KB = (Kp + 127) / 128;
   TORCH_CHECK(sf.numel() >= (int64_t)(R / bn) * KB * std::min<int64_t>(bn, 32) * 16, "gather_quant: sf capacity");
   auto st = at::cuda::getCurrentCUDAStream();
-  const int threads = 256, blocks = (R * 32 + threads - 1) / threads;
+  const int64_t items = (int64_t)R * KB * 4;
+  const int threads = 128, blocks = (int)((items + threads - 1) / threads);
   snb::launch_pdl(gather_quant_mxfp8_kernel, blocks, threads, 0, st, (const __nv_bfloat16*)x.data_ptr(), x.stride(0),
                                                        src ? src->data_ptr<int32_t>() : nullptr, R, H, Kp, bn,
                                                        (uint8_t*)q.data_ptr(), (uint8_t*)sf.data_ptr(),
@@ -320,8 +345,10 @@ void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor inv_map, torc
   if (T == 0) return;
   const int K = w.size(1);
   TORCH_CHECK(H % 8 == 0, "moe_combine: H");
+  TORCH_CHECK(K <= kMaxCombineK, "moe_combine: at most 16 experts per token");
   auto st = at::cuda::getCurrentCUDAStream();
-  snb::launch_pdl(moe_combine_kernel, T, 128, 0, st, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
+  const int threads = std::min(1024, (H / 8 + 31) / 32 * 32);
+  snb::launch_pdl(moe_combine_kernel, T, threads, 0, st, (const __nv_bfloat16*)y.data_ptr(), y.stride(0), inv_map.data_ptr<int32_t>(),
                                         w.data_ptr<float>(), K, H, (__nv_bfloat16*)out.data_ptr(), out.stride(0),
                                         accumulate);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

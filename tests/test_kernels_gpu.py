@@ -197,6 +197,29 @@ def test_topk_route_and_align_combine():
     _close(out, ref, 2e-2, 1e-2, "combine")
 
 
+@pytest.mark.parametrize("H,K,accumulate", [(2880, 4, True), (2048, 6, False), (256, 16, True)])
+def test_moe_combine_rows_missing_and_accumulate(H, K, accumulate):
+    """Combine against fp32: tokens whose experts live on another EP rank (inv_map -1), accumulation into the
+    residual, K from 4 to 16."""
+    from sglang_neuron_b200.ops.moe import moe_combine
+    torch.manual_seed(8)
+    T, R = 37, 300
+    y = torch.randn(R, H, device=DEV, dtype=torch.bfloat16)
+    inv = torch.randint(0, R, (T * K,), dtype=torch.int32)
+    inv[torch.rand(T * K) < 0.3] = -1
+    w = torch.rand(T, K, device=DEV)
+    base = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
+    out = base.clone()
+    moe_combine(out, y, inv.to(DEV), w, accumulate)
+    ref = base.float().cpu() if accumulate else torch.zeros(T, H)
+    for t in range(T):
+        for j in range(K):
+            r = int(inv[t * K + j])
+            if r >= 0:
+                ref[t] += float(w[t, j]) * y[r].float().cpu()
+    _close(out, ref, 2e-2, 2e-2, "combine")
+
+
 @pytest.mark.parametrize("bn", [16, 64, 128])
 def test_gather_quant_mxfp8(bn):
     from sglang_neuron_b200.ops.moe import gather_quant_mxfp8
