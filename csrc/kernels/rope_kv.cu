@@ -3,8 +3,9 @@
 // Parity: the reference's dense prefill op `qkv_paged` (sglang_neuron/ops/attention/qkv_paged.py:18-41)
 // applies per-head RMSNorm to Q and K, RoPE, and writes K/V into the paged pool at `slot_mapping`.
 // Here the QKV GEMM stays a separate launch (it is a plain GEMM) and everything after it is one
-// memory-bound kernel: one warp per (token, head) row, the row staged in shared memory so any
-// rotary pairing (NeoX halves, interleaved pairs, partial rotary) reads its partner directly.
+// memory-bound kernel: one warp per (token, head) row, each lane moving a contiguous run of the row as one
+// vector, the row staged in shared memory so any rotary pairing (NeoX halves, interleaved pairs, partial
+// rotary) reads its partner directly.
 //
 // Paged cache layout: [num_pages, num_kv_heads, page_size, head_dim] (head-major within a page),
 // bf16 or fp8-e4m3 (stored value = x / scale). A negative slot skips the write (padding rows).
@@ -16,6 +17,100 @@ namespace {
 
 constexpr int kWarps = 8;
 
+// A lane's run of `per` consecutive elements (per = D / 32) as one vector access where the width allows.
+template <typename T>
+SNB_DEVICE void load_run(const T* p, int per, float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    if (per == 2) {
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(p);
+      f[0] = __bfloat162float(v.x), f[1] = __bfloat162float(v.y);
+      return;
+    }
+    if (per == 4 || per == 8) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (c * 4 < per) {
+          const uint2 u = reinterpret_cast<const uint2*>(p)[c];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+          f[c * 4 + 0] = __bfloat162float(h[0].x), f[c * 4 + 1] = __bfloat162float(h[0].y);
+          f[c * 4 + 2] = __bfloat162float(h[1].x), f[c * 4 + 3] = __bfloat162float(h[1].y);
+        }
+      }
+      return;
+    }
+  } else {
+    if (per == 2 || per == 4 || per == 8) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c * 2 < per) {
+          const float2 u = reinterpret_cast<const float2*>(p)[c];
+          f[c * 2] = u.x, f[c * 2 + 1] = u.y;
+        }
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < per) f[i] = (float)p[i];
+}
+
+template <typename T>
+SNB_DEVICE void store_run(T* p, int per, const float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    if (per == 2) {
+      *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(f[0], f[1]);
+      return;
+    }
+    if (per == 4 || per == 8) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (c * 4 < per) {
+          uint2 u;
+          __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+          h[0] = __floats2bfloat162_rn(f[c * 4], f[c * 4 + 1]);
+          h[1] = __floats2bfloat162_rn(f[c * 4 + 2], f[c * 4 + 3]);
+          reinterpret_cast<uint2*>(p)[c] = u;
+        }
+      }
+      return;
+    }
+  } else if constexpr (sizeof(T) == 4) {
+    if (per == 2 || per == 4 || per == 8) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c * 2 < per) reinterpret_cast<float2*>(p)[c] = make_float2(f[c * 2], f[c * 2 + 1]);
+      return;
+    }
+  } else {  // fp8 e4m3 bytes
+    if (per == 2 || per == 4 || per == 8) {
+      uint8_t b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < per) b[i] = snb::f_to_fp8e4m3(f[i]);
+      if (per == 2) {
+        *reinterpret_cast<uint16_t*>(p) = (uint16_t)(b[0] | (b[1] << 8));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          if (c * 4 < per)
+            reinterpret_cast<uint32_t*>(p)[c] = (uint32_t)b[c * 4] | ((uint32_t)b[c * 4 + 1] << 8) |
+                                                ((uint32_t)b[c * 4 + 2] << 16) | ((uint32_t)b[c * 4 + 3] << 24);
+      }
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < per) reinterpret_cast<uint8_t*>(p)[i] = snb::f_to_fp8e4m3(f[i]);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < per) p[i] = (T)f[i];
+}
+
+// One warp per (token, head) row; lane l owns elements [l * per, (l + 1) * per), read and written as one vector
+// each, so a warp moves a whole row per access.
 template <typename T, typename CacheT>
 __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __restrict__ v,
                                int stride_q, int stride_k, int stride_v, int Hq, int Hkv, int D,
@@ -35,11 +130,12 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
   const int t = row / heads_per_tok;
   const int h = row % heads_per_tok;
   const int per = D / 32;
+  const int e0 = lane * per;
   float vals[8];
   int64_t slot = slots != nullptr ? slots[t] : -1;
   if (slot >= 0 && slot / page_size >= num_pages) {
     // a slot past the pool: recorded (SNB_ERR_BOUNDS, the slot in status[1]) and not written
-    if (status != nullptr && (threadIdx.x & 31) == 0 && atomicCAS(status, 0, SNB_ERR_BOUNDS) == 0)
+    if (status != nullptr && lane == 0 && atomicCAS(status, 0, SNB_ERR_BOUNDS) == 0)
       status[1] = (int)(slot & 0x7fffffff);
     slot = -1;
   }
@@ -47,20 +143,11 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
   if (h >= Hq + Hkv) {  // V row: copy into the cache only
     if (slot < 0 || v_cache == nullptr) return;
     const int hv = h - Hq - Hkv;
-    const T* src = v + (size_t)t * stride_v + (size_t)hv * D;
-    const int64_t page = slot / page_size, off = slot % page_size;
-    CacheT* dst = v_cache + (((size_t)page * Hkv + hv) * page_size + off) * D;
+    load_run(v + (size_t)t * stride_v + (size_t)hv * D + e0, per, vals);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < per) {
-        float f = (float)src[lane + 32 * i];
-        if constexpr (sizeof(CacheT) == 1) {
-          dst[lane + 32 * i] = snb::f_to_fp8e4m3(f * inv_v_scale);
-        } else {
-          dst[lane + 32 * i] = (CacheT)f;
-        }
-      }
-    }
+    for (int i = 0; i < 8; ++i) vals[i] *= (sizeof(CacheT) == 1 ? inv_v_scale : 1.f);
+    const int64_t page = slot / page_size, off = slot % page_size;
+    store_run(v_cache + (((size_t)page * Hkv + hv) * page_size + off) * D + e0, per, vals);
     return;
   }
 
@@ -68,65 +155,56 @@ __global__ void rope_kv_kernel(T* __restrict__ q, T* __restrict__ k, const T* __
   T* base = is_q ? q + (size_t)t * stride_q + (size_t)h * D
                  : k + (size_t)t * stride_k + (size_t)(h - Hq) * D;
   const T* nw = is_q ? q_norm_w : k_norm_w;
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (i < per) {
-      vals[i] = (float)base[lane + 32 * i];
-      ss += vals[i] * vals[i];
-    }
-  }
+  load_run(base + e0, per, vals);
   if (nw != nullptr) {
-    ss = snb::warp_sum(ss);
-    const float inv = rsqrtf(ss / (float)D + norm_eps);
+    float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if (i < per) vals[i] = vals[i] * inv * (float)nw[lane + 32 * i];
+      if (i < per) ss += vals[i] * vals[i];
+    ss = snb::warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)D + norm_eps);
+    float w[8];
+    load_run(nw + e0, per, w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < per) vals[i] = vals[i] * inv * w[i];
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    if (i < per) rowbuf[warp][lane + 32 * i] = vals[i];
+    if (i < per) rowbuf[warp][e0 + i] = vals[i];
   __syncwarp();
   const int64_t pos = positions[t];
   const int half = rot_dim / 2;
   const float* cs = cos_sin + (size_t)pos * rot_dim;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    if (i < per) {
-      const int e = lane + 32 * i;
-      if (e < rot_dim) {
-        int partner, f;
-        bool first;
-        if (neox) {
-          first = e < half;
-          partner = first ? e + half : e - half;
-          f = first ? e : e - half;
-        } else {
-          first = (e & 1) == 0;
-          partner = e ^ 1;
-          f = e >> 1;
-        }
-        const float c = cs[f], s = cs[half + f];
-        const float xp = rowbuf[warp][partner];
-        vals[i] = first ? vals[i] * c - xp * s : vals[i] * c + xp * s;
+    const int e = e0 + i;
+    if (i < per && e < rot_dim) {
+      int partner, f;
+      bool first;
+      if (neox) {
+        first = e < half;
+        partner = first ? e + half : e - half;
+        f = first ? e : e - half;
+      } else {
+        first = (e & 1) == 0;
+        partner = e ^ 1;
+        f = e >> 1;
       }
-      base[e] = (T)vals[i];
+      const float c = cs[f], s = cs[half + f];
+      const float xp = rowbuf[warp][partner];
+      vals[i] = first ? vals[i] * c - xp * s : vals[i] * c + xp * s;
     }
   }
+  store_run(base + e0, per, vals);
   if (!is_q && slot >= 0 && k_cache != nullptr) {
     const int hk = h - Hq;
     const int64_t page = slot / page_size, off = slot % page_size;
-    CacheT* dst = k_cache + (((size_t)page * Hkv + hk) * page_size + off) * D;
+    if constexpr (sizeof(CacheT) == 1) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < per) {
-        if constexpr (sizeof(CacheT) == 1) {
-          dst[lane + 32 * i] = snb::f_to_fp8e4m3(vals[i] * inv_k_scale);
-        } else {
-          dst[lane + 32 * i] = (CacheT)vals[i];
-        }
-      }
+      for (int i = 0; i < 8; ++i) vals[i] *= inv_k_scale;
     }
+    store_run(k_cache + (((size_t)page * Hkv + hk) * page_size + off) * D + e0, per, vals);
   }
 }
 

@@ -37,12 +37,14 @@ def test_rmsnorm(H):
     _close(xx, ref, 3e-2, 2e-2, "fused norm")
 
 
-@pytest.mark.parametrize("D,neox,norm,fp8", [(64, True, False, True), (128, True, True, False), (64, False, False, False)])
-def test_rope_kv_write(D, neox, norm, fp8):
+@pytest.mark.parametrize("D,neox,norm,fp8,rot", [(64, True, False, True, 64), (128, True, True, False, 128),
+                                                  (64, False, False, False, 64), (128, True, False, True, 64),
+                                                  (256, False, True, False, 256), (128, False, True, True, 96)])
+def test_rope_kv_write(D, neox, norm, fp8, rot):
     from sglang_neuron_b200.ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
     torch.manual_seed(1)
     T, Hq, Hkv, P = 21, 8, 2, 16
-    cs = build_cos_sin_cache(D, 4096, 150000.0, {"rope_type": "yarn", "factor": 32.0,
+    cs = build_cos_sin_cache(rot, 4096, 150000.0, {"rope_type": "yarn", "factor": 32.0,
                                                  "original_max_position_embeddings": 4096,
                                                  "beta_fast": 32.0, "beta_slow": 1.0, "truncate": False}, DEV)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV, dtype=torch.bfloat16)
@@ -61,10 +63,10 @@ def test_rope_kv_write(D, neox, norm, fp8):
     qc, kc_ref_in = qc.clone(), kc_ref_in.clone()
     kcache_ref = torch.zeros(4, Hkv, P, D, dtype=torch.float32)
     vcache_ref = torch.zeros_like(kcache_ref)
-    rope_qk_norm_kv_write(qc, kc_ref_in, vc_in, pos.cpu(), cs.cpu(), Hq, Hkv, D, D, neox,
+    rope_qk_norm_kv_write(qc, kc_ref_in, vc_in, pos.cpu(), cs.cpu(), Hq, Hkv, D, rot, neox,
                           qn.cpu().float() if norm else None, kn.cpu().float() if norm else None, 1e-6,
                           kcache_ref, vcache_ref, slots.cpu(), P, 0.5 if fp8 else 1.0, 0.25 if fp8 else 1.0)
-    rope_qk_norm_kv_write(q, k, v, pos, cs, Hq, Hkv, D, D, neox, qn, kn, 1e-6, kc, vc, slots, P,
+    rope_qk_norm_kv_write(q, k, v, pos, cs, Hq, Hkv, D, rot, neox, qn, kn, 1e-6, kc, vc, slots, P,
                           0.5 if fp8 else 1.0, 0.25 if fp8 else 1.0)
     _close(q, qc, 3e-2, 2e-2, "q")
     _close(k, kc_ref_in, 3e-2, 2e-2, "k")
