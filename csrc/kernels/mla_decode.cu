@@ -52,6 +52,14 @@ SNB_DEVICE void cp_async16(uint32_t dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 SNB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// four 8x8 b16 matrices, each transposed: with row-major [k][n] tiles in shared memory the results are the
+// col-major B fragments of mma.m16n8k16 (matrix i from the row addresses of lanes 8i .. 8i+7)
+SNB_DEVICE void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
 template <int N>
 SNB_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
@@ -113,9 +121,14 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   }
   __syncthreads();
 
+  // page arithmetic without divisions for power-of-two page sizes (the usual case)
+  const bool pow2 = (page_size & (page_size - 1)) == 0;
+  const int pshift = __ffs(page_size) - 1;
+  auto page_idx = [&](int tok) { return pow2 ? tok >> pshift : tok / page_size; };
+  auto page_off = [&](int tok) { return pow2 ? tok & (page_size - 1) : tok % page_size; };
   auto page_of = [&](int tok) -> int {
-    const int pi = tok / page_size - pg0;
-    return pi < kMaxSplitPages ? sbt[pi] : bt[tok / page_size];
+    const int pi = page_idx(tok) - pg0;
+    return pi < kMaxSplitPages ? sbt[pi] : bt[page_idx(tok)];
   };
   // tile k -> stage k & 1; rows past the split end are zero-filled (src size 0)
   auto load_tile = [&](int k) {
@@ -126,7 +139,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
       const int tok = t0 + row;
       const bool ok = tok < s1;
       const __nv_bfloat16* src =
-          cache + ((size_t)(ok ? page_of(tok) : 0) * page_size + (ok ? tok % page_size : 0)) * DK + col;
+          cache + ((size_t)(ok ? page_of(tok) : 0) * page_size + (ok ? page_off(tok) : 0)) * DK + col;
       cp_async16(snb::smem_u32(dst + row * RSK + col), src, ok ? 16 : 0);
     }
     cp_async_commit();
@@ -232,16 +245,16 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
         pa[1] = *reinterpret_cast<const uint32_t*>(ps + (gq + 8) * RSP + kk * 16 + qd * 2);
         pa[2] = *reinterpret_cast<const uint32_t*>(ps + gq * RSP + kk * 16 + 8 + qd * 2);
         pa[3] = *reinterpret_cast<const uint32_t*>(ps + (gq + 8) * RSP + kk * 16 + 8 + qd * 2);
-        const __nv_bfloat16* v0 = kt + (kk * 16 + qd * 2) * RSK + warp * 128 + gq;
+        // V fragments by transposing loads: lane l addresses token kk*16 + 8 ((l >> 3) & 1) + (l & 7) of the
+        // n-tile pair member l >> 4, giving b0 / b1 of two n8 tiles per instruction
+        const uint32_t vrow = snb::smem_u32(kt + (kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * RSK + warp * 128 +
+                                            (lane >> 4) * 8);
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          const __nv_bfloat16* vc = v0 + n * 8;
-          __nv_bfloat162 lo, hi;
-          lo.x = vc[0];
-          lo.y = vc[RSK];
-          hi.x = vc[8 * RSK];
-          hi.y = vc[9 * RSK];
-          mma_bf16_16816(o[n], pa, *reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+        for (int n = 0; n < 16; n += 2) {
+          uint32_t b[4];
+          ldmatrix_x4_trans(b, vrow + n * 8 * 2);
+          mma_bf16_16816(o[n], pa, b[0], b[1]);
+          mma_bf16_16816(o[n + 1], pa, b[2], b[3]);
         }
       }
     }

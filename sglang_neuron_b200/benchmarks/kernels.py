@@ -4,6 +4,7 @@
     python -m sglang_neuron_b200.benchmarks.kernels moe_stages --tokens 1087 --ep 8   # per-stage, one EP rank
     python -m sglang_neuron_b200.benchmarks.kernels gemm --tokens 64 --n 5120 --k 2880
     python -m sglang_neuron_b200.benchmarks.kernels attn --batch 64 --ctx 1536
+    python -m sglang_neuron_b200.benchmarks.kernels mla --batch 32 --ctx 4096       # DeepSeek-V2-Lite MLA
 
 Peaks come from MEASURED_PEAKS.json at the repository root when present (hbm_gbs, bf16_tflops), else the
 pool's fallback figures (6650 GB/s, 1590 TFLOP/s). Pass --iters 1 --warmup 1 for a profiler capture.
@@ -253,9 +254,43 @@ def bench_attn(a):
     print(json.dumps(res))
 
 
+def bench_mla(a):
+    """Absorbed-MLA kernels at DeepSeek-V2-Lite shape (16 heads, 576-wide latent rows, 16-token pages): one
+    prompt of --ctx tokens prefilled (extend), and a decode batch of --batch requests at --ctx tokens."""
+    from ..ops.mla import mla_decode, mla_extend
+    H, P, L = a.mla_heads, a.page, a.ctx
+    scale = 1.0 / (192 ** 0.5)
+    pages = (L + P - 1) // P
+    res = {"kernel": "mla (absorbed, bf16 latent pool)", "heads": H, "ctx": L, "page": P}
+    # extend: one request, the whole prompt in one chunk
+    cache = (torch.randn(pages + 1, 1, P, 576, device="cuda") * 0.5).to(torch.bfloat16)
+    bt = torch.arange(1, pages + 1, device="cuda", dtype=torch.int32).view(1, pages)
+    q = (torch.randn(L, H, 576, device="cuda") * 0.5).to(torch.bfloat16)
+    lens = torch.tensor([L], dtype=torch.int32, device="cuda")
+    qo = torch.tensor([0, L], dtype=torch.int32, device="cuda")
+    us = timeit(lambda: mla_extend(q, cache, bt, lens, qo, L, P, scale), a.iters, a.warmup)
+    flops = 2.0 * H * (576 + 512) * L * (L + 1) / 2
+    _, tf, src = peaks()
+    res.update({"extend_us": round(us, 1), "extend_tflops": round(flops / us / 1e6, 1),
+                f"extend_frac_of_{src}_bf16": round(flops / us / 1e6 / tf, 3)})
+    # decode: batch B at context L
+    B = a.batch
+    cache = (torch.randn(B * pages + 1, 1, P, 576, device="cuda") * 0.5).to(torch.bfloat16)
+    bt = (torch.arange(B * pages, device="cuda", dtype=torch.int32) + 1).view(B, pages)
+    q = (torch.randn(B, H, 576, device="cuda") * 0.5).to(torch.bfloat16)
+    seq = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    S = a.splits or max(1, min(16, 4 * 148 // max(1, B)))
+    us = timeit(lambda: mla_decode(q, cache, bt, seq, P, scale, S), a.iters, a.warmup)
+    hbm, _, src = peaks()
+    byt = B * L * 576 * 2
+    res.update({"decode_batch": B, "decode_splits": S, "decode_us": round(us, 1),
+                f"decode_hbm_frac_of_{src}": round(byt / (us * 1e-6) / 1e9 / hbm, 3)})
+    print(json.dumps(res))
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["moe", "moe_stages", "route", "gemm", "attn"])
+    p.add_argument("which", choices=["moe", "moe_stages", "route", "gemm", "attn", "mla"])
     p.add_argument("--ep", type=int, default=1)
     p.add_argument("--bn", type=int, default=0, help="moe_stages: force the token tile (16/32/64/128)")
     p.add_argument("--only", default="", help="moe_stages: comma-separated stages to time")
@@ -269,12 +304,13 @@ def main():
     p.add_argument("--hq", type=int, default=64)
     p.add_argument("--hkv", type=int, default=8)
     p.add_argument("--page", type=int, default=16)
+    p.add_argument("--mla-heads", type=int, default=16)
     p.add_argument("--variant", type=int, default=1, help="attn: FP8 kernel, 0 head-major, 1 token-major (bulk copies), 2 token-major (cp.async)")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     a = p.parse_args()
     {"moe": bench_moe, "moe_stages": bench_moe_stages, "route": bench_route, "gemm": bench_gemm,
-     "attn": bench_attn}[a.which](a)
+     "attn": bench_attn, "mla": bench_mla}[a.which](a)
 
 
 if __name__ == "__main__":
