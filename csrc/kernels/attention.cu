@@ -396,11 +396,11 @@ bool decode_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_ca
                           int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
                           const float* sinks, int64_t num_splits, float* o_part, float* lse_part);
 
-bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
-                          torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
-                          int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
-                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status,
-                          int* merge_cnt, float v_scale_out);
+bool decode_attention_pipelined(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads,
+                                int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
+                                float scale_log2, float v_scale_final, const float* sinks, int64_t num_splits,
+                                float* o_part, float* lse_part, int* status, int* merge_cnt, float v_scale_out);
 
 bool extend_attention_mma(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                           torch::Tensor block_table, torch::Tensor qo_indptr, torch::Tensor kv_lens, int64_t max_extend,
@@ -440,8 +440,9 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
   auto outp = (__nv_bfloat16*)out.data_ptr();
   const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
   TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16, "decode_attention: cache dtype");
-  // fp8 cache: bulk-async pipelined tensor-core kernel; else the register-prefetch tensor-core kernel for every
-  // GQA group up to 16 heads; the CUDA-core kernel below covers the rest
+  // the bulk-async pipelined tensor-core kernels (token-major for e4m3 and bf16 caches, head-major for e4m3),
+  // else the register-prefetch tensor-core kernel for every GQA group up to 16 heads; the CUDA-core kernel
+  // below covers the rest
   int* stp = status ? status->data_ptr<int>() : nullptr;
   int* mcnt = nullptr;
   if (merge_counters && S > 1) {
@@ -449,9 +450,10 @@ void decode_attention(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache,
                 "decode_attention: merge counters");
     mcnt = merge_counters->data_ptr<int>();
   }
-  const bool fp8_done = stp != nullptr && decode_attention_fp8(out, q, k_cache, v_cache, block_table, seq_lens,
-                                                               num_q_heads, num_kv_heads, head_dim, page_size, window,
-                                                               scale, vs, sk, S, op, lp, stp, mcnt, (float)v_scale);
+  const bool fp8_done = stp != nullptr && decode_attention_pipelined(out, q, k_cache, v_cache, block_table, seq_lens,
+                                                                     num_q_heads, num_kv_heads, head_dim, page_size,
+                                                                     window, scale, vs, sk, S, op, lp, stp, mcnt,
+                                                                     (float)v_scale);
   const bool merged = fp8_done && mcnt != nullptr;
   const bool mma_done = fp8_done ||
       decode_attention_mma(out, q, k_cache, v_cache, block_table, seq_lens, num_q_heads, num_kv_heads, head_dim,

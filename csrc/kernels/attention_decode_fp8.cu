@@ -81,6 +81,20 @@ SNB_DEVICE void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(snb::smem_u32(bar)) : "memory");
 }
 
+SNB_DEVICE void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+SNB_DEVICE uint32_t f32x2_to_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 SNB_DEVICE uint32_t f32x2_to_f16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -419,18 +433,23 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_kernel(
 // G = 8, a thread holds four scores of two heads per 16 tokens (the row-sum stays a per-thread partial until the
 // end), the scale is folded into Q, and O is rescaled only when some running max moved. P^T leaves the
 // accumulator layout as the B operand of the second MMA through one `movmatrix.trans` per 8x8 block.
-// CTA = one (split, KV head, request); 4 compute warps take 32 tokens each of a 128-token stage.
+// CTA = one (split, KV head, request); 4 compute warps take 32 tokens each of a 128-token stage (e4m3 cache,
+// f16 MMAs after one cvt per byte pair) or 16 tokens each of a 64-token stage (bf16 cache, bf16 MMAs on the
+// cached values as they are, scores scaled after the MMA).
 //
 // Index maps (all bijections, chosen so every shared-memory fetch is a contiguous 8/16-byte load):
 //   * contraction index of S^T (head dim): step ks, column kk = 2qq + e + 8h -> dim qq*(D/4) + 4ks + 2h + e;
 //   * row r = r3 r2 r1 r0 (bits) of a 16-token block -> token 8r3 + 4r0 + 2r2 + r1, so the k-rows a thread
 //     owns in O^T = V^T P^T (2qd, 2qd+1, 2qd+8, 2qd+9) are tokens qd, qd+4, qd+8, qd+12;
 //   * O^T row (m-tile mt, row 8h + g) -> head dim g*(D/8) + 2mt + h.
-template <int D, int NG>
-struct Fp8TokCfg {
-  static constexpr int TILE = 128;                      // tokens per stage
-  static constexpr int NST = D == 64 ? 3 : 2;           // ring stages
-  static constexpr int STAGE = 2 * TILE * D;            // K tile then V tile, fp8
+template <int D, int NG, typename CT>
+struct TokCfg {
+  static constexpr int ES = (int)sizeof(CT);            // bytes per cached element (e4m3: 1, bf16: 2)
+  static constexpr int TPW = ES == 1 ? 32 : 16;         // tokens per compute warp per stage
+  static constexpr int U = TPW / 16;                    // 16-token blocks per warp
+  static constexpr int TILE = kCWarps * TPW;            // tokens per stage
+  static constexpr int NST = ES == 1 ? (D == 64 ? 3 : 2) : (D == 64 ? 4 : 3);  // ring stages
+  static constexpr int STAGE = 2 * TILE * D * ES;       // K tile then V tile
   static constexpr int MERGE = kCWarps * 16 * D * 4;    // fp32 [warp][16 heads][D], reuses the ring
   static constexpr int RING = NST * STAGE > MERGE ? NST * STAGE : MERGE;
   static constexpr int SMEM = RING + 2 * NST * 8 + kCWarps * 16 * 2 * 4 + 64 + kMaxSplitPages * 4;
@@ -446,18 +465,20 @@ SNB_DEVICE int tok_of_row(int r) {  // row r of a 16-token block -> token offset
   return ((r >> 3) & 1) * 8 + (r & 1) * 4 + ((r >> 2) & 1) * 2 + ((r >> 1) & 1);
 }
 
-template <int D, int NG, bool BULK>
-__global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
-    const __nv_bfloat16* __restrict__ q, int q_stride, const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
+template <int D, int NG, bool BULK, typename CT>
+__global__ void __launch_bounds__(kThreads) decode_attn_tok_kernel(
+    const __nv_bfloat16* __restrict__ q, int q_stride, const CT* __restrict__ kc, const CT* __restrict__ vc,
     const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ seq_lens, int page_size,
     int Hkv, int G, int window, float scale_log2, float v_scale, const float* __restrict__ sinks,
     __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part, float* __restrict__ lse_part,
     int num_splits, int* status, int* __restrict__ merge_cnt, float v_scale_out) {
-  using C = Fp8TokCfg<D, NG>;
-  constexpr int TILE = C::TILE;
+  using C = TokCfg<D, NG, CT>;
+  constexpr int TILE = C::TILE, ES = C::ES, TPW = C::TPW, U = C::U;
   constexpr int KS = D / 16;     // contraction steps of S^T = m-tiles of O^T
-  constexpr int KB = D / 4;      // K bytes per thread per token row
-  constexpr int VB = D / 8;      // V bytes per thread per token row
+  constexpr int KB = D / 4;      // K elements per thread per token row
+  constexpr int VB = D / 8;      // V elements per thread per token row
+  constexpr int RB = D * ES;     // bytes per cached token row
+  constexpr int KBB = KB * ES, VBB = VB * ES;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING);
@@ -502,7 +523,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
     // for pages of at most one stage: s0 is a multiple of the stage and the stage a multiple of the page.
     const int nseg = TILE / seg;
     const size_t pstride = (size_t)Hkv * page_size * D, hoff = (size_t)hk * page_size * D;
-    auto seg_offset = [&](int k, int i) -> size_t {  // byte offset of segment i of stage k in the cache
+    auto seg_offset = [&](int k, int i) -> size_t {  // element offset of segment i of stage k in the cache
       int pi, inpage = 0;
       if (page_size <= TILE) {
         pi = k * nseg + i;
@@ -524,26 +545,28 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
       }
       if (!ok) break;
       const int t0 = s0 + k * TILE;
-      const uint32_t kd = snb::smem_u32(ring + s * C::STAGE), vd = kd + TILE * D;
+      const uint32_t kd = snb::smem_u32(ring + s * C::STAGE), vd = kd + TILE * RB;
       if constexpr (BULK) {
         const int ta = t0 + lane * seg;
         const bool valid = lane < nseg && ta + seg > lo && ta < s1;
         const uint32_t nvalid = __popc(__ballot_sync(0xffffffffu, valid));
-        if (lane == 0) snb::mbar_arrive_expect_tx(&full[s], nvalid * 2u * seg * D);
+        if (lane == 0) snb::mbar_arrive_expect_tx(&full[s], nvalid * 2u * seg * RB);
         __syncwarp();
         if (valid) {
           const size_t off = seg_offset(k, lane);
-          bulk_load_nohint(kd + lane * seg * D, kc + off, seg * D, snb::smem_u32(&full[s]));
-          bulk_load_nohint(vd + lane * seg * D, vc + off, seg * D, snb::smem_u32(&full[s]));
+          bulk_load_nohint(kd + lane * seg * RB, kc + off, seg * RB, snb::smem_u32(&full[s]));
+          bulk_load_nohint(vd + lane * seg * RB, vc + off, seg * RB, snb::smem_u32(&full[s]));
         }
       } else {
         for (int i = 0; i < nseg; ++i) {
           const int ta = t0 + i * seg;
           if (!(ta + seg > lo && ta < s1)) continue;
           const size_t off = seg_offset(k, i);
-          for (int c = lane * 16; c < seg * D; c += 32 * 16) {
-            cp_async16(kd + i * seg * D + c, kc + off + c);
-            cp_async16(vd + i * seg * D + c, vc + off + c);
+          const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(kc + off);
+          const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(vc + off);
+          for (int c = lane * 16; c < seg * RB; c += 32 * 16) {
+            cp_async16(kd + i * seg * RB + c, ksrc + c);
+            cp_async16(vd + i * seg * RB + c, vsrc + c);
           }
         }
         cp_async_arrive_noinc(&full[s]);
@@ -554,8 +577,9 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
   } else {
     // ---------------- compute warps
     const int gq = lane >> 2, qd = lane & 3;
-    // Q^T fragments (B operand of S^T): head ng*8 + gq, dims qd*KB + 4ks + {0,1} and {2,3}, pre-scaled by
-    // scale * log2(e) (f16 keeps 11 mantissa bits, more than the bf16 input has)
+    // Q^T fragments (B operand of S^T): head ng*8 + gq, dims qd*KB + 4ks + {0,1} and {2,3}. For an e4m3 cache
+    // (f16 MMAs) Q is pre-scaled by scale * log2(e): f16 keeps 11 mantissa bits, more than the bf16 input has;
+    // for a bf16 cache (bf16 MMAs) Q stays as it is and the scores are scaled.
     uint32_t qb[NG][KS][2];
     {
       const __nv_bfloat16* qh = q + (size_t)b * q_stride + (size_t)hk * G * D;
@@ -569,7 +593,12 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
             if (h < G) {
               const __nv_bfloat162 v =
                   *reinterpret_cast<const __nv_bfloat162*>(qh + (size_t)h * D + qd * KB + ks * 4 + e * 2);
-              qb[ng][ks][e] = f32x2_to_f16x2(__bfloat162float(v.x) * scale_log2, __bfloat162float(v.y) * scale_log2);
+              if constexpr (ES == 1) {
+                qb[ng][ks][e] =
+                    f32x2_to_f16x2(__bfloat162float(v.x) * scale_log2, __bfloat162float(v.y) * scale_log2);
+              } else {
+                qb[ng][ks][e] = *reinterpret_cast<const uint32_t*>(&v);
+              }
             } else {
               qb[ng][ks][e] = 0u;
             }
@@ -595,65 +624,77 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
         sh[2] = 1;
         break;
       }
-      const uint8_t* kt = ring + s * C::STAGE + warp * 32 * D;
-      const uint8_t* vt = ring + s * C::STAGE + TILE * D + warp * 32 * D;
-      const int tw = s0 + k * TILE + warp * 32;  // first token of this warp's 32
-      const bool whole = tw >= lo && tw + 32 <= s1;
-      // K rows krow0 / krow1 of both 16-token blocks: KB bytes at qd*KB
-      uint32_t kw[2][2][KB / 4];
+      const uint8_t* kt = ring + s * C::STAGE + warp * TPW * RB;
+      const uint8_t* vt = ring + s * C::STAGE + TILE * RB + warp * TPW * RB;
+      const int tw = s0 + k * TILE + warp * TPW;  // first token of this warp's TPW
+      const bool whole = tw >= lo && tw + TPW <= s1;
+      // K rows krow0 / krow1 of each 16-token block: KBB bytes at qd*KBB
+      uint32_t kw[U][2][KBB / 4];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int r = 0; r < 2; ++r)
 #pragma unroll
-          for (int i = 0; i < KB / 16; ++i) {
-            const uint4 a = *reinterpret_cast<const uint4*>(kt + (u * 16 + (r ? krow1 : krow0)) * D + qd * KB + i * 16);
+          for (int i = 0; i < KBB / 16; ++i) {
+            const uint4 a = *reinterpret_cast<const uint4*>(kt + (u * 16 + (r ? krow1 : krow0)) * RB + qd * KBB + i * 16);
             kw[u][r][i * 4] = a.x;
             kw[u][r][i * 4 + 1] = a.y;
             kw[u][r][i * 4 + 2] = a.z;
             kw[u][r][i * 4 + 3] = a.w;
           }
-      // V rows qd + 4i of both blocks: VB bytes at gq*VB; tokens outside [lo, s1) zeroed (stale page bytes)
-      uint32_t vw[2][4][VB / 4];
+      // V rows qd + 4i of each block: VBB bytes at gq*VBB; tokens outside [lo, s1) zeroed (stale page bytes)
+      uint32_t vw[U][4][VBB / 4];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int row = u * 16 + qd + 4 * i;
-          const uint8_t* src = vt + row * D + gq * VB;
+          const uint8_t* src = vt + row * RB + gq * VBB;
           const bool ok = whole || (tw + row >= lo && tw + row < s1);
-          if constexpr (VB == 8) {
+          if constexpr (VBB == 8) {
             const uint2 v = *reinterpret_cast<const uint2*>(src);
             vw[u][i][0] = ok ? v.x : 0u;
             vw[u][i][1] = ok ? v.y : 0u;
           } else {
-            const uint4 v = *reinterpret_cast<const uint4*>(src);
-            vw[u][i][0] = ok ? v.x : 0u;
-            vw[u][i][1] = ok ? v.y : 0u;
-            vw[u][i][2] = ok ? v.z : 0u;
-            vw[u][i][3] = ok ? v.w : 0u;
+#pragma unroll
+            for (int c = 0; c < VBB / 16; ++c) {
+              const uint4 v = reinterpret_cast<const uint4*>(src)[c];
+              vw[u][i][c * 4] = ok ? v.x : 0u;
+              vw[u][i][c * 4 + 1] = ok ? v.y : 0u;
+              vw[u][i][c * 4 + 2] = ok ? v.z : 0u;
+              vw[u][i][c * 4 + 3] = ok ? v.w : 0u;
+            }
           }
         }
       __syncwarp();
       if (lane == 0) snb::mbar_arrive(&empty[s]);  // this warp's bytes of the stage are in registers
-      // ---- S^T = K Q^T: sc[u][ng] rows (krow0, krow1) x heads (2qd, 2qd+1), already in log2 units
-      float sc[2][NG][4];
+      // ---- S^T = K Q^T: sc[u][ng] rows (krow0, krow1) x heads (2qd, 2qd+1), in log2 units
+      float sc[U][NG][4];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int ng = 0; ng < NG; ++ng) {
           sc[u][ng][0] = sc[u][ng][1] = sc[u][ng][2] = sc[u][ng][3] = 0.f;
 #pragma unroll
           for (int ks = 0; ks < KS; ++ks) {
-            const uint32_t w0 = kw[u][0][ks], w1 = kw[u][1][ks];
-            const uint32_t a[4] = {e4m3x2_to_f16x2(w0), e4m3x2_to_f16x2(w1), e4m3x2_hi_to_f16x2(w0),
-                                   e4m3x2_hi_to_f16x2(w1)};
-            mma_f16_16816(sc[u][ng], a, qb[ng][ks][0], qb[ng][ks][1]);
+            if constexpr (ES == 1) {
+              const uint32_t w0 = kw[u][0][ks], w1 = kw[u][1][ks];
+              const uint32_t a[4] = {e4m3x2_to_f16x2(w0), e4m3x2_to_f16x2(w1), e4m3x2_hi_to_f16x2(w0),
+                                     e4m3x2_hi_to_f16x2(w1)};
+              mma_f16_16816(sc[u][ng], a, qb[ng][ks][0], qb[ng][ks][1]);
+            } else {
+              const uint32_t a[4] = {kw[u][0][2 * ks], kw[u][1][2 * ks], kw[u][0][2 * ks + 1], kw[u][1][2 * ks + 1]};
+              mma_bf16_16816(sc[u][ng], a, qb[ng][ks][0], qb[ng][ks][1]);
+            }
+          }
+          if constexpr (ES == 2) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[u][ng][j] *= scale_log2;
           }
         }
       if (!whole) {
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < U; ++u) {
           const int t0 = tw + u * 16 + krow0, t1 = t0 + 8;
           const bool ok0 = t0 >= lo && t0 < s1, ok1 = t1 >= lo && t1 < s1;
 #pragma unroll
@@ -663,14 +704,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
           }
         }
       }
-      // ---- online softmax per head column over the warp's 32 tokens
+      // ---- online softmax per head column over the warp's TPW tokens
       bool moved = false;
       float alpha[NG][2];
 #pragma unroll
       for (int ng = 0; ng < NG; ++ng)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          float mx = fmaxf(fmaxf(sc[0][ng][j], sc[0][ng][2 + j]), fmaxf(sc[1][ng][j], sc[1][ng][2 + j]));
+          float mx = -INFINITY;
+#pragma unroll
+          for (int u = 0; u < U; ++u) mx = fmaxf(mx, fmaxf(sc[u][ng][j], sc[u][ng][2 + j]));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
@@ -681,19 +724,24 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
           l_r[ng][j] *= alpha[ng][j];
         }
       // P^T as the B operand of O^T = V^T P^T: pack a row's two head columns, transpose each 8x8 block
-      uint32_t pb[2][NG][2];
+      uint32_t pb[U][NG][2];
 #pragma unroll
       for (int ng = 0; ng < NG; ++ng) {
         const float r0 = m_r[ng][0] == -INFINITY ? 0.f : m_r[ng][0];
         const float r1 = m_r[ng][1] == -INFINITY ? 0.f : m_r[ng][1];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < U; ++u) {
           const float p0 = ex2_approx(sc[u][ng][0] - r0), p1 = ex2_approx(sc[u][ng][1] - r1);
           const float p2 = ex2_approx(sc[u][ng][2] - r0), p3 = ex2_approx(sc[u][ng][3] - r1);
           l_r[ng][0] += p0 + p2;
           l_r[ng][1] += p1 + p3;
-          pb[u][ng][0] = movmatrix_trans(f32x2_to_f16x2(p0, p1));
-          pb[u][ng][1] = movmatrix_trans(f32x2_to_f16x2(p2, p3));
+          if constexpr (ES == 1) {
+            pb[u][ng][0] = movmatrix_trans(f32x2_to_f16x2(p0, p1));
+            pb[u][ng][1] = movmatrix_trans(f32x2_to_f16x2(p2, p3));
+          } else {
+            pb[u][ng][0] = movmatrix_trans(f32x2_to_bf16x2(p0, p1));
+            pb[u][ng][1] = movmatrix_trans(f32x2_to_bf16x2(p2, p3));
+          }
         }
       }
       if (__any_sync(0xffffffffu, moved)) {
@@ -707,20 +755,29 @@ __global__ void __launch_bounds__(kThreads) decode_attn_fp8_tok_kernel(
             o[mt][ng][3] *= alpha[ng][1];
           }
       }
-      // ---- O^T += V^T P^T: A rows are head dims (byte 2mt + h of the thread's V slice), k = tokens
-      // qd, qd+4 | qd+8, qd+12 of each 16-token block; one byte permute gathers both dims of a token pair
+      // ---- O^T += V^T P^T: A rows are head dims (element 2mt + h of the thread's V slice), k = tokens
+      // qd, qd+4 | qd+8, qd+12 of each 16-token block; one permute gathers both dims of a token pair
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) {
-        const int w = mt >> 1;
-        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const uint32_t p01 = __byte_perm(vw[u][0][w], vw[u][1][w], sel);
-          const uint32_t p23 = __byte_perm(vw[u][2][w], vw[u][3][w], sel);
-          const uint32_t a[4] = {e4m3x2_to_f16x2(p01), e4m3x2_hi_to_f16x2(p01), e4m3x2_to_f16x2(p23),
-                                 e4m3x2_hi_to_f16x2(p23)};
+        for (int u = 0; u < U; ++u) {
+          if constexpr (ES == 1) {
+            const int w = mt >> 1;
+            const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+            const uint32_t p01 = __byte_perm(vw[u][0][w], vw[u][1][w], sel);
+            const uint32_t p23 = __byte_perm(vw[u][2][w], vw[u][3][w], sel);
+            const uint32_t a[4] = {e4m3x2_to_f16x2(p01), e4m3x2_hi_to_f16x2(p01), e4m3x2_to_f16x2(p23),
+                                   e4m3x2_hi_to_f16x2(p23)};
 #pragma unroll
-          for (int ng = 0; ng < NG; ++ng) mma_f16_16816(o[mt][ng], a, pb[u][ng][0], pb[u][ng][1]);
+            for (int ng = 0; ng < NG; ++ng) mma_f16_16816(o[mt][ng], a, pb[u][ng][0], pb[u][ng][1]);
+          } else {
+            // bf16: word mt of the slice holds dims 2mt (low half) and 2mt + 1 (high half)
+            const uint32_t x0 = vw[u][0][mt], x1 = vw[u][1][mt], x2 = vw[u][2][mt], x3 = vw[u][3][mt];
+            const uint32_t a[4] = {__byte_perm(x0, x1, 0x5410u), __byte_perm(x0, x1, 0x7632u),
+                                   __byte_perm(x2, x3, 0x5410u), __byte_perm(x2, x3, 0x7632u)};
+#pragma unroll
+            for (int ng = 0; ng < NG; ++ng) mma_bf16_16816(o[mt][ng], a, pb[u][ng][0], pb[u][ng][1]);
+          }
         }
       }
     }
@@ -775,9 +832,10 @@ static int fp8_smem_attr() {
   return Cfg::SMEM;
 }
 
-// Which FP8 kernel serves a call: 1 (default) the token-major kernel fed by bulk copies, 2 the token-major kernel
-// fed by 16-byte cp.async, 0 the head-major kernel (variants 1 and 2 fall back to it for page sizes that do not
-// tile 128 tokens). Tests and the attention microbenchmark compare them.
+// Which kernel serves a call: 1 (default) the token-major kernel fed by bulk copies, 2 the token-major kernel
+// fed by 16-byte cp.async, 0 the head-major kernel for an e4m3 cache and the register-prefetch kernel
+// (attention_decode_mma.cu) for a bf16 cache. Page sizes that do not tile the token-major stage fall back the
+// same way. Tests and the attention microbenchmark compare them.
 static int g_fp8_decode_variant = 1;
 
 void set_decode_fp8_variant(int64_t v) {
@@ -785,53 +843,68 @@ void set_decode_fp8_variant(int64_t v) {
   g_fp8_decode_variant = (int)v;
 }
 
-// Same contract as decode_attention_mma() for an fp8 cache; false when not covered (head_dim not 64/128, G > 16,
-// or a page size that is neither a divisor nor a multiple of the 64-token tile). With merge_cnt (zeroed int32
-// per (request, KV head)) and more than one split, the split merge runs inside this launch (v_scale_out is
-// applied there) and no merge kernel follows.
-bool decode_attention_fp8(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
-                          torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads, int64_t num_kv_heads,
-                          int64_t head_dim, int64_t page_size, int64_t window, float scale_log2, float v_scale_final,
-                          const float* sinks, int64_t num_splits, float* o_part, float* lse_part, int* status,
-                          int* merge_cnt, float v_scale_out) {
+template <int D, int NG, typename CT>
+static bool tok_tiles(int64_t page_size) {
+  constexpr int T = TokCfg<D, NG, CT>::TILE;
+  return (page_size >= 16 && T % page_size == 0) || (page_size >= T && page_size % T == 0);
+}
+
+// Same contract as decode_attention_mma() for an e4m3 or bf16 cache, served by the pipelined tensor-core
+// kernels of this file; false when not covered (head_dim not 64/128, G > 16, a page size that tiles neither
+// stage, or a bf16 cache with the token-major kernel switched off). With merge_cnt (zeroed int32 per
+// (request, KV head)) and more than one split, the split merge runs inside this launch (v_scale_out is applied
+// there) and no merge kernel follows.
+bool decode_attention_pipelined(torch::Tensor out, torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                torch::Tensor block_table, torch::Tensor seq_lens, int64_t num_q_heads,
+                                int64_t num_kv_heads, int64_t head_dim, int64_t page_size, int64_t window,
+                                float scale_log2, float v_scale_final, const float* sinks, int64_t num_splits,
+                                float* o_part, float* lse_part, int* status, int* merge_cnt, float v_scale_out) {
   const int G = num_q_heads / num_kv_heads;
-  if (k_cache.scalar_type() != at::kFloat8_e4m3fn || G > 16 || (head_dim != 64 && head_dim != 128)) return false;
-  if (!((page_size >= 16 && kTile % page_size == 0) || (page_size >= kTile && page_size % kTile == 0))) return false;
+  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  const bool bf16 = k_cache.scalar_type() == at::kBFloat16;
+  if (!(fp8 || bf16) || G > 16 || (head_dim != 64 && head_dim != 128)) return false;
   if (k_cache.data_ptr() == nullptr || reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % 16 ||
       reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % 16 || !k_cache.is_contiguous() || !v_cache.is_contiguous())
     return false;
+  const bool head_major_ok =
+      fp8 && ((page_size >= 16 && kTile % page_size == 0) || (page_size >= kTile && page_size % kTile == 0));
+  const bool tok = g_fp8_decode_variant != 0 &&
+                   (fp8 ? tok_tiles<64, 1, uint8_t>(page_size) : tok_tiles<64, 1, __nv_bfloat16>(page_size));
+  if (!tok && !head_major_ok) return false;
   const int B = q.size(0);
   auto st = at::cuda::getCurrentCUDAStream();
   dim3 grid(num_splits, num_kv_heads, B);
-  constexpr int kTok = Fp8TokCfg<64, 1>::TILE;
-  const bool tok = g_fp8_decode_variant != 0 &&
-                   ((page_size >= 16 && kTok % page_size == 0) || (page_size >= kTok && page_size % kTok == 0));
-  auto launch = [&](auto kernel, int smem) {
+  auto launch = [&](auto kernel, int smem, auto* elem) {
+    using E = std::remove_pointer_t<decltype(elem)>;
     C10_CUDA_CHECK(snb::launch_pdl(kernel, grid, kThreads, smem, st, (const __nv_bfloat16*)q.data_ptr(),
-                                   (int)q.stride(0), (const uint8_t*)k_cache.data_ptr(),
-                                   (const uint8_t*)v_cache.data_ptr(), block_table.data_ptr<int32_t>(),
-                                   (int)block_table.stride(0), seq_lens.data_ptr<int32_t>(), (int)page_size,
-                                   (int)num_kv_heads, G, (int)window, scale_log2, v_scale_final, sinks,
-                                   (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), o_part, lse_part,
-                                   (int)num_splits, status, merge_cnt, v_scale_out));
+                                   (int)q.stride(0), (const E*)k_cache.data_ptr(), (const E*)v_cache.data_ptr(),
+                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
+                                   seq_lens.data_ptr<int32_t>(), (int)page_size, (int)num_kv_heads, G, (int)window,
+                                   scale_log2, v_scale_final, sinks, (__nv_bfloat16*)out.data_ptr(),
+                                   (int)out.stride(0), o_part, lse_part, (int)num_splits, status, merge_cnt,
+                                   v_scale_out));
   };
   const bool bulk = g_fp8_decode_variant == 1;
-#define SNB_TOK(DD, NGG, BB) launch(decode_attn_fp8_tok_kernel<DD, NGG, BB>, \
-                                    fp8_smem_attr<Fp8TokCfg<DD, NGG>, decode_attn_fp8_tok_kernel<DD, NGG, BB>>())
+#define SNB_TOK(DD, NGG, BB, CT) launch(decode_attn_tok_kernel<DD, NGG, BB, CT>,                              \
+                                        fp8_smem_attr<TokCfg<DD, NGG, CT>, decode_attn_tok_kernel<DD, NGG, BB, CT>>(), \
+                                        (CT*)nullptr)
+#define SNB_TOK_D(DD, CT)                                                                                   \
+  {                                                                                                         \
+    if (G <= 8) { if (bulk) SNB_TOK(DD, 1, true, CT); else SNB_TOK(DD, 1, false, CT); }                     \
+    else { if (bulk) SNB_TOK(DD, 2, true, CT); else SNB_TOK(DD, 2, false, CT); }                            \
+  }
   if (tok) {
-    const int ng = G <= 8 ? 1 : 2;
-    if (head_dim == 64) {
-      if (ng == 1) { if (bulk) SNB_TOK(64, 1, true); else SNB_TOK(64, 1, false); }
-      else { if (bulk) SNB_TOK(64, 2, true); else SNB_TOK(64, 2, false); }
+    if (fp8) {
+      if (head_dim == 64) SNB_TOK_D(64, uint8_t) else SNB_TOK_D(128, uint8_t)
     } else {
-      if (ng == 1) { if (bulk) SNB_TOK(128, 1, true); else SNB_TOK(128, 1, false); }
-      else { if (bulk) SNB_TOK(128, 2, true); else SNB_TOK(128, 2, false); }
+      if (head_dim == 64) SNB_TOK_D(64, __nv_bfloat16) else SNB_TOK_D(128, __nv_bfloat16)
     }
   } else if (head_dim == 64) {
-    launch(decode_attn_fp8_kernel<64>, fp8_smem_attr<Fp8Cfg<64>, decode_attn_fp8_kernel<64>>());
+    launch(decode_attn_fp8_kernel<64>, fp8_smem_attr<Fp8Cfg<64>, decode_attn_fp8_kernel<64>>(), (uint8_t*)nullptr);
   } else {
-    launch(decode_attn_fp8_kernel<128>, fp8_smem_attr<Fp8Cfg<128>, decode_attn_fp8_kernel<128>>());
+    launch(decode_attn_fp8_kernel<128>, fp8_smem_attr<Fp8Cfg<128>, decode_attn_fp8_kernel<128>>(), (uint8_t*)nullptr);
   }
+#undef SNB_TOK_D
 #undef SNB_TOK
   return true;
 }

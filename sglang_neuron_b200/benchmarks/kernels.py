@@ -222,11 +222,12 @@ def bench_gemm(a):
 
 def bench_attn(a):
     from ..ops.attention import DecodeScratch, decode_attention, default_num_splits
-    B, L, P, Hq, Hkv, D = a.batch, a.ctx, a.page, a.hq, a.hkv, 64
+    B, L, P, Hq, Hkv, D = a.batch, a.ctx, a.page, a.hq, a.hkv, a.head_dim
+    kv_dt = torch.bfloat16 if a.kv == "bf16" else torch.float8_e4m3fn
     pages_per = (L + P - 1) // P
     n_pages = B * pages_per + 1
-    kc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(torch.float8_e4m3fn)
-    vc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(torch.float8_e4m3fn)
+    kc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(kv_dt)
+    vc = torch.randn(n_pages, Hkv, P, D, device="cuda").to(kv_dt)
     bt = (torch.arange(B * pages_per, device="cuda", dtype=torch.int32) + 1).view(B, pages_per)
     seq = torch.full((B,), L, device="cuda", dtype=torch.int32)
     q = torch.randn(B, Hq * D, device="cuda").to(torch.bfloat16)
@@ -237,7 +238,8 @@ def bench_attn(a):
     kernels().set_decode_fp8_variant(a.variant)
     us = timeit(lambda: decode_attention(q, kc, vc, bt, seq, Hq, Hkv, D, P, 0, None, 1.0, 1.0, sinks, S, sc),
                 a.iters, a.warmup)
-    res = {"kernel": "decode_attention (paged GQA, fp8 KV, sinks)", "batch": B, "ctx": L, "splits": S,
+    res = {"kernel": f"decode_attention (paged GQA, {a.kv} KV, sinks)", "batch": B, "ctx": L, "splits": S,
+           "head_dim": D,
            "heads": f"{Hq}/{Hkv}", "page": P,
            "variant": ["head-major", "token-major bulk", "token-major cp.async"][a.variant],
            "us_single_cold": round(us, 2)}
@@ -249,7 +251,7 @@ def bench_attn(a):
                                                       1.0, sinks, S, sc) for i in range(n)])
         res["us_in_graph"] = round(us, 2)
     hbm, tf, src = peaks()
-    byt = B * L * Hkv * D * 2
+    byt = B * L * Hkv * D * 2 * kc.element_size()
     res[f"hbm_frac_of_{src}"] = round(byt / (us * 1e-6) / 1e9 / hbm, 3)
     print(json.dumps(res))
 
@@ -305,6 +307,8 @@ def main():
     p.add_argument("--hkv", type=int, default=8)
     p.add_argument("--page", type=int, default=16)
     p.add_argument("--mla-heads", type=int, default=16)
+    p.add_argument("--head-dim", type=int, default=64)
+    p.add_argument("--kv", default="fp8", choices=["fp8", "bf16"])
     p.add_argument("--variant", type=int, default=1, help="attn: FP8 kernel, 0 head-major, 1 token-major (bulk copies), 2 token-major (cp.async)")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)

@@ -491,35 +491,42 @@ def test_fused_route_matches_separate_launches(T, E, K, mode, El, e_lo):
     assert torch.equal(sfb[idx], sf2[idx])
 
 
+@pytest.mark.parametrize("kv", ["fp8", "bf16"])
 @pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("D,Hq,Hkv,window,sinks,splits,P", [
     (64, 32, 2, 0, True, 2, 16), (128, 32, 2, 50, False, 1, 32), (64, 64, 8, 200, True, 1, 64),
-    (128, 64, 8, 0, True, 2, 128), (64, 32, 8, 0, False, 1, 16)])
-def test_decode_attention_fp8_variants(variant, D, Hq, Hkv, window, sinks, splits, P):
-    """Both FP8 decode kernels (head-major rows of query heads, token-major S^T = K Q^T) against the fp32
-    reference, GQA groups of 4, 8 and 16 heads, stale NaN bytes past each request's end."""
+    (128, 64, 8, 0, True, 2, 128), (64, 32, 8, 0, False, 1, 16), (128, 32, 8, 0, False, 3, 16)])
+def test_decode_attention_pipelined_variants(kv, variant, D, Hq, Hkv, window, sinks, splits, P):
+    """The decode kernels behind one switch against the fp32 reference: for e4m3 caches the head-major kernel
+    (query heads as MMA rows) and the token-major kernel (S^T = K Q^T) fed by bulk copies or cp.async; for bf16
+    caches the register-prefetch kernel and the same token-major kernel. GQA groups of 4, 8 and 16 heads; stale
+    NaN bytes past each request's end (except for the register-prefetch kernel, which the engine feeds zeroed
+    pools)."""
     from sglang_neuron_b200._ext import kernels
     from sglang_neuron_b200.ops.attention import decode_attention, decode_attention_ref
     torch.manual_seed(5)
     ctx = [1, 17, 300, 1000, 64, 129, 128, 33]
     B = len(ctx)
-    kc, vc, bt = _make_paged(B, ctx, Hkv, D, P, torch.float8_e4m3fn)
-    for b, c in enumerate(ctx):
-        for t in range(c, ((c + P - 1) // P + 1) * P):
-            pg = int(bt[b, t // P])
-            kc[pg, :, t % P] = float("nan")
-            vc[pg, :, t % P] = float("nan")
+    fp8 = kv == "fp8"
+    kc, vc, bt = _make_paged(B, ctx, Hkv, D, P, torch.float8_e4m3fn if fp8 else torch.bfloat16)
+    if fp8 or variant != 0:
+        for b, c in enumerate(ctx):
+            for t in range(c, ((c + P - 1) // P + 1) * P):
+                pg = int(bt[b, t // P])
+                kc[pg, :, t % P] = float("nan")
+                vc[pg, :, t % P] = float("nan")
     q = torch.randn(B, Hq * D, dtype=torch.bfloat16)
     sk = torch.randn(Hq) if sinks else None
     seq = torch.tensor(ctx, dtype=torch.int32)
-    ref = decode_attention_ref(q.float(), kc, vc, bt, seq, Hq, Hkv, D, P, window, None, 0.8, 1.3, sk)
+    ks, vs = (0.8, 1.3) if fp8 else (1.0, 1.0)
+    ref = decode_attention_ref(q.float(), kc, vc, bt, seq, Hq, Hkv, D, P, window, None, ks, vs, sk)
     kernels().set_decode_fp8_variant(variant)
     try:
         out = decode_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), seq.to(DEV), Hq, Hkv, D, P, window,
-                               None, 0.8, 1.3, sk.to(DEV) if sinks else None, num_splits=splits)
+                               None, ks, vs, sk.to(DEV) if sinks else None, num_splits=splits)
     finally:
         kernels().set_decode_fp8_variant(1)
-    _close(out, ref, 2e-2, 2e-2, f"decode fp8 variant {variant}")
+    _close(out, ref, 2e-2, 2e-2, f"decode {kv} variant {variant}")
 
 
 def test_decode_attention_merge_counters_rearm():
