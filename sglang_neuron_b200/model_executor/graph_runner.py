@@ -11,6 +11,7 @@ embedding -> layers -> LM head -> sampler -> token relay with no host work in be
 from __future__ import annotations
 
 import bisect
+import gc
 import logging
 from typing import Dict
 
@@ -91,8 +92,18 @@ class CudaGraphRunner:
                         self._body(bs, filtered)
                     g = torch.cuda.CUDAGraph()
                     n0 = _ext.launch_count()
-                    with torch.cuda.graph(g, pool=self.pool, stream=stream):
-                        self._body(bs, filtered)
+                    # no garbage collection inside the capture: collecting an unreachable object that owns a
+                    # CUDA graph (an earlier engine's runner, say) destroys that graph, a call the capture
+                    # forbids, and the capture is invalidated
+                    gc.collect()
+                    gc_was_on = gc.isenabled()
+                    gc.disable()
+                    try:
+                        with torch.cuda.graph(g, pool=self.pool, stream=stream):
+                            self._body(bs, filtered)
+                    finally:
+                        if gc_was_on:
+                            gc.enable()
                     launches[bs] = _ext.launch_count() - n0
                     if self.pool is None:
                         self.pool = g.pool()
