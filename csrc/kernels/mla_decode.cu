@@ -13,7 +13,8 @@
 // Extend (prefill / chunked prefill, `qo_indptr` given): the 16 M rows of a CTA are 16 consecutive
 // (query token, head) pairs of one request (token-major), each with its own causal limit prefix + t + 1;
 // the CTA walks the context up to its last row's limit. One query token per request with all its heads is
-// the decode case, so both share the tile pipeline.
+// the decode case, so both share the tile pipeline. Extend CTAs run two such groups of 16 rows (8 warps) over
+// one latent-tile pipeline, so each tile is read once for 32 rows.
 //
 // Decode context parallelism (dcp_size D > 1): logical page j of a request lives on DCP rank j % D, and the
 // block table given here lists only this rank's pages (local page i = logical page i * D + dcp_rank). Keys
@@ -38,7 +39,13 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int SMEM_K = 2 * TT * RSK * 2;           // two stages
 constexpr int SMEM_SP = 4 * 16 * TT * 4;           // partial scores per warp
 constexpr int SMEM_P = 16 * RSP * 2;
-constexpr int SMEM_TOTAL = SMEM_K + SMEM_SP + SMEM_P + 4 * 16 * 4 + kMaxSplitPages * 4;
+// MT row groups of 16 per CTA (4 warps each) share one latent-tile pipeline: decode uses one group (the heads
+// of a token), extend two (each latent tile is read once for 32 (token, head) rows)
+template <int MT>
+struct MlaCfg {
+  static constexpr int THR = kThr * MT;
+  static constexpr int SMEM = SMEM_K + MT * (SMEM_SP + SMEM_P + 4 * 16 * 4) + kMaxSplitPages * 4;
+};
 
 SNB_DEVICE void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -63,7 +70,8 @@ SNB_DEVICE void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
 template <int N>
 SNB_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__global__ void __launch_bounds__(kThr) mla_decode_kernel(
+template <int MT>
+__global__ void __launch_bounds__(kThr * MT) mla_decode_kernel(
     const __nv_bfloat16* __restrict__ q, int q_stride, const __nv_bfloat16* __restrict__ cache,
     const int32_t* __restrict__ block_table, int bt_stride, const int32_t* __restrict__ seq_lens, int page_size,
     int H, float scale_log2, __nv_bfloat16* __restrict__ out, int out_stride, float* __restrict__ o_part,
@@ -73,24 +81,26 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   snb::pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem);                   // [2][TT][RSK]
-  float* sp = reinterpret_cast<float*>(smem + SMEM_K);                          // [4][16][TT]
-  __nv_bfloat16* ps = reinterpret_cast<__nv_bfloat16*>(smem + SMEM_K + SMEM_SP);  // [16][RSP]
-  float* alpha_s = reinterpret_cast<float*>(smem + SMEM_K + SMEM_SP + SMEM_P);  // [16]
-  float* m_s = alpha_s + 16;
-  float* l_s = m_s + 16;
-  int32_t* lim_s = reinterpret_cast<int32_t*>(l_s + 16);  // per-row key limit (0: row unused)
-  int32_t* sbt = lim_s + 16;
+  constexpr int THR = kThr * MT, R = 16 * MT;  // threads, rows per CTA
+  float* sp = reinterpret_cast<float*>(smem + SMEM_K);                               // [MT][4][16][TT]
+  __nv_bfloat16* ps = reinterpret_cast<__nv_bfloat16*>(smem + SMEM_K + MT * SMEM_SP);  // [MT][16][RSP]
+  float* alpha_s = reinterpret_cast<float*>(smem + SMEM_K + MT * (SMEM_SP + SMEM_P));  // [R]
+  float* m_s = alpha_s + R;
+  float* l_s = m_s + R;
+  int32_t* lim_s = reinterpret_cast<int32_t*>(l_s + R);  // per-row key limit (0: row unused)
+  int32_t* sbt = lim_s + R;
 
   const int split = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, qd = lane & 3;
-  const int h0 = hg * 16;
+  const int grp = warp >> 2, wq = warp & 3;  // row group of this warp, its quarter within the group
+  const int h0 = hg * R;
   // rows of this CTA: decode -> heads h0.. of request b's token; extend -> (token, head) pairs h0..
   const bool ext = qo_indptr != nullptr;
   const int q0 = ext ? qo_indptr[b] : b;
   const int nq = ext ? qo_indptr[b + 1] - q0 : 1;
-  const int nrows = ext ? nq * H - h0 : min(16, H - h0);
+  const int nrows = ext ? nq * H - h0 : min(R, H - h0);
   if (nrows <= 0) return;  // extend: this request has fewer rows than the grid's row groups
-  const int hn = min(16, nrows);
+  const int hn = min(R, nrows);
   const int kv_len = seq_lens[b];
   const int prefix = kv_len - nq;
   auto row_tok = [&](int row) { return ext ? q0 + (h0 + row) / H : b; };
@@ -113,8 +123,8 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   const int32_t* bt = block_table + (size_t)b * bt_stride;
   const int pg0 = s0 / page_size;
   const int npg = s0 < s1 ? (s1 - 1) / page_size - pg0 + 1 : 0;
-  for (int i = tid; i < min(npg, kMaxSplitPages); i += kThr) sbt[i] = bt[pg0 + i];
-  if (tid < 16) {
+  for (int i = tid; i < min(npg, kMaxSplitPages); i += THR) sbt[i] = bt[pg0 + i];
+  if (tid < R) {
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.f;
     lim_s[tid] = row_lim(tid);
@@ -134,7 +144,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
   auto load_tile = [&](int k) {
     const int t0 = s0 + k * TT;
     __nv_bfloat16* dst = ks + (k & 1) * TT * RSK;
-    for (int c = tid; c < TT * (DK / 8); c += kThr) {
+    for (int c = tid; c < TT * (DK / 8); c += THR) {
       const int row = c / (DK / 8), col = (c % (DK / 8)) * 8;
       const int tok = t0 + row;
       const bool ok = tok < s1;
@@ -151,12 +161,12 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     const __nv_bfloat16* qr[2];
 #pragma unroll
     for (int rh = 0; rh < 2; ++rh) {
-      const int row = gq + rh * 8;
+      const int row = grp * 16 + gq + rh * 8;
       qr[rh] = row < hn ? q + (size_t)row_tok(row) * q_stride + (size_t)row_head(row) * DK : nullptr;
     }
 #pragma unroll
     for (int kk = 0; kk < 9; ++kk) {
-      const int k0 = (warp * 9 + kk) * 16;
+      const int k0 = (wq * 9 + kk) * 16;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int col = k0 + qd * 2 + (r >> 1) * 8;
@@ -176,30 +186,33 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     __syncthreads();
     const __nv_bfloat16* kt = ks + (k & 1) * TT * RSK;
     const int t0 = s0 + k * TT;
-    // 1. partial scores over this warp's quarter of the 576-wide contraction
+    // 1. partial scores over this warp's quarter of the 576-wide contraction (its group's 16 rows)
+    float* spg = sp + grp * 4 * 16 * TT;
     float sc[4][4];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < 9; ++kk) {
-        const __nv_bfloat16* kr = kt + (nt * 8 + gq) * RSK + (warp * 9 + kk) * 16 + qd * 2;
+        const __nv_bfloat16* kr = kt + (nt * 8 + gq) * RSK + (wq * 9 + kk) * 16 + qd * 2;
         mma_bf16_16816(sc[nt], qa[kk], *reinterpret_cast<const uint32_t*>(kr),
                        *reinterpret_cast<const uint32_t*>(kr + 8));
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) sp[(warp * 16 + gq + (j >> 1) * 8) * TT + nt * 8 + qd * 2 + (j & 1)] = sc[nt][j];
+      for (int j = 0; j < 4; ++j) spg[(wq * 16 + gq + (j >> 1) * 8) * TT + nt * 8 + qd * 2 + (j & 1)] = sc[nt][j];
     }
     __syncthreads();
-    // 2. online softmax: thread -> (head row tid / 8, tokens 4 * (tid % 8) .. + 3)
+    // 2. online softmax: thread -> (group tid / 128, row (tid % 128) / 8, tokens 4 * (tid % 8) .. + 3)
     {
-      const int row = tid >> 3, c4 = (tid & 7) * 4;
+      const int g2 = tid >> 7, lrow = (tid & 127) >> 3, row = g2 * 16 + lrow, c4 = (tid & 7) * 4;
+      const float* spr = sp + g2 * 4 * 16 * TT;
+      __nv_bfloat16* psr = ps + g2 * 16 * RSP;
       float s[4], mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int col = c4 + j;
-        float v = sp[row * TT + col] + sp[(16 + row) * TT + col] + sp[(32 + row) * TT + col] +
-                  sp[(48 + row) * TT + col];
+        float v = spr[lrow * TT + col] + spr[(16 + lrow) * TT + col] + spr[(32 + lrow) * TT + col] +
+                  spr[(48 + lrow) * TT + col];
         v = (t0 + col < s1 && logical(t0 + col) < lim_s[row]) ? v * scale_log2 : -INFINITY;
         s[j] = v;
         mx = fmaxf(mx, v);
@@ -215,7 +228,7 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
       for (int j = 0; j < 4; ++j) {
         const float p = s[j] == -INFINITY ? 0.f : exp2f(s[j] - m_new);
         rs += p;
-        ps[row * RSP + c4 + j] = __float2bfloat16(p);
+        psr[lrow * RSP + c4 + j] = __float2bfloat16(p);
       }
       rs += __shfl_xor_sync(0xffffffffu, rs, 1);
       rs += __shfl_xor_sync(0xffffffffu, rs, 2);
@@ -228,9 +241,10 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
       }
     }
     __syncthreads();
-    // 3. O = alpha O + P V over this warp's 128 value columns
+    // 3. O = alpha O + P V over this warp's 128 value columns of its group's rows
     {
-      const float a0 = alpha_s[gq], a1 = alpha_s[gq + 8];
+      const float a0 = alpha_s[grp * 16 + gq], a1 = alpha_s[grp * 16 + gq + 8];
+      const __nv_bfloat16* psg = ps + grp * 16 * RSP;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         o[n][0] *= a0;
@@ -241,13 +255,13 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk) {
         uint32_t pa[4];
-        pa[0] = *reinterpret_cast<const uint32_t*>(ps + gq * RSP + kk * 16 + qd * 2);
-        pa[1] = *reinterpret_cast<const uint32_t*>(ps + (gq + 8) * RSP + kk * 16 + qd * 2);
-        pa[2] = *reinterpret_cast<const uint32_t*>(ps + gq * RSP + kk * 16 + 8 + qd * 2);
-        pa[3] = *reinterpret_cast<const uint32_t*>(ps + (gq + 8) * RSP + kk * 16 + 8 + qd * 2);
+        pa[0] = *reinterpret_cast<const uint32_t*>(psg + gq * RSP + kk * 16 + qd * 2);
+        pa[1] = *reinterpret_cast<const uint32_t*>(psg + (gq + 8) * RSP + kk * 16 + qd * 2);
+        pa[2] = *reinterpret_cast<const uint32_t*>(psg + gq * RSP + kk * 16 + 8 + qd * 2);
+        pa[3] = *reinterpret_cast<const uint32_t*>(psg + (gq + 8) * RSP + kk * 16 + 8 + qd * 2);
         // V fragments by transposing loads: lane l addresses token kk*16 + 8 ((l >> 3) & 1) + (l & 7) of the
         // n-tile pair member l >> 4, giving b0 / b1 of two n8 tiles per instruction
-        const uint32_t vrow = snb::smem_u32(kt + (kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * RSK + warp * 128 +
+        const uint32_t vrow = snb::smem_u32(kt + (kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * RSK + wq * 128 +
                                             (lane >> 4) * 8);
 #pragma unroll
         for (int n = 0; n < 16; n += 2) {
@@ -261,10 +275,10 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     __syncthreads();  // the stage and P are reused by the next tile
     if (k + 2 < ntiles) load_tile(k + 2);
   }
-  // write: rows gq / gq + 8, columns warp * 128 + n * 8 + qd * 2 + {0, 1}
+  // write: rows gq / gq + 8 of the warp's group, columns wq * 128 + n * 8 + qd * 2 + {0, 1}
 #pragma unroll
   for (int rh = 0; rh < 2; ++rh) {
-    const int row = gq + rh * 8;
+    const int row = grp * 16 + gq + rh * 8;
     if (row >= hn) continue;
     const float L = l_s[row], M = m_s[row];
     const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -272,18 +286,18 @@ __global__ void __launch_bounds__(kThr) mla_decode_kernel(
     const int tok = row_tok(row);
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
-      const int col = warp * 128 + n * 8 + qd * 2;
+      const int col = wq * 128 + n * 8 + qd * 2;
       const float x0 = o[n][rh * 2] * inv, x1 = o[n][rh * 2 + 1] * inv;
       if (num_splits == 1) {
         *reinterpret_cast<__nv_bfloat162*>(out + (size_t)tok * out_stride + (size_t)h * DV + col) =
             __floats2bfloat162_rn(x0, x1);
-        if (lse_out != nullptr && warp == 0 && n == 0 && qd == 0)
+        if (lse_out != nullptr && wq == 0 && n == 0 && qd == 0)
           lse_out[(size_t)tok * H + h] = L > 0.f ? M + log2f(L) : -INFINITY;
       } else {
         const size_t pidx = ((size_t)b * H + h) * num_splits + split;
         o_part[pidx * DV + col] = x0;
         o_part[pidx * DV + col + 1] = x1;
-        if (warp == 0 && n == 0 && qd == 0) lse_part[pidx] = L > 0.f ? M + log2f(L) : -INFINITY;
+        if (wq == 0 && n == 0 && qd == 0) lse_part[pidx] = L > 0.f ? M + log2f(L) : -INFINITY;
       }
     }
   }
@@ -327,13 +341,15 @@ void mla_decode(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
   auto st = at::cuda::getCurrentCUDAStream();
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mla_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        MlaCfg<1>::SMEM));
     attr = true;
   }
   dim3 grid(S, (H + 15) / 16, B);
   float* op = S > 1 ? o_part.data_ptr<float>() : nullptr;
   float* lp = S > 1 ? lse_part.data_ptr<float>() : nullptr;
-  C10_CUDA_CHECK(snb::launch_pdl(mla_decode_kernel, grid, kThr, SMEM_TOTAL, st, (const __nv_bfloat16*)q.data_ptr(),
+  C10_CUDA_CHECK(snb::launch_pdl(mla_decode_kernel<1>, grid, MlaCfg<1>::THR, MlaCfg<1>::SMEM, st,
+                                 (const __nv_bfloat16*)q.data_ptr(),
                                  (int)q.stride(0), (const __nv_bfloat16*)cache.data_ptr(),
                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                  seq_lens.data_ptr<int32_t>(), (int)page_size, H, (float)sm_scale * kLog2e,
@@ -360,19 +376,22 @@ void mla_extend(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::
   TORCH_CHECK(qo_indptr.scalar_type() == at::kInt && qo_indptr.numel() >= B + 1, "mla_extend: qo_indptr");
   TORCH_CHECK(seq_lens.scalar_type() == at::kInt && block_table.scalar_type() == at::kInt, "mla_extend: int32 tables");
   auto st = at::cuda::getCurrentCUDAStream();
+  constexpr int kExtMT = 2;
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mla_decode_kernel<kExtMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        MlaCfg<kExtMT>::SMEM));
     attr = true;
   }
   TORCH_CHECK(dcp_size >= 1 && dcp_rank >= 0 && dcp_rank < dcp_size, "mla_extend: dcp rank");
   if (lse_out)
     TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->is_contiguous() && lse_out->numel() >= (int64_t)T * H,
                 "mla_extend: lse_out");
-  const int64_t groups = (std::max<int64_t>(1, max_extend) * H + 15) / 16;
+  const int64_t groups = (std::max<int64_t>(1, max_extend) * H + 16 * kExtMT - 1) / (16 * kExtMT);
   TORCH_CHECK(groups <= 65535, "mla_extend: too many rows per request");
   dim3 grid(1, (unsigned)groups, B);
-  C10_CUDA_CHECK(snb::launch_pdl(mla_decode_kernel, grid, kThr, SMEM_TOTAL, st, (const __nv_bfloat16*)q.data_ptr(),
+  C10_CUDA_CHECK(snb::launch_pdl(mla_decode_kernel<kExtMT>, grid, MlaCfg<kExtMT>::THR, MlaCfg<kExtMT>::SMEM, st,
+                                 (const __nv_bfloat16*)q.data_ptr(),
                                  (int)q.stride(0), (const __nv_bfloat16*)cache.data_ptr(),
                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                  seq_lens.data_ptr<int32_t>(), (int)page_size, H, (float)sm_scale * kLog2e,
