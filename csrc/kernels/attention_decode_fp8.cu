@@ -591,8 +591,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tok_kernel(
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             if (h < G) {
-              const __nv_bfloat162 v =
-                  *reinterpret_cast<const __nv_bfloat162*>(qh + (size_t)h * D + qd * KB + ks * 4 + e * 2);
+              // dim of contraction column (ks, 2qd + 8e): e4m3 -> qd*KB + 4ks + 2e (contiguous per thread);
+              // bf16 -> (4 (ks / 2) + qd) * 8 + 4 (ks % 2) + 2e (interleaved 16-byte chunks, as K is read)
+              const int dq = ES == 1 ? qd * KB + ks * 4 + e * 2 : ((ks >> 1) * 4 + qd) * 8 + (ks & 1) * 4 + e * 2;
+              const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(qh + (size_t)h * D + dq);
               if constexpr (ES == 1) {
                 qb[ng][ks][e] =
                     f32x2_to_f16x2(__bfloat162float(v.x) * scale_log2, __bfloat162float(v.y) * scale_log2);
@@ -628,20 +630,42 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tok_kernel(
       const uint8_t* vt = ring + s * C::STAGE + TILE * RB + warp * TPW * RB;
       const int tw = s0 + k * TILE + warp * TPW;  // first token of this warp's TPW
       const bool whole = tw >= lo && tw + TPW <= s1;
-      // K rows krow0 / krow1 of each 16-token block: KBB bytes at qd*KBB
+      // K rows krow0 / krow1 of each 16-token block. e4m3: KBB contiguous bytes at qd*KBB. bf16: the thread's
+      // 16-byte chunks c sit at (4c + qd) * 16 (interleaved with the other lanes of its row), and lanes of odd
+      // gq fetch them in XOR-1 order, then swap back with selects: the two rows a quarter-warp reads land in
+      // different banks (256-byte rows all start at bank 0).
+      constexpr int NKC = KBB / 16;
       uint32_t kw[U][2][KBB / 4];
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int r = 0; r < 2; ++r) {
+          const uint8_t* krow = kt + (u * 16 + (r ? krow1 : krow0)) * RB;
+          if constexpr (ES == 1) {
 #pragma unroll
-          for (int i = 0; i < KBB / 16; ++i) {
-            const uint4 a = *reinterpret_cast<const uint4*>(kt + (u * 16 + (r ? krow1 : krow0)) * RB + qd * KBB + i * 16);
-            kw[u][r][i * 4] = a.x;
-            kw[u][r][i * 4 + 1] = a.y;
-            kw[u][r][i * 4 + 2] = a.z;
-            kw[u][r][i * 4 + 3] = a.w;
+            for (int i = 0; i < NKC; ++i) {
+              const uint4 a = *reinterpret_cast<const uint4*>(krow + qd * KBB + i * 16);
+              kw[u][r][i * 4] = a.x;
+              kw[u][r][i * 4 + 1] = a.y;
+              kw[u][r][i * 4 + 2] = a.z;
+              kw[u][r][i * 4 + 3] = a.w;
+            }
+          } else {
+            const int rot = NKC > 1 ? (gq & 1) : 0;
+            uint4 t[NKC];
+#pragma unroll
+            for (int i = 0; i < NKC; ++i)
+              t[i] = *reinterpret_cast<const uint4*>(krow + (((NKC > 1 ? (i ^ rot) : i) * 4 + qd) * 16));
+#pragma unroll
+            for (int i = 0; i < NKC; ++i) {
+              const uint4 a = rot ? t[NKC > 1 ? (i ^ 1) : i] : t[i];
+              kw[u][r][i * 4] = a.x;
+              kw[u][r][i * 4 + 1] = a.y;
+              kw[u][r][i * 4 + 2] = a.z;
+              kw[u][r][i * 4 + 3] = a.w;
+            }
           }
+        }
       // V rows qd + 4i of each block: VBB bytes at gq*VBB; tokens outside [lo, s1) zeroed (stale page bytes)
       uint32_t vw[U][4][VBB / 4];
 #pragma unroll
@@ -656,9 +680,16 @@ __global__ void __launch_bounds__(kThreads) decode_attn_tok_kernel(
             vw[u][i][0] = ok ? v.x : 0u;
             vw[u][i][1] = ok ? v.y : 0u;
           } else {
+            // two or more chunks: lanes of odd qd fetch them in XOR-1 order (the four rows of a quarter-warp share
+            // bank offsets) and swap back with selects
+            constexpr int NVC = VBB / 16;
+            const int rot = NVC > 1 ? (qd & 1) : 0;
+            uint4 t[NVC];
 #pragma unroll
-            for (int c = 0; c < VBB / 16; ++c) {
-              const uint4 v = reinterpret_cast<const uint4*>(src)[c];
+            for (int c = 0; c < NVC; ++c) t[c] = reinterpret_cast<const uint4*>(src)[NVC > 1 ? (c ^ rot) : c];
+#pragma unroll
+            for (int c = 0; c < NVC; ++c) {
+              const uint4 v = rot ? t[NVC > 1 ? (c ^ 1) : c] : t[c];
               vw[u][i][c * 4] = ok ? v.x : 0u;
               vw[u][i][c * 4 + 1] = ok ? v.y : 0u;
               vw[u][i][c * 4 + 2] = ok ? v.z : 0u;
