@@ -9,7 +9,9 @@ page's heads are contiguous, so a prefill rank copies exactly the overlap of its
 rank's (any TP sizes on the two sides; a head held by several prefill ranks is sent by the lowest of them).
 Settle-then-ack: a prefill rank posts pd/done/<seq>/<src>/<dst> only after its copy kernel completed, and a
 decode rank admits the request once every done key it expects exists. On the CPU tier the data plane is
-gloo send/recv of a packed buffer.
+gloo send/recv of packed head slices along the same plan (whole pages rank to rank when both groups shard
+alike). The two groups may differ in TP size: launch them as DP replicas with `replica_tp_sizes` (prefill first)
+and give each PDLink the other group's size.
 
 Parity: the reference's PD path (sglang_neuron/disaggregation/*, sglang_patches/nixl_*, pd_*): the decode
 side pre-allocates pages and publishes where the KV must land (TransferInfo), the prefill side writes the
@@ -70,6 +72,35 @@ def scatter_pages(pool, pages: torch.Tensor, buf: torch.Tensor) -> None:
     for li, (k, v) in enumerate(zip(_k_buffers(pool), _v_buffers(pool))):
         k.index_copy_(0, pages, buf[li, 0])
         v.index_copy_(0, pages, buf[li, 1])
+
+
+def _is_mha(pool) -> bool:
+    return hasattr(pool, "k_buffers")
+
+
+def head_slice(pool, buf: torch.Tensor, off_bytes: int, nbytes: int) -> torch.Tensor:
+    """The heads [off, off + n) of a packed [L, 2, n_pages, heads, page, D] buffer (byte offsets within a page,
+    as slice_plan gives them), contiguous; the whole buffer when the slice covers every head (and for latent
+    pools, whose page is one 'head')."""
+    geo = pool_geometry(pool, 0)
+    h0, nh = off_bytes // geo["head_bytes"], nbytes // geo["head_bytes"]
+    if not _is_mha(pool) or (h0 == 0 and nh == geo["heads"]):
+        return buf
+    return buf[:, :, :, h0:h0 + nh].contiguous()
+
+
+def scatter_head_slice(pool, pages: torch.Tensor, buf: torch.Tensor, off_bytes: int, nbytes: int) -> None:
+    """Write a packed head slice (head_slice's layout) into the given pages at heads [off, off + n)."""
+    geo = pool_geometry(pool, 0)
+    h0, nh = off_bytes // geo["head_bytes"], nbytes // geo["head_bytes"]
+    if not _is_mha(pool) or (h0 == 0 and nh == geo["heads"]):
+        scatter_pages(pool, pages, buf)
+        return
+    for li, (k, v) in enumerate(zip(_k_buffers(pool), _v_buffers(pool))):
+        for src, dst in ((buf[li, 0], k), (buf[li, 1], v)):
+            rows = dst.index_select(0, pages)
+            rows[:, h0:h0 + nh] = src
+            dst.index_copy_(0, pages, rows)
 
 
 def _k_buffers(pool):
@@ -187,10 +218,15 @@ class PeerPools:
 class PDLink:
     """Store-based control plane + rank-to-rank data plane between the two groups."""
 
-    def __init__(self, role: str, tp_size: int, store, timeout_s: float = 60.0):
+    def __init__(self, role: str, tp_size: int, store, timeout_s: float = 60.0, peer_tp: Optional[int] = None):
+        """tp_size: this group's TP size; peer_tp: the other group's (default: the same). The prefill group holds
+        global ranks [0, n_prefill), the decode group the n_decode ranks after it."""
         st = get_state()
         self.role = role
         self.tp = tp_size
+        other = tp_size if peer_tp is None else int(peer_tp)
+        self.n_prefill = tp_size if role == "prefill" else other
+        self.n_decode = tp_size if role == "decode" else other
         self.store = store
         self.timeout_s = timeout_s
         self.peer = (st.tp_rank + tp_size) if role == "prefill" else st.tp_rank
@@ -262,6 +298,33 @@ class PDLink:
             work = dist.irecv(buf, self.peer)
         return Transfer(work)
 
+    def prefill_rank(self, i: int) -> int:
+        return i
+
+    def decode_rank(self, j: int) -> int:
+        return self.n_prefill + j
+
+    def send_to(self, buf: torch.Tensor, dst: int):
+        peer, self.peer = self.peer, dst
+        try:
+            return self.send(buf)
+        finally:
+            self.peer = peer
+
+    def recv_from(self, buf: torch.Tensor, src: int):
+        peer, self.peer = self.peer, src
+        try:
+            return self.recv(buf)
+        finally:
+            self.peer = peer
+
+    def done_all(self, works) -> bool:
+        return all(self.done(w) for w in works)
+
+    def finish_all(self, works) -> None:
+        for w in works:
+            self.finish(w)
+
 
 def _head_start(engine) -> int:
     a = engine.runner.model.attention_layers()[0]
@@ -285,26 +348,27 @@ class PrefillSide:
         self._orig_finish = sched._finish
         sched._finish = self._on_finish  # keep pages of finished prefills until their KV left
         self.peers: Optional[PeerPools] = None
-        self.plan: List[Tuple[int, int, int, int, int]] = []
+        self.plan: Optional[List[Tuple[int, int, int, int, int]]] = None
+        pool = engine.runner.kv_pool
+        self.geo = pool_geometry(pool, _head_start(engine))
+        link.put(f"pd/pgeo/{link.tp_rank}", self.geo)
         if link.p2p:
-            pool = engine.runner.kv_pool
-            self.geo = pool_geometry(pool, _head_start(engine))
-            link.put(f"pd/pgeo/{link.tp_rank}", self.geo)
             self.src_bases = torch.tensor([b.data_ptr() for b in _pool_buffers(pool)], dtype=torch.int64,
                                           device=link.device)
 
     def _ensure_peers(self) -> None:
-        """Map the decode group's pools (once every decode rank exported them) and keep this rank's rows of the
-        head-slice plan."""
-        if self.peers is not None:
+        """Keep this rank's rows of the head-slice plan (once every decode rank published its pool) and, on
+        GPUs, map the decode group's pools."""
+        if self.plan is not None:
             return
         link = self.link
-        n_dec, n_pre = link.tp, link.tp
+        n_dec, n_pre = link.n_decode, link.n_prefill
         link.wait_keys([f"pd/ipc/{j}" for j in range(n_dec)] + [f"pd/pgeo/{i}" for i in range(n_pre)])
         metas = [link.get(f"pd/ipc/{j}") for j in range(n_dec)]
         pgeo = [link.get(f"pd/pgeo/{i}") for i in range(n_pre)]
         self.plan = [p for p in slice_plan(pgeo, metas) if p[0] == link.tp_rank]
-        self.peers = PeerPools(metas, link.device)
+        if link.p2p:
+            self.peers = PeerPools(metas, link.device)
 
     def _send_p2p(self, seq: int, pages: List[int], dst_pages: List[int]):
         """One copy launch per destination rank on the transfer stream; returns (event, done keys)."""
@@ -371,10 +435,18 @@ class PrefillSide:
                     ev, keys, keep = self._send_p2p(seq, pages, list(status[1]))
                     self.sending.append((seq, (ev, keys), keep, r))
                     continue
+                # packed transfer (CPU tier): this rank's head slice of the pages to every decode rank that holds
+                # those heads (the whole pages rank to rank when both groups shard alike)
+                self._ensure_peers()
+                pool = self.engine.runner.kv_pool
                 idx = torch.tensor(pages, dtype=torch.long, device=self.link.device)
-                buf = gather_pages(self.engine.runner.kv_pool, idx)
-                work = self.link.send(buf)
-                self.sending.append((seq, work, buf, r))
+                buf = gather_pages(pool, idx)
+                works, keep = [], []
+                for _i, j, so, _do, nb in self.plan:
+                    piece = head_slice(pool, buf, so, nb)
+                    works.append(self.link.send_to(piece, self.link.decode_rank(j)))
+                    keep.append(piece)
+                self.sending.append((seq, works, keep, r))
             elif time.time() - t0 > self.link.timeout_s:
                 # peer never acknowledged: abort and free (nothing was sent, nothing can land)
                 del self.pending[seq]
@@ -393,7 +465,7 @@ class PrefillSide:
                     self.sent += 1
                 else:
                     still.append((seq, work, buf, r))
-            elif self.link.done(work):
+            elif self.link.done_all(work):
                 self._release(r)
                 self.sent += 1
             else:
@@ -421,19 +493,25 @@ class DecodeSide:
         # (sglang_neuron/disaggregation/poll_reduce.py:68-108).
         from ..managers.scheduler import _make_shm
         self._poll = _make_shm(get_state(), POLL_WIDTH, "pdpoll")
-        self._expect: Optional[List[Tuple[int, int]]] = None  # (src rank, dst rank) rows feeding this rank
+        self._rows: Optional[List[Tuple[int, int, int, int, int]]] = None  # plan rows feeding this rank
         self.on_admit = None  # test seam: called with (header, pages) when a request's KV has landed
-        if link.p2p:
-            link.put(f"pd/ipc/{link.tp_rank}", export_pool(engine.runner.kv_pool, _head_start(engine)))
+        pool = engine.runner.kv_pool
+        link.put(f"pd/ipc/{link.tp_rank}", export_pool(pool, _head_start(engine)) if link.p2p
+                 else pool_geometry(pool, _head_start(engine)))
+
+    def _plan_rows(self) -> List[Tuple[int, int, int, int, int]]:
+        """The head-slice plan rows whose destination is this rank (once both groups published their pools)."""
+        if self._rows is None:
+            link = self.link
+            link.wait_keys([f"pd/ipc/{j}" for j in range(link.n_decode)] +
+                           [f"pd/pgeo/{i}" for i in range(link.n_prefill)])
+            metas = [link.get(f"pd/ipc/{j}") for j in range(link.n_decode)]
+            pgeo = [link.get(f"pd/pgeo/{i}") for i in range(link.n_prefill)]
+            self._rows = [p for p in slice_plan(pgeo, metas) if p[1] == link.tp_rank]
+        return self._rows
 
     def _done_keys(self, seq: int) -> List[str]:
-        if self._expect is None:
-            link = self.link
-            link.wait_keys([f"pd/ipc/{j}" for j in range(link.tp)] + [f"pd/pgeo/{i}" for i in range(link.tp)])
-            metas = [link.get(f"pd/ipc/{j}") for j in range(link.tp)]
-            pgeo = [link.get(f"pd/pgeo/{i}") for i in range(link.tp)]
-            self._expect = [(i, j) for i, j, *_ in slice_plan(pgeo, metas) if j == link.tp_rank]
-        return [f"pd/done/{seq}/{i}/{j}" for i, j in self._expect]
+        return [f"pd/done/{seq}/{i}/{j}" for i, j, *_ in self._plan_rows()]
 
     def poll(self) -> None:
         sched = self.engine.scheduler
@@ -467,9 +545,16 @@ class DecodeSide:
                 if self.link.is_leader:
                     self.link.put(f"pd/ready/{h.seq}", ("ready", list(pages)))
             else:
-                buf = torch.empty(page_buffer_shape(self.engine.runner.kv_pool, h.n_pages),
-                                  dtype=self.engine.runner.kv_pool.dtype, device=self.link.device)
-                work = self.link.recv(buf)
+                # packed transfer (CPU tier): one receive per prefill rank holding some of this rank's heads
+                pool = self.engine.runner.kv_pool
+                shape = page_buffer_shape(pool, h.n_pages)
+                head_bytes = pool_geometry(pool, 0)["head_bytes"]
+                work, buf = [], []
+                for i, _j, _so, do, nb in self._plan_rows():
+                    shp = shape[:3] + (nb // head_bytes,) + shape[4:] if _is_mha(pool) else shape
+                    b = torch.empty(shp, dtype=pool.dtype, device=self.link.device)
+                    work.append(self.link.recv_from(b, self.link.prefill_rank(i)))
+                    buf.append((do, nb, b))
                 if self.link.is_leader:
                     self.link.put(f"pd/ready/{h.seq}", "ready")
             self.receiving.append((h, work, buf, pages, sched.epoch, time.time()))
@@ -479,7 +564,7 @@ class DecodeSide:
         if self._poll is not None:
             items = self.receiving[:POLL_WIDTH]
             now = time.time()
-            states = [2 if self.link.done(work) else (0 if now - t0 > self.link.timeout_s else 1)
+            states = [2 if self._done(work) else (0 if now - t0 > self.link.timeout_s else 1)
                       for _h, work, _b, _p, _e, t0 in items]
             red = self._poll.min(states + [2] * (POLL_WIDTH - len(states)), timeout_s=1800.0)
             for (h, *_rest), s in zip(items, red):
@@ -489,7 +574,7 @@ class DecodeSide:
                     done_seqs.append(-h.seq - 1)  # abort marker
         elif self.link.is_leader:
             for h, work, buf, pages, _e, t0 in self.receiving:
-                if self.link.done(work):
+                if self._done(work):
                     done_seqs.append(h.seq)
                 elif time.time() - t0 > self.link.timeout_s:
                     done_seqs.append(-h.seq - 1)  # abort marker
@@ -500,7 +585,10 @@ class DecodeSide:
         for item in self.receiving:
             h, work, buf, pages, _e, _t = item
             if h.seq in done_seqs:
-                self.link.finish(work)
+                if isinstance(work, list):
+                    self.link.finish_all(work)
+                else:
+                    self.link.finish(work)
                 self._admit(h, buf, pages)
             elif (-h.seq - 1) in done_seqs:
                 self.quarantined += pages  # the peer may still write them: never reuse
@@ -512,11 +600,12 @@ class DecodeSide:
     def _admit(self, h: Header, buf: torch.Tensor, pages: List[int]) -> None:
         sched = self.engine.scheduler
         runner = self.engine.runner
-        if buf is not None:  # packed transfer (CPU tier); P2P copies already landed in the pages
+        if buf is not None:  # packed head slices (CPU tier); P2P copies already landed in the pages
             idx = torch.tensor(pages, dtype=torch.long, device=self.link.device)
             if self.link.stream is not None:
                 torch.cuda.current_stream(self.link.device).wait_stream(self.link.stream)
-            scatter_pages(runner.kv_pool, idx, buf)
+            for do, nb, b in buf:
+                scatter_head_slice(runner.kv_pool, idx, b, do, nb)
         if self.on_admit is not None:
             self.on_admit(h, pages)
         r = Req(h.rid, h.prompt, h.params, eos_ids=[] if h.params.ignore_eos else sched.eos)
@@ -536,6 +625,9 @@ class DecodeSide:
             sched._finish(r, "length")
         else:
             sched.running.append(r)
+
+    def _done(self, work) -> bool:
+        return self.link.done_all(work) if isinstance(work, list) else self.link.done(work)
 
     def step(self) -> None:
         self.poll()

@@ -64,7 +64,8 @@ class Engine:
             raise ValueError("decode context parallelism splits the latent (MLA) KV pool; "
                              f"{self.cfg.architecture} has none")
         st = initialize_parallel(args.tp_size, args.ep_size, args.dp_size, device, pp_size=args.pp_size,
-                                 dp_attention=args.enable_dp_attention, dcp_size=args.dcp_size)
+                                 dp_attention=args.enable_dp_attention, dcp_size=args.dcp_size,
+                                 replica_tp=args.replica_tp_sizes)
         self.rank = st.rank
         self.custom_ar = None
         if st.tp_size > 1 and device.type == "cuda":

@@ -183,7 +183,8 @@ class ModelRunner:
         from ..parallel.contract import assert_fleet_consistent
         self.fleet_digest = assert_fleet_consistent({
             "arch": cfg.architecture, "layers": cfg.num_layers, "hidden": cfg.hidden_size,
-            "windows": [cfg.layer_window(i) for i in range(cfg.num_layers)], "tp": st.tp_size, "pp": st.pp_size,
+            "windows": [cfg.layer_window(i) for i in range(cfg.num_layers)],
+            "tp": list(st.replica_tp) if st.replica_tp else st.tp_size, "pp": st.pp_size,
             "dp": st.dp_size, "page": args.page_size, "kv": str(args.kv_cache_dtype), "dtype": str(self.dtype),
             "spec": args.speculative_algorithm or ""})
         self.page_size = args.page_size

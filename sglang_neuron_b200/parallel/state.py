@@ -24,7 +24,7 @@ from __future__ import annotations
 import dataclasses
 import os
 from datetime import timedelta
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -54,6 +54,8 @@ class ParallelState:
     dcp_size: int = 1                           # decode context parallelism: ranks sharing one latent KV
     dcp_rank: int = 0
     dcp_group: Optional[object] = None          # consecutive TP ranks tp_rank // dcp_size
+    replica_base_rank: int = -1                 # set when replicas differ in size (see initialize_replicas)
+    replica_tp: tuple = ()                      # every replica's TP size when they differ (rank order)
 
     @property
     def is_first_rank(self) -> bool:
@@ -70,6 +72,8 @@ class ParallelState:
     @property
     def replica_base(self) -> int:
         """Global rank of this replica's rank 0."""
+        if self.replica_base_rank >= 0:
+            return self.replica_base_rank
         return self.dp_rank * self.replica_size
 
     @property
@@ -126,9 +130,20 @@ def init_process_group_from_env(backend: Optional[str] = None, timeout_s: int = 
 
 def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size: int = 1,
                         device: Optional[torch.device] = None, pp_size: int = 1,
-                        dp_attention: bool = False, dcp_size: int = 1) -> ParallelState:
+                        dp_attention: bool = False, dcp_size: int = 1,
+                        replica_tp: Optional[Sequence[int]] = None) -> ParallelState:
     """Build the groups. Ranks are laid out DP-major, then PP: rank = (dp_rank * pp_size + pp_rank) * tp_size
-    + tp_rank. With dp_attention, dp_size attention groups split the tp_size ranks instead (one replica)."""
+    + tp_rank. With dp_attention, dp_size attention groups split the tp_size ranks instead (one replica).
+    With replica_tp, the DP replicas have the given tensor-parallel sizes (see initialize_replicas)."""
+    if replica_tp:
+        if pp_size != 1 or dp_attention or dcp_size != 1 or len(replica_tp) != dp_size:
+            raise ValueError("replicas of different TP sizes take one pipeline stage, no DP attention or DCP, and "
+                             "dp_size equal to the number of replicas")
+        st = initialize_replicas(replica_tp, device)
+        if st.tp_size != tp_size or (ep_size not in (None, tp_size)):
+            raise ValueError(f"rank {st.rank} belongs to a TP{st.tp_size} replica but was launched with tp_size "
+                             f"{tp_size}")
+        return st
     if dp_attention and dp_size > 1:
         return _initialize_dp_attention(tp_size, ep_size, dp_size, device, pp_size)
     ep_size = tp_size if ep_size is None else ep_size
@@ -179,6 +194,38 @@ def initialize_parallel(tp_size: int = 1, ep_size: Optional[int] = None, dp_size
                        cpu_group=cpu_group, device=device, pp_size=pp_size, pp_rank=pp_rank,
                        replica_group=replica_group, replica_cpu_group=replica_cpu_group,
                        dcp_size=dcp_size, dcp_rank=tp_rank % dcp_size, dcp_group=dcp_group)
+    set_state(st)
+    return st
+
+
+def initialize_replicas(replica_tp: Sequence[int], device: Optional[torch.device] = None) -> ParallelState:
+    """DP replicas of different tensor-parallel sizes, laid out in order: replica r holds ranks
+    [sum(replica_tp[:r]), sum(replica_tp[:r + 1])). Used by disaggregated prefill/decode on one box, where the
+    prefill group and the decode group may shard attention differently (the KV hand-off slices pages by head).
+    Experts span each replica's TP group, as in initialize_parallel."""
+    sizes = [int(t) for t in replica_tp]
+    if not sizes or min(sizes) < 1:
+        raise ValueError(f"replica_tp {replica_tp}: every replica needs at least one rank")
+    world, rank = (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
+    if sum(sizes) != world:
+        raise ValueError(f"replica TP sizes {sizes} sum to {sum(sizes)}, not the world size {world}")
+    bases = [sum(sizes[:r]) for r in range(len(sizes))]
+    dp_rank = max(r for r in range(len(sizes)) if bases[r] <= rank)
+    tp_size, tp_rank = sizes[dp_rank], rank - bases[dp_rank]
+    tp_group = cpu_group = None
+    if world > 1:
+        for r, (b, t) in enumerate(zip(bases, sizes)):  # every rank creates every group, in the same order
+            ranks = list(range(b, b + t))
+            g = dist.new_group(ranks)
+            cg = dist.new_group(ranks, backend="gloo")
+            if r == dp_rank:
+                tp_group, cpu_group = g, cg
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    st = ParallelState(world_size=world, rank=rank, tp_size=tp_size, tp_rank=tp_rank, ep_size=tp_size,
+                       ep_rank=tp_rank, dp_size=len(sizes), dp_rank=dp_rank, tp_group=tp_group, cpu_group=cpu_group,
+                       device=device, replica_group=tp_group, replica_cpu_group=cpu_group,
+                       replica_base_rank=bases[dp_rank], replica_tp=tuple(sizes))
     set_state(st)
     return st
 

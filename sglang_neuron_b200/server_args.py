@@ -51,6 +51,8 @@ class ServerArgs:
     speculative_algorithm: Optional[str] = None   # None | "MTP"
     speculative_num_draft_tokens: int = 3
     disaggregation_mode: str = "null"        # null | prefill | decode
+    replica_tp_sizes: Optional[List[int]] = None  # DP replicas of different TP sizes, in rank order (PD on one box:
+                                                  # [prefill TP, decode TP]); tp_size is this rank's own replica's
     host: str = "127.0.0.1"
     port: int = 30000
     log_level: str = "info"
@@ -91,7 +93,7 @@ class ServerArgs:
             name = "--" + f.name.replace("_", "-")
             if f.type in ("bool", bool):
                 p.add_argument(name, action="store_true", default=f.default)
-            elif f.name == "cuda_graph_bs":
+            elif f.name in ("cuda_graph_bs", "replica_tp_sizes"):
                 p.add_argument(name, type=int, nargs="+", default=None)
             else:
                 typ = {"int": int, "float": float, "str": str}.get(str(f.type).replace("Optional[", "").rstrip("]"), str)

@@ -25,7 +25,7 @@ def _prompts():
     return [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (21, 40, 9)]
 
 
-def _engine(dp_size, tp_size=1):
+def _engine(dp_size, tp_size=1, replica_tp=None):
     from sglang_neuron_b200.configs import model_config as mc
     from sglang_neuron_b200.engine import Engine
     from sglang_neuron_b200.parallel.state import destroy_parallel
@@ -34,7 +34,7 @@ def _engine(dp_size, tp_size=1):
     mc.PRESETS["pd-tiny"] = dict(mc.PRESETS["qwen3-0.6b"], **TINY)
     return Engine(ServerArgs(model="pd-tiny", device="cpu", dtype="float32", tp_size=tp_size, dp_size=dp_size,
                              context_length=256, max_running_requests=4, chunked_prefill_size=32,
-                             random_weight_std=0.05))
+                             random_weight_std=0.05, replica_tp_sizes=replica_tp))
 
 
 def _worker(rank, port, drop_ack, q):
@@ -169,6 +169,77 @@ def test_pd_tp2_groups_match_aggregated():
     ref = _engine(1).generate(_prompts(), {"max_new_tokens": 7})
     assert res[0]["sent"] == 3 and res[1]["sent"] == 3
     for r in (2, 3):
+        assert [res[r][f"pd{i}"] for i in range(3)] == [o["output_ids"] for o in ref]
+
+
+def _worker_mixed_tp(rank, port, tp_p, tp_d, q):
+    """Prefill group of TP tp_p (ranks 0 .. tp_p - 1) and decode group of TP tp_d after it: the KV moves as
+    head slices of each page (every decode rank gets its heads from the prefill ranks that hold them)."""
+    world = tp_p + tp_d
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK="0")
+    import time
+    import torch.distributed as dist
+    from sglang_neuron_b200.disaggregation.pd import DecodeSide, PDLink, PrefillSide
+    from sglang_neuron_b200.managers.schedule_batch import SamplingParams
+    from sglang_neuron_b200.parallel.state import get_state
+    role = "prefill" if rank < tp_p else "decode"
+    own, other = (tp_p, tp_d) if role == "prefill" else (tp_d, tp_p)
+    eng = _engine(2, tp_size=own, replica_tp=[tp_p, tp_d])
+    store = dist.distributed_c10d._get_default_store()
+    link = PDLink(role, own, store, timeout_s=60.0, peer_tp=other)
+    group = get_state().cpu_group
+    result = None
+    t0 = time.time()
+    if role == "prefill":
+        side = PrefillSide(eng, link)
+        for i, p in enumerate(_prompts()):
+            side.submit(f"pd{i}", p, SamplingParams(max_new_tokens=7))
+        while time.time() - t0 < 120:
+            side.step()
+            done = torch.tensor([int(side.sent == 3 and not side.pending and not side.sending)])
+            if group is not None:
+                dist.all_reduce(done, op=dist.ReduceOp.MIN, group=group)
+            if int(done):
+                break
+            time.sleep(0.001)
+        result = {"sent": side.sent, "aborted": sorted(side.aborted)}
+    else:
+        side = DecodeSide(eng, link)
+        want = {"pd0", "pd1", "pd2"}
+        while time.time() - t0 < 120:
+            side.step()
+            done = torch.tensor([int(want.issubset(eng.scheduler.finished_by_rid))])
+            if group is not None:
+                dist.all_reduce(done, op=dist.ReduceOp.MIN, group=group)
+            if int(done):
+                break
+            time.sleep(0.001)
+        eng.scheduler.drain()
+        result = {rid: eng.scheduler.finished_by_rid[rid].output_ids for rid in sorted(want)
+                  if rid in eng.scheduler.finished_by_rid}
+    q.put((rank, result))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tp_p,tp_d", [(1, 2), (2, 1)])
+def test_pd_groups_of_different_tp_sizes_match_aggregated(tp_p, tp_d):
+    """Prefill TP1 -> decode TP2 and prefill TP2 -> decode TP1 (two KV heads): every decode rank decodes the
+    same tokens as the aggregated engine."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker_mixed_tp, args=(r, port, tp_p, tp_d, q)) for r in range(tp_p + tp_d)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    ref = _engine(1).generate(_prompts(), {"max_new_tokens": 7})
+    for r in range(tp_p):
+        assert res[r]["sent"] == 3 and res[r]["aborted"] == []
+    for r in range(tp_p, tp_p + tp_d):
         assert [res[r][f"pd{i}"] for i in range(3)] == [o["output_ids"] for o in ref]
 
 
