@@ -2,9 +2,9 @@
 
 Parity: the reference keeps per-family config classes (sglang_neuron/models/transformer/config.py:13
 `TransformerConfig`, models/deepseek_v2/config.py, models/gpt_oss/config.py:29-72) and a catalog of
-ModelSpecs (models/catalog.py:41-144). Here a single dataclass covers the four BASELINE families and the
-named presets give the exact BASELINE.json shapes for random-init runs (no checkpoint download exists on
-this machine).
+ModelSpecs (models/catalog.py:41-144). Here a single dataclass covers the four benchmarked families and the
+named presets give the exact shapes of the benchmark configurations (Qwen3-0.6B/8B, Qwen3-30B-A3B,
+DeepSeek-V2-Lite, GPT-OSS-120B) for random-init runs where no checkpoint is at hand.
 """
 from __future__ import annotations
 
@@ -183,7 +183,7 @@ def _gpt_oss(layers: int, experts: int) -> Dict[str, Any]:
     }
 
 
-# BASELINE.json configurations (random-init shapes).
+# The benchmark configurations' model shapes (random-init runs).
 PRESETS: Dict[str, Dict[str, Any]] = {
     "qwen3-0.6b": {
         "architectures": ["Qwen3ForCausalLM"], "hidden_size": 1024, "num_hidden_layers": 28,
