@@ -46,3 +46,19 @@ class ForwardBatch:
     @property
     def is_decode(self) -> bool:
         return self.mode == ForwardMode.DECODE
+
+    def slice_decode(self, b0: int, b1: int) -> "ForwardBatch":
+        """Requests [b0, b1) of a plain decode step (one token per request, row i = request i) as a step of
+        their own: the same split count and context bound, fresh per-step caches."""
+        assert self.is_decode and self.spec_tokens == 1 and self.num_tokens == self.batch_size
+
+        def sl(t):
+            return None if t is None else t[b0:b1]
+
+        extra = {k: self.extra[k] for k in ("logprob_k", "dp_rows") if k in self.extra}
+        extra["num_decode"] = b1 - b0
+        return dataclasses.replace(
+            self, batch_size=b1 - b0, num_tokens=b1 - b0, input_ids=sl(self.input_ids), positions=sl(self.positions),
+            out_cache_loc=sl(self.out_cache_loc), seq_lens=sl(self.seq_lens), block_table=sl(self.block_table),
+            logits_idx=self.logits_idx[b0:b1] - b0, temperature=sl(self.temperature), seeds=sl(self.seeds),
+            top_k=sl(self.top_k), top_p=sl(self.top_p), extra=extra)

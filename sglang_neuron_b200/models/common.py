@@ -29,7 +29,8 @@ from ..ops import moe as moe_ops
 from ..ops.norm import fused_add_rmsnorm, rmsnorm
 from ..ops.rope import build_cos_sin_cache, rope_qk_norm_kv_write
 from ..parallel.collectives import (FusedNorm, deferred_reduction, dp_gather_rows, dp_scatter_rows,
-                                    fused_combine_all_reduce, pp_recv_hidden, pp_send_hidden, sp_all_gather,
+                                    fused_combine_all_reduce, pp_isend_hidden, pp_recv_hidden, pp_send_hidden,
+                                    sp_all_gather,
                                     sp_gather_rows, sp_reduce_scatter, tp_all_reduce)
 from ..parallel.state import get_state, pp_layer_range
 from .. import env_registry
@@ -342,6 +343,9 @@ class CausalLM(nn.Module):
         rows = self.sp_rows(fb)
         if rows:
             return self._forward_sp(fb, rows)
+        if (get_state().pp_size > 1 and fb.is_decode and fb.spec_tokens == 1 and fb.batch_size > 1
+                and fb.num_tokens == fb.batch_size):
+            return self._forward_pp_microbatched(fb)
         if self.first_stage:
             h = self.embed_tokens(fb.input_ids)
             residual = None
@@ -363,6 +367,43 @@ class CausalLM(nn.Module):
         r_last = residual.index_select(0, fb.logits_idx)
         h_last, pre = self.norm(h_last, r_last)
         self.last_prenorm = pre  # h + residual of the sampled rows (consumed by the MTP draft head)
+        return h_last
+
+    def _forward_pp_microbatched(self, fb: ForwardBatch) -> Optional[torch.Tensor]:
+        """Pipeline-parallel decode in micro-batches: the step's requests split into as many micro-batches as
+        there are stages; a stage sends micro-batch m to the next one without waiting and goes on with m + 1,
+        so the stages work on different micro-batches at the same time (P stages over M micro-batches take
+        about (M + P - 1) / M stage-times instead of P). Every row is computed as in the whole batch (same
+        split count, row-independent ops), so the tokens are the same. Parity: the reference's overlapped
+        PP seam (sglang_neuron/distributed/pp_seam.py:306)."""
+        P = get_state().pp_size
+        M = min(P, fb.batch_size)
+        bounds = [fb.batch_size * m // M for m in range(M + 1)]
+        sends, outs = [], []
+        n = len(self.layers)
+        for m in range(M):
+            sub = fb.slice_decode(bounds[m], bounds[m + 1])
+            if self.first_stage:
+                h, residual = self.embed_tokens(sub.input_ids), None
+            else:
+                h, residual = pp_recv_hidden(sub.num_tokens, self.cfg.hidden_size, self.dtype, self.device)
+            for i, layer in enumerate(self.layers):
+                nxt = self.layers[i + 1].input_layernorm if i + 1 < n else None
+                h, residual = layer(h, residual, sub, next_norm=nxt)
+            if residual is None:
+                residual = torch.zeros_like(h)
+            if not self.last_stage:
+                sends.append(pp_isend_hidden(h, residual))
+            else:
+                outs.append((h, residual))
+        for work, _buf in sends:
+            work.wait()
+        if not self.last_stage:
+            return None
+        h = torch.cat([o[0] for o in outs])
+        residual = torch.cat([o[1] for o in outs])
+        h_last, pre = self.norm(h.index_select(0, fb.logits_idx), residual.index_select(0, fb.logits_idx))
+        self.last_prenorm = pre
         return h_last
 
     def forward_idle(self, rows: int) -> None:

@@ -264,6 +264,13 @@ def pp_send_hidden(h: torch.Tensor, residual: torch.Tensor) -> None:
     dist.send(torch.stack([h, residual]).contiguous(), dst=st.stage_rank(st.pp_rank + 1))
 
 
+def pp_isend_hidden(h: torch.Tensor, residual: torch.Tensor):
+    """Non-blocking stage-boundary send: (work, buffer); the buffer must stay alive until work.wait()."""
+    st = get_state()
+    buf = torch.stack([h, residual]).contiguous()
+    return dist.isend(buf, dst=st.stage_rank(st.pp_rank + 1)), buf
+
+
 def pp_recv_hidden(num_tokens: int, hidden: int, dtype, device):
     st = get_state()
     buf = torch.empty(2, num_tokens, hidden, dtype=dtype, device=device)

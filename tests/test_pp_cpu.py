@@ -1,6 +1,6 @@
 """Pipeline parallelism on CPU ranks (gloo): layers split into contiguous stages, (hidden, residual) sent
 stage to stage, the last stage's sampled ids broadcast to every rank. Greedy tokens of PP=2 and PP=2 x TP=2
-equal the single-rank run, on every rank."""
+equal the single-rank run, on every rank; decode steps run pipelined in micro-batches."""
 import os
 import socket
 
@@ -29,7 +29,16 @@ def _run(rank, world, port, base, over, tp, pp, q, sp_min_tokens=0):
     from sglang_neuron_b200.engine import Engine
     from sglang_neuron_b200.parallel.state import destroy_parallel
     from sglang_neuron_b200.server_args import ServerArgs
+    from sglang_neuron_b200.models import common
     destroy_parallel()
+    calls = [0]
+    orig = common.CausalLM._forward_pp_microbatched
+
+    def spy(self, fb):
+        calls[0] += 1
+        return orig(self, fb)
+
+    common.CausalLM._forward_pp_microbatched = spy  # counts the micro-batched (overlapped) decode steps
     mc.PRESETS["pp-tiny"] = dict(mc.PRESETS[base], **over)
     eng = Engine(ServerArgs(model="pp-tiny", device="cpu", dtype="float32", tp_size=tp, pp_size=pp,
                             context_length=256, max_running_requests=4, chunked_prefill_size=32,
@@ -37,7 +46,7 @@ def _run(rank, world, port, base, over, tp, pp, q, sp_min_tokens=0):
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, 1000, (n,), generator=g).tolist() for n in (23, 7, 40)]
     outs = eng.generate(prompts, {"max_new_tokens": 6})
-    q.put((rank, [o["output_ids"] for o in outs]))
+    q.put((rank, ([o["output_ids"] for o in outs], calls[0])))
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -61,9 +70,12 @@ def _launch(base, over, tp, pp, sp_min_tokens=0):
 
 @pytest.mark.parametrize("base,over", [("qwen3-0.6b", TINY_QWEN), ("qwen3-30b-a3b", TINY_MOE)])
 def test_pp2_equals_pp1(base, over):
-    one = _launch(base, over, 1, 1)[0]
+    """Decode steps of more than one request run as micro-batches pipelined over the two stages."""
+    one, n1 = _launch(base, over, 1, 1)[0]
     two = _launch(base, over, 1, 2)
-    assert two[0] == one and two[1] == one
+    assert n1 == 0
+    for r in (0, 1):
+        assert two[r][0] == one and two[r][1] > 0, f"rank {r}"
 
 
 @pytest.mark.slow
@@ -71,10 +83,10 @@ def test_pp2_equals_pp1(base, over):
 def test_pp2_tp2_equals_pp1(sp_min_tokens):
     """sp_min_tokens=1: every prefill step sequence-parallel inside each stage; the stage boundary carries
     each TP rank's block of rows."""
-    one = _launch("qwen3-0.6b", TINY_QWEN, 1, 1)[0]
+    one = _launch("qwen3-0.6b", TINY_QWEN, 1, 1)[0][0]
     four = _launch("qwen3-0.6b", TINY_QWEN, 2, 2, sp_min_tokens)
     for r in range(4):
-        assert four[r] == one, f"rank {r}"
+        assert four[r][0] == one and four[r][1] > 0, f"rank {r}"
 
 
 def test_stage_layer_ranges():
