@@ -13,7 +13,6 @@ Parity (reference layer by layer):
 """
 from __future__ import annotations
 
-import math
 from typing import Iterable, List, Optional, Tuple
 
 import torch
