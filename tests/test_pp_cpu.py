@@ -95,3 +95,35 @@ def test_stage_layer_ranges():
     assert [pp_layer_range(7, 3, r) for r in range(3)] == [(0, 3), (3, 5), (5, 7)]
     with pytest.raises(ValueError):
         pp_layer_range(2, 3, 0)
+
+
+def test_slice_decode_rebases_rows():
+    """A decode step's requests [b0, b1) as a step of their own: per-request tensors sliced, the sampled-row
+    index rebased, the split count kept, per-step caches dropped."""
+    from sglang_neuron_b200.model_executor.forward_batch import ForwardBatch, ForwardMode
+    B = 5
+    fb = ForwardBatch(mode=ForwardMode.DECODE, batch_size=B, num_tokens=B, input_ids=torch.arange(B) + 100,
+                      positions=torch.arange(B) + 7, out_cache_loc=torch.arange(B) * 16,
+                      seq_lens=torch.arange(B, dtype=torch.int32) + 8,
+                      block_table=torch.arange(B * 3, dtype=torch.int32).view(B, 3), logits_idx=torch.arange(B),
+                      temperature=torch.rand(B), seeds=torch.arange(B), top_k=torch.zeros(B, dtype=torch.int64),
+                      top_p=torch.ones(B), decode_splits=3)
+    fb.extra.update(num_decode=B, logprob_k=-1, swa_fb="cached")
+    sub = fb.slice_decode(2, 5)
+    assert sub.batch_size == sub.num_tokens == 3 and sub.decode_splits == 3
+    assert torch.equal(sub.input_ids, fb.input_ids[2:]) and torch.equal(sub.block_table, fb.block_table[2:])
+    assert torch.equal(sub.logits_idx, torch.arange(3)) and torch.equal(sub.seq_lens, fb.seq_lens[2:])
+    assert sub.extra == {"num_decode": 3, "logprob_k": -1}
+
+
+def test_replica_sizes_must_cover_the_world():
+    """Replicas of different TP sizes: on one rank a single TP1 replica is the plain layout; sizes that do not
+    add up to the world are refused."""
+    from sglang_neuron_b200.parallel.state import destroy_parallel, initialize_parallel, initialize_replicas
+    st = initialize_replicas([1])
+    assert (st.tp_size, st.tp_rank, st.dp_rank, st.replica_base, st.replica_tp) == (1, 0, 0, 0, (1,))
+    with pytest.raises(ValueError):
+        initialize_replicas([1, 2])
+    with pytest.raises(ValueError):
+        initialize_parallel(2, dp_size=1, replica_tp=[2])
+    destroy_parallel()
